@@ -1,0 +1,475 @@
+#!/usr/bin/env python3
+"""Benchmark of the delta-rule core on B200: prefill and decode tokens/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload deltanet|gdn-decode|deltaproduct2|deltaproduct3|gdn2]
+
+One JSON line on rank 0.  The default workload is BASELINE config 2 (the
+DeltaNet prefill in bf16, B=8 T=4096 H=16 dk=dv=128, chunk 64, fp32 state):
+a "step" is one dc_chunk_fwd over that batch.  With N GPUs (torchrun, one
+rank per GPU) every rank owns its own batch of 8 sequences — batch x head
+sharding with no collective on the data path — so the work per GPU is fixed
+("scaling": "weak") and ``value`` counts the tokens of all ranks.  The decode
+of BASELINE config 3 (256 sequences, H=16, fp32 state, one fused tick per
+step) is measured in the same run and reported under "decode".
+
+Inputs are synthetic (seeded, the configs' recipes) and larger than L2; every
+number is device time from CUDA events on the launching stream, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+H, D, L = 16, 128, 64
+WORKLOADS = {
+    # name: (config index, batch per GPU, tokens, n_householder, gates)
+    "deltanet": (2, 8, 4096, 1, "deltanet"),
+    "deltaproduct2": (4, 4, 8192, 2, "deltaproduct"),
+    "deltaproduct3": (4, 4, 8192, 3, "deltaproduct"),
+    "gdn2": (5, 16, 16384, 1, "gdn2"),
+}
+DECODE = dict(batch=256, heads=16, d=128)
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# Synthetic inputs (the configs' recipes), generated on the device.
+# ---------------------------------------------------------------------------
+def l2n(x):
+    return x / torch.sqrt((x.float() * x.float()).sum(-1, keepdim=True) + 1e-6)
+
+
+def make_prefill(kind, batch, tokens, u, device, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    rn = lambda *s: torch.randn(*s, device=device, generator=g)
+    bf = torch.bfloat16
+    su = tokens * u
+    q = l2n(rn(batch, tokens, H, D)).to(bf)
+    k = l2n(rn(batch, su, H, D)).to(bf)
+    v = rn(batch, su, H, D).to(bf)
+    gate = None
+    if kind == "deltanet":
+        erase = write = torch.sigmoid(rn(batch, su, H, 1))
+    elif kind == "deltaproduct":
+        erase = write = 2 * torch.sigmoid(rn(batch, su, H, 1))
+        a = torch.rand(1, 1, H, 1, device=device, generator=g) * math.log(16.0)
+        gate = (-torch.exp(a) * torch.nn.functional.softplus(rn(batch, tokens, H, 1))).float()
+    elif kind == "gdn2":
+        erase = torch.sigmoid(rn(batch, su, H, D))
+        write = torch.sigmoid(rn(batch, su, H, D))
+        a = torch.rand(1, 1, H, D, device=device, generator=g) * math.log(16.0)
+        gate = (-torch.exp(a) * torch.nn.functional.softplus(rn(batch, tokens, H, D))).float()
+    else:
+        raise ValueError(kind)
+    # The gates stay float32 (one dtype for erase, write and g; g needs it).
+    erase, write = erase.float(), write.float()
+    state = torch.zeros(batch, H, D, D, device=device)
+    return dict(q=q, k=k, v=v, erase=erase.contiguous(), write=write.contiguous(), g=gate, state=state)
+
+
+def make_decode(device, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    b, h, d = DECODE["batch"], DECODE["heads"], DECODE["d"]
+    rn = lambda *s: torch.randn(*s, device=device, generator=g)
+    bf = torch.bfloat16
+    a = torch.rand(1, h, 1, device=device, generator=g) * math.log(16.0)
+    return dict(
+        q=l2n(rn(b, h, d)).to(bf), k=l2n(rn(b, h, d)).to(bf), v=rn(b, h, d).to(bf),
+        erase=torch.sigmoid(rn(b, h, 1)), g=(-torch.exp(a) * torch.nn.functional.softplus(rn(b, h, 1))),
+        state=torch.randn(b, h, d, d, device=device, generator=g) * 0.02,
+    )
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region.
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(self.NAMES, parts[3:7]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# Distributed plumbing (one process per GPU).
+# ---------------------------------------------------------------------------
+def setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle (the reference algorithm restated in C) on the
+# host cores, bounded sample.
+# ---------------------------------------------------------------------------
+def cpu_baseline(workload, budget_s=12.0):
+    import oracle
+
+    _, _, tokens_full, u, kind = WORKLOADS[workload]
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from _inputs import config_inputs
+
+    cfg = {"deltanet": 2, "deltaproduct": 4, "gdn2": 5}[kind]
+    tokens = 256
+    batch = max(1, -(-threads // H))  # enough (batch, head) pairs for every host thread
+    samples = []
+    while True:
+        raw = config_inputs(cfg, rng, batch, tokens, H, D, D, u=u)
+        raw = {k: (None if v is None else v.astype(np.float32)) for k, v in raw.items()}
+        t0 = time.perf_counter()
+        oracle.householder("chunk", raw["q"], raw["k"], raw["v"], raw["erase"], raw["write"], raw["g"],
+                           raw["state"], u, chunk_len=L, dtype=np.float32, threads=threads)
+        dt = time.perf_counter() - t0
+        samples.append((tokens, dt))
+        if dt > budget_s / 4 or tokens >= tokens_full:
+            break
+        tokens = min(tokens_full, tokens * 4)
+    tokens, dt = samples[-1]
+    return {"value": batch * tokens / dt, "unit": "tok/s", "cores": min(threads, batch * H), "kind": "port",
+            "sample": f"oracle chunk path fp32 (chunk 64, OpenMP over heads), B={batch} T={tokens} H={H} d={D}"
+                      f"{' u=' + str(u) if u > 1 else ''}, {dt:.2f} s"}
+
+
+# ---------------------------------------------------------------------------
+# Measurements
+# ---------------------------------------------------------------------------
+def algorithmic_bytes(x, tokens_out):
+    """Bytes a prefill call must move: every input once, y once, the state in and out."""
+    n = sum(t.numel() * t.element_size() for k, t in x.items() if t is not None)
+    n += tokens_out * H * D * 2  # y (bf16)
+    n += x["state"].numel() * 4  # final state
+    return n
+
+
+def time_prefill(dn, x, u, steps, warmup):
+    b, s = x["q"].shape[0], x["q"].shape[1]
+    y = torch.empty(b, s, H, D, device="cuda", dtype=torch.bfloat16)
+    s_out = torch.empty_like(x["state"])
+    gated = x["g"] is not None
+
+    def call():
+        dn.delta_chunk_recalculated(x["q"], x["k"], x["v"], x["erase"], x["write"], x["g"], x["state"],
+                                    gated, L, 1.0 / math.sqrt(D), n_householder=u, y_out=y, state_out=s_out)
+
+    for _ in range(warmup):
+        call()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        call()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def time_prefill_e2e(dn, x, u, steps, warmup):
+    """Through the public API from pinned host buffers: H2D inputs, the kernel,
+    D2H of y and the final state, every step."""
+    host = {k: (None if t is None else t.cpu().pin_memory()) for k, t in x.items()}
+    dev = {k: (None if t is None else torch.empty_like(t)) for k, t in x.items()}
+    b, s = x["q"].shape[0], x["q"].shape[1]
+    y = torch.empty(b, s, H, D, device="cuda", dtype=torch.bfloat16)
+    s_out = torch.empty_like(x["state"])
+    y_host = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+    s_host = torch.empty(s_out.shape, dtype=s_out.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values() if t is not None)
+    d2h = y_host.numel() * 2 + s_host.numel() * 4
+    gated = x["g"] is not None
+
+    def call():
+        for k, t in host.items():
+            if t is not None:
+                dev[k].copy_(t, non_blocking=True)
+        dn.delta_chunk_recalculated(dev["q"], dev["k"], dev["v"], dev["erase"], dev["write"], dev["g"],
+                                    dev["state"], gated, L, 1.0 / math.sqrt(D), n_householder=u,
+                                    y_out=y, state_out=s_out)
+        y_host.copy_(y, non_blocking=True)
+        s_host.copy_(s_out, non_blocking=True)
+
+    for _ in range(warmup):
+        call()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        call()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps, h2d, d2h
+
+
+def time_decode(dn, steps, warmup):
+    """Config 3's decode: one fused tick for 256 sequences x 16 heads per step,
+    the state updated in place; the K ticks replay from one CUDA graph."""
+    x = make_decode("cuda", 1234)
+    y = torch.empty(DECODE["batch"], H, D, device="cuda", dtype=torch.bfloat16)
+    st = x["state"]
+
+    def tick():
+        dn.delta_step(x["q"], x["k"], x["v"], x["erase"], x["erase"], x["g"], st, 1.0 / math.sqrt(D),
+                      y_out=y, state_out=st)
+
+    for _ in range(max(3, warmup)):
+        tick()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(steps):
+                tick()
+    torch.cuda.current_stream().wait_stream(side)
+    graph.replay()  # warm
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    heads = DECODE["batch"] * H
+    step_bytes = heads * (2 * D * D * 4 + 3 * D * 2 + 2 * 4 + D * 2)
+    del graph
+    return ms, step_bytes
+
+
+def run_ours(args):
+    rank, world, local = setup(args.gpus)
+    dn = importlib.import_module("burn-deltanet_b200")
+    hbm_peak, tc_peak, peak_kind = measured_peaks()
+    cfg, batch, tokens, u, kind = WORKLOADS[args.workload]
+    x = make_prefill(kind, batch, tokens, u, "cuda", 1000 + rank)
+    launches = args.steps  # one dc_chunk_fwd kernel per step
+    clocks = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    with clocks:
+        ms = time_prefill(dn, x, u, args.steps, args.warmup)
+    barrier(world)
+    ms = max_over_ranks(ms, world)
+    tok_per_rank = batch * tokens
+    value = tok_per_rank * world / (ms / 1e3)
+    nbytes = algorithmic_bytes(x, batch * tokens)
+    achieved = nbytes / (ms / 1e3) / 1e9
+    ms_e2e, h2d, d2h = time_prefill_e2e(dn, x, u, max(1, min(args.steps, 5)), 1)
+    ms_e2e = max_over_ranks(ms_e2e, world)
+    flops = 2 * (5 * L * D + 3 * D * D) * batch * tokens * u * H
+    dec_ms, dec_bytes = time_decode(dn, 256, args.warmup)
+    dec_ms = max_over_ranks(dec_ms, world)
+    dec_tok = DECODE["batch"] * world / (dec_ms / 1e3)
+    traffic = profiled_traffic(args.workload)
+    line = {
+        "metric": f"prefill tok/s ({kind}, bf16 in, fp32 state, H={H} dk=dv={D}, chunk {L})",
+        "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded, BASELINE config recipes)",
+        "config": {"workload": f"config {cfg}: {kind} prefill B={batch} per GPU, T={tokens}, H={H}, "
+                               f"dk=dv={D}" + (f", u={u}" if u > 1 else ""),
+                   "global_batch": batch * world, "seq_len": tokens, "parallelism": f"batch x head over {world} GPU",
+                   "l2": "inputs larger than L2 (no flush needed)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": nbytes,
+                     "tensor_tflops": flops / (ms / 1e3) / 1e12, "tensor_peak": tc_peak},
+        "e2e": {"value": tok_per_rank * world / (ms_e2e / 1e3), "unit": "tok/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
+        "gpu_launches": launches,
+        "decode": {"metric": "decode tok/s (config 3: GDN step, 256 sequences x 16 heads, fp32 state)",
+                   "value": dec_tok, "unit": "tok/s", "ms_per_step": dec_ms, "steps": 256,
+                   "roofline": {"bound": "hbm", "achieved": dec_bytes / (dec_ms / 1e3) / 1e9, "peak": hbm_peak,
+                                "unit": "GB/s", "frac": dec_bytes / (dec_ms / 1e3) / 1e9 / hbm_peak},
+                   "gpu_launches": 256},
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.workload)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def profiled_traffic(workload):
+    """DRAM bytes per launch of the prefill kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"chunk_fwd_{workload}.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":")[1])
+    return None
+
+
+def run_reference(args):
+    """The reference's algorithm on the host cores: this build cannot compile
+    the Rust reference (no cargo, Burn deps not vendored), so the arm times its
+    C restatement (oracle/), rank 0 only, one bounded sample per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from _inputs import config_inputs
+
+    cfg, batch, tokens, u, kind = WORKLOADS[args.workload]
+    threads = os.cpu_count() or 1
+    sample_tokens = 512
+    sample_batch = max(1, -(-threads // H))  # enough (batch, head) pairs for every host thread
+    rng = np.random.default_rng(0)
+    raw = config_inputs({"deltanet": 2, "deltaproduct": 4, "gdn2": 5}[kind], rng, sample_batch, sample_tokens,
+                        H, D, D, u=u)
+    raw = {k: (None if v is None else v.astype(np.float32)) for k, v in raw.items()}
+
+    def step():
+        oracle.householder("chunk", raw["q"], raw["k"], raw["v"], raw["erase"], raw["write"], raw["g"],
+                           raw["state"], u, chunk_len=L, dtype=np.float32, threads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = sample_batch * sample_tokens / dt
+    line = {
+        "impl": "reference", "metric": f"prefill tok/s ({kind}, bf16 in, fp32 state, H={H} dk=dv={D}, chunk {L})",
+        "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded, BASELINE config recipes)",
+        "config": {"workload": f"config {cfg}: {kind} prefill, sample B={sample_batch} T={sample_tokens} H={H} "
+                               f"dk=dv={D}",
+                   "global_batch": sample_batch, "seq_len": sample_tokens, "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": min(threads, sample_batch * H), "kind": "port",
+                         "sample": f"oracle chunk path fp32 (the reference algorithm restated in C, OpenMP), "
+                                   f"B={sample_batch} T={sample_tokens} H={H} per step"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="deltanet")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,32 @@
+"""B200 (sm_100a) delta-rule core: a drop-in for burn-deltanet's src/delta path.
+
+The package directory name is not a Python identifier; import it with
+``importlib.import_module("burn-deltanet_b200")`` with the repository root on
+``sys.path``.
+
+* ``libdeltacore.so`` — the CUDA kernels behind the C ABI of include/deltacore.h
+  (built in-tree by ``build.py``);
+* :mod:`.core`     — the reference's interface (DeltaInput, DeltaPath, delta_step, ...)
+  over that ABI;
+* :mod:`.sharding` — batch x head partitioning across the GPUs of one node.
+"""
+from . import _abi
+from .core import (
+    DeltaCoreError,
+    DeltaInput,
+    DeltaPath,
+    DeltaShapeError,
+    TriSolve,
+    beta_gates,
+    delta_chunk_recalculated,
+    delta_step,
+)
+
+__all__ = [
+    "DeltaCoreError", "DeltaInput", "DeltaPath", "DeltaShapeError", "TriSolve",
+    "beta_gates", "delta_chunk_recalculated", "delta_step", "library_path",
+]
+
+
+def library_path() -> str:
+    return _abi.LIB_PATH

@@ -1,0 +1,98 @@
+"""ctypes binding of libdeltacore.so (the C ABI declared in include/deltacore.h).
+
+The library is loaded from this package directory and nowhere else.  There is
+no fallback: if the library is missing the import of the binding raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdeltacore.so")
+
+# enum dc_status
+DC_OK = 0
+DC_EINVAL_SHAPE = 1
+DC_EINVAL_WIDTH = 2
+DC_EUNSUPPORTED_DTYPE = 3
+DC_EINVAL_ARG = 4
+DC_EUNSUPPORTED = 5
+DC_ECUDA = 6
+DC_EDEVICE = 7
+
+# enum dc_dtype
+DC_F32 = 0
+DC_BF16 = 1
+
+DC_FLAG_FORCE_SIMT = 0x1
+
+EXPORTS = (
+    "dc_chunk_fwd", "dc_step", "dc_status_string", "dc_last_cuda_error",
+    "dc_chunk_kernel_choice", "dc_chunk_launches", "dc_version",
+)
+
+
+class ChunkArgs(ctypes.Structure):
+    """struct dc_chunk_args."""
+    _fields_ = [
+        ("batch", ctypes.c_int64), ("seq", ctypes.c_int64), ("heads", ctypes.c_int64),
+        ("dk", ctypes.c_int64), ("dv", ctypes.c_int64),
+        ("n_householder", ctypes.c_int32),
+        ("erase_w", ctypes.c_int32), ("write_w", ctypes.c_int32), ("g_w", ctypes.c_int32),
+        ("chunk_len", ctypes.c_int32),
+        ("in_dtype", ctypes.c_int32), ("gate_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32),
+        ("flags", ctypes.c_uint32),
+        ("scale", ctypes.c_double),
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+        ("erase", ctypes.c_void_p), ("write", ctypes.c_void_p), ("g", ctypes.c_void_p),
+        ("state_in", ctypes.c_void_p), ("y", ctypes.c_void_p), ("state_out", ctypes.c_void_p),
+    ]
+
+
+class StepArgs(ctypes.Structure):
+    """struct dc_step_args."""
+    _fields_ = [
+        ("batch", ctypes.c_int64), ("heads", ctypes.c_int64), ("dk", ctypes.c_int64), ("dv", ctypes.c_int64),
+        ("n_householder", ctypes.c_int32),
+        ("erase_w", ctypes.c_int32), ("write_w", ctypes.c_int32), ("g_w", ctypes.c_int32),
+        ("in_dtype", ctypes.c_int32), ("gate_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32),
+        ("flags", ctypes.c_uint32),
+        ("scale", ctypes.c_double),
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+        ("erase", ctypes.c_void_p), ("write", ctypes.c_void_p), ("g", ctypes.c_void_p),
+        ("state_in", ctypes.c_void_p), ("y", ctypes.c_void_p), ("state_out", ctypes.c_void_p),
+    ]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library.  Raises OSError if libdeltacore.so was not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"{LIB_PATH} is missing: build it with `python burn-deltanet_b200/build.py` "
+                          "(the delta-rule core has no CPU fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        L.dc_chunk_fwd.argtypes = [ctypes.POINTER(ChunkArgs), ctypes.c_void_p]
+        L.dc_chunk_fwd.restype = ctypes.c_int
+        L.dc_step.argtypes = [ctypes.POINTER(StepArgs), ctypes.c_void_p]
+        L.dc_step.restype = ctypes.c_int
+        L.dc_status_string.argtypes = [ctypes.c_int]
+        L.dc_status_string.restype = ctypes.c_char_p
+        L.dc_last_cuda_error.argtypes = []
+        L.dc_last_cuda_error.restype = ctypes.c_int
+        L.dc_chunk_kernel_choice.argtypes = [ctypes.POINTER(ChunkArgs)]
+        L.dc_chunk_kernel_choice.restype = ctypes.c_int
+        L.dc_chunk_launches.argtypes = [ctypes.POINTER(ChunkArgs)]
+        L.dc_chunk_launches.restype = ctypes.c_int
+        L.dc_version.argtypes = []
+        L.dc_version.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return lib().dc_status_string(status).decode()

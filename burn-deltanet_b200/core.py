@@ -1,0 +1,346 @@
+"""Host-side mirror of burn-deltanet's delta-rule core interface.
+
+Same names, argument meaning and error behaviour as the reference's
+``src/delta`` public surface (src/delta/mod.rs:132-137), on CUDA tensors:
+
+* :class:`DeltaPath`  — src/delta/path.rs:21-99
+* :class:`TriSolve`   — src/delta/tri.rs:53-64
+* :class:`DeltaInput` — src/delta/path.rs:120-231 (``dims``, ``resolved_scale``,
+  ``has_channel_decay``, ``sanity``, ``run``)
+* :func:`beta_gates`  — src/delta/path.rs:147-150
+* :func:`delta_step`  — src/delta/recurrent.rs:41-99
+* :func:`delta_chunk_recalculated` — the backend-extension op
+  ``DeltaChunkBackendExt::delta_chunk_recalculated``
+  (src/delta/chunk_recalculated/chunk_recalculated.rs:115-126)
+
+Every evaluation goes through the C ABI in libdeltacore.so; the reference's
+``assert!`` panics become :class:`DeltaCoreError` (``DeltaShapeError`` for the
+shape and width checks).  There is no CPU path: CPU tensors are rejected.
+
+One extension over the reference: ``n_householder`` (DeltaProduct's ``u``)
+folds the micro-steps inside the kernel instead of building the zero-padded
+sequence on the host (src/delta_product/delta_product.rs:178-228).  With
+``n_householder == 1`` (the default) the arguments are the reference's.
+"""
+from __future__ import annotations
+
+import enum
+import math
+from dataclasses import dataclass
+from typing import Optional, Tuple
+
+import torch
+
+from . import _abi
+
+
+class DeltaCoreError(RuntimeError):
+    """A status other than DC_OK from the C ABI."""
+
+    def __init__(self, status: int, what: str = ""):
+        self.status = status
+        msg = _abi.status_string(status)
+        if status == _abi.DC_ECUDA:
+            msg += f" (cudaError {_abi.lib().dc_last_cuda_error()})"
+        super().__init__(f"{what}: {msg}" if what else msg)
+
+
+class DeltaShapeError(DeltaCoreError, ValueError):
+    """The shape / width checks of DeltaInput::sanity (src/delta/path.rs:177-208)."""
+
+
+def _raise(status: int, what: str) -> None:
+    if status == _abi.DC_OK:
+        return
+    if status in (_abi.DC_EINVAL_SHAPE, _abi.DC_EINVAL_WIDTH):
+        raise DeltaShapeError(status, what)
+    raise DeltaCoreError(status, what)
+
+
+class TriSolve(enum.Enum):
+    """How (I - N)^-1 is evaluated (src/delta/tri.rs:53-64).  The kernels always
+    substitute; both variants compute the same T and are accepted for parity."""
+    Blocked = "blocked"
+    Neumann = "neumann"
+
+
+@dataclass(frozen=True)
+class DeltaPath:
+    """Which evaluation of the delta rule runs (src/delta/path.rs:21-99).
+
+    ``kind`` is ``"recurrent"``, ``"chunk"`` or ``"chunk_recalculated"`` (the
+    default).  ``Recurrent`` runs the fused step kernel token by token;
+    both chunk kinds run the chunkwise prefill kernel (their forwards are
+    identical in the reference, path.rs:39-45)."""
+    kind: str = "chunk_recalculated"
+    chunk_len: Optional[int] = None
+    solve: TriSolve = TriSolve.Blocked
+
+    DEFAULT_CHUNK_LEN = 64
+
+    @classmethod
+    def Recurrent(cls) -> "DeltaPath":
+        return cls("recurrent", None)
+
+    @classmethod
+    def Chunk(cls, chunk_len: Optional[int] = None, solve: TriSolve = TriSolve.Blocked) -> "DeltaPath":
+        return cls("chunk", chunk_len, solve)
+
+    @classmethod
+    def ChunkRecalculated(cls, chunk_len: Optional[int] = None) -> "DeltaPath":
+        return cls("chunk_recalculated", chunk_len)
+
+    @classmethod
+    def default(cls) -> "DeltaPath":
+        return cls.ChunkRecalculated(None)
+
+    @classmethod
+    def chunk(cls) -> "DeltaPath":
+        return cls.default()
+
+    @classmethod
+    def with_chunk_len(cls, chunk_len: int) -> "DeltaPath":
+        """``DeltaPath::chunk_len`` (path.rs:74-78)."""
+        return cls.ChunkRecalculated(chunk_len)
+
+    @classmethod
+    def chunk_len_on_tape(cls, chunk_len: int) -> "DeltaPath":
+        return cls.Chunk(chunk_len)
+
+    def resolved_chunk_len(self) -> int:
+        if self.kind == "recurrent":
+            return 1
+        return self.chunk_len if self.chunk_len is not None else self.DEFAULT_CHUNK_LEN
+
+
+def _dtype_code(t: torch.Tensor, what: str) -> int:
+    if t.dtype == torch.float32:
+        return _abi.DC_F32
+    if t.dtype == torch.bfloat16:
+        return _abi.DC_BF16
+    raise DeltaCoreError(_abi.DC_EUNSUPPORTED_DTYPE, f"{what} has dtype {t.dtype}")
+
+
+def _check_tensor(t: torch.Tensor, what: str) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{what} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise DeltaCoreError(_abi.DC_EDEVICE, f"{what} is on {t.device}: the delta-rule core runs on CUDA only")
+    if not t.is_contiguous():
+        raise DeltaCoreError(_abi.DC_EINVAL_ARG, f"{what} must be contiguous")
+
+
+def _same_dtype(ts, what: str) -> int:
+    codes = {_dtype_code(t, what) for t in ts if t is not None}
+    if len(codes) != 1:
+        raise DeltaCoreError(_abi.DC_EUNSUPPORTED_DTYPE, f"{what} must share one dtype")
+    return codes.pop()
+
+
+def beta_gates(beta: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The (erase, write) pair a per-head beta stands for (src/delta/path.rs:147-150)."""
+    gate = beta.unsqueeze(-1)
+    return gate, gate
+
+
+def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv,
+                             has_gate: bool, chunk_len: int, scale: float, *, n_householder: int = 1,
+                             out_dtype: Optional[torch.dtype] = None, force_simt: bool = False,
+                             y_out: Optional[torch.Tensor] = None, state_out: Optional[torch.Tensor] = None):
+    """The backend-extension op (chunk_recalculated.rs:115-126) on CUDA tensors.
+
+    Shapes: q [b, s, h, dk]; k [b, s*u, h, dk]; v [b, s*u, h, dv];
+    erase [b, s*u, h, 1|dk]; write [b, s*u, h, 1|dv]; g [b, s, h, 1|dk]
+    (ignored unless ``has_gate``); state [b, h, dk, dv] float32.
+    Returns ``(y [b, s, h, dv], final_state [b, h, dk, dv])`` as new tensors
+    unless ``y_out`` / ``state_out`` are given (``state_out`` may be ``state_bhkv``).
+    """
+    ts = dict(q=q_bshk, k=k_bshk, v=v_bshv, erase=erase_bshK, write=write_bshV, state=state_bhkv)
+    if has_gate:
+        ts["g"] = g_bshK
+    for name, t in ts.items():
+        _check_tensor(t, name)
+    if q_bshk.dim() != 4 or v_bshv.dim() != 4 or state_bhkv.dim() != 4:
+        raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, "q, v and state must be rank 4")
+    b, s, h, dk = q_bshk.shape
+    dv = v_bshv.shape[3]
+    u = int(n_householder)
+    want = {
+        "k": (b, s * u, h, dk), "v": (b, s * u, h, dv), "state": (b, h, dk, dv),
+    }
+    for name, shape in want.items():
+        if tuple(ts[name].shape) != shape:
+            raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, f"{name} has shape {tuple(ts[name].shape)}, want {shape}")
+    for name, rows, full in (("erase", s * u, dk), ("write", s * u, dv)) + ((("g", s, dk),) if has_gate else ()):
+        t = ts[name]
+        if t.dim() != 4 or tuple(t.shape[:3]) != (b, rows, h):
+            raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, f"{name} has shape {tuple(t.shape)}")
+        if t.shape[3] not in (1, full):
+            raise DeltaShapeError(_abi.DC_EINVAL_WIDTH, f"{name}: last axis must be 1 or {full}, got {t.shape[3]}")
+    if state_bhkv.dtype != torch.float32:
+        raise DeltaCoreError(_abi.DC_EUNSUPPORTED_DTYPE, "the state is float32")
+    in_dt = _same_dtype((q_bshk, k_bshk, v_bshv), "q, k, v")
+    gate_dt = _same_dtype((erase_bshK, write_bshV, g_bshK if has_gate else None), "erase, write, g")
+    out_torch = out_dtype or q_bshk.dtype
+    y = y_out if y_out is not None else torch.empty((b, s, h, dv), device=q_bshk.device, dtype=out_torch)
+    s_out = state_out if state_out is not None else torch.empty_like(state_bhkv)
+    a = _abi.ChunkArgs()
+    a.batch, a.seq, a.heads, a.dk, a.dv = b, s, h, dk, dv
+    a.n_householder = u
+    a.erase_w, a.write_w = erase_bshK.shape[3], write_bshV.shape[3]
+    a.g_w = g_bshK.shape[3] if has_gate else 0
+    a.chunk_len = int(chunk_len)
+    a.in_dtype, a.gate_dtype, a.out_dtype = in_dt, gate_dt, _dtype_code(y, "y")
+    a.flags = _abi.DC_FLAG_FORCE_SIMT if force_simt else 0
+    a.scale = float(scale)
+    a.q, a.k, a.v = q_bshk.data_ptr(), k_bshk.data_ptr(), v_bshv.data_ptr()
+    a.erase, a.write = erase_bshK.data_ptr(), write_bshV.data_ptr()
+    a.g = g_bshK.data_ptr() if has_gate else None
+    a.state_in, a.y, a.state_out = state_bhkv.data_ptr(), y.data_ptr(), s_out.data_ptr()
+    with torch.cuda.device(q_bshk.device):
+        stream = torch.cuda.current_stream(q_bshk.device).cuda_stream
+        _raise(_abi.lib().dc_chunk_fwd(a, stream), "dc_chunk_fwd")
+    return y, s_out
+
+
+def delta_step(q_bhk, k_bhk, v_bhv, erase_bhK, write_bhV, g_bhK, state_bhkv, scale: float, *,
+               n_householder: int = 1, out_dtype: Optional[torch.dtype] = None,
+               y_out: Optional[torch.Tensor] = None, state_out: Optional[torch.Tensor] = None):
+    """One delta-rule tick for all heads (src/delta/recurrent.rs:41-99).
+
+    Shapes: q [b, h, dk]; k [b, h, dk] (or [b, u, h, dk] with ``n_householder=u``);
+    v [b, h, dv] (or [b, u, h, dv]); erase [b, h, 1|dk]; write [b, h, 1|dv];
+    g ``None`` or [b, h, 1|dk]; state [b, h, dk, dv] float32.
+    Returns ``(y [b, h, dv], next_state)``; pass ``state_out=state_bhkv`` to
+    update the state in place.
+    """
+    u = int(n_householder)
+    for name, t in dict(q=q_bhk, k=k_bhk, v=v_bhv, erase=erase_bhK, write=write_bhV, state=state_bhkv).items():
+        _check_tensor(t, name)
+    if g_bhK is not None:
+        _check_tensor(g_bhK, "g")
+    if q_bhk.dim() != 3:
+        raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, "q must be [batch, nheads, head_k_dim]")
+    b, h, dk = q_bhk.shape
+    lift = lambda t: t.unsqueeze(1) if t.dim() == 3 else t  # [b, h, .] -> [b, 1, h, .]
+    k4, v4, e4, w4 = (lift(t) for t in (k_bhk, v_bhv, erase_bhK, write_bhV))
+    dv = v4.shape[3]
+    if tuple(k4.shape) != (b, u, h, dk) or tuple(v4.shape[:3]) != (b, u, h):
+        raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, "k / v do not match q and n_householder")
+    if tuple(state_bhkv.shape) != (b, h, dk, dv):
+        raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, f"state has shape {tuple(state_bhkv.shape)}")
+    for name, t, full in (("erase", e4, dk), ("write", w4, dv)):
+        if tuple(t.shape[:3]) != (b, u, h):
+            raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, f"{name} has shape {tuple(t.shape)}")
+        if t.shape[3] not in (1, full):
+            raise DeltaShapeError(_abi.DC_EINVAL_WIDTH, f"{name}: last axis must be 1 or {full}")
+    if g_bhK is not None:
+        if tuple(g_bhK.shape[:2]) != (b, h) or g_bhK.shape[2] not in (1, dk):
+            raise DeltaShapeError(_abi.DC_EINVAL_WIDTH, f"forget gate has shape {tuple(g_bhK.shape)}")
+    if state_bhkv.dtype != torch.float32:
+        raise DeltaCoreError(_abi.DC_EUNSUPPORTED_DTYPE, "the state is float32")
+    in_dt = _same_dtype((q_bhk, k_bhk, v_bhv), "q, k, v")
+    gate_dt = _same_dtype((erase_bhK, write_bhV, g_bhK), "erase, write, g")
+    y = y_out if y_out is not None else torch.empty((b, h, dv), device=q_bhk.device,
+                                                    dtype=out_dtype or q_bhk.dtype)
+    s_out = state_out if state_out is not None else torch.empty_like(state_bhkv)
+    a = _abi.StepArgs()
+    a.batch, a.heads, a.dk, a.dv = b, h, dk, dv
+    a.n_householder = u
+    a.erase_w, a.write_w = e4.shape[3], w4.shape[3]
+    a.g_w = 0 if g_bhK is None else g_bhK.shape[2]
+    a.in_dtype, a.gate_dtype, a.out_dtype = in_dt, gate_dt, _dtype_code(y, "y")
+    a.flags = 0
+    a.scale = float(scale)
+    a.q, a.k, a.v = q_bhk.data_ptr(), k_bhk.data_ptr(), v_bhv.data_ptr()
+    a.erase, a.write = erase_bhK.data_ptr(), write_bhV.data_ptr()
+    a.g = None if g_bhK is None else g_bhK.data_ptr()
+    a.state_in, a.y, a.state_out = state_bhkv.data_ptr(), y.data_ptr(), s_out.data_ptr()
+    with torch.cuda.device(q_bhk.device):
+        stream = torch.cuda.current_stream(q_bhk.device).cuda_stream
+        _raise(_abi.lib().dc_step(a, stream), "dc_step")
+    return y, s_out
+
+
+@dataclass
+class DeltaInput:
+    """Everything the delta-rule core consumes (src/delta/path.rs:120-141).
+
+    q/k arrive activated and L2-normalised but not scaled; gates arrive
+    squashed into their ranges; ``scale=None`` means 1/sqrt(head_k_dim)."""
+    q_bshk: torch.Tensor
+    k_bshk: torch.Tensor
+    v_bshv: torch.Tensor
+    erase_bshK: torch.Tensor
+    write_bshV: torch.Tensor
+    g_bshK: Optional[torch.Tensor]
+    state_bhkv: torch.Tensor
+    scale: Optional[float] = None
+    n_householder: int = 1
+
+    def dims(self):
+        """(batch, sequence, nheads, head_k_dim, head_v_dim) — path.rs:154-158."""
+        b, s, h, dk = self.q_bshk.shape
+        return b, s, h, dk, self.v_bshv.shape[3]
+
+    def resolved_scale(self) -> float:
+        """path.rs:161-165."""
+        return self.scale if self.scale is not None else 1.0 / math.sqrt(self.q_bshk.shape[3])
+
+    def has_channel_decay(self) -> bool:
+        """path.rs:170-172."""
+        return self.g_bshK is not None and self.g_bshK.shape[3] > 1
+
+    def sanity(self) -> None:
+        """Shape and width checks (path.rs:177-208), plus the NaN/Inf guard the
+        reference compiles in under its check-nan/check-inf features."""
+        b, s, h, dk, dv = self.dims()
+        u = self.n_householder
+        if s < 1:
+            raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, "sequence length must be at least 1")
+        if tuple(self.k_bshk.shape) != (b, s * u, h, dk):
+            raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, "k does not match q")
+        if tuple(self.v_bshv.shape[:3]) != (b, s * u, h):
+            raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, "v does not match q")
+        if tuple(self.state_bhkv.shape) != (b, h, dk, dv):
+            raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, "state does not match q / v")
+        gates = [("erase gate", self.erase_bshK, s * u, dk), ("write gate", self.write_bshV, s * u, dv)]
+        if self.g_bshK is not None:
+            gates.append(("forget gate", self.g_bshK, s, dk))
+        for what, t, rows, full in gates:
+            if tuple(t.shape[:3]) != (b, rows, h):
+                raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, what)
+            if t.shape[3] not in (1, full):
+                raise DeltaShapeError(_abi.DC_EINVAL_WIDTH,
+                                      f"{what}: last axis must be 1 or {full}, got {t.shape[3]}")
+
+    def run(self, path: DeltaPath = DeltaPath.default()):
+        """Run the selected algorithm (path.rs:215-231); returns (y_bshv, final_state_bhkv)."""
+        self.sanity()
+        if path.kind != "recurrent":
+            chunk_len = path.resolved_chunk_len()
+            if chunk_len < 1:
+                raise DeltaCoreError(_abi.DC_EINVAL_ARG, "chunk_len must be at least 1")
+            return delta_chunk_recalculated(
+                self.q_bshk, self.k_bshk, self.v_bshv, self.erase_bshK, self.write_bshV, self.g_bshK,
+                self.state_bhkv, self.g_bshK is not None, chunk_len, self.resolved_scale(),
+                n_householder=self.n_householder)
+        return self.delta_recurrent()
+
+    def delta_recurrent(self):
+        """Unroll the fused step over the sequence (src/delta/recurrent.rs:107-142)."""
+        b, s, h, dk, dv = self.dims()
+        u = self.n_householder
+        scale = self.resolved_scale()
+        state = self.state_bhkv.clone()
+        ys = torch.empty((b, s, h, dv), device=self.q_bshk.device, dtype=self.q_bshk.dtype)
+        rows = lambda t: t.view(b, s, u, h, t.shape[3])
+        k, v, e, w = (rows(t) for t in (self.k_bshk, self.v_bshv, self.erase_bshK, self.write_bshV))
+        for t in range(s):
+            y, _ = delta_step(
+                self.q_bshk[:, t].contiguous(), k[:, t].contiguous(), v[:, t].contiguous(),
+                e[:, t].contiguous(), w[:, t].contiguous(),
+                None if self.g_bshK is None else self.g_bshK[:, t].contiguous(),
+                state, scale, n_householder=u, state_out=state)
+            ys[:, t] = y
+        return ys, state

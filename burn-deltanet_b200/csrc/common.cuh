@@ -1,0 +1,29 @@
+// common.cuh — element access and launch parameters shared by the delta-rule kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dc {
+
+__device__ __forceinline__ float ld(const float *p) { return *p; }
+__device__ __forceinline__ float ld(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
+__device__ __forceinline__ void st(float *p, float v) { *p = v; }
+__device__ __forceinline__ void st(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
+
+// Everything a delta-rule kernel reads, in the reference's layouts
+// (src/delta/path.rs:120-141).  `seq` counts tokens; k, v, erase and write
+// carry seq * u rows (the micro-step fold), q and g carry seq rows.
+struct CoreParams {
+    int64_t batch, seq, heads, dk, dv;
+    int32_t u;                 // n_householder
+    int32_t ew, ww, gw;        // gate widths: erase {1, dk}, write {1, dv}, g {0, 1, dk}
+    float scale;
+    const void *q, *k, *v, *erase, *write, *g;
+    const float *state_in;
+    void *y;
+    float *state_out;
+};
+
+}  // namespace dc

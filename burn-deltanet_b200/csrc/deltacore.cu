@@ -1,0 +1,241 @@
+// deltacore.cu — the C ABI (include/deltacore.h): host-side validation and
+// kernel dispatch for the delta-rule core on sm_100a.
+//
+// Validation mirrors the reference's asserts (src/delta/path.rs:177-208,
+// src/delta/recurrent.rs:51-54, path.rs:219) but returns a status code before
+// anything is enqueued instead of panicking.  Nothing here allocates device
+// memory and nothing falls back to the host: an unsupported request is an
+// error, not a slower path.
+#include <math.h>
+#include <stdint.h>
+
+#include <cuda_runtime.h>
+
+#include "../../include/deltacore.h"
+#include "chunk_simt.cuh"
+#include "chunk_tc.cuh"
+#include "common.cuh"
+#include "step.cuh"
+
+namespace {
+
+thread_local int g_last_cuda_error = 0;
+
+int cuda_fail(cudaError_t e) {
+    g_last_cuda_error = (int)e;
+    return DC_ECUDA;
+}
+
+// Whether the current device is an sm_100 part, checked once per device.
+int check_device(int *dev_out) {
+    static int verdict[64];  // 0 unknown, 1 ok, 2 wrong arch
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev_out) *dev_out = dev;
+    if (dev >= 0 && dev < 64 && verdict[dev]) return verdict[dev] == 1 ? DC_OK : DC_EDEVICE;
+    int major = 0, minor = 0;
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    const int ok = (major == 10 && minor == 0);
+    if (dev >= 0 && dev < 64) verdict[dev] = ok ? 1 : 2;
+    return ok ? DC_OK : DC_EDEVICE;
+}
+
+bool valid_dtype(int32_t t) { return t == DC_F32 || t == DC_BF16; }
+size_t dtype_size(int32_t t) { return t == DC_F32 ? 4 : 2; }
+bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+// Shared checks of the two entry points.  `rows` is the number of token rows
+// of q, g and y (seq for the prefill, 1 for the step).
+int validate_common(int64_t batch, int64_t rows, int64_t heads, int64_t dk, int64_t dv, int32_t u,
+                    int32_t ew, int32_t ww, int32_t gw, int32_t in_dt, int32_t gate_dt, int32_t out_dt,
+                    double scale, const void *q, const void *k, const void *v, const void *erase,
+                    const void *write, const void *g, const float *s_in, const void *y, const float *s_out) {
+    if (batch < 0 || heads < 0 || dk < 1 || dv < 1 || rows < 1) return DC_EINVAL_SHAPE;
+    if (!(ew == 1 || ew == dk)) return DC_EINVAL_WIDTH;
+    if (!(ww == 1 || ww == dv)) return DC_EINVAL_WIDTH;
+    if (!(gw == 0 || gw == 1 || gw == dk)) return DC_EINVAL_WIDTH;
+    if (!valid_dtype(in_dt) || !valid_dtype(gate_dt) || !valid_dtype(out_dt)) return DC_EUNSUPPORTED_DTYPE;
+    if (u < 1) return DC_EINVAL_ARG;
+    if (!isfinite(scale)) return DC_EINVAL_ARG;
+    if (dk > dc::kMaxDk || u > dc::kMaxHouseholder) return DC_EUNSUPPORTED;
+    if (batch == 0 || heads == 0) return DC_OK;  // empty: nothing to do
+    if (!q || !k || !v || !erase || !write || !s_in || !y || !s_out) return DC_EINVAL_ARG;
+    if (gw != 0 && !g) return DC_EINVAL_ARG;
+    const size_t is = dtype_size(in_dt), gs = dtype_size(gate_dt), os = dtype_size(out_dt);
+    if (!aligned(q, is) || !aligned(k, is) || !aligned(v, is)) return DC_EINVAL_ARG;
+    if (!aligned(erase, gs) || !aligned(write, gs) || (g && !aligned(g, gs))) return DC_EINVAL_ARG;
+    if (!aligned(y, os) || !aligned(s_in, 4) || !aligned(s_out, 4)) return DC_EINVAL_ARG;
+    // Outputs must not alias inputs (state_out == state_in is the one allowed in-place update).
+    const void *ins[] = {q, k, v, erase, write, g};
+    for (const void *in : ins)
+        if (in && (in == y || in == (const void *)s_out)) return DC_EINVAL_ARG;
+    if ((const void *)y == (const void *)s_in || (const void *)y == (const void *)s_out) return DC_EINVAL_ARG;
+    return DC_OK;
+}
+
+dc::CoreParams make_params(int64_t batch, int64_t seq, int64_t heads, int64_t dk, int64_t dv, int32_t u,
+                           int32_t ew, int32_t ww, int32_t gw, double scale, const void *q, const void *k,
+                           const void *v, const void *erase, const void *write, const void *g,
+                           const float *s_in, void *y, float *s_out) {
+    dc::CoreParams p;
+    p.batch = batch; p.seq = seq; p.heads = heads; p.dk = dk; p.dv = dv;
+    p.u = u; p.ew = ew; p.ww = ww; p.gw = gw;
+    p.scale = (float)scale;
+    p.q = q; p.k = k; p.v = v; p.erase = erase; p.write = write; p.g = gw ? g : nullptr;
+    p.state_in = s_in; p.y = y; p.state_out = s_out;
+    return p;
+}
+
+// ---------------------------------------------------------------------------
+// Decode
+// ---------------------------------------------------------------------------
+template <typename TI, typename TG, typename TO, int VEC, int CW, int NP>
+int launch_step_cfg(const dc::CoreParams &p, cudaStream_t stream) {
+    const dim3 grid((unsigned)(p.batch * p.heads), (unsigned)((p.dv + CW - 1) / CW));
+    const size_t smem = dc::step_smem_bytes((int)p.dk, p.u, CW);
+    dc::step_kernel<TI, TG, TO, VEC, CW, NP><<<grid, dc::kStepThreads, smem, stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? DC_OK : cuda_fail(e);
+}
+
+template <typename TI, typename TG, typename TO>
+int launch_step_typed(const dc::CoreParams &p, cudaStream_t stream) {
+    const bool vec4 = (p.dv % 4 == 0) && aligned(p.state_in, 16) && aligned(p.state_out, 16);
+    if (vec4) {
+        if (p.dk <= 128) return launch_step_cfg<TI, TG, TO, 4, 64, 16>(p, stream);
+        return launch_step_cfg<TI, TG, TO, 4, 32, 16>(p, stream);
+    }
+    if (p.dk <= 128) return launch_step_cfg<TI, TG, TO, 1, 16, 16>(p, stream);
+    return launch_step_cfg<TI, TG, TO, 1, 8, 16>(p, stream);
+}
+
+template <template <typename, typename, typename> class F, typename... A>
+int dispatch_types(int32_t in_dt, int32_t gate_dt, int32_t out_dt, A &&...args) {
+    using f32 = float;
+    using b16 = __nv_bfloat16;
+    const int key = in_dt * 4 + gate_dt * 2 + out_dt;
+    switch (key) {
+        case 0: return F<f32, f32, f32>::run(args...);
+        case 1: return F<f32, f32, b16>::run(args...);
+        case 2: return F<f32, b16, f32>::run(args...);
+        case 3: return F<f32, b16, b16>::run(args...);
+        case 4: return F<b16, f32, f32>::run(args...);
+        case 5: return F<b16, f32, b16>::run(args...);
+        case 6: return F<b16, b16, f32>::run(args...);
+        case 7: return F<b16, b16, b16>::run(args...);
+    }
+    return DC_EUNSUPPORTED_DTYPE;
+}
+
+template <typename TI, typename TG, typename TO>
+struct StepLauncher {
+    static int run(const dc::CoreParams &p, cudaStream_t s) { return launch_step_typed<TI, TG, TO>(p, s); }
+};
+
+// ---------------------------------------------------------------------------
+// Prefill
+// ---------------------------------------------------------------------------
+template <typename TI, typename TG, typename TO, int LC>
+int launch_simt_cfg(const dc::CoreParams &p, int cw, cudaStream_t stream) {
+    const dc::SimtLayout ly((int)p.dk, cw, LC, p.gw);
+    const size_t smem = sizeof(float) * (size_t)ly.total;
+    auto kern = dc::chunk_simt_kernel<TI, TG, TO, LC>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e);
+    const dim3 grid((unsigned)(p.batch * p.heads), (unsigned)((p.dv + cw - 1) / cw));
+    kern<<<grid, dc::kSimtThreads, smem, stream>>>(p, cw);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? DC_OK : cuda_fail(e);
+}
+
+template <typename TI, typename TG, typename TO>
+struct SimtLauncher {
+    static int run(const dc::CoreParams &p, cudaStream_t s) {
+        if (p.dk <= 128) return launch_simt_cfg<TI, TG, TO, 32>(p, (int)(p.dv < 64 ? p.dv : 64), s);
+        return launch_simt_cfg<TI, TG, TO, 16>(p, (int)(p.dv < 32 ? p.dv : 32), s);
+    }
+};
+
+int validate_chunk(const dc_chunk_args *a) {
+    if (!a) return DC_EINVAL_ARG;
+    if (a->chunk_len < 1) return DC_EINVAL_ARG;
+    return validate_common(a->batch, a->seq, a->heads, a->dk, a->dv, a->n_householder, a->erase_w, a->write_w,
+                           a->g_w, a->in_dtype, a->gate_dtype, a->out_dtype, a->scale, a->q, a->k, a->v,
+                           a->erase, a->write, a->g, a->state_in, a->y, a->state_out);
+}
+
+int validate_step(const dc_step_args *a) {
+    if (!a) return DC_EINVAL_ARG;
+    return validate_common(a->batch, 1, a->heads, a->dk, a->dv, a->n_householder, a->erase_w, a->write_w, a->g_w,
+                           a->in_dtype, a->gate_dtype, a->out_dtype, a->scale, a->q, a->k, a->v, a->erase,
+                           a->write, a->g, a->state_in, a->y, a->state_out);
+}
+
+}  // namespace
+
+extern "C" {
+
+int dc_version(void) { return 100; }
+
+const char *dc_status_string(int status) {
+    switch (status) {
+        case DC_OK: return "ok";
+        case DC_EINVAL_SHAPE: return "invalid shape";
+        case DC_EINVAL_WIDTH: return "gate width must be 1 or the full channel count";
+        case DC_EUNSUPPORTED_DTYPE: return "unsupported dtype";
+        case DC_EINVAL_ARG: return "invalid argument";
+        case DC_EUNSUPPORTED: return "unsupported size (dk > 256 or n_householder > 8)";
+        case DC_ECUDA: return "CUDA error";
+        case DC_EDEVICE: return "current device is not an sm_100 GPU";
+    }
+    return "unknown status";
+}
+
+int dc_last_cuda_error(void) { return g_last_cuda_error; }
+
+int dc_chunk_kernel_choice(const dc_chunk_args *a) {
+    const int st = validate_chunk(a);
+    if (st != DC_OK) return -st;
+    return dc::tc_applies(a->dk, a->dv, a->in_dtype, a->flags) ? 1 : 0;
+}
+
+int dc_chunk_launches(const dc_chunk_args *a) {
+    const int st = validate_chunk(a);
+    if (st != DC_OK) return -st;
+    return (a->batch == 0 || a->heads == 0) ? 0 : 1;
+}
+
+int dc_chunk_fwd(const dc_chunk_args *a, dc_stream_t stream) {
+    int st = validate_chunk(a);
+    if (st != DC_OK || a->batch == 0 || a->heads == 0) return st;
+    st = check_device(nullptr);
+    if (st != DC_OK) return st;
+    const dc::CoreParams p = make_params(a->batch, a->seq, a->heads, a->dk, a->dv, a->n_householder, a->erase_w,
+                                         a->write_w, a->g_w, a->scale, a->q, a->k, a->v, a->erase, a->write, a->g,
+                                         a->state_in, a->y, a->state_out);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (dc::tc_applies(a->dk, a->dv, a->in_dtype, a->flags)) {
+        st = dc::launch_chunk_tc(p, a->gate_dtype, a->out_dtype, s);
+        if (st == DC_ECUDA) g_last_cuda_error = dc::tc_last_error();
+        return st;
+    }
+    return dispatch_types<SimtLauncher>(a->in_dtype, a->gate_dtype, a->out_dtype, p, s);
+}
+
+int dc_step(const dc_step_args *a, dc_stream_t stream) {
+    int st = validate_step(a);
+    if (st != DC_OK || a->batch == 0 || a->heads == 0) return st;
+    st = check_device(nullptr);
+    if (st != DC_OK) return st;
+    const dc::CoreParams p = make_params(a->batch, 1, a->heads, a->dk, a->dv, a->n_householder, a->erase_w,
+                                         a->write_w, a->g_w, a->scale, a->q, a->k, a->v, a->erase, a->write, a->g,
+                                         a->state_in, a->y, a->state_out);
+    return dispatch_types<StepLauncher>(a->in_dtype, a->gate_dtype, a->out_dtype, p,
+                                        reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,154 @@
+/*
+ * deltacore.h — C ABI of the B200 (sm_100a) delta-rule core.
+ *
+ * A drop-in for the two device entry points of burn-deltanet's shared
+ * delta-rule core (src/delta):
+ *
+ *   dc_chunk_fwd  replaces  DeltaChunkBackendExt::delta_chunk_recalculated
+ *                           (src/delta/chunk_recalculated/chunk_recalculated.rs:105-151),
+ *                           the chunkwise WY prefill forward every family's
+ *                           `forward` reaches through DeltaInput::run
+ *                           (src/delta/path.rs:215-231).
+ *   dc_step       replaces  delta_step (src/delta/recurrent.rs:41-99), the
+ *                           decode tick every family's `step` calls, and the
+ *                           u-micro-step recurrence of DeltaProduct / GDN-2
+ *                           decode (src/delta/recurrent.rs:107-142 on the
+ *                           sequence built at src/delta_product/delta_product.rs:270-305).
+ *
+ * Layouts are the reference's (src/delta/path.rs:120-141), row-major and
+ * contiguous, on the CUDA device that is current when the call is made:
+ *   q            [batch, seq, heads, dk]
+ *   k            [batch, seq*u, heads, dk]       u = n_householder
+ *   v            [batch, seq*u, heads, dv]
+ *   erase        [batch, seq*u, heads, erase_w]  erase_w in {1, dk}
+ *   write        [batch, seq*u, heads, write_w]  write_w in {1, dv}
+ *   g            [batch, seq, heads, g_w]        g_w in {0 (no gate), 1, dk}
+ *   state_in/out [batch, heads, dk, dv]          float32 always
+ *   y            [batch, seq, heads, dv]
+ * With u > 1 the micro-step fold of DeltaProduct / GDN-2 runs inside the
+ * kernel: token t's u micro-steps use rows t*u .. t*u+u-1 of k, v, erase and
+ * write; q is read on the last micro-step and g applied on the first, and y
+ * holds the last micro-step's readout (src/delta_product/delta_product.rs:178-228).
+ * With u == 1 this is exactly the reference op's argument list.
+ *
+ * Ownership and threading: the caller owns every buffer; nothing is
+ * allocated, nothing is freed.  The call validates on the host, enqueues the
+ * kernel(s) on `stream` and returns; it is asynchronous like every Burn
+ * device op.  state_out may alias state_in (in-place update); no other
+ * output may alias an input.  Calls on different streams are independent.
+ *
+ * Errors: the reference panics (assert!) on shape and width violations
+ * (src/delta/path.rs:177-208, chunk_recalculated.rs:74-78,
+ * recurrent.rs:51-54).  Here the same checks return a status code before
+ * anything is enqueued.
+ */
+#ifndef DELTACORE_H
+#define DELTACORE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define DC_API __attribute__((visibility("default")))
+#else
+#define DC_API
+#endif
+
+/* Binary-compatible with cudaStream_t / CUstream (NULL = the legacy default stream). */
+typedef struct CUstream_st *dc_stream_t;
+
+enum dc_status {
+    DC_OK = 0,
+    DC_EINVAL_SHAPE = 1,       /* a dimension is inconsistent (e.g. seq == 0, path.rs:179) */
+    DC_EINVAL_WIDTH = 2,       /* a gate's last axis is not 1 / full (path.rs:187-195) */
+    DC_EUNSUPPORTED_DTYPE = 3, /* dtype code not in dc_dtype */
+    DC_EINVAL_ARG = 4,         /* null pointer, chunk_len < 1 (path.rs:219), n_householder < 1,
+                                  non-finite scale, misaligned pointer, aliasing outputs */
+    DC_EUNSUPPORTED = 5,       /* beyond this build's limits: dk > 256 or n_householder > 8 */
+    DC_ECUDA = 6,              /* a CUDA runtime call failed: see dc_last_cuda_error() */
+    DC_EDEVICE = 7             /* the current device is not an sm_100 (B200-class) GPU */
+};
+
+enum dc_dtype {
+    DC_F32 = 0,
+    DC_BF16 = 1
+};
+
+/* dc_chunk_args.flags */
+#define DC_FLAG_FORCE_SIMT 0x1u /* run the CUDA-core chunk kernel even where the tensor-core one applies */
+
+/*
+ * Chunkwise prefill.  Mirrors
+ *   fn delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK,
+ *                               state_bhkv, has_gate: bool, chunk_len: usize, scale: f64)
+ *       -> (y_bshv, final_state_bhkv)
+ * (src/delta/chunk_recalculated/chunk_recalculated.rs:115-126); has_gate is g_w != 0.
+ * `scale` is already resolved (1/sqrt(dk) is the reference default, path.rs:161-165).
+ * `chunk_len` is validated (>= 1) and, as in the reference, does not change the
+ * result (src/delta/tests.rs:340-363): the kernels pick their own tile length.
+ */
+typedef struct dc_chunk_args {
+    int64_t batch, seq, heads, dk, dv;
+    int32_t n_householder;
+    int32_t erase_w, write_w, g_w;
+    int32_t chunk_len;
+    int32_t in_dtype;   /* q, k, v: DC_F32 or DC_BF16 */
+    int32_t gate_dtype; /* erase, write, g */
+    int32_t out_dtype;  /* y */
+    uint32_t flags;
+    double scale;
+    const void *q, *k, *v, *erase, *write, *g;
+    const float *state_in;
+    void *y;
+    float *state_out;
+} dc_chunk_args;
+
+DC_API int dc_chunk_fwd(const dc_chunk_args *args, dc_stream_t stream);
+
+/*
+ * One decode token for every (batch, head).  Mirrors
+ *   fn delta_step(q_bhk, k_bhk, v_bhv, erase_bhK, write_bhV, g_bhK: Option<_>,
+ *                 state_bhkv, scale: f64) -> (y_bhv, next_state_bhkv)
+ * (src/delta/recurrent.rs:41-50), with n_householder micro-steps folded in:
+ *   q [batch, heads, dk]; k, v, erase, write [batch, u, heads, .]; g [batch, heads, g_w].
+ * The state is read once and written once per call however large u is.
+ */
+typedef struct dc_step_args {
+    int64_t batch, heads, dk, dv;
+    int32_t n_householder;
+    int32_t erase_w, write_w, g_w;
+    int32_t in_dtype, gate_dtype, out_dtype;
+    uint32_t flags;
+    double scale;
+    const void *q, *k, *v, *erase, *write, *g;
+    const float *state_in;
+    void *y;
+    float *state_out;
+} dc_step_args;
+
+DC_API int dc_step(const dc_step_args *args, dc_stream_t stream);
+
+/* Human-readable name of a dc_status. */
+DC_API const char *dc_status_string(int status);
+
+/* The cudaError_t behind the most recent DC_ECUDA returned on this thread (0 if none). */
+DC_API int dc_last_cuda_error(void);
+
+/* Which chunk kernel dc_chunk_fwd would launch for `args`: 1 = tensor-core (tcgen05),
+ * 0 = CUDA-core; negative = the dc_status the call would return. Pure host logic. */
+DC_API int dc_chunk_kernel_choice(const dc_chunk_args *args);
+
+/* Number of kernels dc_chunk_fwd / dc_step enqueue per call (for launch accounting). */
+DC_API int dc_chunk_launches(const dc_chunk_args *args);
+
+/* ABI version: major * 10000 + minor * 100 + patch. */
+DC_API int dc_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DELTACORE_H */

@@ -1,0 +1,153 @@
+"""The C ABI without a GPU: the library loads, exports every symbol
+include/deltacore.h declares, its structs match the header's layout, and the
+host-side validation (the reference's asserts, src/delta/path.rs:177-208)
+returns the documented status codes before anything touches a device."""
+import ctypes
+import importlib
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+dn = importlib.import_module("burn-deltanet_b200")
+abi = importlib.import_module("burn-deltanet_b200._abi")
+
+
+def header_functions():
+    text = open(os.path.join(ROOT, "include", "deltacore.h")).read()
+    return re.findall(r"DC_API\s+[\w\s\*]+?\b(dc_\w+)\s*\(", text)
+
+
+def test_library_exports_every_declared_symbol():
+    declared = header_functions()
+    assert set(declared) >= {"dc_chunk_fwd", "dc_step"}
+    lib = ctypes.CDLL(abi.LIB_PATH)
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert set(abi.EXPORTS) >= set(declared)
+
+
+def test_version_and_status_strings():
+    lib = abi.lib()
+    assert lib.dc_version() >= 100
+    for code in range(8):
+        assert abi.status_string(code)
+    assert lib.dc_last_cuda_error() == 0
+
+
+def test_struct_layout_matches_the_header(tmp_path):
+    """ctypes offsets equal what a C compiler gives the header's structs."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    fields = {
+        "dc_chunk_args": [f for f, _ in abi.ChunkArgs._fields_],
+        "dc_step_args": [f for f, _ in abi.StepArgs._fields_],
+    }
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "deltacore.h"', "int main(void) {"]
+    for st, names in fields.items():
+        lines.append(f'printf("{st} sizeof %zu\\n", sizeof({st}));')
+        for n in names:
+            lines.append(f'printf("{st} {n} %zu\\n", offsetof({st}, {n}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    want = {tuple(l.split()[:2]): int(l.split()[2]) for l in out if l}
+    for st, cls in (("dc_chunk_args", abi.ChunkArgs), ("dc_step_args", abi.StepArgs)):
+        assert want[(st, "sizeof")] == ctypes.sizeof(cls)
+        for n, _ in cls._fields_:
+            assert want[(st, n)] == getattr(cls, n).offset, (st, n)
+
+
+def _args(**over):
+    a = abi.ChunkArgs()
+    a.batch, a.seq, a.heads, a.dk, a.dv = 2, 9, 2, 4, 6
+    a.n_householder, a.erase_w, a.write_w, a.g_w, a.chunk_len = 1, 1, 1, 1, 64
+    a.in_dtype = a.gate_dtype = a.out_dtype = abi.DC_F32
+    a.scale = 0.5
+    fake = 0x10000  # never dereferenced: validation fails or passes before any device work
+    a.q, a.k, a.v, a.erase, a.write, a.g = fake, fake + 256, fake + 512, fake + 768, fake + 1024, fake + 1280
+    a.state_in, a.y, a.state_out = fake + 2048, fake + 4096, fake + 8192
+    for k, v in over.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize(
+    "over,status",
+    [
+        (dict(seq=0), abi.DC_EINVAL_SHAPE),            # path.rs:179 sequence > 0
+        (dict(dk=0), abi.DC_EINVAL_SHAPE),
+        (dict(erase_w=3), abi.DC_EINVAL_WIDTH),        # path.rs:187-195
+        (dict(write_w=4), abi.DC_EINVAL_WIDTH),
+        (dict(g_w=2), abi.DC_EINVAL_WIDTH),
+        (dict(chunk_len=0), abi.DC_EINVAL_ARG),        # path.rs:219 chunk_len >= 1
+        (dict(n_householder=0), abi.DC_EINVAL_ARG),
+        (dict(scale=float("nan")), abi.DC_EINVAL_ARG),
+        (dict(in_dtype=7), abi.DC_EUNSUPPORTED_DTYPE),
+        (dict(q=None), abi.DC_EINVAL_ARG),
+        (dict(g=None), abi.DC_EINVAL_ARG),             # gated without a gate
+        (dict(y=0x10000), abi.DC_EINVAL_ARG),          # output aliases an input
+        (dict(q=0x10001), abi.DC_EINVAL_ARG),          # misaligned
+        (dict(dk=512, erase_w=1), abi.DC_EUNSUPPORTED),
+        (dict(n_householder=9), abi.DC_EUNSUPPORTED),
+    ],
+)
+def test_validation_status_codes(over, status):
+    a = _args(**over)
+    assert abi.lib().dc_chunk_fwd(a, None) == status
+    assert abi.lib().dc_chunk_kernel_choice(a) == -status
+
+
+def test_empty_batch_is_a_no_op():
+    assert abi.lib().dc_chunk_fwd(_args(batch=0), None) == abi.DC_OK
+    assert abi.lib().dc_chunk_launches(_args(batch=0)) == 0
+
+
+def test_kernel_choice_is_host_logic():
+    assert abi.lib().dc_chunk_kernel_choice(_args()) == 0  # f32, dk=4: CUDA-core kernel
+    a = _args(dk=128, dv=128, in_dtype=abi.DC_BF16, flags=abi.DC_FLAG_FORCE_SIMT)
+    assert abi.lib().dc_chunk_kernel_choice(a) == 0
+
+
+def test_step_validation():
+    s = abi.StepArgs()
+    s.batch, s.heads, s.dk, s.dv = 2, 2, 4, 6
+    s.n_householder, s.erase_w, s.write_w, s.g_w = 1, 1, 5, 0
+    s.scale = 0.5
+    s.q = s.k = s.v = s.erase = s.write = 0x10000
+    s.state_in = s.state_out = 0x20000
+    s.y = 0x30000
+    assert abi.lib().dc_step(s, None) == abi.DC_EINVAL_WIDTH
+
+
+def test_python_mirror_rejects_cpu_tensors():
+    import torch
+    q = torch.zeros(1, 2, 1, 4)
+    inp = dn.DeltaInput(q, q, torch.zeros(1, 2, 1, 6), torch.zeros(1, 2, 1, 1), torch.zeros(1, 2, 1, 1),
+                        None, torch.zeros(1, 1, 4, 6))
+    with pytest.raises(dn.DeltaCoreError):
+        inp.run()
+
+
+def test_python_mirror_sanity_mirrors_the_reference_asserts():
+    import torch
+    q = torch.zeros(1, 2, 1, 4)
+    bad = dn.DeltaInput(q, q, torch.zeros(1, 2, 1, 6), torch.zeros(1, 2, 1, 3), torch.zeros(1, 2, 1, 1),
+                        None, torch.zeros(1, 1, 4, 6))
+    with pytest.raises(dn.DeltaShapeError):
+        bad.sanity()
+    empty = dn.DeltaInput(torch.zeros(1, 0, 1, 4), torch.zeros(1, 0, 1, 4), torch.zeros(1, 0, 1, 6),
+                          torch.zeros(1, 0, 1, 1), torch.zeros(1, 0, 1, 1), None, torch.zeros(1, 1, 4, 6))
+    with pytest.raises(dn.DeltaShapeError):
+        empty.sanity()
+    assert dn.DeltaPath.default().resolved_chunk_len() == 64
+    assert dn.DeltaPath.Recurrent().resolved_chunk_len() == 1
+    assert dn.DeltaPath.with_chunk_len(16).resolved_chunk_len() == 16

@@ -28,7 +28,7 @@ DC_BF16 = 1
 DC_FLAG_FORCE_SIMT = 0x1
 
 EXPORTS = (
-    "dc_chunk_fwd", "dc_step", "dc_status_string", "dc_last_cuda_error",
+    "dc_chunk_fwd", "dc_step", "dc_status_string", "dc_last_cuda_error", "dc_device_status",
     "dc_chunk_kernel_choice", "dc_chunk_launches", "dc_version",
 )
 
@@ -84,6 +84,8 @@ def lib() -> ctypes.CDLL:
         L.dc_status_string.restype = ctypes.c_char_p
         L.dc_last_cuda_error.argtypes = []
         L.dc_last_cuda_error.restype = ctypes.c_int
+        L.dc_device_status.argtypes = [ctypes.c_int]
+        L.dc_device_status.restype = ctypes.c_int
         L.dc_chunk_kernel_choice.argtypes = [ctypes.POINTER(ChunkArgs)]
         L.dc_chunk_kernel_choice.restype = ctypes.c_int
         L.dc_chunk_launches.argtypes = [ctypes.POINTER(ChunkArgs)]

@@ -1,18 +1,700 @@
-// chunk_tc.cuh — tensor-core (tcgen05) chunkwise WY prefill for bf16 inputs.
+// chunk_tc.cuh — the tensor-core (tcgen05 / TMEM / TMA) chunkwise WY prefill.
+//
+// Serves dc_chunk_fwd for bf16 q/k/v with dk = dv = 128 and per-head gates
+// (the DeltaNet and Gated DeltaNet families).  One CTA owns one (batch, head)
+// and walks its chunks of L = 64 steps serially; the fp32 state S lives in
+// tensor memory for the whole sequence and never touches HBM in between.
+//
+// Per chunk (rows i, j in [0, 64); G = chunk cumsum of g, gam_i = e^{G_i}):
+//
+//   D1   = [K; Q] K^T                                   M=128 N=64  K=128   (tcgen05)
+//   Akk  = tril(e_i (k_i.k_j) e^{G_i-G_j}, -1)           fp32, shared memory (CUDA cores)
+//   Aqk  = tril(s (q_i.k_j) e^{G_i-G_j}, 0)              bf16 operand
+//   T    = (I + Akk)^-1                                  blocked 16x16 forward substitution
+//   Tb   = T diag(w),  Tw = T diag(e gam)                bf16 operands
+//   D_P  = Aqk [Tb | Tw]                                 M=64  N=128 K=64    (tcgen05)
+//   D_UY = [Tb; Aqk Tb] V      = [U; Aqk U]              M=128 N=128 K=64    (tcgen05)
+//   D_W  = [Tw; Aqk Tw] K      = [W; Aqk W]              M=128 N=128 K=64    (tcgen05)
+//   A6   = [-W; s gam Q - Aqk W]                         bf16 operand
+//   D_UY += A6 S               = [U - W S; y]            M=128 N=128 K=128   (tcgen05)
+//   D_S  = Gam S + K^T diag(e^{G_63 - G_j}) V'           M=128 N=128 K=64    (tcgen05, accumulate)
+//
+// The second-to-last line is the reference's scan step (src/delta/chunk.rs:
+// 177-187) with its two S products stacked into one M=128 MMA: V' = U - W S
+// comes out in the top 64 TMEM lanes and y = (s gam Q) S + Aqk V' =
+// (s gam Q - Aqk W) S + Aqk U in the bottom 64, because Aqk U and Aqk W are
+// S-independent and are formed before S is needed.  The last line is
+// chunk.rs:191-202 with the per-row decay folded into V'.
+//
+// Operand layouts in shared memory are the 128-byte-swizzled canonical ones
+// (8 rows x 128 B atoms): tiles written by TMA with CU_TENSOR_MAP_SWIZZLE_128B
+// and tiles written by threads through ptx::sw128 share one pattern, so the
+// same bytes serve as a K-major operand of one MMA and an MN-major operand of
+// another (K is both the A of D1 and the B of D_W / the A of D_S).
+//
+// Every mbarrier wait is bounded (ptx::kWaitLimitNs); a wait that runs out
+// sets the library's device status word, waits (bounded) for its own TMA loads
+// still in flight, frees its tensor memory and returns.
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace dc {
 
-// Whether the tensor-core kernel serves this request.
-inline bool tc_applies(int64_t dk, int64_t dv, int32_t in_dtype, uint32_t flags) {
-    (void)dk; (void)dv; (void)in_dtype; (void)flags;
-    return false;
+// Device status word written by kernels whose bounded waits run out (0 = ok).
+__device__ int g_device_status;
+constexpr int kStatusTimeout = 1;
+
+namespace tc {
+
+constexpr int kThreads = 256;
+constexpr int kL = 64;    // chunk rows
+constexpr int kD = 128;   // dk = dv
+
+// Shared-memory map (bytes from a 1024-aligned base).
+constexpr uint32_t kStageBytes = 49152;                 // [K|Q d0-63][K|Q d64-127][V d0-63][V d64-127]
+constexpr uint32_t OFF_STAGE = 0;                       // two stages
+constexpr uint32_t OFF_AU = 2 * kStageBytes;            // [Tb; Pb] 128x64 bf16 K-major; A6 block 0
+constexpr uint32_t OFF_AW = OFF_AU + 16384;             // [Tw; Pw];                     A6 block 1
+constexpr uint32_t OFF_S = OFF_AW + 16384;              // S bf16, MN-major, two 64-column blocks of 16 KB
+constexpr uint32_t OFF_AQK = OFF_S + 32768;             // Aqk bf16 64x64 K-major
+constexpr uint32_t OFF_AF = OFF_AQK + 8192;             // Akk fp32 [64][65]; later V' operand (2 x 8 KB)
+constexpr uint32_t OFF_TF = OFF_AF + 64 * 65 * 4;       // T fp32 [64][65]
+constexpr uint32_t OFF_X = OFF_TF + 64 * 65 * 4;        // solve scratch: 3 blocks [16][17] fp32
+constexpr uint32_t OFF_GATE = OFF_X + 3 * 16 * 17 * 4;  // per stage: e[64], w[64], g[64]
+constexpr uint32_t OFF_G = OFF_GATE + 2 * 3 * 64 * 4;   // G[64], gam[64]
+constexpr uint32_t OFF_BAR = OFF_G + 2 * 64 * 4;        // mbarriers: tma[2], mma
+constexpr uint32_t OFF_TMEMPTR = OFF_BAR + 3 * 8;
+constexpr uint32_t OFF_FLAG = OFF_TMEMPTR + 4;
+constexpr uint32_t kSmemUsed = OFF_FLAG + 4;
+constexpr uint32_t kSmemBytes = kSmemUsed + 1024;       // alignment slack
+static_assert(OFF_AF % 1024 == 0 && OFF_AQK % 1024 == 0 && OFF_S % 1024 == 0, "operand tiles need 1 KB alignment");
+static_assert(kSmemBytes <= 232448, "over the 227 KB per-CTA shared-memory limit");
+
+// TMEM columns (512 allocated): region A = D1 / D_P, B = D_W, C = D_UY, D = D_S.
+constexpr uint32_t TM_A = 0, TM_W = 128, TM_UY = 256, TM_S = 384;
+
+struct Smem {
+    uint8_t *base;
+    uint32_t sbase;  // shared-window address of base
+};
+
+__device__ __forceinline__ float gate_at(const float *p) { return *p; }
+__device__ __forceinline__ float gate_at(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
+
+// e, w (per folded row) and g (per token, on micro-step 0) of one chunk row.
+template <typename TG>
+__device__ __forceinline__ float load_gate(const CoreParams &p, int64_t b, int64_t h, int64_t c, int tid) {
+    const int which = tid >> 6, l = tid & 63;
+    const int64_t P = p.seq * p.u;
+    const int64_t pos = c * kL + l;
+    if (pos >= P) return 0.f;
+    const TG *e = static_cast<const TG *>(p.erase), *w = static_cast<const TG *>(p.write);
+    const TG *g = static_cast<const TG *>(p.g);
+    if (which == 0) return gate_at(e + (b * P + pos) * p.heads + h);
+    if (which == 1) return gate_at(w + (b * P + pos) * p.heads + h);
+    if (p.gw == 0 || (pos % p.u) != 0) return 0.f;
+    return gate_at(g + (b * p.seq + pos / p.u) * p.heads + h);
 }
 
-inline int tc_last_error() { return 0; }
+// Every thread waits; returns false (uniformly across the CTA) if any timed out.
+__device__ __forceinline__ bool wait_all(uint64_t *bar, uint32_t parity, volatile int *flag) {
+    if (!ptx::mbar_wait(bar, parity)) *flag = 1;
+    __syncthreads();
+    return *flag == 0;
+}
 
-inline int launch_chunk_tc(const CoreParams &, int32_t, int32_t, cudaStream_t) { return 5; }
+template <typename TG, typename TO>
+__global__ void __launch_bounds__(kThreads, 1)
+    chunk_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
+                    const __grid_constant__ CUtensorMap tm_v, const CoreParams p, int *status) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sb = ptx::smem_u32(base);
+    float *Af = reinterpret_cast<float *>(base + OFF_AF);
+    float *Tf = reinterpret_cast<float *>(base + OFF_TF);
+    float *Xs = reinterpret_cast<float *>(base + OFF_X);
+    float *gates = reinterpret_cast<float *>(base + OFF_GATE);  // [stage][3][64]
+    float *Gc = reinterpret_cast<float *>(base + OFF_G);        // G[64]
+    float *gam = Gc + 64;                                       // e^G[64]
+    uint64_t *bar_tma = reinterpret_cast<uint64_t *>(base + OFF_BAR);
+    uint64_t *bar_mma = bar_tma + 2;
+    uint32_t *tmem_ptr = reinterpret_cast<uint32_t *>(base + OFF_TMEMPTR);
+    volatile int *flag = reinterpret_cast<volatile int *>(base + OFF_FLAG);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int sp = warp & 3, ch = warp >> 2;  // TMEM subpartition, column half
+    const int r = 32 * sp + lane;             // the TMEM lane (accumulator row) this thread reads
+    const int64_t bh = blockIdx.x, b = bh / p.heads, h = bh % p.heads;
+    const int64_t P = p.seq * p.u;
+    const int64_t nchunks = (P + kL - 1) / kL;
+    const bool gated = p.gw > 0;
+    const float scale = p.scale;
+    const bool leader = (tid == 0);
+
+    if (tid == 0) {
+        *flag = 0;
+        ptx::mbar_init(&bar_tma[0], 1);
+        ptx::mbar_init(&bar_tma[1], 1);
+        ptx::mbar_init(bar_mma, 1);
+        ptx::fence_mbar_init();
+        ptx::prefetch_tmap(&tm_k);
+        ptx::prefetch_tmap(&tm_q);
+        ptx::prefetch_tmap(&tm_v);
+    }
+    if (warp == 0) {
+        ptx::tmem_alloc(tmem_ptr, 512);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_ptr;
+    const uint32_t lane_base = (uint32_t)(32 * sp) << 16;
+
+    int pending = -1;  // stage whose TMA load is in flight and not yet waited on
+    uint32_t pending_parity = 0;
+    uint32_t mma_phase = 0;
+
+    auto issue_tma = [&](int64_t c, int st) {
+        uint64_t *bar = &bar_tma[st];
+        uint8_t *stg = base + OFF_STAGE + st * kStageBytes;
+        const int row = (int)(c * kL);
+        ptx::mbar_arrive_expect_tx(bar, kStageBytes);
+        ptx::tma_load_4d(stg + 0, &tm_k, bar, 0, (int)h, row, (int)b);
+        ptx::tma_load_4d(stg + 16384, &tm_k, bar, 64, (int)h, row, (int)b);
+        ptx::tma_load_4d(stg + 8192, &tm_q, bar, 0, (int)h, row, (int)b);
+        ptx::tma_load_4d(stg + 24576, &tm_q, bar, 64, (int)h, row, (int)b);
+        ptx::tma_load_4d(stg + 32768, &tm_v, bar, 0, (int)h, row, (int)b);
+        ptx::tma_load_4d(stg + 40960, &tm_v, bar, 64, (int)h, row, (int)b);
+    };
+
+    // Chunk-local cumulative gate of the chunk whose gates sit in stage `st`.
+    auto gate_scan = [&](int st) {
+        if (warp == 0) {
+            const float *g = gates + (st * 3 + 2) * 64;
+            const float x0 = g[2 * lane], x1 = g[2 * lane + 1];
+            float s = x0 + x1;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const float t = __shfl_up_sync(0xffffffffu, s, off);
+                if (lane >= off) s += t;
+            }
+            Gc[2 * lane + 1] = s;
+            Gc[2 * lane] = s - x1;
+            gam[2 * lane + 1] = __expf(s);
+            gam[2 * lane] = __expf(s - x1);
+        }
+    };
+
+    bool ok = true;
+    if (nchunks > 0) {
+        if (leader) {
+            issue_tma(0, 0);
+        }
+        pending = 0;
+        if (tid < 192) gates[tid] = load_gate<TG>(p, b, h, 0, tid);
+        __syncthreads();
+        gate_scan(0);
+        __syncthreads();
+        // S0 -> TMEM (scaled by the first chunk's total decay) and its bf16 copy.
+        {
+            const float Gam = gam[63];
+            const float *src = p.state_in + (bh * kD + r) * kD + 64 * ch;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t v[32];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 f = *reinterpret_cast<const float4 *>(src + 32 * hh + 4 * q);
+                    const float fs[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) v[4 * q + e] = __float_as_uint(fs[e]);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    ptx::st_shared_v4(sb + OFF_S + ch * 16384 + ptx::sw128(r, 32 * hh + 8 * q),
+                                      ptx::pack_bf16(__uint_as_float(v[8 * q + 0]), __uint_as_float(v[8 * q + 1])),
+                                      ptx::pack_bf16(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3])),
+                                      ptx::pack_bf16(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5])),
+                                      ptx::pack_bf16(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7])));
+                }
+#pragma unroll
+                for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * Gam);
+                ptx::tmem_st32(tmem + lane_base + TM_S + 64 * ch + 32 * hh, v);
+            }
+            ptx::tmem_wait_st();
+        }
+        ptx::fence_async_smem();
+        ptx::tc_fence_before();
+        __syncthreads();
+    }
+
+    for (int64_t c = 0; c < nchunks && ok; ++c) {
+        const int stage = (int)(c & 1);
+        const uint32_t stg = sb + OFF_STAGE + stage * kStageBytes;
+        const float *ge = gates + (stage * 3 + 0) * 64;
+        const float *gw = gates + (stage * 3 + 1) * 64;
+
+        // ---- inputs of chunk c; start chunk c+1's loads ----
+        ok = wait_all(&bar_tma[stage], (uint32_t)((c >> 1) & 1), flag);
+        if (!ok) break;
+        pending = -1;
+        const bool has_next = (c + 1 < nchunks);
+        if (has_next) {
+            if (leader) issue_tma(c + 1, stage ^ 1);
+            pending = stage ^ 1;
+            pending_parity = (uint32_t)(((c + 1) >> 1) & 1);
+        }
+        float gate_next = 0.f;
+        if (has_next && tid < 192) gate_next = load_gate<TG>(p, b, h, c + 1, tid);
+
+        // ---- D1 = [K; Q] K^T ----
+        if (leader) {
+            ptx::tc_fence_after();
+            const uint32_t id = ptx::idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                const uint64_t d = ptx::sdesc(stg + off, 16, 1024);
+                ptx::umma_bf16(tmem + TM_A, d, d, id, kk > 0);
+            }
+            ptx::umma_commit(bar_mma);
+        }
+        ok = wait_all(bar_mma, mma_phase, flag);
+        mma_phase ^= 1;
+        if (!ok) break;
+
+        // ---- masks: Akk (fp32) and Aqk (bf16 operand) ----
+        ptx::tc_fence_after();
+        {
+            uint32_t v[32];
+            ptx::tmem_ld32(tmem + lane_base + TM_A + 32 * ch, v);
+            ptx::tmem_wait_ld();
+            if (r < 64) {
+                const int i = r;
+                const float ei = ge[i], Gi = Gc[i];
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) {
+                    const int j = 32 * ch + jj;
+                    float a = 0.f;
+                    if (j < i) a = ei * __uint_as_float(v[jj]) * (gated ? __expf(Gi - Gc[j]) : 1.f);
+                    Af[i * 65 + j] = a;
+                }
+            } else {
+                const int i = r - 64;
+                const float Gi = Gc[i];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    float a[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const int j = 32 * ch + 8 * q + e;
+                        a[e] = (j <= i) ? scale * __uint_as_float(v[8 * q + e]) * (gated ? __expf(Gi - Gc[j]) : 1.f)
+                                        : 0.f;
+                    }
+                    ptx::st_shared_v4(sb + OFF_AQK + ptx::sw128(i, 32 * ch + 8 * q), ptx::pack_bf16(a[0], a[1]),
+                                      ptx::pack_bf16(a[2], a[3]), ptx::pack_bf16(a[4], a[5]),
+                                      ptx::pack_bf16(a[6], a[7]));
+                }
+            }
+        }
+        ptx::fence_async_smem();
+        ptx::tc_fence_before();
+        __syncthreads();
+
+        // ---- T = (I + Akk)^-1, blocked: 16x16 diagonal blocks, then block substitution ----
+        if (tid < 64) {
+            const int pb = tid >> 4, j = tid & 15;
+            const float *A = Af + (16 * pb) * 65 + 16 * pb;
+            float tcol[16];
+#pragma unroll
+            for (int a = 0; a < 16; ++a) {
+                float acc = (a == j) ? 1.f : 0.f;
+#pragma unroll
+                for (int m = 0; m < a; ++m) acc = fmaf(-A[a * 65 + m], tcol[m], acc);
+                tcol[a] = acc;
+            }
+#pragma unroll
+            for (int a = 0; a < 16; ++a) Tf[(16 * pb + a) * 65 + 16 * pb + j] = tcol[a];
+        }
+        for (int idx = tid; idx < 6 * 256; idx += kThreads) {  // strictly-upper blocks are zero
+            const int blk = idx >> 8, e = idx & 255;
+            const int pr = blk < 3 ? 0 : (blk < 5 ? 1 : 2);   // (0,1) (0,2) (0,3) (1,2) (1,3) (2,3)
+            const int qc = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+            Tf[(16 * pr + (e >> 4)) * 65 + 16 * qc + (e & 15)] = 0.f;
+        }
+        __syncthreads();
+#pragma unroll 1
+        for (int lvl = 1; lvl < 4; ++lvl) {
+            const int nb = 4 - lvl;
+            // X_pq = sum_{r=q}^{p-1} A_pr T_rq,   p = q + lvl
+            for (int idx = tid; idx < nb * 256; idx += kThreads) {
+                const int q = idx >> 8, a = (idx >> 4) & 15, j = idx & 15, pr = q + lvl;
+                float acc = 0.f;
+                for (int rr = q; rr < pr; ++rr) {
+#pragma unroll
+                    for (int m = 0; m < 16; ++m)
+                        acc = fmaf(Af[(16 * pr + a) * 65 + 16 * rr + m], Tf[(16 * rr + m) * 65 + 16 * q + j], acc);
+                }
+                Xs[(q * 16 + a) * 17 + j] = acc;
+            }
+            __syncthreads();
+            // T_pq = -T_pp X_pq
+            for (int idx = tid; idx < nb * 256; idx += kThreads) {
+                const int q = idx >> 8, a = (idx >> 4) & 15, j = idx & 15, pr = q + lvl;
+                float acc = 0.f;
+#pragma unroll
+                for (int m = 0; m < 16; ++m)
+                    acc = fmaf(Tf[(16 * pr + a) * 65 + 16 * pr + m], Xs[(q * 16 + m) * 17 + j], acc);
+                Tf[(16 * pr + a) * 65 + 16 * q + j] = -acc;
+            }
+            __syncthreads();
+        }
+        // Tb = T diag(w), Tw = T diag(e gam): the tops of A_U and A_W.
+        {
+            const int i = tid >> 2, j0 = (tid & 3) * 16;
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int j = j0 + 8 * q;
+                float tb[8], tw[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float t = Tf[i * 65 + j + e];
+                    tb[e] = t * gw[j + e];
+                    tw[e] = t * ge[j + e] * gam[j + e];
+                }
+                ptx::st_shared_v4(sb + OFF_AU + ptx::sw128(i, j), ptx::pack_bf16(tb[0], tb[1]),
+                                  ptx::pack_bf16(tb[2], tb[3]), ptx::pack_bf16(tb[4], tb[5]),
+                                  ptx::pack_bf16(tb[6], tb[7]));
+                ptx::st_shared_v4(sb + OFF_AW + ptx::sw128(i, j), ptx::pack_bf16(tw[0], tw[1]),
+                                  ptx::pack_bf16(tw[2], tw[3]), ptx::pack_bf16(tw[4], tw[5]),
+                                  ptx::pack_bf16(tw[6], tw[7]));
+            }
+        }
+        ptx::fence_async_smem();
+        __syncthreads();
+
+        // ---- D_P = Aqk [Tb | Tw] ----
+        if (leader) {
+            ptx::tc_fence_after();
+            const uint32_t id = ptx::idesc_bf16(64, 128, 0, 1);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t a = ptx::sdesc(sb + OFF_AQK + kk * 32, 16, 1024);
+                const uint64_t bd = ptx::sdesc(sb + OFF_AU + kk * 2048, 16384, 1024);
+                ptx::umma_bf16(tmem + TM_A, a, bd, id, kk > 0);
+            }
+            ptx::umma_commit(bar_mma);
+        }
+        ok = wait_all(bar_mma, mma_phase, flag);
+        mma_phase ^= 1;
+        if (!ok) break;
+
+        // ---- Pb, Pw: the bottoms of A_U and A_W (M=64 accumulator: rows in lanes 0-15) ----
+        ptx::tc_fence_after();
+        {
+            const uint32_t dst = sb + (ch ? OFF_AW : OFF_AU);
+            const int i = 16 * sp + lane;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t v[32];
+                ptx::tmem_ld32(tmem + lane_base + TM_A + 64 * ch + 32 * hh, v);
+                ptx::tmem_wait_ld();
+                if (lane < 16) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float *f = reinterpret_cast<const float *>(v + 8 * q);
+                        ptx::st_shared_v4(dst + ptx::sw128(64 + i, 32 * hh + 8 * q), ptx::pack_bf16(f[0], f[1]),
+                                          ptx::pack_bf16(f[2], f[3]), ptx::pack_bf16(f[4], f[5]),
+                                          ptx::pack_bf16(f[6], f[7]));
+                    }
+                }
+            }
+        }
+        ptx::fence_async_smem();
+        ptx::tc_fence_before();
+        __syncthreads();
+
+        // ---- D_UY = [Tb; Pb] V,  D_W = [Tw; Pw] K ----
+        if (leader) {
+            ptx::tc_fence_after();
+            const uint32_t id = ptx::idesc_bf16(128, 128, 0, 1);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                ptx::umma_bf16(tmem + TM_UY, ptx::sdesc(sb + OFF_AU + kk * 32, 16, 1024),
+                               ptx::sdesc(stg + 32768 + kk * 2048, 8192, 1024), id, kk > 0);
+                ptx::umma_bf16(tmem + TM_W, ptx::sdesc(sb + OFF_AW + kk * 32, 16, 1024),
+                               ptx::sdesc(stg + kk * 2048, 16384, 1024), id, kk > 0);
+            }
+            ptx::umma_commit(bar_mma);
+        }
+        ok = wait_all(bar_mma, mma_phase, flag);
+        mma_phase ^= 1;
+        if (!ok) break;
+
+        // ---- A6 = [-W; s gam Q - Aqk W] (K-major over d, blocks of 64 columns) ----
+        ptx::tc_fence_after();
+        {
+            const uint32_t blk = sb + (ch ? OFF_AW : OFF_AU);
+            const uint32_t qblk = stg + ch * 16384 + 8192;
+            const float qs = (r >= 64) ? scale * gam[r - 64] : 0.f;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t v[32];
+                ptx::tmem_ld32(tmem + lane_base + TM_W + 64 * ch + 32 * hh, v);
+                ptx::tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    float a[8];
+                    const float *f = reinterpret_cast<const float *>(v + 8 * q);
+                    if (r < 64) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) a[e] = -f[e];
+                    } else {
+                        const uint4 qv = ptx::ld_shared_v4(qblk + ptx::sw128(r - 64, 32 * hh + 8 * q));
+                        const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            a[2 * e] = qs * ptx::bf16lo(qw[e]) - f[2 * e];
+                            a[2 * e + 1] = qs * ptx::bf16hi(qw[e]) - f[2 * e + 1];
+                        }
+                    }
+                    ptx::st_shared_v4(blk + ptx::sw128(r, 32 * hh + 8 * q), ptx::pack_bf16(a[0], a[1]),
+                                      ptx::pack_bf16(a[2], a[3]), ptx::pack_bf16(a[4], a[5]),
+                                      ptx::pack_bf16(a[6], a[7]));
+                }
+            }
+        }
+        ptx::fence_async_smem();
+        ptx::tc_fence_before();
+        __syncthreads();
+
+        // ---- D_UY += A6 S  ->  [V'; y] ----
+        if (leader) {
+            ptx::tc_fence_after();
+            const uint32_t id = ptx::idesc_bf16(128, 128, 0, 1);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                ptx::umma_bf16(tmem + TM_UY, ptx::sdesc(sb + OFF_AU + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                               ptx::sdesc(sb + OFF_S + kk * 2048, 16384, 1024), id, 1);
+            }
+            ptx::umma_commit(bar_mma);
+        }
+        ok = wait_all(bar_mma, mma_phase, flag);
+        mma_phase ^= 1;
+        if (!ok) break;
+
+        // ---- V' (decayed to the chunk end) -> operand; y -> HBM ----
+        ptx::tc_fence_after();
+        {
+            const float Glast = Gc[63];
+            const float vs = (r < 64 && gated) ? __expf(Glast - Gc[r]) : 1.f;
+            const int64_t pos = c * kL + (r - 64);
+            const bool write_y = (r >= 64) && pos < P && (pos % p.u) == (p.u - 1);
+            TO *yrow = static_cast<TO *>(p.y) + ((b * p.seq + (write_y ? pos / p.u : 0)) * p.heads + h) * kD;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t v[32];
+                ptx::tmem_ld32(tmem + lane_base + TM_UY + 64 * ch + 32 * hh, v);
+                ptx::tmem_wait_ld();
+                const float *f = reinterpret_cast<const float *>(v);
+                if (r < 64) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        ptx::st_shared_v4(sb + OFF_AF + ch * 8192 + ptx::sw128(r, 32 * hh + 8 * q),
+                                          ptx::pack_bf16(vs * f[8 * q + 0], vs * f[8 * q + 1]),
+                                          ptx::pack_bf16(vs * f[8 * q + 2], vs * f[8 * q + 3]),
+                                          ptx::pack_bf16(vs * f[8 * q + 4], vs * f[8 * q + 5]),
+                                          ptx::pack_bf16(vs * f[8 * q + 6], vs * f[8 * q + 7]));
+                    }
+                } else if (write_y) {
+                    TO *dst = yrow + 64 * ch + 32 * hh;
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) st(dst + e, f[e]);
+                }
+            }
+        }
+        ptx::fence_async_smem();
+        ptx::tc_fence_before();
+        __syncthreads();
+
+        // ---- D_S = Gam S + K^T V~' ----
+        if (leader) {
+            ptx::tc_fence_after();
+            const uint32_t id = ptx::idesc_bf16(128, 128, 1, 1);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                ptx::umma_bf16(tmem + TM_S, ptx::sdesc(stg + kk * 2048, 16384, 1024),
+                               ptx::sdesc(sb + OFF_AF + kk * 2048, 8192, 1024), id, 1);
+            }
+            ptx::umma_commit(bar_mma);
+        }
+        ok = wait_all(bar_mma, mma_phase, flag);
+        mma_phase ^= 1;
+        if (!ok) break;
+
+        // ---- next chunk's gates, then S -> bf16 operand and the pre-scaled accumulator ----
+        if (has_next) {
+            if (tid < 192) gates[(stage ^ 1) * 192 + tid] = gate_next;
+            __syncthreads();
+            gate_scan(stage ^ 1);
+            __syncthreads();
+            const float Gam = gam[63];
+            ptx::tc_fence_after();
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t v[32];
+                const uint32_t ta = tmem + lane_base + TM_S + 64 * ch + 32 * hh;
+                ptx::tmem_ld32(ta, v);
+                ptx::tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float *f = reinterpret_cast<const float *>(v + 8 * q);
+                    ptx::st_shared_v4(sb + OFF_S + ch * 16384 + ptx::sw128(r, 32 * hh + 8 * q),
+                                      ptx::pack_bf16(f[0], f[1]), ptx::pack_bf16(f[2], f[3]),
+                                      ptx::pack_bf16(f[4], f[5]), ptx::pack_bf16(f[6], f[7]));
+                }
+                if (gated) {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * Gam);
+                    ptx::tmem_st32(ta, v);
+                }
+            }
+            ptx::tmem_wait_st();
+            ptx::fence_async_smem();
+            ptx::tc_fence_before();
+            __syncthreads();
+        } else {
+            ptx::tc_fence_after();
+            float *dst = p.state_out + (bh * kD + r) * kD + 64 * ch;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t v[32];
+                ptx::tmem_ld32(tmem + lane_base + TM_S + 64 * ch + 32 * hh, v);
+                ptx::tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    *reinterpret_cast<float4 *>(dst + 32 * hh + 4 * q) =
+                        make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                    __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+                }
+            }
+        }
+    }
+
+    if (!ok) {
+        // A wait ran out: report it, let our own TMA loads land, then release TMEM.
+        if (tid == 0) atomicExch(status, kStatusTimeout);
+        if (pending >= 0) ptx::mbar_wait(&bar_tma[pending], pending_parity);
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) ptx::tmem_dealloc(tmem, 512);
+}
+
+}  // namespace tc
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+inline bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+// Whether the tensor-core kernel serves this request.
+inline bool tc_applies(const CoreParams &p, int32_t in_dtype, uint32_t flags) {
+    if (flags & 0x1u) return false;  // DC_FLAG_FORCE_SIMT
+    if (in_dtype != 1) return false; // bf16 q, k, v
+    if (p.dk != 128 || p.dv != 128) return false;
+    if (p.ew != 1 || p.ww != 1 || p.gw > 1) return false;
+    if (p.u != 1) return false;
+    if (!aligned16(p.q) || !aligned16(p.k) || !aligned16(p.v) || !aligned16(p.y) || !aligned16(p.state_in) ||
+        !aligned16(p.state_out))
+        return false;
+    if (p.seq * p.u > 0x7fffffff || p.batch * p.heads > 0x7fffffff) return false;
+    return true;
+}
+
+inline thread_local int g_tc_error = 0;
+inline int tc_last_error() { return g_tc_error; }
+
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+// [batch, rows, heads, 128] bf16 viewed as a 4-D tensor (128, heads, rows, batch),
+// read in 64 x 1 x 64 x 1 boxes (64 rows of 128 bytes, 128-byte swizzle).
+inline bool encode_rows(CUtensorMap *m, const void *ptr, int64_t heads, int64_t rows, int64_t batch) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[4] = {128, (cuuint64_t)heads, (cuuint64_t)rows, (cuuint64_t)batch};
+    const cuuint64_t strides[3] = {256, (cuuint64_t)(256 * heads), (cuuint64_t)(256 * heads * rows)};
+    const cuuint32_t box[4] = {64, 1, 64, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(ptr), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline int *device_status_ptr() {
+    static int *ptrs[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!ptrs[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
+        ptrs[dev] = static_cast<int *>(p);
+    }
+    return ptrs[dev];
+}
+
+template <typename TG, typename TO>
+int launch_tc_typed(const CoreParams &p, cudaStream_t stream) {
+    CUtensorMap mk, mq, mv;
+    const int64_t P = p.seq * p.u;
+    if (!encode_rows(&mk, p.k, p.heads, P, p.batch) || !encode_rows(&mq, p.q, p.heads, p.seq, p.batch) ||
+        !encode_rows(&mv, p.v, p.heads, P, p.batch)) {
+        g_tc_error = (int)cudaErrorInvalidValue;
+        return 6;  // DC_ECUDA
+    }
+    int *status = device_status_ptr();
+    if (!status) {
+        g_tc_error = (int)cudaErrorInvalidSymbol;
+        return 6;
+    }
+    auto kern = tc::chunk_tc_kernel<TG, TO>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes);
+    if (e == cudaSuccess) {
+        kern<<<(unsigned)(p.batch * p.heads), tc::kThreads, tc::kSmemBytes, stream>>>(mk, mq, mv, p, status);
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) {
+        g_tc_error = (int)e;
+        return 6;
+    }
+    return 0;
+}
+
+inline int launch_chunk_tc(const CoreParams &p, int32_t gate_dtype, int32_t out_dtype, cudaStream_t stream) {
+    const int key = gate_dtype * 2 + out_dtype;
+    switch (key) {
+        case 0: return launch_tc_typed<float, float>(p, stream);
+        case 1: return launch_tc_typed<float, __nv_bfloat16>(p, stream);
+        case 2: return launch_tc_typed<__nv_bfloat16, float>(p, stream);
+        case 3: return launch_tc_typed<__nv_bfloat16, __nv_bfloat16>(p, stream);
+    }
+    return 3;  // DC_EUNSUPPORTED_DTYPE
+}
 
 }  // namespace dc

@@ -197,10 +197,26 @@ const char *dc_status_string(int status) {
 
 int dc_last_cuda_error(void) { return g_last_cuda_error; }
 
+int dc_device_status(int reset) {
+    int st = check_device(nullptr);
+    if (st != DC_OK) return -st;
+    int value = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&value, dc::g_device_status, sizeof(int));
+    if (e == cudaSuccess && reset) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(dc::g_device_status, &zero, sizeof(int));
+    }
+    if (e != cudaSuccess) return -cuda_fail(e);
+    return value;
+}
+
 int dc_chunk_kernel_choice(const dc_chunk_args *a) {
     const int st = validate_chunk(a);
     if (st != DC_OK) return -st;
-    return dc::tc_applies(a->dk, a->dv, a->in_dtype, a->flags) ? 1 : 0;
+    const dc::CoreParams p = make_params(a->batch, a->seq, a->heads, a->dk, a->dv, a->n_householder, a->erase_w,
+                                         a->write_w, a->g_w, a->scale, a->q, a->k, a->v, a->erase, a->write, a->g,
+                                         a->state_in, a->y, a->state_out);
+    return dc::tc_applies(p, a->in_dtype, a->flags) ? 1 : 0;
 }
 
 int dc_chunk_launches(const dc_chunk_args *a) {
@@ -218,7 +234,7 @@ int dc_chunk_fwd(const dc_chunk_args *a, dc_stream_t stream) {
                                          a->write_w, a->g_w, a->scale, a->q, a->k, a->v, a->erase, a->write, a->g,
                                          a->state_in, a->y, a->state_out);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (dc::tc_applies(a->dk, a->dv, a->in_dtype, a->flags)) {
+    if (dc::tc_applies(p, a->in_dtype, a->flags)) {
         st = dc::launch_chunk_tc(p, a->gate_dtype, a->out_dtype, s);
         if (st == DC_ECUDA) g_last_cuda_error = dc::tc_last_error();
         return st;

@@ -138,6 +138,12 @@ DC_API const char *dc_status_string(int status);
 /* The cudaError_t behind the most recent DC_ECUDA returned on this thread (0 if none). */
 DC_API int dc_last_cuda_error(void);
 
+/* The device status word of the current device (synchronising): 0 while every kernel
+ * ran to completion; 1 after a kernel's bounded wait on its own tensor-core or TMA
+ * work ran out (its outputs are then invalid).  `reset` != 0 clears it.  A negative
+ * value is -dc_status of a failed query. */
+DC_API int dc_device_status(int reset);
+
 /* Which chunk kernel dc_chunk_fwd would launch for `args`: 1 = tensor-core (tcgen05),
  * 0 = CUDA-core; negative = the dc_status the call would return. Pure host logic. */
 DC_API int dc_chunk_kernel_choice(const dc_chunk_args *args);

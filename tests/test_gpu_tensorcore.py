@@ -1,0 +1,106 @@
+"""GPU parity of the tensor-core (tcgen05) chunk kernel: bf16 q/k/v, fp32
+gates, fp32 state and accumulation, dk = dv = 128.
+
+Bar: max |gpu - oracle| < 2e-2 on y and on the final state, the oracle
+(float64) run on the same bf16-rounded inputs; and the kernel's device
+status word stays 0 (no bounded wait ran out)."""
+import importlib
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from _inputs import config_inputs, constant_raw, random_raw
+
+pytestmark = pytest.mark.gpu
+dn = importlib.import_module("burn-deltanet_b200")
+abi = importlib.import_module("burn-deltanet_b200._abi")
+
+BF16_TOL = 2e-2
+
+
+def dev(x, dtype=torch.float32):
+    return None if x is None else torch.from_numpy(np.ascontiguousarray(x)).to("cuda", dtype)
+
+
+def run_tc(raw, force_simt=False, out_dtype=torch.float32):
+    q, k, v = (dev(raw[n], torch.bfloat16) for n in ("q", "k", "v"))
+    e, w, g = (dev(raw[n]) for n in ("erase", "write", "g"))
+    st = dev(raw["state"])
+    y, s = dn.delta_chunk_recalculated(q, k, v, e, w, g, st, g is not None, 64, 1 / np.sqrt(128),
+                                       out_dtype=out_dtype, force_simt=force_simt)
+    torch.cuda.synchronize()
+    return y.double().cpu().numpy(), s.double().cpu().numpy(), (q, k, v)
+
+
+def reference(raw, qkv):
+    q, k, v = (t.double().cpu().numpy() for t in qkv)
+    return oracle.recurrent(q, k, v, raw["erase"], raw["write"], raw["g"], raw["state"])
+
+
+def kernel_choice(raw):
+    a = abi.ChunkArgs()
+    b, s, h, d = raw["q"].shape
+    a.batch, a.seq, a.heads, a.dk, a.dv = b, s, h, d, raw["v"].shape[3]
+    a.n_householder, a.erase_w, a.write_w = 1, raw["erase"].shape[3], raw["write"].shape[3]
+    a.g_w = 0 if raw["g"] is None else raw["g"].shape[3]
+    a.chunk_len, a.in_dtype, a.gate_dtype, a.out_dtype, a.scale = 64, abi.DC_BF16, abi.DC_F32, abi.DC_F32, 0.1
+    a.q = a.k = a.v = a.erase = a.write = a.g = 1 << 20
+    a.state_in = a.state_out = 2 << 20
+    a.y = 3 << 20
+    return abi.lib().dc_chunk_kernel_choice(a)
+
+
+def check(raw, tol=BF16_TOL):
+    assert kernel_choice(raw) == 1, "expected the tensor-core kernel"
+    assert abi.lib().dc_device_status(1) == 0
+    y, s, qkv = run_tc(raw)
+    assert abi.lib().dc_device_status(1) == 0, "a bounded wait in the kernel ran out"
+    y0, s0 = reference(raw, qkv)
+    ey, es = np.abs(y - y0).max(), np.abs(s - s0).max()
+    assert ey < tol and es < tol, (ey, es)
+    return ey, es
+
+
+@pytest.mark.parametrize("seq", [64, 1, 63, 65, 200, 1000])
+def test_deltanet_prefill(seq):
+    check(config_inputs(2, np.random.default_rng(seq), 2, seq, 3, 128, 128))
+
+
+def test_deltanet_negative_eigenvalues():
+    check(config_inputs(2, np.random.default_rng(5), 2, 300, 2, 128, 128, neg_eig=True))
+
+
+@pytest.mark.parametrize("seq", [64, 130, 777])
+def test_gated_deltanet_prefill(seq):
+    check(config_inputs(1, np.random.default_rng(seq + 7), 2, seq, 2, 128, 128))
+
+
+def test_carried_state_and_reference_gates():
+    raw = random_raw(np.random.default_rng(3), 2, 150, 2, 128, 128, 0.95, True, True)
+    check(raw)
+
+
+def test_constant_input():
+    check(constant_raw(np.random.default_rng(4), 1, 256, 2, 128, 128, 1.8, True))
+
+
+def test_long_sequence_drift():
+    """bf16 operands against the fp32 state over 4096 steps (the config 2 length)."""
+    ey, es = check(config_inputs(2, np.random.default_rng(6), 1, 4096, 2, 128, 128))
+    print(f"T=4096 max err y {ey:.3e} state {es:.3e}")
+
+
+def test_matches_the_cuda_core_kernel():
+    raw = config_inputs(1, np.random.default_rng(8), 2, 333, 4, 128, 128)
+    y1, s1, _ = run_tc(raw)
+    y2, s2, _ = run_tc(raw, force_simt=True)
+    assert np.abs(y1 - y2).max() < BF16_TOL and np.abs(s1 - s2).max() < BF16_TOL
+
+
+def test_bf16_output():
+    raw = config_inputs(2, np.random.default_rng(9), 1, 128, 2, 128, 128)
+    y, s, qkv = run_tc(raw, out_dtype=torch.bfloat16)
+    y0, s0 = reference(raw, qkv)
+    assert np.abs(y - y0).max() < BF16_TOL and np.abs(s - s0).max() < BF16_TOL

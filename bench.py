@@ -348,9 +348,18 @@ def run_ours(args):
     clocks = ClockSampler(local)
     barrier(world)
     torch.cuda.synchronize()
+    if args.only == "decode":
+        dec_ms, dec_bytes = time_decode(dn, 256, args.warmup)
+        if rank == 0:
+            print(json.dumps({"decode_ms_per_step": dec_ms, "decode_gbs": dec_bytes / (dec_ms / 1e3) / 1e9}))
+        return
     with clocks:
         ms = time_prefill(dn, x, u, args.steps, args.warmup)
     barrier(world)
+    if args.only == "prefill":
+        if rank == 0:
+            print(json.dumps({"prefill_ms_per_step": ms, "tok_s": batch * tokens * world / (ms / 1e3)}))
+        return
     ms = max_over_ranks(ms, world)
     tok_per_rank = batch * tokens
     value = tok_per_rank * world / (ms / 1e3)
@@ -462,6 +471,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="deltanet")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["prefill", "decode"], default=None,
+                    help="time one kernel alone and print a short line (for profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -11,13 +11,19 @@
 //   Akk  = tril(e_i (k_i.k_j) e^{G_i-G_j}, -1)           fp32, shared memory (CUDA cores)
 //   Aqk  = tril(s (q_i.k_j) e^{G_i-G_j}, 0)              bf16 operand
 //   T    = (I + Akk)^-1                                  blocked 16x16 forward substitution
-//   Tb   = T diag(w),  Tw = T diag(e gam)                bf16 operands
+//   Tb   = T diag(w),  Tw = T diag(e gam)                bf16 hi + lo operands
 //   D_P  = Aqk [Tb | Tw]                                 M=64  N=128 K=64    (tcgen05)
 //   D_UY = [Tb; Aqk Tb] V      = [U; Aqk U]              M=128 N=128 K=64    (tcgen05)
 //   D_W  = [Tw; Aqk Tw] K      = [W; Aqk W]              M=128 N=128 K=64    (tcgen05)
 //   A6   = [-W; s gam Q - Aqk W]                         bf16 operand
 //   D_UY += A6 S               = [U - W S; y]            M=128 N=128 K=128   (tcgen05)
 //   D_S  = Gam S + K^T diag(e^{G_63 - G_j}) V'           M=128 N=128 K=64    (tcgen05, accumulate)
+//
+// T (through Tb, Tw and their Aqk products) and V' enter their products as
+// two bf16 terms each (hi + lo, the rounding residual of hi), i.e. at ~16
+// significant bits instead of bf16's 8.  T's long alternating tails (a
+// chunk of near-parallel keys) and V''s rounding are otherwise the two
+// largest errors in the fp32 state; the inputs q, k, v are exact in bf16.
 //
 // The second-to-last line is the reference's scan step (src/delta/chunk.rs:
 // 177-187) with its two S products stacked into one M=128 MMA: V' = U - W S
@@ -62,9 +68,9 @@ constexpr uint32_t OFF_AU = 2 * kStageBytes;            // [Tb; Pb] 128x64 bf16 
 constexpr uint32_t OFF_AW = OFF_AU + 16384;             // [Tw; Pw];                     A6 block 1
 constexpr uint32_t OFF_S = OFF_AW + 16384;              // S bf16, MN-major, two 64-column blocks of 16 KB
 constexpr uint32_t OFF_AQK = OFF_S + 32768;             // Aqk bf16 64x64 K-major
-constexpr uint32_t OFF_AF = OFF_AQK + 8192;             // Akk fp32 [64][65]; later V' operand (2 x 8 KB)
-constexpr uint32_t OFF_TF = OFF_AF + 64 * 65 * 4;       // T fp32 [64][65]
-constexpr uint32_t OFF_X = OFF_TF + 64 * 65 * 4;        // solve scratch: 3 blocks [16][17] fp32
+constexpr uint32_t OFF_AF = OFF_AQK + 8192;             // Akk fp32 [64][65]; later V' high part (2 x 8 KB)
+constexpr uint32_t OFF_TF = OFF_AF + 17408;             // T fp32 [64][65];   later V' low part (2 x 8 KB)
+constexpr uint32_t OFF_X = OFF_TF + 17408;              // solve scratch: 3 blocks [16][17] fp32
 constexpr uint32_t OFF_GATE = OFF_X + 3 * 16 * 17 * 4;  // per stage: e[64], w[64], g[64]
 constexpr uint32_t OFF_G = OFF_GATE + 2 * 3 * 64 * 4;   // G[64], gam[64]
 constexpr uint32_t OFF_BAR = OFF_G + 2 * 64 * 4;        // mbarriers: tma[2], mma
@@ -72,7 +78,8 @@ constexpr uint32_t OFF_TMEMPTR = OFF_BAR + 3 * 8;
 constexpr uint32_t OFF_FLAG = OFF_TMEMPTR + 4;
 constexpr uint32_t kSmemUsed = OFF_FLAG + 4;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;       // alignment slack
-static_assert(OFF_AF % 1024 == 0 && OFF_AQK % 1024 == 0 && OFF_S % 1024 == 0, "operand tiles need 1 KB alignment");
+static_assert(OFF_AF % 1024 == 0 && OFF_TF % 1024 == 0 && OFF_AQK % 1024 == 0 && OFF_S % 1024 == 0,
+              "operand tiles need 1 KB alignment");
 static_assert(kSmemBytes <= 232448, "over the 227 KB per-CTA shared-memory limit");
 
 // TMEM columns (512 allocated): region A = D1 / D_P, B = D_W, C = D_UY, D = D_S.
@@ -355,25 +362,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             __syncthreads();
         }
-        // Tb = T diag(w), Tw = T diag(e gam): the tops of A_U and A_W.
+        // Tb = T diag(w), Tw = T diag(e gam) as bf16 hi + lo: the tops of A_U / A_W
+        // and of their low-part twins (which reuse the Akk and T buffers).
         {
             const int i = tid >> 2, j0 = (tid & 3) * 16;
+            float t[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) t[e] = Tf[i * 65 + j0 + e];
+            __syncthreads();  // every T read is done before the T buffer is overwritten
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
                 const int j = j0 + 8 * q;
-                float tb[8], tw[8];
+                uint32_t bh[4], bl[4], wh[4], wl[4];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float t = Tf[i * 65 + j + e];
-                    tb[e] = t * gw[j + e];
-                    tw[e] = t * ge[j + e] * gam[j + e];
+                for (int e = 0; e < 4; ++e) {
+                    const int j1 = j + 2 * e;
+                    const float b0 = t[8 * q + 2 * e] * gw[j1], b1 = t[8 * q + 2 * e + 1] * gw[j1 + 1];
+                    const float w0 = t[8 * q + 2 * e] * ge[j1] * gam[j1];
+                    const float w1 = t[8 * q + 2 * e + 1] * ge[j1 + 1] * gam[j1 + 1];
+                    bh[e] = ptx::pack_bf16(b0, b1);
+                    bl[e] = ptx::pack_bf16(b0 - ptx::bf16lo(bh[e]), b1 - ptx::bf16hi(bh[e]));
+                    wh[e] = ptx::pack_bf16(w0, w1);
+                    wl[e] = ptx::pack_bf16(w0 - ptx::bf16lo(wh[e]), w1 - ptx::bf16hi(wh[e]));
                 }
-                ptx::st_shared_v4(sb + OFF_AU + ptx::sw128(i, j), ptx::pack_bf16(tb[0], tb[1]),
-                                  ptx::pack_bf16(tb[2], tb[3]), ptx::pack_bf16(tb[4], tb[5]),
-                                  ptx::pack_bf16(tb[6], tb[7]));
-                ptx::st_shared_v4(sb + OFF_AW + ptx::sw128(i, j), ptx::pack_bf16(tw[0], tw[1]),
-                                  ptx::pack_bf16(tw[2], tw[3]), ptx::pack_bf16(tw[4], tw[5]),
-                                  ptx::pack_bf16(tw[6], tw[7]));
+                const uint32_t off = ptx::sw128(i, j);
+                ptx::st_shared_v4(sb + OFF_AU + off, bh[0], bh[1], bh[2], bh[3]);
+                ptx::st_shared_v4(sb + OFF_AF + off, bl[0], bl[1], bl[2], bl[3]);
+                ptx::st_shared_v4(sb + OFF_AW + off, wh[0], wh[1], wh[2], wh[3]);
+                ptx::st_shared_v4(sb + OFF_TF + off, wl[0], wl[1], wl[2], wl[3]);
             }
         }
         ptx::fence_async_smem();
@@ -395,10 +411,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_phase ^= 1;
         if (!ok) break;
 
-        // ---- Pb, Pw: the bottoms of A_U and A_W (M=64 accumulator: rows in lanes 0-15) ----
+        // ---- Pb, Pw (hi + lo): the bottoms of the four A operands (M=64 accumulator: rows in lanes 0-15) ----
         ptx::tc_fence_after();
         {
-            const uint32_t dst = sb + (ch ? OFF_AW : OFF_AU);
+            const uint32_t dst_hi = sb + (ch ? OFF_AW : OFF_AU), dst_lo = sb + (ch ? OFF_TF : OFF_AF);
             const int i = 16 * sp + lane;
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
@@ -409,9 +425,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const float *f = reinterpret_cast<const float *>(v + 8 * q);
-                        ptx::st_shared_v4(dst + ptx::sw128(64 + i, 32 * hh + 8 * q), ptx::pack_bf16(f[0], f[1]),
-                                          ptx::pack_bf16(f[2], f[3]), ptx::pack_bf16(f[4], f[5]),
-                                          ptx::pack_bf16(f[6], f[7]));
+                        uint32_t hi[4], lo[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            hi[e] = ptx::pack_bf16(f[2 * e], f[2 * e + 1]);
+                            lo[e] = ptx::pack_bf16(f[2 * e] - ptx::bf16lo(hi[e]), f[2 * e + 1] - ptx::bf16hi(hi[e]));
+                        }
+                        const uint32_t off = ptx::sw128(64 + i, 32 * hh + 8 * q);
+                        ptx::st_shared_v4(dst_hi + off, hi[0], hi[1], hi[2], hi[3]);
+                        ptx::st_shared_v4(dst_lo + off, lo[0], lo[1], lo[2], lo[3]);
                     }
                 }
             }
@@ -425,11 +447,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::tc_fence_after();
             const uint32_t id = ptx::idesc_bf16(128, 128, 0, 1);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                ptx::umma_bf16(tmem + TM_UY, ptx::sdesc(sb + OFF_AU + kk * 32, 16, 1024),
-                               ptx::sdesc(stg + 32768 + kk * 2048, 8192, 1024), id, kk > 0);
-                ptx::umma_bf16(tmem + TM_W, ptx::sdesc(sb + OFF_AW + kk * 32, 16, 1024),
-                               ptx::sdesc(stg + kk * 2048, 16384, 1024), id, kk > 0);
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t au = (kk < 4) ? OFF_AU : OFF_AF, aw = (kk < 4) ? OFF_AW : OFF_TF;
+                ptx::umma_bf16(tmem + TM_UY, ptx::sdesc(sb + au + (kk & 3) * 32, 16, 1024),
+                               ptx::sdesc(stg + 32768 + (kk & 3) * 2048, 8192, 1024), id, kk > 0);
+                ptx::umma_bf16(tmem + TM_W, ptx::sdesc(sb + aw + (kk & 3) * 32, 16, 1024),
+                               ptx::sdesc(stg + (kk & 3) * 2048, 16384, 1024), id, kk > 0);
             }
             ptx::umma_commit(bar_mma);
         }
@@ -506,11 +529,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (r < 64) {
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        ptx::st_shared_v4(sb + OFF_AF + ch * 8192 + ptx::sw128(r, 32 * hh + 8 * q),
-                                          ptx::pack_bf16(vs * f[8 * q + 0], vs * f[8 * q + 1]),
-                                          ptx::pack_bf16(vs * f[8 * q + 2], vs * f[8 * q + 3]),
-                                          ptx::pack_bf16(vs * f[8 * q + 4], vs * f[8 * q + 5]),
-                                          ptx::pack_bf16(vs * f[8 * q + 6], vs * f[8 * q + 7]));
+                        uint32_t hi[4], lo[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float x0 = vs * f[8 * q + 2 * e], x1 = vs * f[8 * q + 2 * e + 1];
+                            hi[e] = ptx::pack_bf16(x0, x1);
+                            lo[e] = ptx::pack_bf16(x0 - ptx::bf16lo(hi[e]), x1 - ptx::bf16hi(hi[e]));
+                        }
+                        const uint32_t off = ch * 8192 + ptx::sw128(r, 32 * hh + 8 * q);
+                        ptx::st_shared_v4(sb + OFF_AF + off, hi[0], hi[1], hi[2], hi[3]);
+                        ptx::st_shared_v4(sb + OFF_TF + off, lo[0], lo[1], lo[2], lo[3]);
                     }
                 } else if (write_y) {
                     TO *dst = yrow + 64 * ch + 32 * hh;
@@ -528,9 +556,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::tc_fence_after();
             const uint32_t id = ptx::idesc_bf16(128, 128, 1, 1);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                ptx::umma_bf16(tmem + TM_S, ptx::sdesc(stg + kk * 2048, 16384, 1024),
-                               ptx::sdesc(sb + OFF_AF + kk * 2048, 8192, 1024), id, 1);
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t vpart = (kk < 4) ? OFF_AF : OFF_TF;
+                ptx::umma_bf16(tmem + TM_S, ptx::sdesc(stg + (kk & 3) * 2048, 16384, 1024),
+                               ptx::sdesc(sb + vpart + (kk & 3) * 2048, 8192, 1024), id, 1);
             }
             ptx::umma_commit(bar_mma);
         }

@@ -59,6 +59,7 @@ def check(raw, tol=BF16_TOL):
     assert abi.lib().dc_device_status(1) == 0, "a bounded wait in the kernel ran out"
     y0, s0 = reference(raw, qkv)
     ey, es = np.abs(y - y0).max(), np.abs(s - s0).max()
+    print(f"max |y - ref| {ey:.3e} (|ref| {np.abs(y0).max():.2f}); max |S - ref| {es:.3e} (|ref| {np.abs(s0).max():.2f})")
     assert ey < tol and es < tol, (ey, es)
     return ey, es
 

@@ -68,10 +68,10 @@ constexpr uint32_t OFF_AU = 2 * kStageBytes;            // [Tb; Pb] 128x64 bf16 
 constexpr uint32_t OFF_AW = OFF_AU + 16384;             // [Tw; Pw];                     A6 block 1
 constexpr uint32_t OFF_S = OFF_AW + 16384;              // S bf16, MN-major, two 64-column blocks of 16 KB
 constexpr uint32_t OFF_AQK = OFF_S + 32768;             // Aqk bf16 64x64 K-major
-constexpr uint32_t OFF_AF = OFF_AQK + 8192;             // Akk fp32 [64][65]; later V' high part (2 x 8 KB)
-constexpr uint32_t OFF_TF = OFF_AF + 17408;             // T fp32 [64][65];   later V' low part (2 x 8 KB)
-constexpr uint32_t OFF_X = OFF_TF + 17408;              // solve scratch: 3 blocks [16][17] fp32
-constexpr uint32_t OFF_GATE = OFF_X + 3 * 16 * 17 * 4;  // per stage: e[64], w[64], g[64]
+constexpr int kAP = 68;                                 // row pitch (floats) of the fp32 Akk and T tiles
+constexpr uint32_t OFF_AF = OFF_AQK + 8192;             // Akk fp32 [64][68]; later T/V' low-part operands
+constexpr uint32_t OFF_TF = OFF_AF + 64 * kAP * 4;      // T fp32 [64][68];   later T/V' low-part operands
+constexpr uint32_t OFF_GATE = OFF_TF + 64 * kAP * 4;    // per stage: e[64], w[64], g[64]
 constexpr uint32_t OFF_G = OFF_GATE + 2 * 3 * 64 * 4;   // G[64], gam[64]
 constexpr uint32_t OFF_BAR = OFF_G + 2 * 64 * 4;        // mbarriers: tma[2], mma
 constexpr uint32_t OFF_TMEMPTR = OFF_BAR + 3 * 8;
@@ -108,6 +108,89 @@ __device__ __forceinline__ float load_gate(const CoreParams &p, int64_t b, int64
     return gate_at(g + (b * p.seq + pos / p.u) * p.heads + h);
 }
 
+// 32 consecutive outputs of one row, as 16-byte stores.
+__device__ __forceinline__ void store_row32(float *dst, const float *f) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+        reinterpret_cast<float4 *>(dst)[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+}
+__device__ __forceinline__ void store_row32(__nv_bfloat16 *dst, const float *f) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        reinterpret_cast<uint4 *>(dst)[q] =
+            make_uint4(ptx::pack_bf16(f[8 * q], f[8 * q + 1]), ptx::pack_bf16(f[8 * q + 2], f[8 * q + 3]),
+                       ptx::pack_bf16(f[8 * q + 4], f[8 * q + 5]), ptx::pack_bf16(f[8 * q + 6], f[8 * q + 7]));
+}
+
+// Phase timestamps for performance work: compiled out unless a build defines
+// DC_TC_MARK(id) (the chunk index `c` is in scope at every mark).
+#ifndef DC_TC_MARK
+#define DC_TC_MARK(id)
+#endif
+
+// Off-diagonal blocks of block column Q of T = (I + A)^-1 (16x16 blocks of a
+// 64x64 unit lower-triangular inverse), given the diagonal blocks T_pp already
+// in Tf:  T_pQ = -T_pp X_p,  X_p = sum_{r=Q}^{p-1} A_pr T_rQ,  p = Q+1 .. 3.
+// G lanes share one column j of the block column and own 16 / G rows each;
+// the full column is gathered by warp shuffles (a column's lanes sit in one
+// warp).  `t` is the thread's index within the group's 16 * G threads.
+template <int Q, int G>
+__device__ __forceinline__ void solve_block_column(const float *Af, float *Tf, int t) {
+    constexpr int R = 16 / G;  // rows per lane
+    const int j = t / G, part = t % G;
+    const int lane = threadIdx.x & 31, base = lane - part;
+    const int col = 16 * Q + j;
+    float tc[4 - Q][16];  // tc[r - Q][m] = T_rQ[m][j] for the blocks known so far
+#pragma unroll
+    for (int m = 0; m < 16; ++m) tc[0][m] = Tf[(16 * Q + m) * kAP + col];
+#pragma unroll
+    for (int pr = Q + 1; pr < 4; ++pr) {
+        float x[R];
+#pragma unroll
+        for (int e = 0; e < R; ++e) {
+            const int a = part * R + e;
+            float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+            for (int rr = Q; rr < pr; ++rr) {
+                const float *Arow = Af + (16 * pr + a) * kAP + 16 * rr;
+#pragma unroll
+                for (int m = 0; m < 16; m += 4) {
+                    const float4 av = *reinterpret_cast<const float4 *>(Arow + m);
+                    acc0 = fmaf(av.x, tc[rr - Q][m], acc0);
+                    acc1 = fmaf(av.y, tc[rr - Q][m + 1], acc1);
+                    acc0 = fmaf(av.z, tc[rr - Q][m + 2], acc0);
+                    acc1 = fmaf(av.w, tc[rr - Q][m + 3], acc1);
+                }
+            }
+            x[e] = acc0 + acc1;
+        }
+        float xf[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) xf[k] = __shfl_sync(0xffffffffu, x[k % R], base + k / R);
+        float tn[R];
+#pragma unroll
+        for (int e = 0; e < R; ++e) {
+            const int a = part * R + e;
+            const float *Trow = Tf + (16 * pr + a) * kAP + 16 * pr;
+            float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+            for (int m = 0; m < 16; m += 4) {
+                const float4 tv = *reinterpret_cast<const float4 *>(Trow + m);
+                acc0 = fmaf(tv.x, xf[m], acc0);
+                acc1 = fmaf(tv.y, xf[m + 1], acc1);
+                acc0 = fmaf(tv.z, xf[m + 2], acc0);
+                acc1 = fmaf(tv.w, xf[m + 3], acc1);
+            }
+            tn[e] = -(acc0 + acc1);
+            Tf[(16 * pr + a) * kAP + col] = tn[e];
+        }
+        if (pr < 3) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) tc[pr - Q][k] = __shfl_sync(0xffffffffu, tn[k % R], base + k / R);
+        }
+    }
+}
+
 // Every thread waits; returns false (uniformly across the CTA) if any timed out.
 __device__ __forceinline__ bool wait_all(uint64_t *bar, uint32_t parity, volatile int *flag) {
     if (!ptx::mbar_wait(bar, parity)) *flag = 1;
@@ -124,7 +207,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sb = ptx::smem_u32(base);
     float *Af = reinterpret_cast<float *>(base + OFF_AF);
     float *Tf = reinterpret_cast<float *>(base + OFF_TF);
-    float *Xs = reinterpret_cast<float *>(base + OFF_X);
     float *gates = reinterpret_cast<float *>(base + OFF_GATE);  // [stage][3][64]
     float *Gc = reinterpret_cast<float *>(base + OFF_G);        // G[64]
     float *gam = Gc + 64;                                       // e^G[64]
@@ -247,6 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float *ge = gates + (stage * 3 + 0) * 64;
         const float *gw = gates + (stage * 3 + 1) * 64;
 
+        DC_TC_MARK(0);
         // ---- inputs of chunk c; start chunk c+1's loads ----
         ok = wait_all(&bar_tma[stage], (uint32_t)((c >> 1) & 1), flag);
         if (!ok) break;
@@ -260,6 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float gate_next = 0.f;
         if (has_next && tid < 192) gate_next = load_gate<TG>(p, b, h, c + 1, tid);
 
+        DC_TC_MARK(1);
         // ---- D1 = [K; Q] K^T ----
         if (leader) {
             ptx::tc_fence_after();
@@ -276,37 +360,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_phase ^= 1;
         if (!ok) break;
 
-        // ---- masks: Akk (fp32) and Aqk (bf16 operand) ----
+        DC_TC_MARK(2);
+        // ---- masks: Akk (fp32, rows 0-63 of D1) and Aqk (bf16 operand, rows 64-127) ----
         ptx::tc_fence_after();
         {
             uint32_t v[32];
             ptx::tmem_ld32(tmem + lane_base + TM_A + 32 * ch, v);
             ptx::tmem_wait_ld();
-            if (r < 64) {
-                const int i = r;
-                const float ei = ge[i], Gi = Gc[i];
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) {
-                    const int j = 32 * ch + jj;
-                    float a = 0.f;
-                    if (j < i) a = ei * __uint_as_float(v[jj]) * (gated ? __expf(Gi - Gc[j]) : 1.f);
-                    Af[i * 65 + j] = a;
-                }
-            } else {
-                const int i = r - 64;
+            const int i = r & 63;
+            const float coef = (r < 64) ? ge[i] : scale;
+            float a[32];
+            if (gated) {
                 const float Gi = Gc[i];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    float a[8];
+                for (int jj = 0; jj < 32; ++jj) a[jj] = coef * __uint_as_float(v[jj]) * __expf(Gi - Gc[32 * ch + jj]);
+            } else {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const int j = 32 * ch + 8 * q + e;
-                        a[e] = (j <= i) ? scale * __uint_as_float(v[8 * q + e]) * (gated ? __expf(Gi - Gc[j]) : 1.f)
-                                        : 0.f;
-                    }
-                    ptx::st_shared_v4(sb + OFF_AQK + ptx::sw128(i, 32 * ch + 8 * q), ptx::pack_bf16(a[0], a[1]),
-                                      ptx::pack_bf16(a[2], a[3]), ptx::pack_bf16(a[4], a[5]),
-                                      ptx::pack_bf16(a[6], a[7]));
+                for (int jj = 0; jj < 32; ++jj) a[jj] = coef * __uint_as_float(v[jj]);
+            }
+            if (r < 64) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int j = 32 * ch + 4 * q;
+                    *reinterpret_cast<float4 *>(Af + i * kAP + j) =
+                        make_float4(j < i ? a[4 * q] : 0.f, j + 1 < i ? a[4 * q + 1] : 0.f,
+                                    j + 2 < i ? a[4 * q + 2] : 0.f, j + 3 < i ? a[4 * q + 3] : 0.f);
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    float m[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) m[e] = (32 * ch + 8 * q + e <= i) ? a[8 * q + e] : 0.f;
+                    ptx::st_shared_v4(sb + OFF_AQK + ptx::sw128(i, 32 * ch + 8 * q), ptx::pack_bf16(m[0], m[1]),
+                                      ptx::pack_bf16(m[2], m[3]), ptx::pack_bf16(m[4], m[5]),
+                                      ptx::pack_bf16(m[6], m[7]));
                 }
             }
         }
@@ -314,61 +402,60 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_before();
         __syncthreads();
 
-        // ---- T = (I + Akk)^-1, blocked: 16x16 diagonal blocks, then block substitution ----
+        DC_TC_MARK(3);
+        // ---- T = (I + Akk)^-1 in 16x16 blocks ----
+        // (1) The diagonal blocks T_pp = (I + A_pp)^-1: one thread substitutes down each column.
         if (tid < 64) {
             const int pb = tid >> 4, j = tid & 15;
-            const float *A = Af + (16 * pb) * 65 + 16 * pb;
+            const float *A = Af + (16 * pb) * kAP + 16 * pb;
             float tcol[16];
 #pragma unroll
             for (int a = 0; a < 16; ++a) {
-                float acc = (a == j) ? 1.f : 0.f;
+                float acc0 = (a == j) ? 1.f : 0.f, acc1 = 0.f;
 #pragma unroll
-                for (int m = 0; m < a; ++m) acc = fmaf(-A[a * 65 + m], tcol[m], acc);
-                tcol[a] = acc;
+                for (int m = 0; m < a; m += 4) {
+                    const float4 av = *reinterpret_cast<const float4 *>(A + a * kAP + m);
+                    acc0 = fmaf(-av.x, tcol[m], acc0);
+                    if (m + 1 < a) acc1 = fmaf(-av.y, tcol[m + 1], acc1);
+                    if (m + 2 < a) acc0 = fmaf(-av.z, tcol[m + 2], acc0);
+                    if (m + 3 < a) acc1 = fmaf(-av.w, tcol[m + 3], acc1);
+                }
+                tcol[a] = acc0 + acc1;
             }
 #pragma unroll
-            for (int a = 0; a < 16; ++a) Tf[(16 * pb + a) * 65 + 16 * pb + j] = tcol[a];
-        }
-        for (int idx = tid; idx < 6 * 256; idx += kThreads) {  // strictly-upper blocks are zero
-            const int blk = idx >> 8, e = idx & 255;
-            const int pr = blk < 3 ? 0 : (blk < 5 ? 1 : 2);   // (0,1) (0,2) (0,3) (1,2) (1,3) (2,3)
-            const int qc = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
-            Tf[(16 * pr + (e >> 4)) * 65 + 16 * qc + (e & 15)] = 0.f;
+            for (int a = 0; a < 16; ++a) Tf[(16 * pb + a) * kAP + 16 * pb + j] = tcol[a];
         }
         __syncthreads();
-#pragma unroll 1
-        for (int lvl = 1; lvl < 4; ++lvl) {
-            const int nb = 4 - lvl;
-            // X_pq = sum_{r=q}^{p-1} A_pr T_rq,   p = q + lvl
-            for (int idx = tid; idx < nb * 256; idx += kThreads) {
-                const int q = idx >> 8, a = (idx >> 4) & 15, j = idx & 15, pr = q + lvl;
-                float acc = 0.f;
-                for (int rr = q; rr < pr; ++rr) {
-#pragma unroll
-                    for (int m = 0; m < 16; ++m)
-                        acc = fmaf(Af[(16 * pr + a) * 65 + 16 * rr + m], Tf[(16 * rr + m) * 65 + 16 * q + j], acc);
-                }
-                Xs[(q * 16 + a) * 17 + j] = acc;
-            }
-            __syncthreads();
-            // T_pq = -T_pp X_pq
-            for (int idx = tid; idx < nb * 256; idx += kThreads) {
-                const int q = idx >> 8, a = (idx >> 4) & 15, j = idx & 15, pr = q + lvl;
-                float acc = 0.f;
-#pragma unroll
-                for (int m = 0; m < 16; ++m)
-                    acc = fmaf(Tf[(16 * pr + a) * 65 + 16 * pr + m], Xs[(q * 16 + m) * 17 + j], acc);
-                Tf[(16 * pr + a) * 65 + 16 * q + j] = -acc;
-            }
-            __syncthreads();
+        DC_TC_MARK(13);
+        DC_TC_MARK(14);
+        // (2) The blocks below the diagonal, T_pq = -T_pp sum_{r=q}^{p-1} A_pr T_rq,
+        //     one block column per warp group: block column 0 on warps 0-3 (8 lanes
+        //     per column, 2 rows each), 1 on warps 4-5 and 2 on warps 6-7 (4 lanes
+        //     per column, 4 rows each).  A column's lanes share one warp, so the
+        //     substitution down the column needs no block-wide barrier.
+        if (warp < 4) {
+            solve_block_column<0, 8>(Af, Tf, tid);
+        } else if (warp < 6) {
+            solve_block_column<1, 4>(Af, Tf, tid - 128);
+        } else {
+            solve_block_column<2, 4>(Af, Tf, tid - 192);
         }
+        __syncthreads();
+        DC_TC_MARK(4);
         // Tb = T diag(w), Tw = T diag(e gam) as bf16 hi + lo: the tops of A_U / A_W
-        // and of their low-part twins (which reuse the Akk and T buffers).
+        // and of their low-part twins (which reuse the Akk and T buffers).  T's
+        // blocks above the diagonal are never written: masked here.
         {
             const int i = tid >> 2, j0 = (tid & 3) * 16;
             float t[16];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) t[e] = Tf[i * 65 + j0 + e];
+            for (int m = 0; m < 16; m += 4) {
+                const float4 tv = *reinterpret_cast<const float4 *>(Tf + i * kAP + j0 + m);
+                t[m] = j0 + m <= i ? tv.x : 0.f;
+                t[m + 1] = j0 + m + 1 <= i ? tv.y : 0.f;
+                t[m + 2] = j0 + m + 2 <= i ? tv.z : 0.f;
+                t[m + 3] = j0 + m + 3 <= i ? tv.w : 0.f;
+            }
             __syncthreads();  // every T read is done before the T buffer is overwritten
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
@@ -395,6 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::fence_async_smem();
         __syncthreads();
 
+        DC_TC_MARK(5);
         // ---- D_P = Aqk [Tb | Tw] ----
         if (leader) {
             ptx::tc_fence_after();
@@ -411,16 +499,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_phase ^= 1;
         if (!ok) break;
 
+        DC_TC_MARK(6);
         // ---- Pb, Pw (hi + lo): the bottoms of the four A operands (M=64 accumulator: rows in lanes 0-15) ----
         ptx::tc_fence_after();
         {
             const uint32_t dst_hi = sb + (ch ? OFF_AW : OFF_AU), dst_lo = sb + (ch ? OFF_TF : OFF_AF);
             const int i = 16 * sp + lane;
+            uint32_t vv[2][32];
+            ptx::tmem_ld32(tmem + lane_base + TM_A + 64 * ch, vv[0]);
+            ptx::tmem_ld32(tmem + lane_base + TM_A + 64 * ch + 32, vv[1]);
+            ptx::tmem_wait_ld();
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-                uint32_t v[32];
-                ptx::tmem_ld32(tmem + lane_base + TM_A + 64 * ch + 32 * hh, v);
-                ptx::tmem_wait_ld();
+                const uint32_t *v = vv[hh];
                 if (lane < 16) {
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
@@ -442,6 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_before();
         __syncthreads();
 
+        DC_TC_MARK(7);
         // ---- D_UY = [Tb; Pb] V,  D_W = [Tw; Pw] K ----
         if (leader) {
             ptx::tc_fence_after();
@@ -460,17 +552,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_phase ^= 1;
         if (!ok) break;
 
+        DC_TC_MARK(8);
         // ---- A6 = [-W; s gam Q - Aqk W] (K-major over d, blocks of 64 columns) ----
         ptx::tc_fence_after();
         {
             const uint32_t blk = sb + (ch ? OFF_AW : OFF_AU);
             const uint32_t qblk = stg + ch * 16384 + 8192;
             const float qs = (r >= 64) ? scale * gam[r - 64] : 0.f;
+            uint32_t vv[2][32];
+            ptx::tmem_ld32(tmem + lane_base + TM_W + 64 * ch, vv[0]);
+            ptx::tmem_ld32(tmem + lane_base + TM_W + 64 * ch + 32, vv[1]);
+            ptx::tmem_wait_ld();
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-                uint32_t v[32];
-                ptx::tmem_ld32(tmem + lane_base + TM_W + 64 * ch + 32 * hh, v);
-                ptx::tmem_wait_ld();
+                const uint32_t *v = vv[hh];
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     float a[8];
@@ -497,6 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_before();
         __syncthreads();
 
+        DC_TC_MARK(9);
         // ---- D_UY += A6 S  ->  [V'; y] ----
         if (leader) {
             ptx::tc_fence_after();
@@ -512,6 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_phase ^= 1;
         if (!ok) break;
 
+        DC_TC_MARK(10);
         // ---- V' (decayed to the chunk end) -> operand; y -> HBM ----
         ptx::tc_fence_after();
         {
@@ -520,12 +617,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t pos = c * kL + (r - 64);
             const bool write_y = (r >= 64) && pos < P && (pos % p.u) == (p.u - 1);
             TO *yrow = static_cast<TO *>(p.y) + ((b * p.seq + (write_y ? pos / p.u : 0)) * p.heads + h) * kD;
+            uint32_t vv[2][32];
+            ptx::tmem_ld32(tmem + lane_base + TM_UY + 64 * ch, vv[0]);
+            ptx::tmem_ld32(tmem + lane_base + TM_UY + 64 * ch + 32, vv[1]);
+            ptx::tmem_wait_ld();
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-                uint32_t v[32];
-                ptx::tmem_ld32(tmem + lane_base + TM_UY + 64 * ch + 32 * hh, v);
-                ptx::tmem_wait_ld();
-                const float *f = reinterpret_cast<const float *>(v);
+                const float *f = reinterpret_cast<const float *>(vv[hh]);
                 if (r < 64) {
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
@@ -541,9 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ptx::st_shared_v4(sb + OFF_TF + off, lo[0], lo[1], lo[2], lo[3]);
                     }
                 } else if (write_y) {
-                    TO *dst = yrow + 64 * ch + 32 * hh;
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) st(dst + e, f[e]);
+                    store_row32(yrow + 64 * ch + 32 * hh, f);
                 }
             }
         }
@@ -551,6 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_before();
         __syncthreads();
 
+        DC_TC_MARK(11);
         // ---- D_S = Gam S + K^T V~' ----
         if (leader) {
             ptx::tc_fence_after();
@@ -567,6 +664,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_phase ^= 1;
         if (!ok) break;
 
+        DC_TC_MARK(12);
         // ---- next chunk's gates, then S -> bf16 operand and the pre-scaled accumulator ----
         if (has_next) {
             if (tid < 192) gates[(stage ^ 1) * 192 + tid] = gate_next;
@@ -575,12 +673,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncthreads();
             const float Gam = gam[63];
             ptx::tc_fence_after();
+            uint32_t vv[2][32];
+            ptx::tmem_ld32(tmem + lane_base + TM_S + 64 * ch, vv[0]);
+            ptx::tmem_ld32(tmem + lane_base + TM_S + 64 * ch + 32, vv[1]);
+            ptx::tmem_wait_ld();
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-                uint32_t v[32];
+                uint32_t(&v)[32] = vv[hh];
                 const uint32_t ta = tmem + lane_base + TM_S + 64 * ch + 32 * hh;
-                ptx::tmem_ld32(ta, v);
-                ptx::tmem_wait_ld();
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     const float *f = reinterpret_cast<const float *>(v + 8 * q);

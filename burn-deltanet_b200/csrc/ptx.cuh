@@ -51,12 +51,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return done != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
+// Bounded wait for the phase with the given parity to complete.  try_wait
+// itself suspends the thread for a while, so the clock is read only every
+// 256 polls.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
+    uint32_t n = 0;
     while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer() - t0 > kWaitLimitNs) return false;
+        if ((++n & 255u) == 0 && globaltimer() - t0 > kWaitLimitNs) return false;
     }
     return true;
 }
@@ -168,10 +171,11 @@ __device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t col) {
     return row * 128u + ((((col >> 3) ^ (row & 7u)) << 4) | ((col & 7u) << 1));
 }
 
+// Two floats to a packed bf16 pair (round to nearest even), low half first.
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-    const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
-    const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
-    return a | (b << 16);
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t saddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {

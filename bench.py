@@ -338,6 +338,31 @@ def time_decode(dn, steps, warmup):
     return ms, step_bytes
 
 
+def time_allgather(batch, tokens, world):
+    """The one collective of the sharded path: all-gather every rank's y
+    (bf16 [batch, T, H, dv]) into the global output on every rank (NCCL).
+    Timed on its own, after the data path; not part of `value`."""
+    sh = importlib.import_module("burn-deltanet_b200.sharding")
+    shards = sh.plan(batch * world, H, world)
+    y = torch.randn(batch, tokens, H, D, device="cuda").to(torch.bfloat16)
+    for _ in range(2):
+        sh.gather(y, shards)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record()
+    for _ in range(reps):
+        out = sh.gather(y, shards)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / reps, world)
+    nbytes = out.numel() * out.element_size()
+    del out
+    return {"ms": ms, "bytes_per_rank_out": nbytes,
+            "bus_gbs": nbytes * (world - 1) / world / (ms / 1e3) / 1e9, "collective": "nccl all_gather_into_tensor"}
+
+
 def run_ours(args):
     rank, world, local = setup(args.gpus)
     dn = importlib.import_module("burn-deltanet_b200")
@@ -372,6 +397,9 @@ def run_ours(args):
     dec_ms = max_over_ranks(dec_ms, world)
     dec_tok = DECODE["batch"] * world / (dec_ms / 1e3)
     traffic = profiled_traffic(args.workload)
+    gather_info = None
+    if world > 1:
+        gather_info = time_allgather(batch, tokens, world)
     line = {
         "metric": f"prefill tok/s ({kind}, bf16 in, fp32 state, H={H} dk=dv={D}, chunk {L})",
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -395,6 +423,8 @@ def run_ours(args):
                    "gpu_launches": 256},
         "clocks": clocks.summary(),
     }
+    if gather_info is not None:
+        line["allgather"] = gather_info
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.workload)
     if rank == 0:

@@ -26,6 +26,7 @@ DC_F32 = 0
 DC_BF16 = 1
 
 DC_FLAG_FORCE_SIMT = 0x1
+DC_FLAG_RECURRENT = 0x2
 
 EXPORTS = (
     "dc_chunk_fwd", "dc_step", "dc_status_string", "dc_last_cuda_error", "dc_device_status",

@@ -146,6 +146,7 @@ def beta_gates(beta: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
 def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv,
                              has_gate: bool, chunk_len: int, scale: float, *, n_householder: int = 1,
                              out_dtype: Optional[torch.dtype] = None, force_simt: bool = False,
+                             recurrent: bool = False,
                              y_out: Optional[torch.Tensor] = None, state_out: Optional[torch.Tensor] = None):
     """The backend-extension op (chunk_recalculated.rs:115-126) on CUDA tensors.
 
@@ -154,6 +155,8 @@ def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_b
     (ignored unless ``has_gate``); state [b, h, dk, dv] float32.
     Returns ``(y [b, s, h, dv], final_state [b, h, dk, dv])`` as new tensors
     unless ``y_out`` / ``state_out`` are given (``state_out`` may be ``state_bhkv``).
+    ``recurrent=True`` evaluates DeltaPath::Recurrent: the fused decode tick walks
+    the sequence token by token (one launch per token).
     """
     ts = dict(q=q_bshk, k=k_bshk, v=v_bshv, erase=erase_bshK, write=write_bshV, state=state_bhkv)
     if has_gate:
@@ -191,7 +194,7 @@ def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_b
     a.g_w = g_bshK.shape[3] if has_gate else 0
     a.chunk_len = int(chunk_len)
     a.in_dtype, a.gate_dtype, a.out_dtype = in_dt, gate_dt, _dtype_code(y, "y")
-    a.flags = _abi.DC_FLAG_FORCE_SIMT if force_simt else 0
+    a.flags = (_abi.DC_FLAG_FORCE_SIMT if force_simt else 0) | (_abi.DC_FLAG_RECURRENT if recurrent else 0)
     a.scale = float(scale)
     a.q, a.k, a.v = q_bshk.data_ptr(), k_bshk.data_ptr(), v_bshv.data_ptr()
     a.erase, a.write = erase_bshK.data_ptr(), write_bshV.data_ptr()
@@ -329,18 +332,7 @@ class DeltaInput:
 
     def delta_recurrent(self):
         """Unroll the fused step over the sequence (src/delta/recurrent.rs:107-142)."""
-        b, s, h, dk, dv = self.dims()
-        u = self.n_householder
-        scale = self.resolved_scale()
-        state = self.state_bhkv.clone()
-        ys = torch.empty((b, s, h, dv), device=self.q_bshk.device, dtype=self.q_bshk.dtype)
-        rows = lambda t: t.view(b, s, u, h, t.shape[3])
-        k, v, e, w = (rows(t) for t in (self.k_bshk, self.v_bshv, self.erase_bshK, self.write_bshV))
-        for t in range(s):
-            y, _ = delta_step(
-                self.q_bshk[:, t].contiguous(), k[:, t].contiguous(), v[:, t].contiguous(),
-                e[:, t].contiguous(), w[:, t].contiguous(),
-                None if self.g_bshK is None else self.g_bshK[:, t].contiguous(),
-                state, scale, n_householder=u, state_out=state)
-            ys[:, t] = y
-        return ys, state
+        return delta_chunk_recalculated(
+            self.q_bshk, self.k_bshk, self.v_bshv, self.erase_bshK, self.write_bshV, self.g_bshK,
+            self.state_bhkv, self.g_bshK is not None, 1, self.resolved_scale(),
+            n_householder=self.n_householder, recurrent=True)

@@ -735,7 +735,7 @@ inline bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
 // Whether the tensor-core kernel serves this request.
 inline bool tc_applies(const CoreParams &p, int32_t in_dtype, uint32_t flags) {
-    if (flags & 0x1u) return false;  // DC_FLAG_FORCE_SIMT
+    if (flags & 0x3u) return false;  // DC_FLAG_FORCE_SIMT, DC_FLAG_RECURRENT
     if (in_dtype != 1) return false; // bf16 q, k, v
     if (p.dk != 128 || p.dv != 128) return false;
     if (p.ew != 1 || p.ww != 1 || p.gw > 1) return false;

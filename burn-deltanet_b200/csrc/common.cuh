@@ -19,6 +19,10 @@ struct CoreParams {
     int64_t batch, seq, heads, dk, dv;
     int32_t u;                 // n_householder
     int32_t ew, ww, gw;        // gate widths: erase {1, dk}, write {1, dv}, g {0, 1, dk}
+    // Rows between consecutive batches, for the decode tick only: of k, v,
+    // erase, write (u for one token; seq * u when the tick walks a sequence in
+    // place) and of q, g, y (1 for one token; seq for a sequence).
+    int64_t kv_bstride, q_bstride;
     float scale;
     const void *q, *k, *v, *erase, *write, *g;
     const float *state_in;

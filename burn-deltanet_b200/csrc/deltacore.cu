@@ -87,6 +87,8 @@ dc::CoreParams make_params(int64_t batch, int64_t seq, int64_t heads, int64_t dk
     p.scale = (float)scale;
     p.q = q; p.k = k; p.v = v; p.erase = erase; p.write = write; p.g = gw ? g : nullptr;
     p.state_in = s_in; p.y = y; p.state_out = s_out;
+    p.kv_bstride = (int64_t)u * seq;
+    p.q_bstride = seq;
     return p;
 }
 
@@ -222,7 +224,33 @@ int dc_chunk_kernel_choice(const dc_chunk_args *a) {
 int dc_chunk_launches(const dc_chunk_args *a) {
     const int st = validate_chunk(a);
     if (st != DC_OK) return -st;
-    return (a->batch == 0 || a->heads == 0) ? 0 : 1;
+    if (a->batch == 0 || a->heads == 0) return 0;
+    return (a->flags & DC_FLAG_RECURRENT) ? (int)a->seq : 1;
+}
+
+// DeltaPath::Recurrent: the fused tick walks the sequence in place, one launch
+// per token, reading each token's rows through the batch strides (no copies).
+static int run_recurrent(const dc_chunk_args *a, cudaStream_t s) {
+    const size_t isz = a->in_dtype == DC_F32 ? 4 : 2, gsz = a->gate_dtype == DC_F32 ? 4 : 2;
+    const size_t osz = a->out_dtype == DC_F32 ? 4 : 2;
+    const int64_t H = a->heads, u = a->n_householder;
+    for (int64_t t = 0; t < a->seq; ++t) {
+        const char *q = static_cast<const char *>(a->q) + (size_t)(t * H * a->dk) * isz;
+        const char *k = static_cast<const char *>(a->k) + (size_t)(t * u * H * a->dk) * isz;
+        const char *v = static_cast<const char *>(a->v) + (size_t)(t * u * H * a->dv) * isz;
+        const char *e = static_cast<const char *>(a->erase) + (size_t)(t * u * H * a->erase_w) * gsz;
+        const char *w = static_cast<const char *>(a->write) + (size_t)(t * u * H * a->write_w) * gsz;
+        const char *g = a->g_w ? static_cast<const char *>(a->g) + (size_t)(t * H * a->g_w) * gsz : nullptr;
+        char *y = static_cast<char *>(a->y) + (size_t)(t * H * a->dv) * osz;
+        dc::CoreParams p = make_params(a->batch, 1, a->heads, a->dk, a->dv, a->n_householder, a->erase_w, a->write_w,
+                                       a->g_w, a->scale, q, k, v, e, w, g, t == 0 ? a->state_in : a->state_out, y,
+                                       a->state_out);
+        p.kv_bstride = a->seq * u;
+        p.q_bstride = a->seq;
+        const int st = dispatch_types<StepLauncher>(a->in_dtype, a->gate_dtype, a->out_dtype, p, s);
+        if (st != DC_OK) return st;
+    }
+    return DC_OK;
 }
 
 int dc_chunk_fwd(const dc_chunk_args *a, dc_stream_t stream) {
@@ -234,6 +262,7 @@ int dc_chunk_fwd(const dc_chunk_args *a, dc_stream_t stream) {
                                          a->write_w, a->g_w, a->scale, a->q, a->k, a->v, a->erase, a->write, a->g,
                                          a->state_in, a->y, a->state_out);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (a->flags & DC_FLAG_RECURRENT) return run_recurrent(a, s);
     if (dc::tc_applies(p, a->in_dtype, a->flags)) {
         st = dc::launch_chunk_tc(p, a->gate_dtype, a->out_dtype, s);
         if (st == DC_ECUDA) g_last_cuda_error = dc::tc_last_error();

@@ -99,23 +99,24 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(CoreParams p) {
     const TG *write = static_cast<const TG *>(p.write);
     const TG *g = static_cast<const TG *>(p.g);
     const int64_t H = p.heads;
+    const int64_t qrow = b * p.q_bstride * H + h;  // row of q, g and y
     for (int idx = tid; idx < u * dk; idx += kStepThreads) {
         const int m = idx / dk, i = idx % dk;
-        const int64_t row = (b * u + m) * H + h;  // [batch, u, heads, .]
+        const int64_t row = (b * p.kv_bstride + m) * H + h;  // [batch, u, heads, .]
         const float kv = ld(k + row * dk + i);
         const float ev = ld(erase + row * p.ew + (p.ew == 1 ? 0 : i));
         kk[idx] = kv;
         ke[idx] = kv * ev;
     }
     for (int i = tid; i < dk; i += kStepThreads) {
-        decay[i] = p.gw ? expf(ld(g + bh * p.gw + (p.gw == 1 ? 0 : i))) : 1.f;
-        sq[i] = p.scale * ld(q + bh * dk + i);
+        decay[i] = p.gw ? expf(ld(g + qrow * p.gw + (p.gw == 1 ? 0 : i))) : 1.f;
+        sq[i] = p.scale * ld(q + qrow * dk + i);
     }
     for (int idx = tid; idx < u * CW; idx += kStepThreads) {
         const int m = idx / CW, j = idx % CW, c = col_base + j;
         float val = 0.f;
         if (c < dv) {
-            const int64_t row = (b * u + m) * H + h;
+            const int64_t row = (b * p.kv_bstride + m) * H + h;
             val = ld(v + row * dv + c) * ld(write + row * p.ww + (p.ww == 1 ? 0 : c));
         }
         wv[idx] = val;
@@ -198,7 +199,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(CoreParams p) {
         if (last && r0 == 0 && col_ok) {
             const float c = sqk[0];
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) st(y + bh * dv + col + e, fmaf(c, du[e], qs[e]));
+            for (int e = 0; e < VEC; ++e) st(y + qrow * dv + col + e, fmaf(c, du[e], qs[e]));
         }
     }
 

@@ -80,6 +80,8 @@ enum dc_dtype {
 
 /* dc_chunk_args.flags */
 #define DC_FLAG_FORCE_SIMT 0x1u /* run the CUDA-core chunk kernel even where the tensor-core one applies */
+#define DC_FLAG_RECURRENT 0x2u  /* DeltaPath::Recurrent: walk the sequence token by token with the fused
+                                   decode tick (one launch per token, state updated in state_out) */
 
 /*
  * Chunkwise prefill.  Mirrors
@@ -148,7 +150,7 @@ DC_API int dc_device_status(int reset);
  * 0 = CUDA-core; negative = the dc_status the call would return. Pure host logic. */
 DC_API int dc_chunk_kernel_choice(const dc_chunk_args *args);
 
-/* Number of kernels dc_chunk_fwd / dc_step enqueue per call (for launch accounting). */
+/* Number of kernels dc_chunk_fwd enqueues for `args` (for launch accounting); dc_step enqueues one. */
 DC_API int dc_chunk_launches(const dc_chunk_args *args);
 
 /* ABI version: major * 10000 + minor * 100 + patch. */

@@ -2,45 +2,54 @@
 //
 // Serves dc_chunk_fwd for bf16 q/k/v with dk = dv = 128 and per-head gates
 // (the DeltaNet and Gated DeltaNet families).  One CTA owns one (batch, head)
-// and walks its chunks of L = 64 steps serially; the fp32 state S lives in
-// tensor memory for the whole sequence and never touches HBM in between.
+// and walks its chunks of L = 64 steps; the fp32 state S lives in tensor
+// memory for the whole sequence and never touches HBM in between.
 //
 // Per chunk (rows i, j in [0, 64); G = chunk cumsum of g, gam_i = e^{G_i}):
 //
 //   D1   = [K; Q] K^T                                   M=128 N=64  K=128   (tcgen05)
 //   Akk  = tril(e_i (k_i.k_j) e^{G_i-G_j}, -1)           fp32, shared memory (CUDA cores)
 //   Aqk  = tril(s (q_i.k_j) e^{G_i-G_j}, 0)              bf16 operand
-//   T    = (I + Akk)^-1                                  blocked 16x16 forward substitution
+//   T    = (I + Akk)^-1                                  16x16 blocks, forward substitution
 //   Tb   = T diag(w),  Tw = T diag(e gam)                bf16 hi + lo operands
 //   D_P  = Aqk [Tb | Tw]                                 M=64  N=128 K=64    (tcgen05)
-//   D_UY = [Tb; Aqk Tb] V      = [U; Aqk U]              M=128 N=128 K=64    (tcgen05)
-//   D_W  = [Tw; Aqk Tw] K      = [W; Aqk W]              M=128 N=128 K=64    (tcgen05)
-//   A6   = [-W; s gam Q - Aqk W]                         bf16 operand
-//   D_UY += A6 S               = [U - W S; y]            M=128 N=128 K=128   (tcgen05)
-//   D_S  = Gam S + K^T diag(e^{G_63 - G_j}) V'           M=128 N=128 K=64    (tcgen05, accumulate)
+//   D_UY = [Tb; Aqk Tb] V      = [U; Aqk U]              M=128 N=128 K=64    (tcgen05, hi + lo)
+//   D_W  = [Tw; Aqk Tw] K      = [W; Aqk W]              M=128 N=128 K=64    (tcgen05, hi + lo)
+//   A6   = [-W; s gam Q - Aqk W]                         bf16, written into TMEM over D_W
+//   D_UY += A6 S               = [U - W S; y]            M=128 N=128 K=128   (tcgen05, A from TMEM)
+//   D_S  = Gam S + K^T diag(e^{G_63 - G_j}) V'           M=128 N=128 K=64    (tcgen05, hi + lo, accumulate)
 //
-// T (through Tb, Tw and their Aqk products) and V' enter their products as
-// two bf16 terms each (hi + lo, the rounding residual of hi), i.e. at ~16
-// significant bits instead of bf16's 8.  T's long alternating tails (a
-// chunk of near-parallel keys) and V''s rounding are otherwise the two
-// largest errors in the fp32 state; the inputs q, k, v are exact in bf16.
-//
-// The second-to-last line is the reference's scan step (src/delta/chunk.rs:
+// The D_UY += A6 S line is the reference's scan step (src/delta/chunk.rs:
 // 177-187) with its two S products stacked into one M=128 MMA: V' = U - W S
 // comes out in the top 64 TMEM lanes and y = (s gam Q) S + Aqk V' =
 // (s gam Q - Aqk W) S + Aqk U in the bottom 64, because Aqk U and Aqk W are
-// S-independent and are formed before S is needed.  The last line is
-// chunk.rs:191-202 with the per-row decay folded into V'.
+// S-independent and formed before S is needed.  The last line is chunk.rs:
+// 191-202 with the per-row decay folded into V'.
+//
+// Warp specialisation.  Everything above D_UY += A6 S depends only on the
+// chunk's own inputs; only the last three lines depend on S.  Warps 0-7
+// (the "parallel" role) build chunk c+1's operands (masks, solve, Tb/Tw,
+// Pb/Pw) while warps 8-11 (the "serial" role) run chunk c's S chain (A6,
+// V'/y, the state update), so the two chains' latencies overlap.  The roles
+// meet on mbarriers: the serial role waits for chunk c's D_UY/D_W, the
+// parallel role for the serial role to release them (after V'/y) before its
+// next D_UY/D_W, and for the chunk's TMA loads.
+//
+// T (through Tb, Tw and their Aqk products) and V' enter their products as
+// two bf16 terms each (hi + lo, the rounding residual of hi), i.e. at ~16
+// significant bits instead of bf16's 8: T's long alternating tails (a chunk
+// of near-parallel keys) and V''s rounding are otherwise the largest errors
+// in the fp32 state.  The inputs q, k, v are exact in bf16.
 //
 // Operand layouts in shared memory are the 128-byte-swizzled canonical ones
 // (8 rows x 128 B atoms): tiles written by TMA with CU_TENSOR_MAP_SWIZZLE_128B
 // and tiles written by threads through ptx::sw128 share one pattern, so the
 // same bytes serve as a K-major operand of one MMA and an MN-major operand of
-// another (K is both the A of D1 and the B of D_W / the A of D_S).
+// another.  V' (hi, lo) is written into the consumed stage's V and Q slots.
 //
 // Every mbarrier wait is bounded (ptx::kWaitLimitNs); a wait that runs out
-// sets the library's device status word, waits (bounded) for its own TMA loads
-// still in flight, frees its tensor memory and returns.
+// sets the library's device status word, the CTA waits (bounded) for its own
+// TMA loads still in flight, frees its tensor memory and returns.
 #pragma once
 
 #include <cuda.h>
@@ -57,46 +66,52 @@ constexpr int kStatusTimeout = 1;
 
 namespace tc {
 
-constexpr int kThreads = 256;
+constexpr int kParThreads = 256;  // warps 0-7: the S-independent ("parallel") role
+constexpr int kSerThreads = 128;  // warps 8-11: the S chain ("serial") role
+constexpr int kThreads = kParThreads + kSerThreads;
 constexpr int kL = 64;    // chunk rows
 constexpr int kD = 128;   // dk = dv
+constexpr int kAP = 68;   // row pitch (floats) of the fp32 Akk and T tiles
 
 // Shared-memory map (bytes from a 1024-aligned base).
 constexpr uint32_t kStageBytes = 49152;                 // [K|Q d0-63][K|Q d64-127][V d0-63][V d64-127]
 constexpr uint32_t OFF_STAGE = 0;                       // two stages
-constexpr uint32_t OFF_AU = 2 * kStageBytes;            // [Tb; Pb] 128x64 bf16 K-major; A6 block 0
-constexpr uint32_t OFF_AW = OFF_AU + 16384;             // [Tw; Pw];                     A6 block 1
+constexpr uint32_t OFF_AU = 2 * kStageBytes;            // [Tb; Pb] hi, 128x64 bf16 K-major
+constexpr uint32_t OFF_AW = OFF_AU + 16384;             // [Tw; Pw] hi
 constexpr uint32_t OFF_S = OFF_AW + 16384;              // S bf16, MN-major, two 64-column blocks of 16 KB
 constexpr uint32_t OFF_AQK = OFF_S + 32768;             // Aqk bf16 64x64 K-major
-constexpr int kAP = 68;                                 // row pitch (floats) of the fp32 Akk and T tiles
-constexpr uint32_t OFF_AF = OFF_AQK + 8192;             // Akk fp32 [64][68]; later T/V' low-part operands
-constexpr uint32_t OFF_TF = OFF_AF + 64 * kAP * 4;      // T fp32 [64][68];   later T/V' low-part operands
+constexpr uint32_t OFF_AF = OFF_AQK + 8192;             // Akk fp32 [64][68]; then [Tb; Pb] lo
+constexpr uint32_t OFF_TF = OFF_AF + 64 * kAP * 4;      // T fp32 [64][68];   then [Tw; Pw] lo
 constexpr uint32_t OFF_GATE = OFF_TF + 64 * kAP * 4;    // per stage: e[64], w[64], g[64]
-constexpr uint32_t OFF_G = OFF_GATE + 2 * 3 * 64 * 4;   // G[64], gam[64]
-constexpr uint32_t OFF_BAR = OFF_G + 2 * 64 * 4;        // mbarriers: tma[2], mma
-constexpr uint32_t OFF_TMEMPTR = OFF_BAR + 3 * 8;
+constexpr uint32_t OFF_G = OFF_GATE + 2 * 3 * 64 * 4;   // per stage: G[64], gam[64]
+constexpr uint32_t OFF_BAR = OFF_G + 2 * 2 * 64 * 4;    // mbarriers (below)
+constexpr int kBars = 10;
+constexpr uint32_t OFF_TMEMPTR = OFF_BAR + kBars * 8;
 constexpr uint32_t OFF_FLAG = OFF_TMEMPTR + 4;
-constexpr uint32_t kSmemUsed = OFF_FLAG + 4;
+constexpr uint32_t OFF_PEND = OFF_FLAG + 4;             // int[2]: parity of a stage's TMA load in flight, or -1
+constexpr uint32_t kSmemUsed = OFF_PEND + 8;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;       // alignment slack
 static_assert(OFF_AF % 1024 == 0 && OFF_TF % 1024 == 0 && OFF_AQK % 1024 == 0 && OFF_S % 1024 == 0,
               "operand tiles need 1 KB alignment");
 static_assert(kSmemBytes <= 232448, "over the 227 KB per-CTA shared-memory limit");
 
-// TMEM columns (512 allocated): region A = D1 / D_P, B = D_W, C = D_UY, D = D_S.
+// mbarrier slots
+enum Bar { B_TMA0 = 0, B_TMA1, B_MMA1, B_MMAP, B_MMA4, B_MMA6, B_MMA7, B_UY_FREE, B_GATE0, B_GATE1 };
+
+// TMEM columns (512 allocated): A = D1 / D_P, W = D_W (then A6), UY = D_UY, S = D_S.
 constexpr uint32_t TM_A = 0, TM_W = 128, TM_UY = 256, TM_S = 384;
 
-struct Smem {
-    uint8_t *base;
-    uint32_t sbase;  // shared-window address of base
-};
+// Named barriers of the two roles (id 0 is __syncthreads).
+constexpr uint32_t NB_PAR = 1, NB_SER = 2;
 
 __device__ __forceinline__ float gate_at(const float *p) { return *p; }
 __device__ __forceinline__ float gate_at(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
 
-// e, w (per folded row) and g (per token, on micro-step 0) of one chunk row.
+// e, w (per folded row) and g (per token, on micro-step 0) of one chunk row;
+// thread `t` in [0, 192) loads e (t < 64), w (t < 128) or g of row t % 64.
 template <typename TG>
-__device__ __forceinline__ float load_gate(const CoreParams &p, int64_t b, int64_t h, int64_t c, int tid) {
-    const int which = tid >> 6, l = tid & 63;
+__device__ __forceinline__ float load_gate(const CoreParams &p, int64_t b, int64_t h, int64_t c, int t) {
+    const int which = t >> 6, l = t & 63;
     const int64_t P = p.seq * p.u;
     const int64_t pos = c * kL + l;
     if (pos >= P) return 0.f;
@@ -104,7 +119,9 @@ __device__ __forceinline__ float load_gate(const CoreParams &p, int64_t b, int64
     const TG *g = static_cast<const TG *>(p.g);
     if (which == 0) return gate_at(e + (b * P + pos) * p.heads + h);
     if (which == 1) return gate_at(w + (b * P + pos) * p.heads + h);
-    if (p.gw == 0 || (pos % p.u) != 0) return 0.f;
+    if (p.gw == 0) return 0.f;
+    if (p.u == 1) return gate_at(g + (b * p.seq + pos) * p.heads + h);
+    if ((pos % p.u) != 0) return 0.f;
     return gate_at(g + (b * p.seq + pos / p.u) * p.heads + h);
 }
 
@@ -131,12 +148,12 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16 *dst, const float *f) 
 // Off-diagonal blocks of block column Q of T = (I + A)^-1 (16x16 blocks of a
 // 64x64 unit lower-triangular inverse), given the diagonal blocks T_pp already
 // in Tf:  T_pQ = -T_pp X_p,  X_p = sum_{r=Q}^{p-1} A_pr T_rQ,  p = Q+1 .. 3.
-// G lanes share one column j of the block column and own 16 / G rows each;
-// the full column is gathered by warp shuffles (a column's lanes sit in one
-// warp).  `t` is the thread's index within the group's 16 * G threads.
+// G lanes share one column j of the block column and own rows part, part + G,
+// ...; the full column is gathered by warp shuffles (a column's lanes sit in
+// one warp).  `t` is the thread's index within the group's 16 * G threads.
 template <int Q, int G>
 __device__ __forceinline__ void solve_block_column(const float *Af, float *Tf, int t) {
-    constexpr int R = 16 / G;  // rows per lane
+    constexpr int R = 16 / G;
     const int j = t / G, part = t % G;
     const int lane = threadIdx.x & 31, base = lane - part;
     const int col = 16 * Q + j;
@@ -148,7 +165,7 @@ __device__ __forceinline__ void solve_block_column(const float *Af, float *Tf, i
         float x[R];
 #pragma unroll
         for (int e = 0; e < R; ++e) {
-            const int a = part * R + e;
+            const int a = part + G * e;
             float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
             for (int rr = Q; rr < pr; ++rr) {
@@ -166,11 +183,11 @@ __device__ __forceinline__ void solve_block_column(const float *Af, float *Tf, i
         }
         float xf[16];
 #pragma unroll
-        for (int k = 0; k < 16; ++k) xf[k] = __shfl_sync(0xffffffffu, x[k % R], base + k / R);
+        for (int k = 0; k < 16; ++k) xf[k] = __shfl_sync(0xffffffffu, x[k / G], base + k % G);
         float tn[R];
 #pragma unroll
         for (int e = 0; e < R; ++e) {
-            const int a = part * R + e;
+            const int a = part + G * e;
             const float *Trow = Tf + (16 * pr + a) * kAP + 16 * pr;
             float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
@@ -186,16 +203,9 @@ __device__ __forceinline__ void solve_block_column(const float *Af, float *Tf, i
         }
         if (pr < 3) {
 #pragma unroll
-            for (int k = 0; k < 16; ++k) tc[pr - Q][k] = __shfl_sync(0xffffffffu, tn[k % R], base + k / R);
+            for (int k = 0; k < 16; ++k) tc[pr - Q][k] = __shfl_sync(0xffffffffu, tn[k / G], base + k % G);
         }
     }
-}
-
-// Every thread waits; returns false (uniformly across the CTA) if any timed out.
-__device__ __forceinline__ bool wait_all(uint64_t *bar, uint32_t parity, volatile int *flag) {
-    if (!ptx::mbar_wait(bar, parity)) *flag = 1;
-    __syncthreads();
-    return *flag == 0;
 }
 
 template <typename TG, typename TO>
@@ -207,29 +217,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sb = ptx::smem_u32(base);
     float *Af = reinterpret_cast<float *>(base + OFF_AF);
     float *Tf = reinterpret_cast<float *>(base + OFF_TF);
-    float *gates = reinterpret_cast<float *>(base + OFF_GATE);  // [stage][3][64]
-    float *Gc = reinterpret_cast<float *>(base + OFF_G);        // G[64]
-    float *gam = Gc + 64;                                       // e^G[64]
-    uint64_t *bar_tma = reinterpret_cast<uint64_t *>(base + OFF_BAR);
-    uint64_t *bar_mma = bar_tma + 2;
+    float *gates = reinterpret_cast<float *>(base + OFF_GATE);  // [stage][e | w | g][64]
+    float *Gs = reinterpret_cast<float *>(base + OFF_G);        // [stage][G | gam][64]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(base + OFF_BAR);
     uint32_t *tmem_ptr = reinterpret_cast<uint32_t *>(base + OFF_TMEMPTR);
     volatile int *flag = reinterpret_cast<volatile int *>(base + OFF_FLAG);
+    volatile int *pend = reinterpret_cast<volatile int *>(base + OFF_PEND);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int sp = warp & 3, ch = warp >> 2;  // TMEM subpartition, column half
-    const int r = 32 * sp + lane;             // the TMEM lane (accumulator row) this thread reads
     const int64_t bh = blockIdx.x, b = bh / p.heads, h = bh % p.heads;
     const int64_t P = p.seq * p.u;
     const int64_t nchunks = (P + kL - 1) / kL;
     const bool gated = p.gw > 0;
     const float scale = p.scale;
-    const bool leader = (tid == 0);
 
     if (tid == 0) {
         *flag = 0;
-        ptx::mbar_init(&bar_tma[0], 1);
-        ptx::mbar_init(&bar_tma[1], 1);
-        ptx::mbar_init(bar_mma, 1);
+        pend[0] = pend[1] = -1;
+        for (int i = 0; i < kBars; ++i) ptx::mbar_init(&bars[i], 1);
         ptx::fence_mbar_init();
         ptx::prefetch_tmap(&tm_k);
         ptx::prefetch_tmap(&tm_q);
@@ -243,16 +248,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_ptr;
-    const uint32_t lane_base = (uint32_t)(32 * sp) << 16;
 
-    int pending = -1;  // stage whose TMA load is in flight and not yet waited on
-    uint32_t pending_parity = 0;
-    uint32_t mma_phase = 0;
-
+    // One chunk's q/k/v tiles into stage `st`, completing on its mbarrier.
     auto issue_tma = [&](int64_t c, int st) {
-        uint64_t *bar = &bar_tma[st];
+        uint64_t *bar = &bars[B_TMA0 + st];
         uint8_t *stg = base + OFF_STAGE + st * kStageBytes;
         const int row = (int)(c * kL);
+        pend[st] = (int)((c >> 1) & 1);
         ptx::mbar_arrive_expect_tx(bar, kStageBytes);
         ptx::tma_load_4d(stg + 0, &tm_k, bar, 0, (int)h, row, (int)b);
         ptx::tma_load_4d(stg + 16384, &tm_k, bar, 64, (int)h, row, (int)b);
@@ -262,467 +264,489 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tma_load_4d(stg + 40960, &tm_v, bar, 64, (int)h, row, (int)b);
     };
 
-    // Chunk-local cumulative gate of the chunk whose gates sit in stage `st`.
-    auto gate_scan = [&](int st) {
-        if (warp == 0) {
-            const float *g = gates + (st * 3 + 2) * 64;
-            const float x0 = g[2 * lane], x1 = g[2 * lane + 1];
-            float s = x0 + x1;
-#pragma unroll
-            for (int off = 1; off < 32; off <<= 1) {
-                const float t = __shfl_up_sync(0xffffffffu, s, off);
-                if (lane >= off) s += t;
-            }
-            Gc[2 * lane + 1] = s;
-            Gc[2 * lane] = s - x1;
-            gam[2 * lane + 1] = __expf(s);
-            gam[2 * lane] = __expf(s - x1);
-        }
-    };
-
-    bool ok = true;
-    if (nchunks > 0) {
+    if (warp < 8) {
+        // =============================== parallel role: chunk c's operands ===============================
+        const int sp = warp & 3, ch = warp >> 2;  // TMEM subpartition, column half
+        const int r = 32 * sp + lane;
+        const uint32_t lane_base = (uint32_t)(32 * sp) << 16;
+        const bool leader = (tid == 0);
+        auto par_wait = [&](int bar, uint32_t parity) {
+            if (!ptx::mbar_wait(&bars[bar], parity)) *flag = 1;
+            ptx::named_sync(NB_PAR, kParThreads);
+            return *flag == 0;
+        };
         if (leader) {
             issue_tma(0, 0);
+            if (nchunks > 1) issue_tma(1, 1);
         }
-        pending = 0;
-        if (tid < 192) gates[tid] = load_gate<TG>(p, b, h, 0, tid);
-        __syncthreads();
-        gate_scan(0);
-        __syncthreads();
-        // S0 -> TMEM (scaled by the first chunk's total decay) and its bf16 copy.
-        {
-            const float Gam = gam[63];
-            const float *src = p.state_in + (bh * kD + r) * kD + 64 * ch;
+        float gnext = (tid < 192) ? load_gate<TG>(p, b, h, 0, tid) : 0.f;
+
+        for (int64_t c = 0; c < nchunks; ++c) {
+            const int st = (int)(c & 1);
+            const uint32_t stg = sb + OFF_STAGE + st * kStageBytes;
+            const float *ge = gates + (st * 3 + 0) * 64;
+            const float *gw = gates + (st * 3 + 1) * 64;
+            float *Gc = Gs + st * 128;
+            float *gam = Gc + 64;
+            DC_TC_MARK(0);
+
+            // ---- chunk c's gates -> G = cumsum(g), gam = e^G; published to the serial role ----
+            if (tid < 192) gates[st * 192 + tid] = gnext;
+            ptx::named_sync(NB_PAR, kParThreads);
+            if (c + 1 < nchunks && tid < 192) gnext = load_gate<TG>(p, b, h, c + 1, tid);
+            if (warp == 0) {
+                const float *g = gates + (st * 3 + 2) * 64;
+                const float x0 = g[2 * lane], x1 = g[2 * lane + 1];
+                float s = x0 + x1;
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
+                for (int off = 1; off < 32; off <<= 1) {
+                    const float t = __shfl_up_sync(0xffffffffu, s, off);
+                    if (lane >= off) s += t;
+                }
+                Gc[2 * lane + 1] = s;
+                Gc[2 * lane] = s - x1;
+                gam[2 * lane + 1] = __expf(s);
+                gam[2 * lane] = __expf(s - x1);
+            }
+            ptx::named_sync(NB_PAR, kParThreads);
+            if (leader) ptx::mbar_arrive(&bars[B_GATE0 + st]);
+
+            // ---- chunk c's tiles; chunk c-1's MMA4 must be done (it reads the lo operands in Af/Tf) ----
+            if (!par_wait(B_TMA0 + st, (uint32_t)((c >> 1) & 1))) break;
+            if (tid == 0) pend[st] = -1;
+            if (c > 0 && !par_wait(B_MMA4, (uint32_t)((c - 1) & 1))) break;
+            DC_TC_MARK(1);
+
+            // ---- D1 = [K; Q] K^T ----
+            if (leader) {
+                ptx::tc_fence_after();
+                const uint32_t id = ptx::idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                    const uint64_t d = ptx::sdesc(stg + off, 16, 1024);
+                    ptx::umma_bf16(tmem + TM_A, d, d, id, kk > 0);
+                }
+                ptx::umma_commit(&bars[B_MMA1]);
+            }
+            if (!par_wait(B_MMA1, (uint32_t)(c & 1))) break;
+            DC_TC_MARK(2);
+
+            // ---- masks: Akk (fp32, rows 0-63 of D1) and Aqk (bf16 operand, rows 64-127) ----
+            ptx::tc_fence_after();
+            {
                 uint32_t v[32];
+                ptx::tmem_ld32(tmem + lane_base + TM_A + 32 * ch, v);
+                ptx::tmem_wait_ld();
+                const int i = r & 63;
+                const float coef = (r < 64) ? ge[i] : scale;
+                float a[32];
+                if (gated) {
+                    const float Gi = Gc[i];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const float4 f = *reinterpret_cast<const float4 *>(src + 32 * hh + 4 * q);
-                    const float fs[4] = {f.x, f.y, f.z, f.w};
+                    for (int jj = 0; jj < 32; ++jj)
+                        a[jj] = coef * __uint_as_float(v[jj]) * __expf(Gi - Gc[32 * ch + jj]);
+                } else {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) v[4 * q + e] = __float_as_uint(fs[e]);
+                    for (int jj = 0; jj < 32; ++jj) a[jj] = coef * __uint_as_float(v[jj]);
+                }
+                if (r < 64) {
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const int j = 32 * ch + 4 * q;
+                        *reinterpret_cast<float4 *>(Af + i * kAP + j) =
+                            make_float4(j < i ? a[4 * q] : 0.f, j + 1 < i ? a[4 * q + 1] : 0.f,
+                                        j + 2 < i ? a[4 * q + 2] : 0.f, j + 3 < i ? a[4 * q + 3] : 0.f);
+                    }
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float m[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) m[e] = (32 * ch + 8 * q + e <= i) ? a[8 * q + e] : 0.f;
+                        ptx::st_shared_v4(sb + OFF_AQK + ptx::sw128(i, 32 * ch + 8 * q), ptx::pack_bf16(m[0], m[1]),
+                                          ptx::pack_bf16(m[2], m[3]), ptx::pack_bf16(m[4], m[5]),
+                                          ptx::pack_bf16(m[6], m[7]));
+                    }
+                }
+            }
+            ptx::fence_async_smem();
+            ptx::tc_fence_before();
+            ptx::named_sync(NB_PAR, kParThreads);
+            DC_TC_MARK(3);
+
+            // ---- T = (I + Akk)^-1 in 16x16 blocks ----
+            // (1) The diagonal blocks, one per warp: a lane substitutes down one column.
+            if (warp < 4 && lane < 16) {
+                const int pb = warp, j = lane;
+                const float *A = Af + (16 * pb) * kAP + 16 * pb;
+                float tcol[16];
+#pragma unroll
+                for (int a = 0; a < 16; ++a) {
+                    float acc0 = (a == j) ? 1.f : 0.f, acc1 = 0.f;
+#pragma unroll
+                    for (int m = 0; m < a; m += 4) {
+                        const float4 av = *reinterpret_cast<const float4 *>(A + a * kAP + m);
+                        acc0 = fmaf(-av.x, tcol[m], acc0);
+                        if (m + 1 < a) acc1 = fmaf(-av.y, tcol[m + 1], acc1);
+                        if (m + 2 < a) acc0 = fmaf(-av.z, tcol[m + 2], acc0);
+                        if (m + 3 < a) acc1 = fmaf(-av.w, tcol[m + 3], acc1);
+                    }
+                    tcol[a] = acc0 + acc1;
                 }
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    ptx::st_shared_v4(sb + OFF_S + ch * 16384 + ptx::sw128(r, 32 * hh + 8 * q),
-                                      ptx::pack_bf16(__uint_as_float(v[8 * q + 0]), __uint_as_float(v[8 * q + 1])),
-                                      ptx::pack_bf16(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3])),
-                                      ptx::pack_bf16(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5])),
-                                      ptx::pack_bf16(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7])));
-                }
-#pragma unroll
-                for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * Gam);
-                ptx::tmem_st32(tmem + lane_base + TM_S + 64 * ch + 32 * hh, v);
+                for (int a = 0; a < 16; ++a) Tf[(16 * pb + a) * kAP + 16 * pb + j] = tcol[a];
             }
-            ptx::tmem_wait_st();
-        }
-        ptx::fence_async_smem();
-        ptx::tc_fence_before();
-        __syncthreads();
-    }
-
-    for (int64_t c = 0; c < nchunks && ok; ++c) {
-        const int stage = (int)(c & 1);
-        const uint32_t stg = sb + OFF_STAGE + stage * kStageBytes;
-        const float *ge = gates + (stage * 3 + 0) * 64;
-        const float *gw = gates + (stage * 3 + 1) * 64;
-
-        DC_TC_MARK(0);
-        // ---- inputs of chunk c; start chunk c+1's loads ----
-        ok = wait_all(&bar_tma[stage], (uint32_t)((c >> 1) & 1), flag);
-        if (!ok) break;
-        pending = -1;
-        const bool has_next = (c + 1 < nchunks);
-        if (has_next) {
-            if (leader) issue_tma(c + 1, stage ^ 1);
-            pending = stage ^ 1;
-            pending_parity = (uint32_t)(((c + 1) >> 1) & 1);
-        }
-        float gate_next = 0.f;
-        if (has_next && tid < 192) gate_next = load_gate<TG>(p, b, h, c + 1, tid);
-
-        DC_TC_MARK(1);
-        // ---- D1 = [K; Q] K^T ----
-        if (leader) {
-            ptx::tc_fence_after();
-            const uint32_t id = ptx::idesc_bf16(128, 64, 0, 0);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                const uint64_t d = ptx::sdesc(stg + off, 16, 1024);
-                ptx::umma_bf16(tmem + TM_A, d, d, id, kk > 0);
-            }
-            ptx::umma_commit(bar_mma);
-        }
-        ok = wait_all(bar_mma, mma_phase, flag);
-        mma_phase ^= 1;
-        if (!ok) break;
-
-        DC_TC_MARK(2);
-        // ---- masks: Akk (fp32, rows 0-63 of D1) and Aqk (bf16 operand, rows 64-127) ----
-        ptx::tc_fence_after();
-        {
-            uint32_t v[32];
-            ptx::tmem_ld32(tmem + lane_base + TM_A + 32 * ch, v);
-            ptx::tmem_wait_ld();
-            const int i = r & 63;
-            const float coef = (r < 64) ? ge[i] : scale;
-            float a[32];
-            if (gated) {
-                const float Gi = Gc[i];
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) a[jj] = coef * __uint_as_float(v[jj]) * __expf(Gi - Gc[32 * ch + jj]);
+            ptx::named_sync(NB_PAR, kParThreads);
+            // (2) The blocks below the diagonal, one block column per warp group.
+            if (warp < 4) {
+                solve_block_column<0, 8>(Af, Tf, tid);
+            } else if (warp < 6) {
+                solve_block_column<1, 4>(Af, Tf, tid - 128);
             } else {
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) a[jj] = coef * __uint_as_float(v[jj]);
+                solve_block_column<2, 4>(Af, Tf, tid - 192);
             }
-            if (r < 64) {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const int j = 32 * ch + 4 * q;
-                    *reinterpret_cast<float4 *>(Af + i * kAP + j) =
-                        make_float4(j < i ? a[4 * q] : 0.f, j + 1 < i ? a[4 * q + 1] : 0.f,
-                                    j + 2 < i ? a[4 * q + 2] : 0.f, j + 3 < i ? a[4 * q + 3] : 0.f);
-                }
-            } else {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    float m[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) m[e] = (32 * ch + 8 * q + e <= i) ? a[8 * q + e] : 0.f;
-                    ptx::st_shared_v4(sb + OFF_AQK + ptx::sw128(i, 32 * ch + 8 * q), ptx::pack_bf16(m[0], m[1]),
-                                      ptx::pack_bf16(m[2], m[3]), ptx::pack_bf16(m[4], m[5]),
-                                      ptx::pack_bf16(m[6], m[7]));
-                }
-            }
-        }
-        ptx::fence_async_smem();
-        ptx::tc_fence_before();
-        __syncthreads();
+            ptx::named_sync(NB_PAR, kParThreads);
+            DC_TC_MARK(4);
 
-        DC_TC_MARK(3);
-        // ---- T = (I + Akk)^-1 in 16x16 blocks ----
-        // (1) The diagonal blocks T_pp = (I + A_pp)^-1: one thread substitutes down each column.
-        if (tid < 64) {
-            const int pb = tid >> 4, j = tid & 15;
-            const float *A = Af + (16 * pb) * kAP + 16 * pb;
-            float tcol[16];
+            // ---- Tb = T diag(w), Tw = T diag(e gam) as bf16 hi + lo (blocks above the diagonal masked) ----
+            {
+                const int i = tid & 63, j0 = (tid >> 6) * 16;
+                float t[16];
 #pragma unroll
-            for (int a = 0; a < 16; ++a) {
-                float acc0 = (a == j) ? 1.f : 0.f, acc1 = 0.f;
-#pragma unroll
-                for (int m = 0; m < a; m += 4) {
-                    const float4 av = *reinterpret_cast<const float4 *>(A + a * kAP + m);
-                    acc0 = fmaf(-av.x, tcol[m], acc0);
-                    if (m + 1 < a) acc1 = fmaf(-av.y, tcol[m + 1], acc1);
-                    if (m + 2 < a) acc0 = fmaf(-av.z, tcol[m + 2], acc0);
-                    if (m + 3 < a) acc1 = fmaf(-av.w, tcol[m + 3], acc1);
+                for (int m = 0; m < 16; m += 4) {
+                    const float4 tv = *reinterpret_cast<const float4 *>(Tf + i * kAP + j0 + m);
+                    t[m] = j0 + m <= i ? tv.x : 0.f;
+                    t[m + 1] = j0 + m + 1 <= i ? tv.y : 0.f;
+                    t[m + 2] = j0 + m + 2 <= i ? tv.z : 0.f;
+                    t[m + 3] = j0 + m + 3 <= i ? tv.w : 0.f;
                 }
-                tcol[a] = acc0 + acc1;
-            }
+                ptx::named_sync(NB_PAR, kParThreads);  // every T read is done before the T buffer is overwritten
 #pragma unroll
-            for (int a = 0; a < 16; ++a) Tf[(16 * pb + a) * kAP + 16 * pb + j] = tcol[a];
-        }
-        __syncthreads();
-        DC_TC_MARK(13);
-        DC_TC_MARK(14);
-        // (2) The blocks below the diagonal, T_pq = -T_pp sum_{r=q}^{p-1} A_pr T_rq,
-        //     one block column per warp group: block column 0 on warps 0-3 (8 lanes
-        //     per column, 2 rows each), 1 on warps 4-5 and 2 on warps 6-7 (4 lanes
-        //     per column, 4 rows each).  A column's lanes share one warp, so the
-        //     substitution down the column needs no block-wide barrier.
-        if (warp < 4) {
-            solve_block_column<0, 8>(Af, Tf, tid);
-        } else if (warp < 6) {
-            solve_block_column<1, 4>(Af, Tf, tid - 128);
-        } else {
-            solve_block_column<2, 4>(Af, Tf, tid - 192);
-        }
-        __syncthreads();
-        DC_TC_MARK(4);
-        // Tb = T diag(w), Tw = T diag(e gam) as bf16 hi + lo: the tops of A_U / A_W
-        // and of their low-part twins (which reuse the Akk and T buffers).  T's
-        // blocks above the diagonal are never written: masked here.
-        {
-            const int i = tid >> 2, j0 = (tid & 3) * 16;
-            float t[16];
+                for (int q = 0; q < 2; ++q) {
+                    const int j = j0 + 8 * q;
+                    uint32_t bhi[4], blo[4], whi[4], wlo[4];
 #pragma unroll
-            for (int m = 0; m < 16; m += 4) {
-                const float4 tv = *reinterpret_cast<const float4 *>(Tf + i * kAP + j0 + m);
-                t[m] = j0 + m <= i ? tv.x : 0.f;
-                t[m + 1] = j0 + m + 1 <= i ? tv.y : 0.f;
-                t[m + 2] = j0 + m + 2 <= i ? tv.z : 0.f;
-                t[m + 3] = j0 + m + 3 <= i ? tv.w : 0.f;
-            }
-            __syncthreads();  // every T read is done before the T buffer is overwritten
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int j = j0 + 8 * q;
-                uint32_t bh[4], bl[4], wh[4], wl[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int j1 = j + 2 * e;
-                    const float b0 = t[8 * q + 2 * e] * gw[j1], b1 = t[8 * q + 2 * e + 1] * gw[j1 + 1];
-                    const float w0 = t[8 * q + 2 * e] * ge[j1] * gam[j1];
-                    const float w1 = t[8 * q + 2 * e + 1] * ge[j1 + 1] * gam[j1 + 1];
-                    bh[e] = ptx::pack_bf16(b0, b1);
-                    bl[e] = ptx::pack_bf16(b0 - ptx::bf16lo(bh[e]), b1 - ptx::bf16hi(bh[e]));
-                    wh[e] = ptx::pack_bf16(w0, w1);
-                    wl[e] = ptx::pack_bf16(w0 - ptx::bf16lo(wh[e]), w1 - ptx::bf16hi(wh[e]));
+                    for (int e = 0; e < 4; ++e) {
+                        const int j1 = j + 2 * e;
+                        const float b0 = t[8 * q + 2 * e] * gw[j1], b1 = t[8 * q + 2 * e + 1] * gw[j1 + 1];
+                        const float w0 = t[8 * q + 2 * e] * ge[j1] * gam[j1];
+                        const float w1 = t[8 * q + 2 * e + 1] * ge[j1 + 1] * gam[j1 + 1];
+                        bhi[e] = ptx::pack_bf16(b0, b1);
+                        blo[e] = ptx::pack_bf16(b0 - ptx::bf16lo(bhi[e]), b1 - ptx::bf16hi(bhi[e]));
+                        whi[e] = ptx::pack_bf16(w0, w1);
+                        wlo[e] = ptx::pack_bf16(w0 - ptx::bf16lo(whi[e]), w1 - ptx::bf16hi(whi[e]));
+                    }
+                    const uint32_t off = ptx::sw128(i, j);
+                    ptx::st_shared_v4(sb + OFF_AU + off, bhi[0], bhi[1], bhi[2], bhi[3]);
+                    ptx::st_shared_v4(sb + OFF_AF + off, blo[0], blo[1], blo[2], blo[3]);
+                    ptx::st_shared_v4(sb + OFF_AW + off, whi[0], whi[1], whi[2], whi[3]);
+                    ptx::st_shared_v4(sb + OFF_TF + off, wlo[0], wlo[1], wlo[2], wlo[3]);
                 }
-                const uint32_t off = ptx::sw128(i, j);
-                ptx::st_shared_v4(sb + OFF_AU + off, bh[0], bh[1], bh[2], bh[3]);
-                ptx::st_shared_v4(sb + OFF_AF + off, bl[0], bl[1], bl[2], bl[3]);
-                ptx::st_shared_v4(sb + OFF_AW + off, wh[0], wh[1], wh[2], wh[3]);
-                ptx::st_shared_v4(sb + OFF_TF + off, wl[0], wl[1], wl[2], wl[3]);
             }
-        }
-        ptx::fence_async_smem();
-        __syncthreads();
+            ptx::fence_async_smem();
+            ptx::named_sync(NB_PAR, kParThreads);
+            DC_TC_MARK(5);
 
-        DC_TC_MARK(5);
-        // ---- D_P = Aqk [Tb | Tw] ----
-        if (leader) {
+            // ---- D_P = Aqk [Tb | Tw] ----
+            if (leader) {
+                ptx::tc_fence_after();
+                const uint32_t id = ptx::idesc_bf16(64, 128, 0, 1);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t a = ptx::sdesc(sb + OFF_AQK + kk * 32, 16, 1024);
+                    const uint64_t bd = ptx::sdesc(sb + OFF_AU + kk * 2048, 16384, 1024);
+                    ptx::umma_bf16(tmem + TM_A, a, bd, id, kk > 0);
+                }
+                ptx::umma_commit(&bars[B_MMAP]);
+            }
+            if (!par_wait(B_MMAP, (uint32_t)(c & 1))) break;
+            DC_TC_MARK(6);
+
+            // ---- Pb, Pw (hi + lo): the bottoms of the four A operands (M=64 accumulator: rows in lanes 0-15) ----
             ptx::tc_fence_after();
-            const uint32_t id = ptx::idesc_bf16(64, 128, 0, 1);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const uint64_t a = ptx::sdesc(sb + OFF_AQK + kk * 32, 16, 1024);
-                const uint64_t bd = ptx::sdesc(sb + OFF_AU + kk * 2048, 16384, 1024);
-                ptx::umma_bf16(tmem + TM_A, a, bd, id, kk > 0);
-            }
-            ptx::umma_commit(bar_mma);
-        }
-        ok = wait_all(bar_mma, mma_phase, flag);
-        mma_phase ^= 1;
-        if (!ok) break;
-
-        DC_TC_MARK(6);
-        // ---- Pb, Pw (hi + lo): the bottoms of the four A operands (M=64 accumulator: rows in lanes 0-15) ----
-        ptx::tc_fence_after();
-        {
-            const uint32_t dst_hi = sb + (ch ? OFF_AW : OFF_AU), dst_lo = sb + (ch ? OFF_TF : OFF_AF);
-            const int i = 16 * sp + lane;
-            uint32_t vv[2][32];
-            ptx::tmem_ld32(tmem + lane_base + TM_A + 64 * ch, vv[0]);
-            ptx::tmem_ld32(tmem + lane_base + TM_A + 64 * ch + 32, vv[1]);
-            ptx::tmem_wait_ld();
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const uint32_t *v = vv[hh];
+            {
+                const uint32_t dst_hi = sb + (ch ? OFF_AW : OFF_AU), dst_lo = sb + (ch ? OFF_TF : OFF_AF);
+                const int i = 16 * sp + lane;
+                uint32_t vv[2][32];
+                ptx::tmem_ld32(tmem + lane_base + TM_A + 64 * ch, vv[0]);
+                ptx::tmem_ld32(tmem + lane_base + TM_A + 64 * ch + 32, vv[1]);
+                ptx::tmem_wait_ld();
                 if (lane < 16) {
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const float *f = reinterpret_cast<const float *>(vv[hh] + 8 * q);
+                            uint32_t hi[4], lo[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                hi[e] = ptx::pack_bf16(f[2 * e], f[2 * e + 1]);
+                                lo[e] = ptx::pack_bf16(f[2 * e] - ptx::bf16lo(hi[e]), f[2 * e + 1] - ptx::bf16hi(hi[e]));
+                            }
+                            const uint32_t off = ptx::sw128(64 + i, 32 * hh + 8 * q);
+                            ptx::st_shared_v4(dst_hi + off, hi[0], hi[1], hi[2], hi[3]);
+                            ptx::st_shared_v4(dst_lo + off, lo[0], lo[1], lo[2], lo[3]);
+                        }
+                    }
+                }
+            }
+            ptx::fence_async_smem();
+            ptx::tc_fence_before();
+            ptx::named_sync(NB_PAR, kParThreads);
+            DC_TC_MARK(7);
+
+            // ---- D_UY = [Tb; Pb] V, D_W = [Tw; Pw] K, once the serial role released chunk c-1's ----
+            if (leader) {
+                if (c > 0 && !ptx::mbar_wait(&bars[B_UY_FREE], (uint32_t)((c - 1) & 1))) {
+                    *flag = 1;
+                } else {
+                    ptx::tc_fence_after();
+                    const uint32_t id = ptx::idesc_bf16(128, 128, 0, 1);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t au = (kk < 4) ? OFF_AU : OFF_AF, aw = (kk < 4) ? OFF_AW : OFF_TF;
+                        ptx::umma_bf16(tmem + TM_UY, ptx::sdesc(sb + au + (kk & 3) * 32, 16, 1024),
+                                       ptx::sdesc(stg + 32768 + (kk & 3) * 2048, 8192, 1024), id, kk > 0);
+                        ptx::umma_bf16(tmem + TM_W, ptx::sdesc(sb + aw + (kk & 3) * 32, 16, 1024),
+                                       ptx::sdesc(stg + (kk & 3) * 2048, 16384, 1024), id, kk > 0);
+                    }
+                    ptx::umma_commit(&bars[B_MMA4]);
+                }
+            }
+            ptx::named_sync(NB_PAR, kParThreads);
+            if (*flag) break;
+        }
+    } else {
+        // =============================== serial role: the S chain of chunk c ===============================
+        const int sp = warp - 8;  // TMEM subpartition
+        const int r = 32 * sp + lane;
+        const uint32_t lane_base = (uint32_t)(32 * sp) << 16;
+        const bool leader = (tid == kParThreads);
+        auto ser_wait = [&](int bar, uint32_t parity) {
+            if (!ptx::mbar_wait(&bars[bar], parity)) *flag = 1;
+            ptx::named_sync(NB_SER, kSerThreads);
+            return *flag == 0;
+        };
+        bool ok = ser_wait(B_GATE0, 0);
+        if (ok) {
+            // S0 -> TMEM (scaled by chunk 0's total decay) and its bf16 copy.
+            const float Gam = Gs[64 + 63];
+            const float *src = p.state_in + (bh * kD + r) * kD;
+#pragma unroll 1
+            for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+                for (int q2 = 0; q2 < 2; ++q2) {
+                    uint32_t v[32];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const float4 f = *reinterpret_cast<const float4 *>(src + 64 * hh + 32 * q2 + 4 * q);
+                        v[4 * q] = __float_as_uint(f.x);
+                        v[4 * q + 1] = __float_as_uint(f.y);
+                        v[4 * q + 2] = __float_as_uint(f.z);
+                        v[4 * q + 3] = __float_as_uint(f.w);
+                    }
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const float *f = reinterpret_cast<const float *>(v + 8 * q);
-                        uint32_t hi[4], lo[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            hi[e] = ptx::pack_bf16(f[2 * e], f[2 * e + 1]);
-                            lo[e] = ptx::pack_bf16(f[2 * e] - ptx::bf16lo(hi[e]), f[2 * e + 1] - ptx::bf16hi(hi[e]));
-                        }
-                        const uint32_t off = ptx::sw128(64 + i, 32 * hh + 8 * q);
-                        ptx::st_shared_v4(dst_hi + off, hi[0], hi[1], hi[2], hi[3]);
-                        ptx::st_shared_v4(dst_lo + off, lo[0], lo[1], lo[2], lo[3]);
+                        ptx::st_shared_v4(sb + OFF_S + hh * 16384 + ptx::sw128(r, 32 * q2 + 8 * q),
+                                          ptx::pack_bf16(f[0], f[1]), ptx::pack_bf16(f[2], f[3]),
+                                          ptx::pack_bf16(f[4], f[5]), ptx::pack_bf16(f[6], f[7]));
                     }
-                }
-            }
-        }
-        ptx::fence_async_smem();
-        ptx::tc_fence_before();
-        __syncthreads();
-
-        DC_TC_MARK(7);
-        // ---- D_UY = [Tb; Pb] V,  D_W = [Tw; Pw] K ----
-        if (leader) {
-            ptx::tc_fence_after();
-            const uint32_t id = ptx::idesc_bf16(128, 128, 0, 1);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t au = (kk < 4) ? OFF_AU : OFF_AF, aw = (kk < 4) ? OFF_AW : OFF_TF;
-                ptx::umma_bf16(tmem + TM_UY, ptx::sdesc(sb + au + (kk & 3) * 32, 16, 1024),
-                               ptx::sdesc(stg + 32768 + (kk & 3) * 2048, 8192, 1024), id, kk > 0);
-                ptx::umma_bf16(tmem + TM_W, ptx::sdesc(sb + aw + (kk & 3) * 32, 16, 1024),
-                               ptx::sdesc(stg + (kk & 3) * 2048, 16384, 1024), id, kk > 0);
-            }
-            ptx::umma_commit(bar_mma);
-        }
-        ok = wait_all(bar_mma, mma_phase, flag);
-        mma_phase ^= 1;
-        if (!ok) break;
-
-        DC_TC_MARK(8);
-        // ---- A6 = [-W; s gam Q - Aqk W] (K-major over d, blocks of 64 columns) ----
-        ptx::tc_fence_after();
-        {
-            const uint32_t blk = sb + (ch ? OFF_AW : OFF_AU);
-            const uint32_t qblk = stg + ch * 16384 + 8192;
-            const float qs = (r >= 64) ? scale * gam[r - 64] : 0.f;
-            uint32_t vv[2][32];
-            ptx::tmem_ld32(tmem + lane_base + TM_W + 64 * ch, vv[0]);
-            ptx::tmem_ld32(tmem + lane_base + TM_W + 64 * ch + 32, vv[1]);
-            ptx::tmem_wait_ld();
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const uint32_t *v = vv[hh];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    float a[8];
-                    const float *f = reinterpret_cast<const float *>(v + 8 * q);
-                    if (r < 64) {
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) a[e] = -f[e];
-                    } else {
-                        const uint4 qv = ptx::ld_shared_v4(qblk + ptx::sw128(r - 64, 32 * hh + 8 * q));
-                        const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            a[2 * e] = qs * ptx::bf16lo(qw[e]) - f[2 * e];
-                            a[2 * e + 1] = qs * ptx::bf16hi(qw[e]) - f[2 * e + 1];
-                        }
-                    }
-                    ptx::st_shared_v4(blk + ptx::sw128(r, 32 * hh + 8 * q), ptx::pack_bf16(a[0], a[1]),
-                                      ptx::pack_bf16(a[2], a[3]), ptx::pack_bf16(a[4], a[5]),
-                                      ptx::pack_bf16(a[6], a[7]));
-                }
-            }
-        }
-        ptx::fence_async_smem();
-        ptx::tc_fence_before();
-        __syncthreads();
-
-        DC_TC_MARK(9);
-        // ---- D_UY += A6 S  ->  [V'; y] ----
-        if (leader) {
-            ptx::tc_fence_after();
-            const uint32_t id = ptx::idesc_bf16(128, 128, 0, 1);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-                ptx::umma_bf16(tmem + TM_UY, ptx::sdesc(sb + OFF_AU + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                               ptx::sdesc(sb + OFF_S + kk * 2048, 16384, 1024), id, 1);
-            }
-            ptx::umma_commit(bar_mma);
-        }
-        ok = wait_all(bar_mma, mma_phase, flag);
-        mma_phase ^= 1;
-        if (!ok) break;
-
-        DC_TC_MARK(10);
-        // ---- V' (decayed to the chunk end) -> operand; y -> HBM ----
-        ptx::tc_fence_after();
-        {
-            const float Glast = Gc[63];
-            const float vs = (r < 64 && gated) ? __expf(Glast - Gc[r]) : 1.f;
-            const int64_t pos = c * kL + (r - 64);
-            const bool write_y = (r >= 64) && pos < P && (pos % p.u) == (p.u - 1);
-            TO *yrow = static_cast<TO *>(p.y) + ((b * p.seq + (write_y ? pos / p.u : 0)) * p.heads + h) * kD;
-            uint32_t vv[2][32];
-            ptx::tmem_ld32(tmem + lane_base + TM_UY + 64 * ch, vv[0]);
-            ptx::tmem_ld32(tmem + lane_base + TM_UY + 64 * ch + 32, vv[1]);
-            ptx::tmem_wait_ld();
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const float *f = reinterpret_cast<const float *>(vv[hh]);
-                if (r < 64) {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        uint32_t hi[4], lo[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float x0 = vs * f[8 * q + 2 * e], x1 = vs * f[8 * q + 2 * e + 1];
-                            hi[e] = ptx::pack_bf16(x0, x1);
-                            lo[e] = ptx::pack_bf16(x0 - ptx::bf16lo(hi[e]), x1 - ptx::bf16hi(hi[e]));
-                        }
-                        const uint32_t off = ch * 8192 + ptx::sw128(r, 32 * hh + 8 * q);
-                        ptx::st_shared_v4(sb + OFF_AF + off, hi[0], hi[1], hi[2], hi[3]);
-                        ptx::st_shared_v4(sb + OFF_TF + off, lo[0], lo[1], lo[2], lo[3]);
-                    }
-                } else if (write_y) {
-                    store_row32(yrow + 64 * ch + 32 * hh, f);
-                }
-            }
-        }
-        ptx::fence_async_smem();
-        ptx::tc_fence_before();
-        __syncthreads();
-
-        DC_TC_MARK(11);
-        // ---- D_S = Gam S + K^T V~' ----
-        if (leader) {
-            ptx::tc_fence_after();
-            const uint32_t id = ptx::idesc_bf16(128, 128, 1, 1);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t vpart = (kk < 4) ? OFF_AF : OFF_TF;
-                ptx::umma_bf16(tmem + TM_S, ptx::sdesc(stg + (kk & 3) * 2048, 16384, 1024),
-                               ptx::sdesc(sb + vpart + (kk & 3) * 2048, 8192, 1024), id, 1);
-            }
-            ptx::umma_commit(bar_mma);
-        }
-        ok = wait_all(bar_mma, mma_phase, flag);
-        mma_phase ^= 1;
-        if (!ok) break;
-
-        DC_TC_MARK(12);
-        // ---- next chunk's gates, then S -> bf16 operand and the pre-scaled accumulator ----
-        if (has_next) {
-            if (tid < 192) gates[(stage ^ 1) * 192 + tid] = gate_next;
-            __syncthreads();
-            gate_scan(stage ^ 1);
-            __syncthreads();
-            const float Gam = gam[63];
-            ptx::tc_fence_after();
-            uint32_t vv[2][32];
-            ptx::tmem_ld32(tmem + lane_base + TM_S + 64 * ch, vv[0]);
-            ptx::tmem_ld32(tmem + lane_base + TM_S + 64 * ch + 32, vv[1]);
-            ptx::tmem_wait_ld();
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                uint32_t(&v)[32] = vv[hh];
-                const uint32_t ta = tmem + lane_base + TM_S + 64 * ch + 32 * hh;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float *f = reinterpret_cast<const float *>(v + 8 * q);
-                    ptx::st_shared_v4(sb + OFF_S + ch * 16384 + ptx::sw128(r, 32 * hh + 8 * q),
-                                      ptx::pack_bf16(f[0], f[1]), ptx::pack_bf16(f[2], f[3]),
-                                      ptx::pack_bf16(f[4], f[5]), ptx::pack_bf16(f[6], f[7]));
-                }
-                if (gated) {
 #pragma unroll
                     for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * Gam);
-                    ptx::tmem_st32(ta, v);
+                    ptx::tmem_st32(tmem + lane_base + TM_S + 64 * hh + 32 * q2, v);
                 }
             }
             ptx::tmem_wait_st();
             ptx::fence_async_smem();
             ptx::tc_fence_before();
-            __syncthreads();
-        } else {
+            ptx::named_sync(NB_SER, kSerThreads);
+        }
+
+        for (int64_t c = 0; c < nchunks && ok; ++c) {
+            const int st = (int)(c & 1);
+            const uint32_t stg = sb + OFF_STAGE + st * kStageBytes;
+            const float *Gc = Gs + st * 128;
+            const float *gam = Gc + 64;
+            DC_TC_MARK(8);
+
+            // ---- A6 = [-W; s gam Q - Aqk W] into TMEM, over D_W (bf16 pairs, two per column) ----
+            if (!(ok = ser_wait(B_MMA4, (uint32_t)(c & 1)))) break;
+            DC_TC_MARK(9);
             ptx::tc_fence_after();
-            float *dst = p.state_out + (bh * kD + r) * kD + 64 * ch;
+            {
+                const float qs = (r >= 64) ? scale * gam[r - 64] : 0.f;
+#pragma unroll 1
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t vv[2][32];
+                    ptx::tmem_ld32(tmem + lane_base + TM_W + 64 * hh, vv[0]);
+                    ptx::tmem_ld32(tmem + lane_base + TM_W + 64 * hh + 32, vv[1]);
+                    ptx::tmem_wait_ld();
+                    uint32_t packed[32];
+                    const uint32_t qblk = stg + hh * 16384 + 8192;
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                uint32_t v[32];
-                ptx::tmem_ld32(tmem + lane_base + TM_S + 64 * ch + 32 * hh, v);
-                ptx::tmem_wait_ld();
+                    for (int q2 = 0; q2 < 2; ++q2) {
+                        const float *f = reinterpret_cast<const float *>(vv[q2]);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    *reinterpret_cast<float4 *>(dst + 32 * hh + 4 * q) =
-                        make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
-                                    __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+                        for (int q = 0; q < 4; ++q) {
+                            float a[8];
+                            if (r < 64) {
+#pragma unroll
+                                for (int e = 0; e < 8; ++e) a[e] = -f[8 * q + e];
+                            } else {
+                                const uint4 qv = ptx::ld_shared_v4(qblk + ptx::sw128(r - 64, 32 * q2 + 8 * q));
+                                const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    a[2 * e] = qs * ptx::bf16lo(qw[e]) - f[8 * q + 2 * e];
+                                    a[2 * e + 1] = qs * ptx::bf16hi(qw[e]) - f[8 * q + 2 * e + 1];
+                                }
+                            }
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) packed[16 * q2 + 4 * q + e] = ptx::pack_bf16(a[2 * e], a[2 * e + 1]);
+                        }
+                    }
+                    ptx::tmem_st32(tmem + lane_base + TM_W + 32 * hh, packed);
+                }
+                ptx::tmem_wait_st();
+            }
+            ptx::tc_fence_before();
+            ptx::named_sync(NB_SER, kSerThreads);
+            DC_TC_MARK(10);
+
+            // ---- D_UY += A6 S  ->  [V'; y] ----
+            if (leader) {
+                ptx::tc_fence_after();
+                const uint32_t id = ptx::idesc_bf16(128, 128, 0, 1);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    ptx::umma_bf16_ts(tmem + TM_UY, tmem + TM_W + 8 * kk, ptx::sdesc(sb + OFF_S + kk * 2048, 16384, 1024),
+                                      id, 1);
+                ptx::umma_commit(&bars[B_MMA6]);
+            }
+            if (!(ok = ser_wait(B_MMA6, (uint32_t)(c & 1)))) break;
+            DC_TC_MARK(11);
+
+            // ---- V' (decayed to the chunk end, hi + lo) -> the stage's V and Q slots; y -> HBM ----
+            ptx::tc_fence_after();
+            {
+                const float vs = (r < 64 && gated) ? __expf(Gc[63] - Gc[r]) : 1.f;
+                const int64_t pos = c * kL + (r - 64);
+                const bool write_y = (r >= 64) && pos < P && (pos % p.u) == (p.u - 1);
+                TO *yrow = static_cast<TO *>(p.y) + ((b * p.seq + (write_y ? pos / p.u : 0)) * p.heads + h) * kD;
+#pragma unroll 1
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t vv[2][32];
+                    ptx::tmem_ld32(tmem + lane_base + TM_UY + 64 * hh, vv[0]);
+                    ptx::tmem_ld32(tmem + lane_base + TM_UY + 64 * hh + 32, vv[1]);
+                    ptx::tmem_wait_ld();
+#pragma unroll
+                    for (int q2 = 0; q2 < 2; ++q2) {
+                        const float *f = reinterpret_cast<const float *>(vv[q2]);
+                        if (r < 64) {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                uint32_t hi[4], lo[4];
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const float x0 = vs * f[8 * q + 2 * e], x1 = vs * f[8 * q + 2 * e + 1];
+                                    hi[e] = ptx::pack_bf16(x0, x1);
+                                    lo[e] = ptx::pack_bf16(x0 - ptx::bf16lo(hi[e]), x1 - ptx::bf16hi(hi[e]));
+                                }
+                                const uint32_t off = ptx::sw128(r, 32 * q2 + 8 * q);
+                                ptx::st_shared_v4(stg + 32768 + hh * 8192 + off, hi[0], hi[1], hi[2], hi[3]);
+                                ptx::st_shared_v4(stg + hh * 16384 + 8192 + off, lo[0], lo[1], lo[2], lo[3]);
+                            }
+                        } else if (write_y) {
+                            store_row32(yrow + 64 * hh + 32 * q2, f);
+                        }
+                    }
+                }
+            }
+            ptx::fence_async_smem();
+            ptx::tc_fence_before();
+            ptx::named_sync(NB_SER, kSerThreads);
+            if (leader) ptx::mbar_arrive(&bars[B_UY_FREE]);  // D_UY and D_W (A6) may be overwritten now
+            DC_TC_MARK(12);
+
+            // ---- D_S = Gam S + K^T (V'hi + V'lo) ----
+            if (leader) {
+                ptx::tc_fence_after();
+                const uint32_t id = ptx::idesc_bf16(128, 128, 1, 1);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint64_t bdesc = (kk < 4) ? ptx::sdesc(stg + 32768 + (kk & 3) * 2048, 8192, 1024)
+                                                    : ptx::sdesc(stg + 8192 + (kk & 3) * 2048, 16384, 1024);
+                    ptx::umma_bf16(tmem + TM_S, ptx::sdesc(stg + (kk & 3) * 2048, 16384, 1024), bdesc, id, 1);
+                }
+                ptx::umma_commit(&bars[B_MMA7]);
+            }
+            if (!(ok = ser_wait(B_MMA7, (uint32_t)(c & 1)))) break;
+            DC_TC_MARK(13);
+            if (leader && c + 2 < nchunks) issue_tma(c + 2, st);  // the stage is fully consumed
+
+            // ---- S -> bf16 operand and the accumulator pre-scaled by the next chunk's decay ----
+            if (c + 1 < nchunks) {
+                if (!(ok = ser_wait(B_GATE0 + (st ^ 1), (uint32_t)(((c + 1) >> 1) & 1)))) break;
+                const float Gam = Gs[(st ^ 1) * 128 + 64 + 63];
+                ptx::tc_fence_after();
+#pragma unroll 1
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t vv[2][32];
+                    ptx::tmem_ld32(tmem + lane_base + TM_S + 64 * hh, vv[0]);
+                    ptx::tmem_ld32(tmem + lane_base + TM_S + 64 * hh + 32, vv[1]);
+                    ptx::tmem_wait_ld();
+#pragma unroll
+                    for (int q2 = 0; q2 < 2; ++q2) {
+                        uint32_t(&v)[32] = vv[q2];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const float *f = reinterpret_cast<const float *>(v + 8 * q);
+                            ptx::st_shared_v4(sb + OFF_S + hh * 16384 + ptx::sw128(r, 32 * q2 + 8 * q),
+                                              ptx::pack_bf16(f[0], f[1]), ptx::pack_bf16(f[2], f[3]),
+                                              ptx::pack_bf16(f[4], f[5]), ptx::pack_bf16(f[6], f[7]));
+                        }
+                        if (gated) {
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * Gam);
+                            ptx::tmem_st32(tmem + lane_base + TM_S + 64 * hh + 32 * q2, v);
+                        }
+                    }
+                }
+                ptx::tmem_wait_st();
+                ptx::fence_async_smem();
+                ptx::tc_fence_before();
+                ptx::named_sync(NB_SER, kSerThreads);
+            } else {
+                ptx::tc_fence_after();
+                float *dst = p.state_out + (bh * kD + r) * kD;
+#pragma unroll 1
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t vv[2][32];
+                    ptx::tmem_ld32(tmem + lane_base + TM_S + 64 * hh, vv[0]);
+                    ptx::tmem_ld32(tmem + lane_base + TM_S + 64 * hh + 32, vv[1]);
+                    ptx::tmem_wait_ld();
+#pragma unroll
+                    for (int q2 = 0; q2 < 2; ++q2)
+                        store_row32(dst + 64 * hh + 32 * q2, reinterpret_cast<const float *>(vv[q2]));
                 }
             }
         }
     }
 
-    if (!ok) {
-        // A wait ran out: report it, let our own TMA loads land, then release TMEM.
-        if (tid == 0) atomicExch(status, kStatusTimeout);
-        if (pending >= 0) ptx::mbar_wait(&bar_tma[pending], pending_parity);
-    }
+    // Both roles meet here exactly once.
     ptx::tc_fence_before();
     __syncthreads();
+    if (*flag) {
+        // A wait ran out: report it and let this CTA's own TMA loads land before the smem goes away.
+        if (tid == 0) {
+            atomicExch(status, kStatusTimeout);
+            for (int s = 0; s < 2; ++s)
+                if (pend[s] >= 0) ptx::mbar_wait(&bars[B_TMA0 + s], (uint32_t)pend[s]);
+        }
+        __syncthreads();
+    }
     if (warp == 0) ptx::tmem_dealloc(tmem, 512);
 }
 

@@ -1,7 +1,7 @@
 // chunk_tc.cuh — the tensor-core (tcgen05 / TMEM / TMA) chunkwise WY prefill.
 //
 // Serves dc_chunk_fwd for bf16 q/k/v with dk = dv = 128 and per-head gates
-// (the DeltaNet and Gated DeltaNet families).  One CTA owns one (batch, head)
+// (DeltaNet, Gated DeltaNet and DeltaProduct with its micro-steps folded in).  One CTA owns one (batch, head)
 // and walks its chunks of L = 64 steps; the fp32 state S lives in tensor
 // memory for the whole sequence and never touches HBM in between.
 //
@@ -123,6 +123,19 @@ __device__ __forceinline__ float load_gate(const CoreParams &p, int64_t b, int64
     if (p.u == 1) return gate_at(g + (b * p.seq + pos) * p.heads + h);
     if ((pos % p.u) != 0) return 0.f;
     return gate_at(g + (b * p.seq + pos / p.u) * p.heads + h);
+}
+
+// The micro-step fold (DeltaProduct / GDN-2, u = n_householder): chunk c
+// covers folded rows 64c .. 64c + 63, and token t reads out at folded row
+// t*u + u - 1 (src/delta_product/delta_product.rs:178-228).  The chunk's Q
+// tile holds the 64 token rows from q_first(c) = floor(64c / u), the first
+// token whose readout falls in the chunk; row i of the tile reads out at
+// chunk row q_pos(c, i), or nowhere (-1).  For u = 1 both are the identity.
+__device__ __forceinline__ int64_t q_first(int64_t c, int u) { return (c * kL) / u; }
+__device__ __forceinline__ int q_pos(int64_t c, int i, const CoreParams &p) {
+    const int64_t t = q_first(c, p.u) + i;
+    const int64_t pos = t * p.u + p.u - 1 - c * kL;
+    return (t < p.seq && pos < kL) ? (int)pos : -1;
 }
 
 // 32 consecutive outputs of one row, as 16-byte stores.
@@ -258,8 +271,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::mbar_arrive_expect_tx(bar, kStageBytes);
         ptx::tma_load_4d(stg + 0, &tm_k, bar, 0, (int)h, row, (int)b);
         ptx::tma_load_4d(stg + 16384, &tm_k, bar, 64, (int)h, row, (int)b);
-        ptx::tma_load_4d(stg + 8192, &tm_q, bar, 0, (int)h, row, (int)b);
-        ptx::tma_load_4d(stg + 24576, &tm_q, bar, 64, (int)h, row, (int)b);
+        const int qrow = (int)q_first(c, p.u);
+        ptx::tma_load_4d(stg + 8192, &tm_q, bar, 0, (int)h, qrow, (int)b);
+        ptx::tma_load_4d(stg + 24576, &tm_q, bar, 64, (int)h, qrow, (int)b);
         ptx::tma_load_4d(stg + 32768, &tm_v, bar, 0, (int)h, row, (int)b);
         ptx::tma_load_4d(stg + 40960, &tm_v, bar, 64, (int)h, row, (int)b);
     };
@@ -338,11 +352,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t v[32];
                 ptx::tmem_ld32(tmem + lane_base + TM_A + 32 * ch, v);
                 ptx::tmem_wait_ld();
-                const int i = r & 63;
-                const float coef = (r < 64) ? ge[i] : scale;
+                // Akk row i = r; Aqk row r - 64 reads out at chunk row pq (causal up to pq).
+                const int i = (r < 64) ? r : q_pos(c, r - 64, p);
+                const float coef = (r < 64) ? ge[r] : (i >= 0 ? scale : 0.f);
                 float a[32];
                 if (gated) {
-                    const float Gi = Gc[i];
+                    const float Gi = Gc[i & 63];
 #pragma unroll
                     for (int jj = 0; jj < 32; ++jj)
                         a[jj] = coef * __uint_as_float(v[jj]) * __expf(Gi - Gc[32 * ch + jj]);
@@ -364,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         float m[8];
 #pragma unroll
                         for (int e = 0; e < 8; ++e) m[e] = (32 * ch + 8 * q + e <= i) ? a[8 * q + e] : 0.f;
-                        ptx::st_shared_v4(sb + OFF_AQK + ptx::sw128(i, 32 * ch + 8 * q), ptx::pack_bf16(m[0], m[1]),
+                        ptx::st_shared_v4(sb + OFF_AQK + ptx::sw128(r - 64, 32 * ch + 8 * q), ptx::pack_bf16(m[0], m[1]),
                                           ptx::pack_bf16(m[2], m[3]), ptx::pack_bf16(m[4], m[5]),
                                           ptx::pack_bf16(m[6], m[7]));
                     }
@@ -576,7 +591,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             DC_TC_MARK(9);
             ptx::tc_fence_after();
             {
-                const float qs = (r >= 64) ? scale * gam[r - 64] : 0.f;
+                const int pq = (r >= 64) ? q_pos(c, r - 64, p) : -1;
+                const float qs = (pq >= 0) ? scale * gam[pq] : 0.f;
 #pragma unroll 1
                 for (int hh = 0; hh < 2; ++hh) {
                     uint32_t vv[2][32];
@@ -632,9 +648,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::tc_fence_after();
             {
                 const float vs = (r < 64 && gated) ? __expf(Gc[63] - Gc[r]) : 1.f;
-                const int64_t pos = c * kL + (r - 64);
-                const bool write_y = (r >= 64) && pos < P && (pos % p.u) == (p.u - 1);
-                TO *yrow = static_cast<TO *>(p.y) + ((b * p.seq + (write_y ? pos / p.u : 0)) * p.heads + h) * kD;
+                const bool write_y = (r >= 64) && q_pos(c, r - 64, p) >= 0;
+                const int64_t tok = write_y ? q_first(c, p.u) + (r - 64) : 0;
+                TO *yrow = static_cast<TO *>(p.y) + ((b * p.seq + tok) * p.heads + h) * kD;
 #pragma unroll 1
                 for (int hh = 0; hh < 2; ++hh) {
                     uint32_t vv[2][32];
@@ -763,7 +779,6 @@ inline bool tc_applies(const CoreParams &p, int32_t in_dtype, uint32_t flags) {
     if (in_dtype != 1) return false; // bf16 q, k, v
     if (p.dk != 128 || p.dv != 128) return false;
     if (p.ew != 1 || p.ww != 1 || p.gw > 1) return false;
-    if (p.u != 1) return false;
     if (!aligned16(p.q) || !aligned16(p.k) || !aligned16(p.v) || !aligned16(p.y) || !aligned16(p.state_in) ||
         !aligned16(p.state_out))
         return false;

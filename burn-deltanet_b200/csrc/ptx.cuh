@@ -199,6 +199,16 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     return r;
 }
 
+__device__ __forceinline__ float bf16lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+
+// Two floats as bf16 hi + lo pairs: hi is x rounded to bf16, lo the fp32
+// residual x - hi rounded to bf16, so hi + lo carries ~16 significant bits.
+__device__ __forceinline__ void split_bf16(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    hi = pack_bf16(x0, x1);
+    lo = pack_bf16(x0 - bf16lo(hi), x1 - bf16hi(hi));
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t saddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(a), "r"(b), "r"(c), "r"(d)
                  : "memory");
@@ -213,8 +223,6 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t saddr) {
     return v;
 }
 
-__device__ __forceinline__ float bf16lo(uint32_t v) { return __uint_as_float(v << 16); }
-__device__ __forceinline__ float bf16hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
 }  // namespace ptx
 }  // namespace dc

@@ -105,3 +105,45 @@ def test_bf16_output():
     y, s, qkv = run_tc(raw, out_dtype=torch.bfloat16)
     y0, s0 = reference(raw, qkv)
     assert np.abs(y - y0).max() < BF16_TOL and np.abs(s - s0).max() < BF16_TOL
+
+
+# ---------------------------------------------------------------------------
+# DeltaProduct: u micro-steps folded inside the tensor-core kernel
+# (src/delta_product/delta_product.rs:178-228), config 4's recipe.
+# ---------------------------------------------------------------------------
+def run_tc_fold(raw, u):
+    q, k, v = (dev(raw[n], torch.bfloat16) for n in ("q", "k", "v"))
+    e, w, g = (dev(raw[n]) for n in ("erase", "write", "g"))
+    st = dev(raw["state"])
+    y, s = dn.delta_chunk_recalculated(q, k, v, e, w, g, st, g is not None, 64, 1 / np.sqrt(128),
+                                       n_householder=u, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    rq, rk, rv = (t.double().cpu().numpy() for t in (q, k, v))
+    y0, s0 = oracle.householder("recurrent", rq, rk, rv, raw["erase"], raw["write"], raw["g"], raw["state"], u)
+    return y.double().cpu().numpy(), s.double().cpu().numpy(), y0, s0
+
+
+@pytest.mark.parametrize("u,seq", [(2, 64), (2, 97), (3, 64), (3, 130), (4, 50)])
+def test_deltaproduct_fold(u, seq):
+    raw = config_inputs(4, np.random.default_rng(20 + u + seq), 2, seq, 2, 128, 128, u=u)
+    a = abi.ChunkArgs()
+    a.batch, a.seq, a.heads, a.dk, a.dv, a.n_householder = 2, seq, 2, 128, 128, u
+    a.erase_w = a.write_w = a.g_w = 1
+    a.chunk_len, a.in_dtype, a.gate_dtype, a.out_dtype, a.scale = 64, abi.DC_BF16, abi.DC_F32, abi.DC_F32, 0.1
+    a.q = a.k = a.v = a.erase = a.write = a.g = 1 << 20
+    a.state_in = a.state_out = 2 << 20
+    a.y = 3 << 20
+    assert abi.lib().dc_chunk_kernel_choice(a) == 1
+    assert abi.lib().dc_device_status(1) == 0
+    y, s, y0, s0 = run_tc_fold(raw, u)
+    assert abi.lib().dc_device_status(1) == 0
+    ey, es = np.abs(y - y0).max(), np.abs(s - s0).max()
+    print(f"u={u} T={seq}: max |y - ref| {ey:.3e}; max |S - ref| {es:.3e} (|ref| {np.abs(s0).max():.2f})")
+    assert ey < BF16_TOL and es < BF16_TOL
+
+
+def test_deltaproduct_fold_ungated():
+    raw = config_inputs(4, np.random.default_rng(31), 1, 150, 3, 128, 128, u=2)
+    raw["g"] = None
+    y, s, y0, s0 = run_tc_fold(raw, 2)
+    assert np.abs(y - y0).max() < BF16_TOL and np.abs(s - s0).max() < BF16_TOL

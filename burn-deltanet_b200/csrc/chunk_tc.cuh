@@ -82,7 +82,9 @@ constexpr uint32_t OFF_S = OFF_AW + 16384;              // S bf16, MN-major, two
 constexpr uint32_t OFF_AQK = OFF_S + 32768;             // Aqk bf16 64x64 K-major
 constexpr uint32_t OFF_AF = OFF_AQK + 8192;             // Akk fp32 [64][68]; then [Tb; Pb] lo
 constexpr uint32_t OFF_TF = OFF_AF + 64 * kAP * 4;      // T fp32 [64][68];   then [Tw; Pw] lo
-constexpr uint32_t OFF_GATE = OFF_TF + 64 * kAP * 4;    // per stage: e[64], w[64], g[64]
+constexpr int kEP = 20;                                 // row pitch (floats) of the E blocks
+constexpr uint32_t OFF_E = OFF_TF + 64 * kAP * 4;       // E_pq = T_pp A_pq: six blocks [16][20] fp32
+constexpr uint32_t OFF_GATE = OFF_E + 6 * 16 * kEP * 4; // per stage: e[64], w[64], g[64]
 constexpr uint32_t OFF_G = OFF_GATE + 2 * 3 * 64 * 4;   // per stage: G[64], gam[64]
 constexpr uint32_t OFF_BAR = OFF_G + 2 * 2 * 64 * 4;    // mbarriers (below)
 constexpr int kBars = 10;
@@ -158,67 +160,35 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16 *dst, const float *f) 
 #define DC_TC_MARK(id)
 #endif
 
-// Off-diagonal blocks of block column Q of T = (I + A)^-1 (16x16 blocks of a
-// 64x64 unit lower-triangular inverse), given the diagonal blocks T_pp already
-// in Tf:  T_pQ = -T_pp X_p,  X_p = sum_{r=Q}^{p-1} A_pr T_rQ,  p = Q+1 .. 3.
-// G lanes share one column j of the block column and own rows part, part + G,
-// ...; the full column is gathered by warp shuffles (a column's lanes sit in
-// one warp).  `t` is the thread's index within the group's 16 * G threads.
-template <int Q, int G>
-__device__ __forceinline__ void solve_block_column(const float *Af, float *Tf, int t) {
-    constexpr int R = 16 / G;
-    const int j = t / G, part = t % G;
-    const int lane = threadIdx.x & 31, base = lane - part;
-    const int col = 16 * Q + j;
-    float tc[4 - Q][16];  // tc[r - Q][m] = T_rQ[m][j] for the blocks known so far
+// Index of block (p, q), p > q, among the six 16x16 blocks below the diagonal.
+__host__ __device__ constexpr int eblk(int p, int q) { return p * (p - 1) / 2 + q; }
+
+// D(16x8) += A(16 x K) B(K x 8) for fp32 operands in shared memory (row
+// pitches lda, ldb), on the warp's tensor cores in three tf32 passes
+// (big*big + big*small + small*big: ~2^-20 relative, fp32-class).
+__device__ __forceinline__ void mma_rows16(float (&d)[4], const float *A, int lda, const float *B, int ldb, int K) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int m = 0; m < 16; ++m) tc[0][m] = Tf[(16 * Q + m) * kAP + col];
+    for (int k0 = 0; k0 < K; k0 += 8) {
+        const float av[4] = {A[g * lda + k0 + t], A[(g + 8) * lda + k0 + t], A[g * lda + k0 + t + 4],
+                             A[(g + 8) * lda + k0 + t + 4]};
+        const float bv[2] = {B[(k0 + t) * ldb + g], B[(k0 + t + 4) * ldb + g]};
+        uint32_t ab[4], as[4], bb[2], bs[2];
 #pragma unroll
-    for (int pr = Q + 1; pr < 4; ++pr) {
-        float x[R];
+        for (int e = 0; e < 4; ++e) ptx::split_tf32(av[e], ab[e], as[e]);
 #pragma unroll
-        for (int e = 0; e < R; ++e) {
-            const int a = part + G * e;
-            float acc0 = 0.f, acc1 = 0.f;
-#pragma unroll
-            for (int rr = Q; rr < pr; ++rr) {
-                const float *Arow = Af + (16 * pr + a) * kAP + 16 * rr;
-#pragma unroll
-                for (int m = 0; m < 16; m += 4) {
-                    const float4 av = *reinterpret_cast<const float4 *>(Arow + m);
-                    acc0 = fmaf(av.x, tc[rr - Q][m], acc0);
-                    acc1 = fmaf(av.y, tc[rr - Q][m + 1], acc1);
-                    acc0 = fmaf(av.z, tc[rr - Q][m + 2], acc0);
-                    acc1 = fmaf(av.w, tc[rr - Q][m + 3], acc1);
-                }
-            }
-            x[e] = acc0 + acc1;
-        }
-        float xf[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) xf[k] = __shfl_sync(0xffffffffu, x[k / G], base + k % G);
-        float tn[R];
-#pragma unroll
-        for (int e = 0; e < R; ++e) {
-            const int a = part + G * e;
-            const float *Trow = Tf + (16 * pr + a) * kAP + 16 * pr;
-            float acc0 = 0.f, acc1 = 0.f;
-#pragma unroll
-            for (int m = 0; m < 16; m += 4) {
-                const float4 tv = *reinterpret_cast<const float4 *>(Trow + m);
-                acc0 = fmaf(tv.x, xf[m], acc0);
-                acc1 = fmaf(tv.y, xf[m + 1], acc1);
-                acc0 = fmaf(tv.z, xf[m + 2], acc0);
-                acc1 = fmaf(tv.w, xf[m + 3], acc1);
-            }
-            tn[e] = -(acc0 + acc1);
-            Tf[(16 * pr + a) * kAP + col] = tn[e];
-        }
-        if (pr < 3) {
-#pragma unroll
-            for (int k = 0; k < 16; ++k) tc[pr - Q][k] = __shfl_sync(0xffffffffu, tn[k / G], base + k % G);
-        }
+        for (int e = 0; e < 2; ++e) ptx::split_tf32(bv[e], bb[e], bs[e]);
+        ptx::mma_tf32_16x8x8(d, as, bb);
+        ptx::mma_tf32_16x8x8(d, ab, bs);
+        ptx::mma_tf32_16x8x8(d, ab, bb);
     }
+}
+
+// Store a D fragment (16x8) to shared memory, scaled.
+__device__ __forceinline__ void store_frag(float *D, int ld, const float (&d)[4], float scale) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    *reinterpret_cast<float2 *>(D + g * ld + 2 * t) = make_float2(scale * d[0], scale * d[1]);
+    *reinterpret_cast<float2 *>(D + (g + 8) * ld + 2 * t) = make_float2(scale * d[2], scale * d[3]);
 }
 
 template <typename TG, typename TO>
@@ -230,6 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sb = ptx::smem_u32(base);
     float *Af = reinterpret_cast<float *>(base + OFF_AF);
     float *Tf = reinterpret_cast<float *>(base + OFF_TF);
+    float *Es = reinterpret_cast<float *>(base + OFF_E);
     float *gates = reinterpret_cast<float *>(base + OFF_GATE);  // [stage][e | w | g][64]
     float *Gs = reinterpret_cast<float *>(base + OFF_G);        // [stage][G | gam][64]
     uint64_t *bars = reinterpret_cast<uint64_t *>(base + OFF_BAR);
@@ -413,15 +384,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int a = 0; a < 16; ++a) Tf[(16 * pb + a) * kAP + 16 * pb + j] = tcol[a];
             }
             ptx::named_sync(NB_PAR, kParThreads);
-            // (2) The blocks below the diagonal, one block column per warp group.
-            if (warp < 4) {
-                solve_block_column<0, 8>(Af, Tf, tid);
-            } else if (warp < 6) {
-                solve_block_column<1, 4>(Af, Tf, tid - 128);
-            } else {
-                solve_block_column<2, 4>(Af, Tf, tid - 192);
+            // (2) The blocks below the diagonal on the warps' tensor cores (fp32-class tf32 passes):
+            //     T_pq = -sum_{r=q}^{p-1} E_pr T_rq with E_pr = T_pp A_pr, by distance p - q.
+            if (warp < 6) {  // E: six independent blocks, one per warp
+                const int pr = warp < 1 ? 1 : (warp < 3 ? 2 : 3), q = warp - eblk(pr, 0);
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                    float d[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma_rows16(d, Tf + (16 * pr) * kAP + 16 * pr, kAP, Af + (16 * pr) * kAP + 16 * q + 8 * nt, kAP, 16);
+                    store_frag(Es + (eblk(pr, q) * 16) * kEP + 8 * nt, kEP, d, 1.f);
+                }
             }
             ptx::named_sync(NB_PAR, kParThreads);
+#pragma unroll
+            for (int dist = 1; dist < 4; ++dist) {
+                // (4 - dist) blocks x 2 column halves, one per warp
+                if (warp < 2 * (4 - dist)) {
+                    const int q = warp >> 1, nt = warp & 1, pr = q + dist;
+                    float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int rr = q; rr < pr; ++rr)
+                        mma_rows16(d, Es + (eblk(pr, rr) * 16) * kEP, kEP, Tf + (16 * rr) * kAP + 16 * q + 8 * nt, kAP, 16);
+                    store_frag(Tf + (16 * pr) * kAP + 16 * q + 8 * nt, kAP, d, -1.f);
+                }
+                ptx::named_sync(NB_PAR, kParThreads);
+            }
             DC_TC_MARK(4);
 
             // ---- Tb = T diag(w), Tw = T diag(e gam) as bf16 hi + lo (blocks above the diagonal masked) ----

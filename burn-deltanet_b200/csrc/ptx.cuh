@@ -149,6 +149,25 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, u
         : "memory");
 }
 
+// Warp-level D(16x8) += A(16x8) B(8x8) on tf32 operands (fp32 registers; the
+// tensor core reads the upper 19 bits).  Fragment layout, g = lane / 4,
+// t = lane % 4: a = {A[g][t], A[g+8][t], A[g][t+4], A[g+8][t+4]},
+// b = {B[t][g], B[t+4][g]}, d = {D[g][2t], D[g][2t+1], D[g+8][2t], D[g+8][2t+1]}.
+__device__ __forceinline__ void mma_tf32_16x8x8(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// x = big + small with big exact in tf32 (the upper 19 bits) and small the
+// exact fp32 remainder; products of big/small pairs recover ~fp32 accuracy.
+__device__ __forceinline__ void split_tf32(float x, uint32_t &big, uint32_t &small) {
+    big = __float_as_uint(x) & 0xFFFFE000u;
+    small = __float_as_uint(x - __uint_as_float(big));
+}
+
 // Arrive on `bar` once every previously issued tcgen05.mma of this thread completes.
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

@@ -83,8 +83,10 @@ constexpr uint32_t OFF_AQK = OFF_S + 32768;             // Aqk bf16 64x64 K-majo
 constexpr uint32_t OFF_AF = OFF_AQK + 8192;             // Akk fp32 [64][68]; then [Tb; Pb] lo
 constexpr uint32_t OFF_TF = OFF_AF + 64 * kAP * 4;      // T fp32 [64][68];   then [Tw; Pw] lo
 constexpr int kEP = 20;                                 // row pitch (floats) of the E blocks
-constexpr uint32_t OFF_E = OFF_TF + 64 * kAP * 4;       // E_pq = T_pp A_pq: six blocks [16][20] fp32
-constexpr uint32_t OFF_GATE = OFF_E + 6 * 16 * kEP * 4; // per stage: e[64], w[64], g[64]
+constexpr uint32_t OFF_E = OFF_AU;                      // E_pq = T_pp A_pq: six blocks [16][20] fp32, during
+                                                        // the solve, while [Tb; Pb] hi is not live
+constexpr uint32_t OFF_Y = OFF_TF + 64 * kAP * 4;       // y bf16 64x128 (two SW128 64x64 boxes) for the TMA store
+constexpr uint32_t OFF_GATE = OFF_Y + 16384;            // per stage: e[64], w[64], g[64]
 constexpr uint32_t OFF_G = OFF_GATE + 2 * 3 * 64 * 4;   // per stage: G[64], gam[64]
 constexpr uint32_t OFF_BAR = OFF_G + 2 * 2 * 64 * 4;    // mbarriers (below)
 constexpr int kBars = 10;
@@ -95,6 +97,8 @@ constexpr uint32_t kSmemUsed = OFF_PEND + 8;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;       // alignment slack
 static_assert(OFF_AF % 1024 == 0 && OFF_TF % 1024 == 0 && OFF_AQK % 1024 == 0 && OFF_S % 1024 == 0,
               "operand tiles need 1 KB alignment");
+static_assert(6 * 16 * kEP * 4 <= 16384, "E blocks overflow the [Tb; Pb] hi region");
+static_assert(OFF_Y % 1024 == 0, "SW128 staging tile must be 1024-byte aligned");
 static_assert(kSmemBytes <= 232448, "over the 227 KB per-CTA shared-memory limit");
 
 // mbarrier slots
@@ -191,10 +195,71 @@ __device__ __forceinline__ void store_frag(float *D, int ld, const float (&d)[4]
     *reinterpret_cast<float2 *>(D + (g + 8) * ld + 2 * t) = make_float2(scale * d[2], scale * d[3]);
 }
 
+// T = (I + A)^-1 for the 64x64 strictly lower A in Af (row pitch kAP), into Tf
+// (same pitch; blocks above the diagonal are left untouched, the upper
+// triangles of the diagonal blocks are written as zeros).  Run by the 256
+// threads of the operand role; Es is scratch for six 16x20 fp32 blocks.
+//  (1) diagonal blocks T_pp = (I + A_pp)^-1, one per warp, a lane substituting
+//      down one column;
+//  (2) E_pq = T_pp A_pq for the six blocks below the diagonal;
+//  (3) T_pq = -sum_{r=q}^{p-1} E_pr T_rq by distance p - q = 1, 2, 3.
+// (2) and (3) run on the warps' tensor cores in three tf32 passes (fp32-class).
+// mark_diag / mark_e are called after (1) and (2) (phase-timing hooks).
+template <typename M1, typename M2>
+__device__ __forceinline__ void solve_unit_lower(const float *Af, float *Tf, float *Es, int warp, int lane,
+                                                 M1 &&mark_diag, M2 &&mark_e) {
+    if (warp < 4 && lane < 16) {
+        const int pb = warp, j = lane;
+        const float *A = Af + (16 * pb) * kAP + 16 * pb;
+        float tcol[16];
+#pragma unroll
+        for (int a = 0; a < 16; ++a) {
+            float acc0 = (a == j) ? 1.f : 0.f, acc1 = 0.f;
+#pragma unroll
+            for (int m = 0; m < a; m += 4) {
+                const float4 av = *reinterpret_cast<const float4 *>(A + a * kAP + m);
+                acc0 = fmaf(-av.x, tcol[m], acc0);
+                if (m + 1 < a) acc1 = fmaf(-av.y, tcol[m + 1], acc1);
+                if (m + 2 < a) acc0 = fmaf(-av.z, tcol[m + 2], acc0);
+                if (m + 3 < a) acc1 = fmaf(-av.w, tcol[m + 3], acc1);
+            }
+            tcol[a] = acc0 + acc1;
+        }
+#pragma unroll
+        for (int a = 0; a < 16; ++a) Tf[(16 * pb + a) * kAP + 16 * pb + j] = tcol[a];
+    }
+    ptx::named_sync(NB_PAR, kParThreads);
+    mark_diag();
+    if (warp < 6) {  // six independent blocks, one per warp
+        const int pr = warp < 1 ? 1 : (warp < 3 ? 2 : 3), q = warp - eblk(pr, 0);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+            mma_rows16(d, Tf + (16 * pr) * kAP + 16 * pr, kAP, Af + (16 * pr) * kAP + 16 * q + 8 * nt, kAP, 16);
+            store_frag(Es + (eblk(pr, q) * 16) * kEP + 8 * nt, kEP, d, 1.f);
+        }
+    }
+    ptx::named_sync(NB_PAR, kParThreads);
+    mark_e();
+#pragma unroll
+    for (int dist = 1; dist < 4; ++dist) {
+        if (warp < 2 * (4 - dist)) {  // (4 - dist) blocks x 2 column halves, one per warp
+            const int q = warp >> 1, nt = warp & 1, pr = q + dist;
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int rr = q; rr < pr; ++rr)
+                mma_rows16(d, Es + (eblk(pr, rr) * 16) * kEP, kEP, Tf + (16 * rr) * kAP + 16 * q + 8 * nt, kAP, 16);
+            store_frag(Tf + (16 * pr) * kAP + 16 * q + 8 * nt, kAP, d, -1.f);
+        }
+        ptx::named_sync(NB_PAR, kParThreads);
+    }
+}
+
 template <typename TG, typename TO>
 __global__ void __launch_bounds__(kThreads, 1)
     chunk_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
-                    const __grid_constant__ CUtensorMap tm_v, const CoreParams p, int *status) {
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_y,
+                    const CoreParams p, int *status) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sb = ptx::smem_u32(base);
@@ -214,6 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t nchunks = (P + kL - 1) / kL;
     const bool gated = p.gw > 0;
     const float scale = p.scale;
+    // bf16 y leaves through a staged TMA store (keeps the load/store pipe free for the operand role);
+    // fp32 y is stored row by row.
+    constexpr bool kYTma = sizeof(TO) == 2;
 
     if (tid == 0) {
         *flag = 0;
@@ -223,6 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::prefetch_tmap(&tm_k);
         ptx::prefetch_tmap(&tm_q);
         ptx::prefetch_tmap(&tm_v);
+        if (kYTma) ptx::prefetch_tmap(&tm_y);
     }
     if (warp == 0) {
         ptx::tmem_alloc(tmem_ptr, 512);
@@ -362,53 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             DC_TC_MARK(3);
 
             // ---- T = (I + Akk)^-1 in 16x16 blocks ----
-            // (1) The diagonal blocks, one per warp: a lane substitutes down one column.
-            if (warp < 4 && lane < 16) {
-                const int pb = warp, j = lane;
-                const float *A = Af + (16 * pb) * kAP + 16 * pb;
-                float tcol[16];
-#pragma unroll
-                for (int a = 0; a < 16; ++a) {
-                    float acc0 = (a == j) ? 1.f : 0.f, acc1 = 0.f;
-#pragma unroll
-                    for (int m = 0; m < a; m += 4) {
-                        const float4 av = *reinterpret_cast<const float4 *>(A + a * kAP + m);
-                        acc0 = fmaf(-av.x, tcol[m], acc0);
-                        if (m + 1 < a) acc1 = fmaf(-av.y, tcol[m + 1], acc1);
-                        if (m + 2 < a) acc0 = fmaf(-av.z, tcol[m + 2], acc0);
-                        if (m + 3 < a) acc1 = fmaf(-av.w, tcol[m + 3], acc1);
-                    }
-                    tcol[a] = acc0 + acc1;
-                }
-#pragma unroll
-                for (int a = 0; a < 16; ++a) Tf[(16 * pb + a) * kAP + 16 * pb + j] = tcol[a];
-            }
-            ptx::named_sync(NB_PAR, kParThreads);
-            // (2) The blocks below the diagonal on the warps' tensor cores (fp32-class tf32 passes):
-            //     T_pq = -sum_{r=q}^{p-1} E_pr T_rq with E_pr = T_pp A_pr, by distance p - q.
-            if (warp < 6) {  // E: six independent blocks, one per warp
-                const int pr = warp < 1 ? 1 : (warp < 3 ? 2 : 3), q = warp - eblk(pr, 0);
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                    float d[4] = {0.f, 0.f, 0.f, 0.f};
-                    mma_rows16(d, Tf + (16 * pr) * kAP + 16 * pr, kAP, Af + (16 * pr) * kAP + 16 * q + 8 * nt, kAP, 16);
-                    store_frag(Es + (eblk(pr, q) * 16) * kEP + 8 * nt, kEP, d, 1.f);
-                }
-            }
-            ptx::named_sync(NB_PAR, kParThreads);
-#pragma unroll
-            for (int dist = 1; dist < 4; ++dist) {
-                // (4 - dist) blocks x 2 column halves, one per warp
-                if (warp < 2 * (4 - dist)) {
-                    const int q = warp >> 1, nt = warp & 1, pr = q + dist;
-                    float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                    for (int rr = q; rr < pr; ++rr)
-                        mma_rows16(d, Es + (eblk(pr, rr) * 16) * kEP, kEP, Tf + (16 * rr) * kAP + 16 * q + 8 * nt, kAP, 16);
-                    store_frag(Tf + (16 * pr) * kAP + 16 * q + 8 * nt, kAP, d, -1.f);
-                }
-                ptx::named_sync(NB_PAR, kParThreads);
-            }
+            solve_unit_lower(Af, Tf, Es, warp, lane, [&] { DC_TC_MARK(14); }, [&] { DC_TC_MARK(15); });
             DC_TC_MARK(4);
 
             // ---- Tb = T diag(w), Tw = T diag(e gam) as bf16 hi + lo (blocks above the diagonal masked) ----
@@ -627,6 +650,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ptx::umma_bf16_ts(tmem + TM_UY, tmem + TM_W + 8 * kk, ptx::sdesc(sb + OFF_S + kk * 2048, 16384, 1024),
                                       id, 1);
                 ptx::umma_commit(&bars[B_MMA6]);
+                // The previous chunk's y store has landed: its tile may be rewritten, and rows it wrote
+                // past its own readouts (u > 1) are rewritten below in order by their own chunk.
+                if (kYTma) ptx::bulk_wait_all();
             }
             if (!(ok = ser_wait(B_MMA6, (uint32_t)(c & 1)))) break;
             DC_TC_MARK(11);
@@ -661,6 +687,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 ptx::st_shared_v4(stg + 32768 + hh * 8192 + off, hi[0], hi[1], hi[2], hi[3]);
                                 ptx::st_shared_v4(stg + hh * 16384 + 8192 + off, lo[0], lo[1], lo[2], lo[3]);
                             }
+                        } else if (kYTma) {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                ptx::st_shared_v4(sb + OFF_Y + hh * 8192 + ptx::sw128(r - 64, 32 * q2 + 8 * q),
+                                                  ptx::pack_bf16(f[8 * q], f[8 * q + 1]),
+                                                  ptx::pack_bf16(f[8 * q + 2], f[8 * q + 3]),
+                                                  ptx::pack_bf16(f[8 * q + 4], f[8 * q + 5]),
+                                                  ptx::pack_bf16(f[8 * q + 6], f[8 * q + 7]));
                         } else if (write_y) {
                             store_row32(yrow + 64 * hh + 32 * q2, f);
                         }
@@ -670,7 +704,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::fence_async_smem();
             ptx::tc_fence_before();
             ptx::named_sync(NB_SER, kSerThreads);
-            if (leader) ptx::mbar_arrive(&bars[B_UY_FREE]);  // D_UY and D_W (A6) may be overwritten now
+            if (leader) {
+                ptx::mbar_arrive(&bars[B_UY_FREE]);  // D_UY and D_W (A6) may be overwritten now
+                if (kYTma) {
+                    // The Q tile's 64 token rows; rows past the sequence are clipped by the tensor map.
+                    const int tok0 = (int)q_first(c, p.u);
+                    ptx::tma_store_4d(&tm_y, sb + OFF_Y, 0, (int)h, tok0, (int)b);
+                    ptx::tma_store_4d(&tm_y, sb + OFF_Y + 8192, 64, (int)h, tok0, (int)b);
+                    ptx::bulk_commit();
+                }
+            }
             DC_TC_MARK(12);
 
             // ---- D_S = Gam S + K^T (V'hi + V'lo) ----
@@ -737,6 +780,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     }
+
+    if (kYTma && tid == kParThreads) ptx::bulk_wait_all();  // the staged y tile is read before smem goes away
 
     // Both roles meet here exactly once.
     ptx::tc_fence_before();
@@ -816,10 +861,11 @@ inline int *device_status_ptr() {
 
 template <typename TG, typename TO>
 int launch_tc_typed(const CoreParams &p, cudaStream_t stream) {
-    CUtensorMap mk, mq, mv;
+    CUtensorMap mk, mq, mv, my;
     const int64_t P = p.seq * p.u;
     if (!encode_rows(&mk, p.k, p.heads, P, p.batch) || !encode_rows(&mq, p.q, p.heads, p.seq, p.batch) ||
-        !encode_rows(&mv, p.v, p.heads, P, p.batch)) {
+        !encode_rows(&mv, p.v, p.heads, P, p.batch) ||
+        (sizeof(TO) == 2 ? !encode_rows(&my, p.y, p.heads, p.seq, p.batch) : (my = mq, false))) {
         g_tc_error = (int)cudaErrorInvalidValue;
         return 6;  // DC_ECUDA
     }
@@ -831,7 +877,7 @@ int launch_tc_typed(const CoreParams &p, cudaStream_t stream) {
     auto kern = tc::chunk_tc_kernel<TG, TO>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes);
     if (e == cudaSuccess) {
-        kern<<<(unsigned)(p.batch * p.heads), tc::kThreads, tc::kSmemBytes, stream>>>(mk, mq, mv, p, status);
+        kern<<<(unsigned)(p.batch * p.heads), tc::kThreads, tc::kSmemBytes, stream>>>(mk, mq, mv, my, p, status);
         e = cudaGetLastError();
     }
     if (e != cudaSuccess) {

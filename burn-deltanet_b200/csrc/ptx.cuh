@@ -90,6 +90,18 @@ __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
 
 // Generic-proxy shared-memory writes become visible to the async proxy
 // (tensor cores, TMA) after this fence plus a thread barrier.
+// Tile store shared -> global through the tensor map (bulk async-group); the
+// shared tile must be made visible to the async proxy (fence_async_smem) and
+// may be overwritten only after bulk_wait_all() or bulk_wait_read().
+__device__ __forceinline__ void tma_store_4d(const void *tmap, uint32_t src, int c0, int c1, int c2, int c3) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(tmap),
+                 "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Every committed bulk store of this thread has written global memory.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // ---------------------------------------------------------------- tcgen05

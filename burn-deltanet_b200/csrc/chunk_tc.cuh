@@ -109,6 +109,10 @@ constexpr uint32_t TM_A = 0, TM_W = 128, TM_UY = 256, TM_S = 384;
 
 // Named barriers of the two roles (id 0 is __syncthreads).
 constexpr uint32_t NB_PAR = 1, NB_SER = 2;
+// Warps 0-6 of the operand role, for the gate phase; warp 7 skips it while it issues the previous chunk's
+// MMA4 (an issue that blocks its thread for as long as the tensor pipe takes to accept 16 MMAs).
+constexpr uint32_t NB_GATE = 3;
+constexpr int kIssueWarp = 7;
 
 __device__ __forceinline__ float gate_at(const float *p) { return *p; }
 __device__ __forceinline__ float gate_at(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
@@ -325,9 +329,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_base = (uint32_t)(32 * sp) << 16;
         const bool leader = (tid == 0);
         auto par_wait = [&](int bar, uint32_t parity) {
-            if (!ptx::mbar_wait(&bars[bar], parity)) *flag = 1;
-            ptx::named_sync(NB_PAR, kParThreads);
-            return *flag == 0;
+            // A wait that ran out anywhere (here, or already flagged by either role) stops every operand
+            // thread at the same point.
+            const bool bad = !ptx::mbar_wait(&bars[bar], parity) || *flag != 0;
+            if (ptx::named_sync_or(NB_PAR, kParThreads, bad)) {
+                *flag = 1;
+                return false;
+            }
+            return true;
         };
         if (leader) {
             issue_tma(0, 0);
@@ -346,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             // ---- chunk c's gates -> G = cumsum(g), gam = e^G; published to the serial role ----
             if (tid < 192) gates[st * 192 + tid] = gnext;
-            ptx::named_sync(NB_PAR, kParThreads);
+            if (warp != kIssueWarp) ptx::named_sync(NB_GATE, kParThreads - 32);
             if (c + 1 < nchunks && tid < 192) gnext = load_gate<TG>(p, b, h, c + 1, tid);
             if (warp == 0) {
                 const float *g = gates + (st * 3 + 2) * 64;
@@ -362,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 gam[2 * lane + 1] = __expf(s);
                 gam[2 * lane] = __expf(s - x1);
             }
-            ptx::named_sync(NB_PAR, kParThreads);
+            if (warp != kIssueWarp) ptx::named_sync(NB_GATE, kParThreads - 32);
             if (leader) ptx::mbar_arrive(&bars[B_GATE0 + st]);
 
             // ---- chunk c's tiles; chunk c-1's MMA4 must be done (it reads the lo operands in Af/Tf) ----
@@ -522,7 +531,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             DC_TC_MARK(7);
 
             // ---- D_UY = [Tb; Pb] V, D_W = [Tw; Pw] K, once the serial role released chunk c-1's ----
-            if (leader) {
+            // Issued by warp 7 while warps 0-6 go on with chunk c+1's gates; everyone meets again at the
+            // next chunk's tile wait, where a wait that ran out here is seen by all.
+            if (tid == kIssueWarp * 32) {
                 if (c > 0 && !ptx::mbar_wait(&bars[B_UY_FREE], (uint32_t)((c - 1) & 1))) {
                     *flag = 1;
                 } else {
@@ -539,8 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ptx::umma_commit(&bars[B_MMA4]);
                 }
             }
-            ptx::named_sync(NB_PAR, kParThreads);
-            if (*flag) break;
+            __syncwarp();
         }
     } else {
         // =============================== serial role: the S chain of chunk c ===============================
@@ -549,9 +559,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_base = (uint32_t)(32 * sp) << 16;
         const bool leader = (tid == kParThreads);
         auto ser_wait = [&](int bar, uint32_t parity) {
-            if (!ptx::mbar_wait(&bars[bar], parity)) *flag = 1;
-            ptx::named_sync(NB_SER, kSerThreads);
-            return *flag == 0;
+            const bool bad = !ptx::mbar_wait(&bars[bar], parity) || *flag != 0;
+            if (ptx::named_sync_or(NB_SER, kSerThreads, bad)) {
+                *flag = 1;
+                return false;
+            }
+            return true;
         };
         bool ok = ser_wait(B_GATE0, 0);
         if (ok) {

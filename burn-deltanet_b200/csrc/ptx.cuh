@@ -72,6 +72,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 __device__ __forceinline__ void named_sync(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
+// Named barrier that also ORs `pred` over its `count` threads: every participant gets the same answer.
+__device__ __forceinline__ bool named_sync_or(uint32_t id, uint32_t count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
 
 // ---------------------------------------------------------------- TMA
 // 4-D tiled load into this CTA's shared memory, completing on `bar`.

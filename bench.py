@@ -369,7 +369,8 @@ def run_ours(args):
     hbm_peak, tc_peak, peak_kind = measured_peaks()
     cfg, batch, tokens, u, kind = WORKLOADS[args.workload]
     x = make_prefill(kind, batch, tokens, u, "cuda", 1000 + rank)
-    launches = args.steps  # one dc_chunk_fwd kernel per step
+    # One dc_chunk_fwd per step: one kernel, or two (prep + scan) for per-channel gates.
+    launches = args.steps * (2 if kind == "gdn2" else 1)
     clocks = ClockSampler(local)
     barrier(world)
     torch.cuda.synchronize()

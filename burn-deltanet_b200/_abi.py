@@ -20,6 +20,7 @@ DC_EINVAL_ARG = 4
 DC_EUNSUPPORTED = 5
 DC_ECUDA = 6
 DC_EDEVICE = 7
+DC_EWORKSPACE = 8
 
 # enum dc_dtype
 DC_F32 = 0
@@ -27,10 +28,11 @@ DC_BF16 = 1
 
 DC_FLAG_FORCE_SIMT = 0x1
 DC_FLAG_RECURRENT = 0x2
+DC_FLAG_FORCE_SPLIT = 0x4
 
 EXPORTS = (
     "dc_chunk_fwd", "dc_step", "dc_status_string", "dc_last_cuda_error", "dc_device_status",
-    "dc_chunk_kernel_choice", "dc_chunk_launches", "dc_version",
+    "dc_chunk_kernel_choice", "dc_chunk_launches", "dc_version", "dc_chunk_workspace_size",
 )
 
 
@@ -48,6 +50,7 @@ class ChunkArgs(ctypes.Structure):
         ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
         ("erase", ctypes.c_void_p), ("write", ctypes.c_void_p), ("g", ctypes.c_void_p),
         ("state_in", ctypes.c_void_p), ("y", ctypes.c_void_p), ("state_out", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
     ]
 
 
@@ -93,6 +96,8 @@ def lib() -> ctypes.CDLL:
         L.dc_chunk_launches.restype = ctypes.c_int
         L.dc_version.argtypes = []
         L.dc_version.restype = ctypes.c_int
+        L.dc_chunk_workspace_size.argtypes = [ctypes.POINTER(ChunkArgs)]
+        L.dc_chunk_workspace_size.restype = ctypes.c_uint64
         _lib = L
     return _lib
 

@@ -146,7 +146,8 @@ def beta_gates(beta: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
 def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv,
                              has_gate: bool, chunk_len: int, scale: float, *, n_householder: int = 1,
                              out_dtype: Optional[torch.dtype] = None, force_simt: bool = False,
-                             recurrent: bool = False,
+                             recurrent: bool = False, force_split: bool = False,
+                             workspace: Optional[torch.Tensor] = None,
                              y_out: Optional[torch.Tensor] = None, state_out: Optional[torch.Tensor] = None):
     """The backend-extension op (chunk_recalculated.rs:115-126) on CUDA tensors.
 
@@ -157,6 +158,10 @@ def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_b
     unless ``y_out`` / ``state_out`` are given (``state_out`` may be ``state_bhkv``).
     ``recurrent=True`` evaluates DeltaPath::Recurrent: the fused decode tick walks
     the sequence token by token (one launch per token).
+    Per-channel gates (GDN-2) run on the tensor cores through a device workspace
+    of ``dc_chunk_workspace_size`` bytes: pass ``workspace`` (a uint8 CUDA tensor)
+    to reuse one, otherwise this layer allocates it for the call.
+    ``force_split=True`` takes that two-kernel path for per-head gates too.
     """
     ts = dict(q=q_bshk, k=k_bshk, v=v_bshv, erase=erase_bshK, write=write_bshV, state=state_bhkv)
     if has_gate:
@@ -194,12 +199,19 @@ def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_b
     a.g_w = g_bshK.shape[3] if has_gate else 0
     a.chunk_len = int(chunk_len)
     a.in_dtype, a.gate_dtype, a.out_dtype = in_dt, gate_dt, _dtype_code(y, "y")
-    a.flags = (_abi.DC_FLAG_FORCE_SIMT if force_simt else 0) | (_abi.DC_FLAG_RECURRENT if recurrent else 0)
+    a.flags = ((_abi.DC_FLAG_FORCE_SIMT if force_simt else 0) | (_abi.DC_FLAG_RECURRENT if recurrent else 0)
+               | (_abi.DC_FLAG_FORCE_SPLIT if force_split else 0))
     a.scale = float(scale)
     a.q, a.k, a.v = q_bshk.data_ptr(), k_bshk.data_ptr(), v_bshv.data_ptr()
     a.erase, a.write = erase_bshK.data_ptr(), write_bshV.data_ptr()
     a.g = g_bshK.data_ptr() if has_gate else None
     a.state_in, a.y, a.state_out = state_bhkv.data_ptr(), y.data_ptr(), s_out.data_ptr()
+    need = int(_abi.lib().dc_chunk_workspace_size(a))
+    if need > 0:
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q_bshk.device)
+        _check_tensor(workspace, "workspace")
+        a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     with torch.cuda.device(q_bshk.device):
         stream = torch.cuda.current_stream(q_bshk.device).cuda_stream
         _raise(_abi.lib().dc_chunk_fwd(a, stream), "dc_chunk_fwd")

@@ -1,0 +1,909 @@
+// chunk_split.cuh — the tensor-core chunkwise prefill for per-channel gates
+// (GDN-2: erase b in R^dk, write w in R^dv, log-decay g in R^dk), as two
+// kernels over a caller-provided workspace.
+//
+// With per-channel decay, e^{G_id - G_jd} sits inside the key-channel sums of
+// Akk and Aqk, and one chunk's gates alone are 96 KB in fp32: the
+// S-independent half of a chunk no longer fits beside the state chain in one
+// SM's shared memory.  The work splits where the chunk algorithm splits
+// (src/delta/chunk.rs:103-157 is S-independent, 167-205 is the scan):
+//
+//   prep_kernel   one CTA per (chunk, batch x head), every chunk in parallel:
+//                 gate scan, decay-aware Akk / Aqk, T = (I + Akk)^-1 and the
+//                 S-independent products, written to the workspace per chunk:
+//                   A6  = [-W; s (q e^G) - Aqk W]   bf16 128 x 128
+//                   U   = T (v w)                   fp32  64 x 128
+//                   Y0  = Aqk U                     bf16  64 x 128
+//                   Kh  = k e^{G_63 - G}            bf16  64 x 128
+//                   gam = e^{G_63}                  fp32  128
+//                 with W = T (b k e^G), the per-channel form of chunk.rs:144-157.
+//   scan_kernel   one CTA per (batch x head), chunks in order, S in TMEM:
+//                   [V'; y] = [U; Y0] + A6 S        (V' = U - W S; y = Q' S + Aqk U)
+//                   S      <- diag(gam) S + Kh^T V'
+//
+// Decay-aware Akk / Aqk without overflow.  G (the chunk-local cumulative log
+// decay) does not increase along the chunk, so for j <= r <= i
+//   e^{G_i - G_j} = e^{G_i - G_r} e^{G_r - G_j},   both factors in [0, 1].
+// The 64 rows are bisected six times (blocks of 64, 32, ..., 2).  At each level
+// a block's second-half rows i meet its first-half rows j through the
+// reference r = the block's midpoint, and each pair i > j meets at exactly one
+// level.  One level is one product of two packed 32-row operands
+//   R[i] = (b k)_i e^{G_i - G_r}   (for Aqk: q_i e^{G_i - G_r}),
+//   C[j] = k_j e^{G_r - G_j},
+// whose block diagonal holds that level's pairs (warp MMAs, bf16).  The
+// factors are running products of alpha = e^g inside each half-block: no
+// exponent is taken of a difference that could overflow, and underflow goes
+// to the exact limit 0.  The diagonal of Aqk (no decay) is a plain reduction.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "chunk_tc.cuh"
+#include "common.cuh"
+#include "ptx.cuh"
+
+// Phase-timing hook of the prep kernel (defined by a timing build; a no-op here).
+#ifndef DC_SPLIT_MARK
+#define DC_SPLIT_MARK(id)
+#endif
+
+namespace dc {
+namespace split {
+
+using tc::kAP;
+constexpr int kOP = 136;  // bf16 row pitch of the level operands (272 B: ldmatrix rows hit distinct banks)
+
+// The workspace, structure of arrays, chunk-major inside each (batch, head).
+struct SplitWs {
+    __nv_bfloat16 *a6;  // [BH * nch * 128][128]
+    float *u;           // [BH * nch * 64][128]
+    __nv_bfloat16 *y0;  // [BH * nch * 64][128]
+    __nv_bfloat16 *kh;  // [BH * nch * 64][128]
+    float *gam;         // [BH * nch][128]
+    int64_t nch;
+};
+
+constexpr uint64_t kWsBytesPerChunk = 32768ull + 32768ull + 16384ull + 16384ull + 512ull;
+
+// ---------------------------------------------------------------- prep kernel
+constexpr int kThreadsA = 256;
+constexpr uint32_t A_RKK = 0;                           // level operands, bf16 [32][kOP] each
+constexpr uint32_t A_RQK = A_RKK + 32 * kOP * 2;
+constexpr uint32_t A_CC = A_RQK + 32 * kOP * 2;
+constexpr uint32_t A_AF = 26624;                        // Akk fp32 [64][kAP] (E blocks in its upper blocks)
+constexpr uint32_t A_TF = A_AF + 64 * kAP * 4;          // T fp32 [64][kAP]
+constexpr uint32_t A_AQK = A_TF + 64 * kAP * 4;         // Aqk bf16 64x64, K-major SW128
+constexpr uint32_t A_TPH = A_AQK + 8192;                // [T; P] hi, 128x64 bf16 K-major SW128
+constexpr uint32_t A_TPL = A_TPH + 16384;               // [T; P] lo
+constexpr uint32_t A_BOP = A_TPL + 16384;               // [v w | b k e^G], four 64-column MN-major blocks
+constexpr uint32_t A_QT = A_BOP + 32768;                // s q e^G bf16 [64][kOP]
+constexpr uint32_t A_X = A_QT + 64 * kOP * 2;           // exchange: fp32 [640]
+constexpr uint32_t A_QKV = 155648;                      // q, k, v tiles (TMA, SW128, two 64-channel boxes each)
+constexpr uint32_t A_BAR = A_QKV + 3 * 16384;           // three mbarriers, TMEM pointer, flag
+constexpr uint32_t A_USED = A_BAR + 32;
+constexpr uint32_t A_QK = A_TPH;                        // q.k per (row, channel), fp32 [64][128], during the scan
+constexpr uint32_t kSmemA = A_USED + 1024;
+static_assert(A_RKK + 3 * 32 * kOP * 2 <= A_AF, "level operands overlap Akk");
+static_assert(A_X + 640 * 4 <= A_QKV && A_QKV % 1024 == 0, "q/k/v tiles misplaced");
+static_assert(A_QK + 64 * 128 * 4 <= A_BOP, "q.k buffer overlaps the B operands");
+static_assert(A_AQK % 1024 == 0 && A_TPH % 1024 == 0 && A_TPL % 1024 == 0 && A_BOP % 1024 == 0,
+              "SW128 tiles must be 1024-byte aligned");
+static_assert(kSmemA <= 232448, "prep kernel over the shared-memory limit");
+constexpr uint32_t TMA_BIG = 0, TMA_P = 256;  // TMEM columns: [U W; Y0 AqkW] (N=256), P = Aqk T (N=64)
+
+__device__ __forceinline__ void st_bf16(uint8_t *p, float x) {
+    *reinterpret_cast<__nv_bfloat16 *>(p) = __float2bfloat16_rn(x);
+}
+
+// Element (t, d) of the q (which = 0) or k (which = 1) tile.
+__device__ __forceinline__ float qk_tile(const uint8_t *base, int which, int t, int d) {
+    return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(
+        base + A_QKV + 16384 * which + (uint32_t)(d >> 6) * 8192u + ptx::sw128(t, d & 63)));
+}
+
+// One bisection level (blocks of s = 2^LS rows): this thread's operand rows, then the warps' MMAs of the
+// packed 32 x 32 product, whose block-diagonal entries are scattered into Akk (fp32) and Aqk (bf16).
+// Thread (d, h2) owns channel d of rows 32 h2 .. 32 h2 + 31; for s <= 32 those rows hold whole blocks.
+template <int LS>
+__device__ __forceinline__ void bisection_level(uint8_t *base, uint32_t sb, float *Af, const uint32_t (&bk2)[16],
+                                                const float (&alpha)[32], float a32, float scale, int d, int h2,
+                                                int warp, int lane) {
+    constexpr int s = 1 << LS, half = s >> 1, lh = LS - 1;
+    uint8_t *Rkk = base + A_RKK, *Rqk = base + A_RQK, *Cc = base + A_CC;
+    auto bk = [&](int i) { return (i & 1) ? ptx::bf16hi(bk2[i / 2]) : ptx::bf16lo(bk2[i / 2]); };
+    auto row_side = [&](int i, int m, float P) {
+        st_bf16(Rkk + 2 * (m * kOP + d), bk(i) * P);
+        st_bf16(Rqk + 2 * (m * kOP + d), qk_tile(base, 0, 32 * h2 + i, d) * P);
+    };
+    auto col_side = [&](int i, int n, float Pb) { st_bf16(Cc + 2 * (n * kOP + d), qk_tile(base, 1, 32 * h2 + i, d) * Pb); };
+    if (LS == 6) {
+        if (h2) {  // rows 32-63: the second half, reference row 32
+            float P = 1.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                P = (i == 0) ? 1.f : P * alpha[i];
+                row_side(i, i, P);
+            }
+        } else {  // rows 0-31: the first half
+            float Pb = a32;
+#pragma unroll
+            for (int i = 31; i >= 0; --i) {
+                if (i < 31) Pb *= alpha[i + 1 < 32 ? i + 1 : 31];
+                col_side(i, i, Pb);
+            }
+        }
+    } else {
+        float P = 1.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int pos = i & (s - 1);
+            if (pos >= half) {
+                P = (pos == half) ? 1.f : P * alpha[i];
+                row_side(i, 16 * h2 + ((i >> LS) << lh) + (pos - half), P);
+            }
+        }
+        float Pb = 1.f;
+#pragma unroll
+        for (int i = 31; i >= 0; --i) {
+            const int pos = i & (s - 1);
+            if (pos < half) {
+                const float an = alpha[i + 1 < 32 ? i + 1 : 31];  // alpha of row t + 1 (inside this half)
+                Pb = (pos == half - 1) ? an : Pb * an;
+                col_side(i, 16 * h2 + ((i >> LS) << lh) + pos, Pb);
+            }
+        }
+    }
+    ptx::named_sync(tc::NB_PAR, kThreadsA);
+    // Tiles of the packed 32 x 32 product that meet its block diagonal: all eight at the top level,
+    // (mt, 2 mt) and (mt, 2 mt + 1) below.  Job = (matrix, m tile, n tile); Akk and Aqk share C.
+    constexpr int njobs = (half == 32) ? 16 : 8;
+#pragma unroll
+    for (int job0 = 0; job0 < njobs; job0 += kThreadsA / 32) {
+        const int job = job0 + warp;
+        const int mat = job & 1;
+        const int mt = (half == 32) ? ((job >> 1) & 1) : ((job >> 2) & 1);
+        const int nt = (half == 32) ? (job >> 2) : (2 * mt + ((job >> 1) & 1));
+        const uint32_t rb = sb + (mat ? A_RQK : A_RKK);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            uint32_t a[4], bb[2];
+            ptx::ldsm_x4(rb + 2u * ((16 * mt + (lane & 15)) * kOP + 16 * ks + 8 * (lane >> 4)), a);
+            ptx::ldsm_x2(sb + A_CC + 2u * ((8 * nt + (lane & 7)) * kOP + 16 * ks + 8 * ((lane >> 3) & 1)), bb);
+            ptx::mma_bf16_16x8x16(acc, a, bb);
+        }
+        const int gq = lane >> 2, t4 = lane & 3;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int m = 16 * mt + gq + 8 * (e >> 1), n = 8 * nt + 2 * t4 + (e & 1);
+            const int blk = m >> lh;
+            if (blk != (n >> lh)) continue;
+            const int i = (blk << LS) + half + (m & (half - 1)), j = (blk << LS) + (n & (half - 1));
+            if (mat == 0)
+                Af[i * kAP + j] = acc[e];
+            else
+                st_bf16(base + A_AQK + ptx::sw128(i, j), scale * acc[e]);
+        }
+    }
+    ptx::named_sync(tc::NB_PAR, kThreadsA);
+}
+
+template <typename TG>
+__global__ void __launch_bounds__(kThreadsA, 1)
+    prep_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                const __grid_constant__ CUtensorMap tm_v, const CoreParams p, const SplitWs ws, int *status) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);  // stays a shared pointer
+    const uint32_t sb = ptx::smem_u32(base);
+    float *Af = reinterpret_cast<float *>(base + A_AF);
+    float *Tf = reinterpret_cast<float *>(base + A_TF);
+    float *X = reinterpret_cast<float *>(base + A_X);
+    __nv_bfloat16 *QT = reinterpret_cast<__nv_bfloat16 *>(base + A_QT);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(base + A_BAR);
+    uint32_t *tmem_ptr = reinterpret_cast<uint32_t *>(base + A_BAR + 24);
+    volatile int *flag = reinterpret_cast<volatile int *>(base + A_BAR + 28);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t c = blockIdx.x, bh = blockIdx.y, nch = ws.nch;
+    const int64_t b = bh / p.heads, h = bh % p.heads;
+    const int64_t row0 = c * tc::kL;
+    const int nvalid = (int)((p.seq - row0) < 64 ? (p.seq - row0) : 64);
+    const int64_t bhc = bh * nch + c;
+    const float scale = p.scale;
+
+    if (tid == 0) {
+        *flag = 0;
+        ptx::mbar_init(&bars[0], 1);
+        ptx::mbar_init(&bars[1], 1);
+        ptx::mbar_init(&bars[2], 1);
+        ptx::fence_mbar_init();
+        // The chunk's q, k, v rows (rows past the sequence read as zeros).
+        ptx::mbar_arrive_expect_tx(&bars[2], 3 * 16384);
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+            ptx::tma_load_4d(base + A_QKV + 8192 * x, &tm_q, &bars[2], 64 * x, (int)h, (int)row0, (int)b);
+            ptx::tma_load_4d(base + A_QKV + 16384 + 8192 * x, &tm_k, &bars[2], 64 * x, (int)h, (int)row0, (int)b);
+            ptx::tma_load_4d(base + A_QKV + 32768 + 8192 * x, &tm_v, &bars[2], 64 * x, (int)h, (int)row0, (int)b);
+        }
+    }
+    if (warp == 0) {
+        ptx::tmem_alloc(tmem_ptr, 512);
+        ptx::tmem_relinquish();
+    }
+    for (int i = tid; i < 512; i += kThreadsA) ptx::st_shared_v4(sb + A_AQK + 16 * i, 0u, 0u, 0u, 0u);
+
+    // One key / value channel per thread, half the chunk's rows each.
+    const int d = tid & 127, h2 = tid >> 7;
+    auto rowidx = [&](int t) -> int64_t { return (b * p.seq + row0 + t) * p.heads + h; };
+    auto gate = [&](const void *ptr, int w, int64_t r) -> float {
+        return ld(static_cast<const TG *>(ptr) + r * w + (w == 1 ? 0 : d));
+    };
+
+    DC_SPLIT_MARK(0);
+    // ---- (0) this half's g (all loads in flight at once) and its sum: the chunk-local offsets of G ----
+    float alpha[32];  // g until the scan below turns it into e^g
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const int t = 32 * h2 + i;
+        alpha[i] = (p.gw > 0 && t < nvalid) ? gate(p.g, p.gw, rowidx(t)) : 0.f;
+    }
+    float gsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) gsum += alpha[i];
+    X[h2 * 128 + d] = gsum;
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_ptr;
+    const float G63 = X[d] + X[128 + d];
+    float G = h2 ? X[d] : 0.f;
+    DC_SPLIT_MARK(1);
+
+    // ---- (1) the scan: G, alpha = e^g, the B operands, s q e^G, Kh, and the level inputs.  q, k, v come
+    //      from the TMA tiles; erase and write are loaded eight rows at a time before any is used. ----
+    const bool tiles_ok = ptx::mbar_wait(&bars[2], 0);
+    const uint32_t cellcol = (uint32_t)(d >> 6) * 8192u;
+    auto tile = [&](int which, int t) -> float { return qk_tile(base, which, t, d); };  // 0 q, 1 k, 2 v
+    float *QK = reinterpret_cast<float *>(base + A_QK);
+    uint32_t bk2[16];  // bf16 pairs of consecutive rows of (b k)
+#pragma unroll
+    for (int i0 = 0; i0 < 32; i0 += 8) {
+        float ex[8], wx[8];
+#pragma unroll
+        for (int o = 0; o < 8; ++o) {
+            const int t = 32 * h2 + i0 + o;
+            ex[o] = wx[o] = 0.f;
+            if (t < nvalid) {
+                const int64_t r = rowidx(t);
+                ex[o] = gate(p.erase, p.ew, r);
+                wx[o] = gate(p.write, p.ww, r);
+            }
+        }
+        float bkx[8];
+#pragma unroll
+        for (int o = 0; o < 8; ++o) {
+            const int i = i0 + o, t = 32 * h2 + i;
+            const float qx = tile(0, t), kx = tile(1, t), vx = tile(2, t);
+            G += alpha[i];
+            alpha[i] = __expf(alpha[i]);
+            const float gam = __expf(G);
+            const uint32_t cell = cellcol + ptx::sw128(t, d & 63);
+            st_bf16(base + A_BOP + cell, vx * wx[o]);
+            st_bf16(base + A_BOP + 16384 + cell, ex[o] * kx * gam);
+            QT[t * kOP + d] = __float2bfloat16_rn(scale * qx * gam);
+            ws.kh[(bhc * 64 + t) * 128 + d] = __float2bfloat16_rn(kx * __expf(G63 - G));
+            QK[t * 128 + d] = qx * kx;
+            bkx[o] = ex[o] * kx;
+        }
+#pragma unroll
+        for (int o = 0; o < 8; o += 2) bk2[(i0 + o) / 2] = ptx::pack_bf16(bkx[o], bkx[o + 1]);
+    }
+    if (h2 == 0) ws.gam[bhc * 128 + d] = __expf(G63);
+    if (h2 == 1) X[256 + d] = alpha[0];  // alpha of row 32, the reference of the top level
+    if (!tiles_ok) *flag = 1;
+    ptx::named_sync(tc::NB_PAR, kThreadsA);
+    // Aqk's diagonal: row t summed over the 128 channels by four threads (rotated reads: no bank conflicts).
+    {
+        const int t = tid >> 2, part = tid & 3;
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc += QK[t * 128 + 32 * part + ((j + t) & 31)];
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        if (part == 0) st_bf16(base + A_AQK + ptx::sw128(t, t), scale * acc);
+    }
+    const float a32 = X[256 + d];
+    DC_SPLIT_MARK(2);
+
+    // ---- (2) Akk (strictly lower) and Aqk (lower) by bisection levels, coarsest first ----
+    bisection_level<6>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
+    bisection_level<5>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
+    bisection_level<4>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
+    bisection_level<3>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
+    bisection_level<2>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
+    bisection_level<1>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
+    DC_SPLIT_MARK(3);
+    // ---- (3) T = (I + Akk)^-1 ----
+    tc::solve_unit_lower(Af, Tf, warp, lane, [] {}, [] {});
+    DC_SPLIT_MARK(4);
+
+    // ---- (4) T hi + lo: rows 0-63 of the A operand (blocks above the diagonal zero) ----
+    {
+        const int i = tid & 63, j0 = (tid >> 6) * 16;
+        float t[16];
+#pragma unroll
+        for (int m = 0; m < 16; m += 4) {
+            const float4 tv = *reinterpret_cast<const float4 *>(Tf + i * kAP + j0 + m);
+            t[m] = j0 + m <= i ? tv.x : 0.f;
+            t[m + 1] = j0 + m + 1 <= i ? tv.y : 0.f;
+            t[m + 2] = j0 + m + 2 <= i ? tv.z : 0.f;
+            t[m + 3] = j0 + m + 3 <= i ? tv.w : 0.f;
+        }
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float x0 = t[8 * q + 2 * e], x1 = t[8 * q + 2 * e + 1];
+                hi[e] = ptx::pack_bf16(x0, x1);
+                lo[e] = ptx::pack_bf16(x0 - ptx::bf16lo(hi[e]), x1 - ptx::bf16hi(hi[e]));
+            }
+            const uint32_t off = ptx::sw128(i, j0 + 8 * q);
+            ptx::st_shared_v4(sb + A_TPH + off, hi[0], hi[1], hi[2], hi[3]);
+            ptx::st_shared_v4(sb + A_TPL + off, lo[0], lo[1], lo[2], lo[3]);
+        }
+    }
+    ptx::fence_async_smem();
+    ptx::tc_fence_before();
+    ptx::named_sync(tc::NB_PAR, kThreadsA);
+
+    auto role_wait = [&](int bar, uint32_t parity) {
+        const bool bad = !ptx::mbar_wait(&bars[bar], parity) || *flag != 0;
+        if (ptx::named_sync_or(tc::NB_PAR, kThreadsA, bad)) {
+            *flag = 1;
+            return false;
+        }
+        return true;
+    };
+
+    // ---- (5) P = Aqk T (hi) ----
+    if (tid == 0) {
+        ptx::tc_fence_after();
+        const uint32_t id = ptx::idesc_bf16(64, 64, 0, 1);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+            ptx::umma_bf16(tmem + TMA_P, ptx::sdesc(sb + A_AQK + kk * 32, 16, 1024),
+                           ptx::sdesc(sb + A_TPH + kk * 2048, 16384, 1024), id, kk > 0);
+        ptx::umma_commit(&bars[0]);
+    }
+    bool ok = role_wait(0, 0);
+    DC_SPLIT_MARK(5);
+
+    // ---- (6) P hi + lo: rows 64-127 of the A operand (M=64 accumulator: rows in lanes 0-15) ----
+    if (ok) {
+        ptx::tc_fence_after();
+        const int sp = warp & 3, ch = warp >> 2;
+        uint32_t v[32];
+        ptx::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + TMA_P + 32 * ch, v);
+        ptx::tmem_wait_ld();
+        if (lane < 16) {
+            const int i = 16 * sp + lane;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float *f = reinterpret_cast<const float *>(v + 8 * q);
+                uint32_t hi[4], lo[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    hi[e] = ptx::pack_bf16(f[2 * e], f[2 * e + 1]);
+                    lo[e] = ptx::pack_bf16(f[2 * e] - ptx::bf16lo(hi[e]), f[2 * e + 1] - ptx::bf16hi(hi[e]));
+                }
+                const uint32_t off = ptx::sw128(64 + i, 32 * ch + 8 * q);
+                ptx::st_shared_v4(sb + A_TPH + off, hi[0], hi[1], hi[2], hi[3]);
+                ptx::st_shared_v4(sb + A_TPL + off, lo[0], lo[1], lo[2], lo[3]);
+            }
+        }
+        ptx::fence_async_smem();
+        ptx::tc_fence_before();
+        ptx::named_sync(tc::NB_PAR, kThreadsA);
+
+        // ---- (7) [U W; Y0 Aqk W] = [T; P] (hi + lo) [v w | b k e^G] ----
+        if (tid == 0) {
+            ptx::tc_fence_after();
+            const uint32_t id = ptx::idesc_bf16(128, 256, 0, 1);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+                ptx::umma_bf16(tmem + TMA_BIG, ptx::sdesc(sb + (kk < 4 ? A_TPH : A_TPL) + (kk & 3) * 32, 16, 1024),
+                               ptx::sdesc(sb + A_BOP + (kk & 3) * 2048, 8192, 1024), id, kk > 0);
+            ptx::umma_commit(&bars[1]);
+        }
+        DC_SPLIT_MARK(6);
+        ok = role_wait(1, 0);
+    }
+    DC_SPLIT_MARK(7);
+
+    // ---- (8) the workspace: U, Y0 (warps 0-3), A6 = [-W; Q'] (warps 4-7) ----
+    if (ok) {
+        ptx::tc_fence_after();
+        const int sp = warp & 3, ch = warp >> 2, r = 32 * sp + lane;
+#pragma unroll 1
+        for (int qq = 0; qq < 4; ++qq) {
+            uint32_t v[32];
+            ptx::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + TMA_BIG + 128 * ch + 32 * qq, v);
+            ptx::tmem_wait_ld();
+            const float *f = reinterpret_cast<const float *>(v);
+            const int col0 = 32 * qq;
+            if (ch == 0 && r < 64) {
+                float4 *dst = reinterpret_cast<float4 *>(ws.u + (bhc * 64 + r) * 128 + col0);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) dst[e] = make_float4(f[4 * e], f[4 * e + 1], f[4 * e + 2], f[4 * e + 3]);
+            } else if (ch == 0) {
+                uint4 *dst = reinterpret_cast<uint4 *>(ws.y0 + (bhc * 64 + r - 64) * 128 + col0);
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    dst[e] = make_uint4(ptx::pack_bf16(f[8 * e], f[8 * e + 1]), ptx::pack_bf16(f[8 * e + 2], f[8 * e + 3]),
+                                        ptx::pack_bf16(f[8 * e + 4], f[8 * e + 5]),
+                                        ptx::pack_bf16(f[8 * e + 6], f[8 * e + 7]));
+            } else {
+                uint4 *dst = reinterpret_cast<uint4 *>(ws.a6 + (bhc * 128 + r) * 128 + col0);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    float x[8];
+                    if (r < 64) {
+#pragma unroll
+                        for (int o = 0; o < 8; ++o) x[o] = -f[8 * e + o];
+                    } else {
+                        const uint4 qv = ptx::ld_shared_v4(sb + A_QT + 2u * ((r - 64) * kOP + col0 + 8 * e));
+                        const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+                        for (int o = 0; o < 4; ++o) {
+                            x[2 * o] = ptx::bf16lo(qw[o]) - f[8 * e + 2 * o];
+                            x[2 * o + 1] = ptx::bf16hi(qw[o]) - f[8 * e + 2 * o + 1];
+                        }
+                    }
+                    dst[e] = make_uint4(ptx::pack_bf16(x[0], x[1]), ptx::pack_bf16(x[2], x[3]), ptx::pack_bf16(x[4], x[5]),
+                                        ptx::pack_bf16(x[6], x[7]));
+                }
+            }
+        }
+    }
+
+    ptx::tc_fence_before();
+    __syncthreads();
+    DC_SPLIT_MARK(8);
+    if (*flag && tid == 0) atomicExch(status, kStatusTimeout);
+    if (warp == 0) ptx::tmem_dealloc(tmem, 512);
+}
+
+// ---------------------------------------------------------------- scan kernel
+constexpr int kThreadsB = 128;
+constexpr uint32_t B_A6 = 0;              // A6: two K-major SW128 blocks (channels 0-63, 64-127), 128 rows
+constexpr uint32_t B_KH = 32768;          // Kh: two MN-major SW128 blocks of 64 channels, 64 rows
+constexpr uint32_t B_U = 49152;           // U fp32: four SW128 blocks of 32 columns, 64 rows
+constexpr uint32_t B_Y0 = 81920;          // Y0: two SW128 blocks of 64 columns, 64 rows
+constexpr uint32_t B_VP = 98304;          // V' hi (two 64-column blocks), then lo
+constexpr uint32_t B_S = 131072;          // S bf16, MN-major, two 64-column blocks of 128 rows
+constexpr uint32_t B_Y = 163840;          // y staging for the TMA store (two SW128 boxes)
+constexpr uint32_t B_BAR = 180224;
+enum BarB { BB_A6 = 0, BB_KH, BB_UY, BB_M6, BB_M7, kBarsB };
+constexpr uint32_t B_TMEMPTR = B_BAR + 8 * kBarsB;
+constexpr uint32_t B_FLAG = B_TMEMPTR + 4;
+constexpr uint32_t B_PEND = B_FLAG + 4;  // int[3]: parity of the A6 / Kh / UY load in flight, or -1
+constexpr uint32_t B_USED = B_PEND + 12;
+constexpr uint32_t kSmemB = B_USED + 1024;
+static_assert(kSmemB <= 232448, "scan kernel over the shared-memory limit");
+constexpr uint32_t TMB_D = 0, TMB_S = 128;  // TMEM columns
+
+// Byte offset of 16-byte chunk `chunk` of row `row` in a SW128 tile.
+__device__ __forceinline__ uint32_t sw128c(uint32_t row, uint32_t chunk) {
+    return row * 128u + ((chunk ^ (row & 7u)) << 4);
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, uint64_t *bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            ptx::smem_u32(dst)),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(ptx::smem_u32(bar))
+        : "memory");
+}
+
+template <typename TO>
+__global__ void __launch_bounds__(kThreadsB, 1)
+    scan_kernel(const __grid_constant__ CUtensorMap tm_a6, const __grid_constant__ CUtensorMap tm_u,
+                const __grid_constant__ CUtensorMap tm_y0, const __grid_constant__ CUtensorMap tm_kh,
+                const __grid_constant__ CUtensorMap tm_y, const CoreParams p, const SplitWs ws, int *status) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);  // stays a shared pointer
+    const uint32_t sb = ptx::smem_u32(base);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(base + B_BAR);
+    uint32_t *tmem_ptr = reinterpret_cast<uint32_t *>(base + B_TMEMPTR);
+    volatile int *flag = reinterpret_cast<volatile int *>(base + B_FLAG);
+    volatile int *pend = reinterpret_cast<volatile int *>(base + B_PEND);
+    constexpr bool kYTma = sizeof(TO) == 2;
+
+    const int tid = threadIdx.x, warp = tid >> 5, r = tid;
+    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    const int64_t bh = blockIdx.x, b = bh / p.heads, h = bh % p.heads, nch = ws.nch;
+    const bool leader = tid == 0;
+
+    if (leader) {
+        *flag = 0;
+        pend[0] = pend[1] = pend[2] = -1;
+        for (int i = 0; i < kBarsB; ++i) ptx::mbar_init(&bars[i], 1);
+        ptx::fence_mbar_init();
+        ptx::prefetch_tmap(&tm_a6);
+        ptx::prefetch_tmap(&tm_u);
+        ptx::prefetch_tmap(&tm_y0);
+        ptx::prefetch_tmap(&tm_kh);
+        if (kYTma) ptx::prefetch_tmap(&tm_y);
+    }
+    if (warp == 0) {
+        ptx::tmem_alloc(tmem_ptr, 256);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_ptr;
+
+    auto load_a6 = [&](int64_t c) {
+        pend[0] = (int)(c & 1);
+        ptx::mbar_arrive_expect_tx(&bars[BB_A6], 32768);
+        const int row = (int)((bh * nch + c) * 128);
+        tma_load_2d(base + B_A6, &tm_a6, &bars[BB_A6], 0, row);
+        tma_load_2d(base + B_A6 + 16384, &tm_a6, &bars[BB_A6], 64, row);
+    };
+    auto load_kh = [&](int64_t c) {
+        pend[1] = (int)(c & 1);
+        ptx::mbar_arrive_expect_tx(&bars[BB_KH], 16384);
+        const int row = (int)((bh * nch + c) * 64);
+        tma_load_2d(base + B_KH, &tm_kh, &bars[BB_KH], 0, row);
+        tma_load_2d(base + B_KH + 8192, &tm_kh, &bars[BB_KH], 64, row);
+    };
+    auto load_uy = [&](int64_t c) {
+        pend[2] = (int)(c & 1);
+        ptx::mbar_arrive_expect_tx(&bars[BB_UY], 49152);
+        const int row = (int)((bh * nch + c) * 64);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tma_load_2d(base + B_U + 8192 * j, &tm_u, &bars[BB_UY], 32 * j, row);
+        tma_load_2d(base + B_Y0, &tm_y0, &bars[BB_UY], 0, row);
+        tma_load_2d(base + B_Y0 + 8192, &tm_y0, &bars[BB_UY], 64, row);
+    };
+    auto role_wait = [&](int bar, uint32_t parity) {
+        const bool bad = !ptx::mbar_wait(&bars[bar], parity) || *flag != 0;
+        if (ptx::named_sync_or(1, kThreadsB, bad)) {
+            *flag = 1;
+            return false;
+        }
+        return true;
+    };
+
+    if (leader) {
+        load_a6(0);
+        load_kh(0);
+        load_uy(0);
+    }
+
+    // S0 -> TMEM (pre-scaled by chunk 0's decay) and its bf16 copy.
+    {
+        const float g0 = ws.gam[(bh * nch) * 128 + r];
+        const float *src = p.state_in + (bh * 128 + r) * 128;
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+            for (int q2 = 0; q2 < 2; ++q2) {
+                uint32_t v[32];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 f = *reinterpret_cast<const float4 *>(src + 64 * hh + 32 * q2 + 4 * q);
+                    v[4 * q] = __float_as_uint(f.x);
+                    v[4 * q + 1] = __float_as_uint(f.y);
+                    v[4 * q + 2] = __float_as_uint(f.z);
+                    v[4 * q + 3] = __float_as_uint(f.w);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float *f = reinterpret_cast<const float *>(v + 8 * q);
+                    ptx::st_shared_v4(sb + B_S + hh * 16384 + ptx::sw128(r, 32 * q2 + 8 * q), ptx::pack_bf16(f[0], f[1]),
+                                      ptx::pack_bf16(f[2], f[3]), ptx::pack_bf16(f[4], f[5]), ptx::pack_bf16(f[6], f[7]));
+                }
+#pragma unroll
+                for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * g0);
+                ptx::tmem_st32(tmem + lane_base + TMB_S + 64 * hh + 32 * q2, v);
+            }
+        }
+        ptx::tmem_wait_st();
+        ptx::fence_async_smem();
+        ptx::tc_fence_before();
+        ptx::named_sync(1, kThreadsB);
+    }
+
+    float gnext = (nch > 1) ? ws.gam[(bh * nch + 1) * 128 + r] : 1.f;
+    bool ok = true;
+    for (int64_t c = 0; c < nch && ok; ++c) {
+        const uint32_t par = (uint32_t)(c & 1);
+        const float gam_next = gnext;
+        if (c + 2 < nch) gnext = ws.gam[(bh * nch + c + 2) * 128 + r];
+
+        // ---- D = A6 S ----
+        if (leader) {
+            if (!ptx::mbar_wait(&bars[BB_A6], par)) {
+                *flag = 1;
+            } else {
+                pend[0] = -1;
+                ptx::tc_fence_after();
+                const uint32_t id = ptx::idesc_bf16(128, 128, 0, 1);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    ptx::umma_bf16(tmem + TMB_D, ptx::sdesc(sb + B_A6 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                                   ptx::sdesc(sb + B_S + kk * 2048, 16384, 1024), id, kk > 0);
+                ptx::umma_commit(&bars[BB_M6]);
+            }
+            if (kYTma) ptx::bulk_wait_all();  // the previous chunk's y tile has been read
+        }
+        if (!(ok = role_wait(BB_M6, par))) break;
+        if (leader && c + 1 < nch) load_a6(c + 1);
+
+        // ---- [V'; y] = D + [U; Y0]: V' hi + lo -> smem (MMA7's B), y -> HBM ----
+        if (!(ok = role_wait(BB_UY, par))) break;
+        if (leader) pend[2] = -1;
+        ptx::tc_fence_after();
+        {
+            const int64_t tok = c * tc::kL + (r - 64);
+            const bool write_y = r >= 64 && tok < p.seq;
+            TO *yrow = static_cast<TO *>(p.y) + ((b * p.seq + (write_y ? tok : 0)) * p.heads + h) * 128;
+#pragma unroll 1
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t vv[2][32];
+                ptx::tmem_ld32(tmem + lane_base + TMB_D + 64 * hh, vv[0]);
+                ptx::tmem_ld32(tmem + lane_base + TMB_D + 64 * hh + 32, vv[1]);
+                ptx::tmem_wait_ld();
+#pragma unroll
+                for (int q2 = 0; q2 < 2; ++q2) {
+                    const float *f = reinterpret_cast<const float *>(vv[q2]);
+                    if (r < 64) {
+                        const uint32_t ub = sb + B_U + 8192 * (2 * hh + q2);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const uint4 u0 = ptx::ld_shared_v4(ub + sw128c(r, 2 * q));
+                            const uint4 u1 = ptx::ld_shared_v4(ub + sw128c(r, 2 * q + 1));
+                            const float x[8] = {f[8 * q] + __uint_as_float(u0.x),     f[8 * q + 1] + __uint_as_float(u0.y),
+                                                f[8 * q + 2] + __uint_as_float(u0.z), f[8 * q + 3] + __uint_as_float(u0.w),
+                                                f[8 * q + 4] + __uint_as_float(u1.x), f[8 * q + 5] + __uint_as_float(u1.y),
+                                                f[8 * q + 6] + __uint_as_float(u1.z), f[8 * q + 7] + __uint_as_float(u1.w)};
+                            uint32_t hi[4], lo[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                hi[e] = ptx::pack_bf16(x[2 * e], x[2 * e + 1]);
+                                lo[e] = ptx::pack_bf16(x[2 * e] - ptx::bf16lo(hi[e]), x[2 * e + 1] - ptx::bf16hi(hi[e]));
+                            }
+                            const uint32_t off = hh * 8192 + ptx::sw128(r, 32 * q2 + 8 * q);
+                            ptx::st_shared_v4(sb + B_VP + off, hi[0], hi[1], hi[2], hi[3]);
+                            ptx::st_shared_v4(sb + B_VP + 16384 + off, lo[0], lo[1], lo[2], lo[3]);
+                        }
+                    } else {
+                        float yv[32];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const uint4 y0 = ptx::ld_shared_v4(sb + B_Y0 + hh * 8192 + ptx::sw128(r - 64, 32 * q2 + 8 * q));
+                            const uint32_t yw[4] = {y0.x, y0.y, y0.z, y0.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                yv[8 * q + 2 * e] = f[8 * q + 2 * e] + ptx::bf16lo(yw[e]);
+                                yv[8 * q + 2 * e + 1] = f[8 * q + 2 * e + 1] + ptx::bf16hi(yw[e]);
+                            }
+                        }
+                        if (kYTma) {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                ptx::st_shared_v4(sb + B_Y + hh * 8192 + ptx::sw128(r - 64, 32 * q2 + 8 * q),
+                                                  ptx::pack_bf16(yv[8 * q], yv[8 * q + 1]),
+                                                  ptx::pack_bf16(yv[8 * q + 2], yv[8 * q + 3]),
+                                                  ptx::pack_bf16(yv[8 * q + 4], yv[8 * q + 5]),
+                                                  ptx::pack_bf16(yv[8 * q + 6], yv[8 * q + 7]));
+                        } else if (write_y) {
+                            tc::store_row32(yrow + 64 * hh + 32 * q2, yv);
+                        }
+                    }
+                }
+            }
+        }
+        ptx::fence_async_smem();
+        ptx::tc_fence_before();
+        ptx::named_sync(1, kThreadsB);
+        if (leader) {
+            if (kYTma) {
+                ptx::tma_store_4d(&tm_y, sb + B_Y, 0, (int)h, (int)(c * tc::kL), (int)b);
+                ptx::tma_store_4d(&tm_y, sb + B_Y + 8192, 64, (int)h, (int)(c * tc::kL), (int)b);
+                ptx::bulk_commit();
+            }
+            if (c + 1 < nch) load_uy(c + 1);
+        }
+
+        // ---- S <- diag(gam) S + Kh^T (V'hi + V'lo); TMEM S already holds diag(gam) S ----
+        if (leader) {
+            if (!ptx::mbar_wait(&bars[BB_KH], par)) {
+                *flag = 1;
+            } else {
+                pend[1] = -1;
+                ptx::tc_fence_after();
+                const uint32_t id = ptx::idesc_bf16(128, 128, 1, 1);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    ptx::umma_bf16(tmem + TMB_S, ptx::sdesc(sb + B_KH + (kk & 3) * 2048, 8192, 1024),
+                                   ptx::sdesc(sb + B_VP + (kk >= 4 ? 16384 : 0) + (kk & 3) * 2048, 8192, 1024), id, 1);
+                ptx::umma_commit(&bars[BB_M7]);
+            }
+        }
+        if (!(ok = role_wait(BB_M7, par))) break;
+        if (leader && c + 1 < nch) load_kh(c + 1);
+
+        // ---- S -> bf16 operand, and the accumulator pre-scaled by the next chunk's decay ----
+        ptx::tc_fence_after();
+        if (c + 1 < nch) {
+#pragma unroll 1
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t vv[2][32];
+                ptx::tmem_ld32(tmem + lane_base + TMB_S + 64 * hh, vv[0]);
+                ptx::tmem_ld32(tmem + lane_base + TMB_S + 64 * hh + 32, vv[1]);
+                ptx::tmem_wait_ld();
+#pragma unroll
+                for (int q2 = 0; q2 < 2; ++q2) {
+                    uint32_t(&v)[32] = vv[q2];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float *f = reinterpret_cast<const float *>(v + 8 * q);
+                        ptx::st_shared_v4(sb + B_S + hh * 16384 + ptx::sw128(r, 32 * q2 + 8 * q), ptx::pack_bf16(f[0], f[1]),
+                                          ptx::pack_bf16(f[2], f[3]), ptx::pack_bf16(f[4], f[5]),
+                                          ptx::pack_bf16(f[6], f[7]));
+                    }
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * gam_next);
+                    ptx::tmem_st32(tmem + lane_base + TMB_S + 64 * hh + 32 * q2, v);
+                }
+            }
+            ptx::tmem_wait_st();
+            ptx::fence_async_smem();
+            ptx::tc_fence_before();
+            ptx::named_sync(1, kThreadsB);
+        } else {
+            float *dst = p.state_out + (bh * 128 + r) * 128;
+#pragma unroll 1
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t vv[2][32];
+                ptx::tmem_ld32(tmem + lane_base + TMB_S + 64 * hh, vv[0]);
+                ptx::tmem_ld32(tmem + lane_base + TMB_S + 64 * hh + 32, vv[1]);
+                ptx::tmem_wait_ld();
+#pragma unroll
+                for (int q2 = 0; q2 < 2; ++q2)
+                    tc::store_row32(dst + 64 * hh + 32 * q2, reinterpret_cast<const float *>(vv[q2]));
+            }
+        }
+    }
+
+    if (kYTma && leader) ptx::bulk_wait_all();
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (*flag) {
+        if (leader) {
+            atomicExch(status, kStatusTimeout);
+            // Let this CTA's own TMA loads land before its shared memory goes away.
+            if (pend[0] >= 0) ptx::mbar_wait(&bars[BB_A6], (uint32_t)pend[0]);
+            if (pend[1] >= 0) ptx::mbar_wait(&bars[BB_KH], (uint32_t)pend[1]);
+            if (pend[2] >= 0) ptx::mbar_wait(&bars[BB_UY], (uint32_t)pend[2]);
+        }
+        __syncthreads();
+    }
+    if (warp == 0) ptx::tmem_dealloc(tmem, 256);
+}
+
+}  // namespace split
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+// Whether the split kernels serve this request (given enough workspace): bf16 q/k/v, d = 128, one
+// micro-step per token, and a per-channel gate somewhere (or DC_FLAG_FORCE_SPLIT = 0x4).
+inline bool split_applies(const CoreParams &p, int32_t in_dtype, uint32_t flags) {
+    if (flags & 0x3u) return false;  // DC_FLAG_FORCE_SIMT, DC_FLAG_RECURRENT
+    if (in_dtype != 1) return false;
+    if (p.dk != 128 || p.dv != 128 || p.u != 1) return false;
+    if (!((flags & 0x4u) || p.ew != 1 || p.ww != 1 || p.gw > 1)) return false;
+    if (!aligned16(p.q) || !aligned16(p.k) || !aligned16(p.v) || !aligned16(p.y) || !aligned16(p.state_in) ||
+        !aligned16(p.state_out))
+        return false;
+    const int64_t bhn = p.batch * p.heads;
+    const int64_t nch = (p.seq + tc::kL - 1) / tc::kL;
+    if (bhn > 65535 || nch > 0x7fffffff || bhn * nch * 128 > 0x7fffffff) return false;
+    return true;
+}
+
+inline uint64_t split_workspace_bytes(const CoreParams &p) {
+    const int64_t nch = (p.seq + tc::kL - 1) / tc::kL;
+    return (uint64_t)(p.batch * p.heads * nch) * split::kWsBytesPerChunk;
+}
+
+inline split::SplitWs split_carve(const CoreParams &p, void *ws) {
+    const int64_t nch = (p.seq + tc::kL - 1) / tc::kL;
+    const uint64_t n = (uint64_t)(p.batch * p.heads * nch);
+    uint8_t *w = static_cast<uint8_t *>(ws);
+    split::SplitWs s;
+    s.a6 = reinterpret_cast<__nv_bfloat16 *>(w);
+    s.u = reinterpret_cast<float *>(w + n * 32768);
+    s.y0 = reinterpret_cast<__nv_bfloat16 *>(w + n * 65536);
+    s.kh = reinterpret_cast<__nv_bfloat16 *>(w + n * 81920);
+    s.gam = reinterpret_cast<float *>(w + n * 98304);
+    s.nch = nch;
+    return s;
+}
+
+// A 2-D [rows][inner] tensor map with a (box_inner, box_rows) SW128 box.
+inline bool encode_2d(CUtensorMap *m, CUtensorMapDataType dt, uint32_t esize, const void *ptr, uint64_t inner,
+                      uint64_t rows, uint32_t box_inner, uint32_t box_rows) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)(inner * esize)};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(m, dt, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename TG, typename TO>
+int launch_split_typed(const CoreParams &p, void *workspace, cudaStream_t stream) {
+    const split::SplitWs ws = split_carve(p, workspace);
+    const int64_t bhn = p.batch * p.heads;
+    const uint64_t n = (uint64_t)(bhn * ws.nch);
+    CUtensorMap ma6, mu, my0, mkh, my, mq, mk, mv;
+    if (!encode_rows(&mq, p.q, p.heads, p.seq, p.batch) || !encode_rows(&mk, p.k, p.heads, p.seq, p.batch) ||
+        !encode_rows(&mv, p.v, p.heads, p.seq, p.batch) || !encode_2d(&ma6, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws.a6, 128, n * 128, 64, 128) ||
+        !encode_2d(&mu, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws.u, 128, n * 64, 32, 64) ||
+        !encode_2d(&my0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws.y0, 128, n * 64, 64, 64) ||
+        !encode_2d(&mkh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws.kh, 128, n * 64, 64, 64) ||
+        (sizeof(TO) == 2 ? !encode_rows(&my, p.y, p.heads, p.seq, p.batch) : (my = ma6, false))) {
+        g_tc_error = (int)cudaErrorInvalidValue;
+        return 6;  // DC_ECUDA
+    }
+    int *status = device_status_ptr();
+    if (!status) {
+        g_tc_error = (int)cudaErrorInvalidSymbol;
+        return 6;
+    }
+    auto ka = split::prep_kernel<TG>;
+    auto kb = split::scan_kernel<TO>;
+    cudaError_t e = cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)split::kSmemA);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)split::kSmemB);
+    if (e == cudaSuccess) {
+        ka<<<dim3((unsigned)ws.nch, (unsigned)bhn), split::kThreadsA, split::kSmemA, stream>>>(mq, mk, mv, p, ws,
+                                                                                                 status);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) {
+        kb<<<(unsigned)bhn, split::kThreadsB, split::kSmemB, stream>>>(ma6, mu, my0, mkh, my, p, ws, status);
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) {
+        g_tc_error = (int)e;
+        return 6;
+    }
+    return 0;
+}
+
+inline int launch_chunk_split(const CoreParams &p, int32_t gate_dtype, int32_t out_dtype, void *workspace,
+                              cudaStream_t stream) {
+    switch (gate_dtype * 2 + out_dtype) {
+        case 0: return launch_split_typed<float, float>(p, workspace, stream);
+        case 1: return launch_split_typed<float, __nv_bfloat16>(p, workspace, stream);
+        case 2: return launch_split_typed<__nv_bfloat16, float>(p, workspace, stream);
+        case 3: return launch_split_typed<__nv_bfloat16, __nv_bfloat16>(p, workspace, stream);
+    }
+    return 3;  // DC_EUNSUPPORTED_DTYPE
+}
+
+}  // namespace dc

@@ -82,9 +82,6 @@ constexpr uint32_t OFF_S = OFF_AW + 16384;              // S bf16, MN-major, two
 constexpr uint32_t OFF_AQK = OFF_S + 32768;             // Aqk bf16 64x64 K-major
 constexpr uint32_t OFF_AF = OFF_AQK + 8192;             // Akk fp32 [64][68]; then [Tb; Pb] lo
 constexpr uint32_t OFF_TF = OFF_AF + 64 * kAP * 4;      // T fp32 [64][68];   then [Tw; Pw] lo
-constexpr int kEP = 20;                                 // row pitch (floats) of the E blocks
-constexpr uint32_t OFF_E = OFF_AU;                      // E_pq = T_pp A_pq: six blocks [16][20] fp32, during
-                                                        // the solve, while [Tb; Pb] hi is not live
 constexpr uint32_t OFF_Y = OFF_TF + 64 * kAP * 4;       // y bf16 64x128 (two SW128 64x64 boxes) for the TMA store
 constexpr uint32_t OFF_GATE = OFF_Y + 16384;            // per stage: e[64], w[64], g[64]
 constexpr uint32_t OFF_G = OFF_GATE + 2 * 3 * 64 * 4;   // per stage: G[64], gam[64]
@@ -97,7 +94,6 @@ constexpr uint32_t kSmemUsed = OFF_PEND + 8;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;       // alignment slack
 static_assert(OFF_AF % 1024 == 0 && OFF_TF % 1024 == 0 && OFF_AQK % 1024 == 0 && OFF_S % 1024 == 0,
               "operand tiles need 1 KB alignment");
-static_assert(6 * 16 * kEP * 4 <= 16384, "E blocks overflow the [Tb; Pb] hi region");
 static_assert(OFF_Y % 1024 == 0, "SW128 staging tile must be 1024-byte aligned");
 static_assert(kSmemBytes <= 232448, "over the 227 KB per-CTA shared-memory limit");
 
@@ -168,8 +164,9 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16 *dst, const float *f) 
 #define DC_TC_MARK(id)
 #endif
 
-// Index of block (p, q), p > q, among the six 16x16 blocks below the diagonal.
-__host__ __device__ constexpr int eblk(int p, int q) { return p * (p - 1) / 2 + q; }
+// E_pq (p > q) is kept in the mirrored block (q, p) of the Akk buffer: the blocks above the diagonal
+// hold values that nothing reads once the solve has started.
+__device__ __forceinline__ float *eblock(float *Af, int p, int q) { return Af + (16 * q) * kAP + 16 * p; }
 
 // D(16x8) += A(16 x K) B(K x 8) for fp32 operands in shared memory (row
 // pitches lda, ldb), on the warp's tensor cores in three tf32 passes
@@ -202,7 +199,8 @@ __device__ __forceinline__ void store_frag(float *D, int ld, const float (&d)[4]
 // T = (I + A)^-1 for the 64x64 strictly lower A in Af (row pitch kAP), into Tf
 // (same pitch; blocks above the diagonal are left untouched, the upper
 // triangles of the diagonal blocks are written as zeros).  Run by the 256
-// threads of the operand role; Es is scratch for six 16x20 fp32 blocks.
+// threads of the operand role; only Af's strictly lower part is read, and the
+// E blocks overwrite its upper blocks.
 //  (1) diagonal blocks T_pp = (I + A_pp)^-1, one per warp, a lane substituting
 //      down one column;
 //  (2) E_pq = T_pp A_pq for the six blocks below the diagonal;
@@ -210,7 +208,7 @@ __device__ __forceinline__ void store_frag(float *D, int ld, const float (&d)[4]
 // (2) and (3) run on the warps' tensor cores in three tf32 passes (fp32-class).
 // mark_diag / mark_e are called after (1) and (2) (phase-timing hooks).
 template <typename M1, typename M2>
-__device__ __forceinline__ void solve_unit_lower(const float *Af, float *Tf, float *Es, int warp, int lane,
+__device__ __forceinline__ void solve_unit_lower(float *Af, float *Tf, int warp, int lane,
                                                  M1 &&mark_diag, M2 &&mark_e) {
     if (warp < 4 && lane < 16) {
         const int pb = warp, j = lane;
@@ -235,12 +233,12 @@ __device__ __forceinline__ void solve_unit_lower(const float *Af, float *Tf, flo
     ptx::named_sync(NB_PAR, kParThreads);
     mark_diag();
     if (warp < 6) {  // six independent blocks, one per warp
-        const int pr = warp < 1 ? 1 : (warp < 3 ? 2 : 3), q = warp - eblk(pr, 0);
+        const int pr = warp < 1 ? 1 : (warp < 3 ? 2 : 3), q = warp - pr * (pr - 1) / 2;
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
             float d[4] = {0.f, 0.f, 0.f, 0.f};
             mma_rows16(d, Tf + (16 * pr) * kAP + 16 * pr, kAP, Af + (16 * pr) * kAP + 16 * q + 8 * nt, kAP, 16);
-            store_frag(Es + (eblk(pr, q) * 16) * kEP + 8 * nt, kEP, d, 1.f);
+            store_frag(eblock(Af, pr, q) + 8 * nt, kAP, d, 1.f);
         }
     }
     ptx::named_sync(NB_PAR, kParThreads);
@@ -252,7 +250,7 @@ __device__ __forceinline__ void solve_unit_lower(const float *Af, float *Tf, flo
             float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int rr = q; rr < pr; ++rr)
-                mma_rows16(d, Es + (eblk(pr, rr) * 16) * kEP, kEP, Tf + (16 * rr) * kAP + 16 * q + 8 * nt, kAP, 16);
+                mma_rows16(d, eblock(Af, pr, rr), kAP, Tf + (16 * rr) * kAP + 16 * q + 8 * nt, kAP, 16);
             store_frag(Tf + (16 * pr) * kAP + 16 * q + 8 * nt, kAP, d, -1.f);
         }
         ptx::named_sync(NB_PAR, kParThreads);
@@ -265,11 +263,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_y,
                     const CoreParams p, int *status) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *base = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);  // stays a shared pointer
     const uint32_t sb = ptx::smem_u32(base);
     float *Af = reinterpret_cast<float *>(base + OFF_AF);
     float *Tf = reinterpret_cast<float *>(base + OFF_TF);
-    float *Es = reinterpret_cast<float *>(base + OFF_E);
     float *gates = reinterpret_cast<float *>(base + OFF_GATE);  // [stage][e | w | g][64]
     float *Gs = reinterpret_cast<float *>(base + OFF_G);        // [stage][G | gam][64]
     uint64_t *bars = reinterpret_cast<uint64_t *>(base + OFF_BAR);
@@ -440,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             DC_TC_MARK(3);
 
             // ---- T = (I + Akk)^-1 in 16x16 blocks ----
-            solve_unit_lower(Af, Tf, Es, warp, lane, [&] { DC_TC_MARK(14); }, [&] { DC_TC_MARK(15); });
+            solve_unit_lower(Af, Tf, warp, lane, [&] { DC_TC_MARK(14); }, [&] { DC_TC_MARK(15); });
             DC_TC_MARK(4);
 
             // ---- Tb = T diag(w), Tw = T diag(e gam) as bf16 hi + lo (blocks above the diagonal masked) ----

@@ -136,11 +136,28 @@ struct DeltaInput {
         require(state_bhkv != nullptr, "state is required");
     }
 
+    // Bytes of device workspace run() can use for `path` (0: none needed).  With
+    // per-channel gates (GDN-2) a workspace of this size lets the tensor cores
+    // take the prefill; without one it runs on the CUDA cores.
+    uint64_t workspace_size(const DeltaPath &path, DType y_dtype) const {
+        const dc_chunk_args a = args(path, nullptr, y_dtype, nullptr, nullptr, 0);
+        return dc_chunk_workspace_size(&a);
+    }
+
     // Run the selected algorithm (path.rs:215-231) into caller-owned outputs:
     // y [batch, seq, heads, dv] of y_dtype, final state [batch, heads, dk, dv]
-    // (final_state may equal state_bhkv: an in-place update).
-    void run(const DeltaPath &path, void *y, DType y_dtype, float *final_state, dc_stream_t stream = nullptr) const {
+    // (final_state may equal state_bhkv: an in-place update), with an optional
+    // caller-owned workspace (see workspace_size).
+    void run(const DeltaPath &path, void *y, DType y_dtype, float *final_state, dc_stream_t stream = nullptr,
+             void *workspace = nullptr, uint64_t workspace_bytes = 0) const {
         sanity();
+        const dc_chunk_args a = args(path, y, y_dtype, final_state, workspace, workspace_bytes);
+        check_status(dc_chunk_fwd(&a, stream), "DeltaInput::run");
+    }
+
+  private:
+    dc_chunk_args args(const DeltaPath &path, void *y, DType y_dtype, float *final_state, void *workspace,
+                       uint64_t workspace_bytes) const {
         const Dims d = dims();
         dc_chunk_args a{};
         a.batch = d.batch;
@@ -169,7 +186,9 @@ struct DeltaInput {
         a.state_in = state_bhkv;
         a.y = y;
         a.state_out = final_state;
-        check_status(dc_chunk_fwd(&a, stream), "DeltaInput::run");
+        a.workspace = workspace;
+        a.workspace_bytes = workspace_bytes;
+        return a;
     }
 };
 

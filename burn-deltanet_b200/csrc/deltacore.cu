@@ -13,6 +13,7 @@
 
 #include "../../include/deltacore.h"
 #include "chunk_simt.cuh"
+#include "chunk_split.cuh"
 #include "chunk_tc.cuh"
 #include "common.cuh"
 #include "step.cuh"
@@ -165,6 +166,7 @@ struct SimtLauncher {
 int validate_chunk(const dc_chunk_args *a) {
     if (!a) return DC_EINVAL_ARG;
     if (a->chunk_len < 1) return DC_EINVAL_ARG;
+    if (a->workspace && !aligned(a->workspace, 16)) return DC_EINVAL_ARG;
     return validate_common(a->batch, a->seq, a->heads, a->dk, a->dv, a->n_householder, a->erase_w, a->write_w,
                            a->g_w, a->in_dtype, a->gate_dtype, a->out_dtype, a->scale, a->q, a->k, a->v,
                            a->erase, a->write, a->g, a->state_in, a->y, a->state_out);
@@ -181,7 +183,7 @@ int validate_step(const dc_step_args *a) {
 
 extern "C" {
 
-int dc_version(void) { return 100; }
+int dc_version(void) { return 200; }
 
 const char *dc_status_string(int status) {
     switch (status) {
@@ -193,6 +195,7 @@ const char *dc_status_string(int status) {
         case DC_EUNSUPPORTED: return "unsupported size (dk > 256 or n_householder > 8)";
         case DC_ECUDA: return "CUDA error";
         case DC_EDEVICE: return "current device is not an sm_100 GPU";
+        case DC_EWORKSPACE: return "workspace smaller than dc_chunk_workspace_size";
     }
     return "unknown status";
 }
@@ -212,20 +215,48 @@ int dc_device_status(int reset) {
     return value;
 }
 
+}  // extern "C"
+
+namespace {
+
+dc::CoreParams chunk_params(const dc_chunk_args *a) {
+    return make_params(a->batch, a->seq, a->heads, a->dk, a->dv, a->n_householder, a->erase_w, a->write_w, a->g_w,
+                       a->scale, a->q, a->k, a->v, a->erase, a->write, a->g, a->state_in, a->y, a->state_out);
+}
+
+// The chunk kernel a validated call takes: 2 split (workspace), 1 fused tensor-core, 0 CUDA-core,
+// or -DC_EWORKSPACE when the split path is required but the workspace is short.
+int chunk_choice(const dc_chunk_args *a, const dc::CoreParams &p) {
+    if (a->flags & DC_FLAG_RECURRENT) return 0;
+    if (dc::split_applies(p, a->in_dtype, a->flags)) {
+        if (a->workspace && a->workspace_bytes >= dc::split_workspace_bytes(p)) return 2;
+        if (a->workspace || (a->flags & DC_FLAG_FORCE_SPLIT)) return -DC_EWORKSPACE;
+    }
+    return dc::tc_applies(p, a->in_dtype, a->flags) ? 1 : 0;
+}
+
+}  // namespace
+
+extern "C" {
+
 int dc_chunk_kernel_choice(const dc_chunk_args *a) {
     const int st = validate_chunk(a);
     if (st != DC_OK) return -st;
-    const dc::CoreParams p = make_params(a->batch, a->seq, a->heads, a->dk, a->dv, a->n_householder, a->erase_w,
-                                         a->write_w, a->g_w, a->scale, a->q, a->k, a->v, a->erase, a->write, a->g,
-                                         a->state_in, a->y, a->state_out);
-    return dc::tc_applies(p, a->in_dtype, a->flags) ? 1 : 0;
+    return chunk_choice(a, chunk_params(a));
+}
+
+uint64_t dc_chunk_workspace_size(const dc_chunk_args *a) {
+    if (validate_chunk(a) != DC_OK) return 0;
+    const dc::CoreParams p = chunk_params(a);
+    return dc::split_applies(p, a->in_dtype, a->flags) ? dc::split_workspace_bytes(p) : 0;
 }
 
 int dc_chunk_launches(const dc_chunk_args *a) {
     const int st = validate_chunk(a);
     if (st != DC_OK) return -st;
     if (a->batch == 0 || a->heads == 0) return 0;
-    return (a->flags & DC_FLAG_RECURRENT) ? (int)a->seq : 1;
+    if (a->flags & DC_FLAG_RECURRENT) return (int)a->seq;
+    return chunk_choice(a, chunk_params(a)) == 2 ? 2 : 1;
 }
 
 // DeltaPath::Recurrent: the fused tick walks the sequence in place, one launch
@@ -263,7 +294,14 @@ int dc_chunk_fwd(const dc_chunk_args *a, dc_stream_t stream) {
                                          a->state_in, a->y, a->state_out);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     if (a->flags & DC_FLAG_RECURRENT) return run_recurrent(a, s);
-    if (dc::tc_applies(p, a->in_dtype, a->flags)) {
+    const int choice = chunk_choice(a, p);
+    if (choice < 0) return -choice;
+    if (choice == 2) {
+        st = dc::launch_chunk_split(p, a->gate_dtype, a->out_dtype, a->workspace, s);
+        if (st == DC_ECUDA) g_last_cuda_error = dc::tc_last_error();
+        return st;
+    }
+    if (choice == 1) {
         st = dc::launch_chunk_tc(p, a->gate_dtype, a->out_dtype, s);
         if (st == DC_ECUDA) g_last_cuda_error = dc::tc_last_error();
         return st;

@@ -183,6 +183,33 @@ __device__ __forceinline__ void mma_tf32_16x8x8(float (&d)[4], const uint32_t (&
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
+// Warp-level D(16x8) += A(16x16) B(16x8) on bf16 operands, fp32 accumulate.
+// a: ldsm_x4 of the 16x16 A tile (row-major); b: ldsm_x2 of B stored as
+// [n][k] (8 rows of 16 k); d as for mma_tf32_16x8x8.
+__device__ __forceinline__ void mma_bf16_16x8x16(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// Four / two 8x8 b16 matrices from shared memory; lane l supplies the row
+// address of matrix l / 8 (lanes beyond the matrix count must still hold a
+// valid shared address).
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t (&r)[2]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];"
+                 : "=r"(r[0]), "=r"(r[1])
+                 : "r"(addr)
+                 : "memory");
+}
+
 // x = big + small with big exact in tf32 (the upper 19 bits) and small the
 // exact fp32 remainder; products of big/small pairs recover ~fp32 accuracy.
 __device__ __forceinline__ void split_tf32(float x, uint32_t &big, uint32_t &small) {

@@ -31,8 +31,9 @@
  * holds the last micro-step's readout (src/delta_product/delta_product.rs:178-228).
  * With u == 1 this is exactly the reference op's argument list.
  *
- * Ownership and threading: the caller owns every buffer; nothing is
- * allocated, nothing is freed.  The call validates on the host, enqueues the
+ * Ownership and threading: the caller owns every buffer, the workspace
+ * included (see dc_chunk_workspace_size); nothing is allocated, nothing is
+ * freed.  The call validates on the host, enqueues the
  * kernel(s) on `stream` and returns; it is asynchronous like every Burn
  * device op.  state_out may alias state_in (in-place update); no other
  * output may alias an input.  Calls on different streams are independent.
@@ -70,7 +71,8 @@ enum dc_status {
                                   non-finite scale, misaligned pointer, aliasing outputs */
     DC_EUNSUPPORTED = 5,       /* beyond this build's limits: dk > 256 or n_householder > 8 */
     DC_ECUDA = 6,              /* a CUDA runtime call failed: see dc_last_cuda_error() */
-    DC_EDEVICE = 7             /* the current device is not an sm_100 (B200-class) GPU */
+    DC_EDEVICE = 7,            /* the current device is not an sm_100 (B200-class) GPU */
+    DC_EWORKSPACE = 8          /* a workspace was passed but is smaller than dc_chunk_workspace_size */
 };
 
 enum dc_dtype {
@@ -82,6 +84,7 @@ enum dc_dtype {
 #define DC_FLAG_FORCE_SIMT 0x1u /* run the CUDA-core chunk kernel even where the tensor-core one applies */
 #define DC_FLAG_RECURRENT 0x2u  /* DeltaPath::Recurrent: walk the sequence token by token with the fused
                                    decode tick (one launch per token, state updated in state_out) */
+#define DC_FLAG_FORCE_SPLIT 0x4u /* take the two-kernel (workspace) tensor-core path even for per-head gates */
 
 /*
  * Chunkwise prefill.  Mirrors
@@ -92,6 +95,12 @@ enum dc_dtype {
  * `scale` is already resolved (1/sqrt(dk) is the reference default, path.rs:161-165).
  * `chunk_len` is validated (>= 1) and, as in the reference, does not change the
  * result (src/delta/tests.rs:340-363): the kernels pick their own tile length.
+ *
+ * Per-channel gates (erase_w == dk, write_w == dv or g_w == dk, i.e. GDN-2) run
+ * on the tensor cores as two kernels that pass per-chunk operands through a
+ * caller-owned device workspace of dc_chunk_workspace_size(args) bytes
+ * (16-byte aligned).  With workspace == NULL such a call runs the CUDA-core
+ * kernel instead; a non-NULL workspace smaller than required is DC_EWORKSPACE.
  */
 typedef struct dc_chunk_args {
     int64_t batch, seq, heads, dk, dv;
@@ -107,6 +116,8 @@ typedef struct dc_chunk_args {
     const float *state_in;
     void *y;
     float *state_out;
+    void *workspace;          /* device scratch for the per-channel-gate path, or NULL */
+    uint64_t workspace_bytes; /* its size */
 } dc_chunk_args;
 
 DC_API int dc_chunk_fwd(const dc_chunk_args *args, dc_stream_t stream);
@@ -147,8 +158,15 @@ DC_API int dc_last_cuda_error(void);
 DC_API int dc_device_status(int reset);
 
 /* Which chunk kernel dc_chunk_fwd would launch for `args`: 1 = tensor-core (tcgen05),
- * 0 = CUDA-core; negative = the dc_status the call would return. Pure host logic. */
+ * 2 = the two-kernel tensor-core path over the workspace, 0 = CUDA-core; negative =
+ * the dc_status the call would return.  Pure host logic. */
 DC_API int dc_chunk_kernel_choice(const dc_chunk_args *args);
+
+/* Bytes of workspace the two-kernel path needs for `args` (0 when the call takes a
+ * path that needs none).  Replaces nothing in the reference, whose chunk path
+ * materialises its intermediates as backend tensors (forward.rs:235-266).  Pure
+ * host logic; about 97 KB per (batch, head, 64-token chunk). */
+DC_API uint64_t dc_chunk_workspace_size(const dc_chunk_args *args);
 
 /* Number of kernels dc_chunk_fwd enqueues for `args` (for launch accounting); dc_step enqueues one. */
 DC_API int dc_chunk_launches(const dc_chunk_args *args);

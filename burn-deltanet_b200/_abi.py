@@ -21,6 +21,8 @@ DC_EUNSUPPORTED = 5
 DC_ECUDA = 6
 DC_EDEVICE = 7
 DC_EWORKSPACE = 8
+DC_ESCRATCH = 9
+DC_NOALLOC_SCRATCH_BYTES = 64 << 20
 
 # enum dc_dtype
 DC_F32 = 0
@@ -33,6 +35,7 @@ DC_FLAG_FORCE_SPLIT = 0x4
 EXPORTS = (
     "dc_chunk_fwd", "dc_step", "dc_status_string", "dc_last_cuda_error", "dc_device_status",
     "dc_chunk_kernel_choice", "dc_chunk_launches", "dc_version", "dc_chunk_workspace_size",
+    "dc_chunk_fwd_noalloc",
 )
 
 
@@ -98,6 +101,8 @@ def lib() -> ctypes.CDLL:
         L.dc_version.restype = ctypes.c_int
         L.dc_chunk_workspace_size.argtypes = [ctypes.POINTER(ChunkArgs)]
         L.dc_chunk_workspace_size.restype = ctypes.c_uint64
+        L.dc_chunk_fwd_noalloc.argtypes = [ctypes.POINTER(ChunkArgs), ctypes.c_void_p]
+        L.dc_chunk_fwd_noalloc.restype = ctypes.c_int
         _lib = L
     return _lib
 

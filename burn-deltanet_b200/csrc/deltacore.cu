@@ -9,6 +9,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include <cuda_runtime.h>
 
 #include "../../include/deltacore.h"
@@ -196,6 +198,7 @@ const char *dc_status_string(int status) {
         case DC_ECUDA: return "CUDA error";
         case DC_EDEVICE: return "current device is not an sm_100 GPU";
         case DC_EWORKSPACE: return "workspace smaller than dc_chunk_workspace_size";
+        case DC_ESCRATCH: return "request needs more scratch than the no-allocation entry point holds";
     }
     return "unknown status";
 }
@@ -307,6 +310,61 @@ int dc_chunk_fwd(const dc_chunk_args *a, dc_stream_t stream) {
         return st;
     }
     return dispatch_types<SimtLauncher>(a->in_dtype, a->gate_dtype, a->out_dtype, p, s);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// dc_chunk_fwd_noalloc: the two-kernel path over a fixed device array, for
+// callers that cannot allocate device memory (an engine whose memory belongs
+// to its own pool and hands an FFI call no raw scratch; a serving loop where
+// a cudaMalloc, which may synchronise the device, is not allowed).
+// ---------------------------------------------------------------------------
+namespace {
+
+// The scratch: every GPU that loads this library holds it until exit.  All
+// calls share it; nothing in it needs to start at zero (the prep kernel
+// writes every element the scan kernel reads).
+static __device__ __align__(256) uint8_t g_noalloc_scratch[DC_NOALLOC_SCRATCH_BYTES];
+
+// In host code g_noalloc_scratch names a host-side stand-in, not device memory:
+// its device address is looked up once per device, with that device current.
+void *noalloc_scratch(int dev, int *status) {
+    static std::atomic<void *> addr[64];
+    if (dev < 0 || dev >= 64) {
+        *status = DC_EUNSUPPORTED;
+        return nullptr;
+    }
+    void *ptr = addr[dev].load(std::memory_order_acquire);
+    if (ptr) return ptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr) {
+        *status = cuda_fail(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+        return nullptr;
+    }
+    addr[dev].store(ptr, std::memory_order_release);
+    return ptr;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dc_chunk_fwd_noalloc(const dc_chunk_args *a, dc_stream_t stream) {
+    int st = validate_chunk(a);
+    if (st != DC_OK || a->batch == 0 || a->heads == 0) return st;
+    if (a->flags & (DC_FLAG_FORCE_SIMT | DC_FLAG_RECURRENT)) return DC_EINVAL_ARG;
+    int dev = 0;
+    st = check_device(&dev);
+    if (st != DC_OK) return st;
+    const dc::CoreParams p = chunk_params(a);
+    if (!dc::split_applies(p, a->in_dtype, DC_FLAG_FORCE_SPLIT)) return DC_EUNSUPPORTED;
+    if (dc::split_workspace_bytes(p) > DC_NOALLOC_SCRATCH_BYTES) return DC_ESCRATCH;
+    void *scratch = noalloc_scratch(dev, &st);
+    if (!scratch) return st;
+    st = dc::launch_chunk_split(p, a->gate_dtype, a->out_dtype, scratch, reinterpret_cast<cudaStream_t>(stream));
+    if (st == DC_ECUDA) g_last_cuda_error = dc::tc_last_error();
+    return st;
 }
 
 int dc_step(const dc_step_args *a, dc_stream_t stream) {

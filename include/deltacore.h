@@ -72,7 +72,8 @@ enum dc_status {
     DC_EUNSUPPORTED = 5,       /* beyond this build's limits: dk > 256 or n_householder > 8 */
     DC_ECUDA = 6,              /* a CUDA runtime call failed: see dc_last_cuda_error() */
     DC_EDEVICE = 7,            /* the current device is not an sm_100 (B200-class) GPU */
-    DC_EWORKSPACE = 8          /* a workspace was passed but is smaller than dc_chunk_workspace_size */
+    DC_EWORKSPACE = 8,         /* a workspace was passed but is smaller than dc_chunk_workspace_size */
+    DC_ESCRATCH = 9            /* dc_chunk_fwd_noalloc: the request needs more than DC_NOALLOC_SCRATCH_BYTES */
 };
 
 enum dc_dtype {
@@ -144,6 +145,37 @@ typedef struct dc_step_args {
 } dc_step_args;
 
 DC_API int dc_step(const dc_step_args *args, dc_stream_t stream);
+
+/*
+ * dc_chunk_fwd without any allocation: the two-kernel tensor-core path with its
+ * per-chunk workspace in a fixed device array inside this library.  It has no
+ * counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory: an engine whose device
+ * memory belongs to its own pool allocator and that hands an FFI call tensors
+ * but no raw scratch buffer, or a latency-critical serving loop in which a
+ * cudaMalloc (which may synchronise the device) is not allowed.  The caller
+ * still passes every input and output; args->workspace is ignored.
+ *
+ * Serves requests the two-kernel path takes (bf16 q/k/v, dk = dv = 128,
+ * n_householder = 1, 16-byte-aligned pointers; per-head gates included) that
+ * need at most DC_NOALLOC_SCRATCH_BYTES of workspace (dc_chunk_workspace_size
+ * with DC_FLAG_FORCE_SPLIT; about 97 KB per (batch, head, 64-token chunk),
+ * e.g. one sequence of 2688 tokens over 16 heads).  Larger requests return
+ * DC_ESCRATCH and others the two-kernel path does not take DC_EUNSUPPORTED,
+ * before anything is enqueued; DC_FLAG_FORCE_SIMT / DC_FLAG_RECURRENT are
+ * DC_EINVAL_ARG.
+ *
+ * Every GPU that loads the library holds the array until the process exits.
+ * The first call on a device looks up the array's device address (with that
+ * device current) and keeps it; make that first call before any stream
+ * capture.  All calls share the one array, which keeps the last call's
+ * contents (nothing in it needs to start at zero), so calls whose work
+ * overlaps on the GPU (different streams, or different host threads) race:
+ * serialise them.
+ */
+#define DC_NOALLOC_SCRATCH_BYTES (64ull << 20)
+DC_API int dc_chunk_fwd_noalloc(const dc_chunk_args *args, dc_stream_t stream);
 
 /* Human-readable name of a dc_status. */
 DC_API const char *dc_status_string(int status);

@@ -170,9 +170,11 @@ __device__ __forceinline__ float *eblock(float *Af, int p, int q) { return Af + 
 
 // D(16x8) += A(16 x K) B(K x 8) for fp32 operands in shared memory (row
 // pitches lda, ldb), on the warp's tensor cores in three tf32 passes
-// (big*big + big*small + small*big: ~2^-20 relative, fp32-class).
+// (big*big + big*small + small*big: ~2^-20 relative, fp32-class), each pass
+// in its own accumulator so the three dependency chains overlap.
 __device__ __forceinline__ void mma_rows16(float (&d)[4], const float *A, int lda, const float *B, int ldb, int K) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    float ds[4] = {0.f, 0.f, 0.f, 0.f}, dt[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int k0 = 0; k0 < K; k0 += 8) {
         const float av[4] = {A[g * lda + k0 + t], A[(g + 8) * lda + k0 + t], A[g * lda + k0 + t + 4],
@@ -183,10 +185,12 @@ __device__ __forceinline__ void mma_rows16(float (&d)[4], const float *A, int ld
         for (int e = 0; e < 4; ++e) ptx::split_tf32(av[e], ab[e], as[e]);
 #pragma unroll
         for (int e = 0; e < 2; ++e) ptx::split_tf32(bv[e], bb[e], bs[e]);
-        ptx::mma_tf32_16x8x8(d, as, bb);
-        ptx::mma_tf32_16x8x8(d, ab, bs);
+        ptx::mma_tf32_16x8x8(ds, as, bb);
+        ptx::mma_tf32_16x8x8(dt, ab, bs);
         ptx::mma_tf32_16x8x8(d, ab, bb);
     }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) d[e] += ds[e] + dt[e];
 }
 
 // Store a D fragment (16x8) to shared memory, scaled.

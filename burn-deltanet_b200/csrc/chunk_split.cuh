@@ -69,39 +69,52 @@ struct SplitWs {
 constexpr uint64_t kWsBytesPerChunk = 32768ull + 32768ull + 16384ull + 16384ull + 512ull;
 
 // ---------------------------------------------------------------- prep kernel
+// Two CTAs per SM (the kernel is latency-bound per chunk; a second CTA hides it), so shared memory is
+// shared between phases (P1 scan, P2 q.k diagonal, P3 bisection, P4 solve, P5 T hi/lo, P6 P = Aqk T,
+// P7 P hi/lo, P8 [T; P] [v w | b k e^G], P9 workspace stores).  Two S-independent intermediates park in
+// the chunk's own workspace slots until their shared memory frees up, and come back by TMA:
+// [v w | b k e^G] in the A6 slot (rows 0-63 | 64-127) and s q e^G in the Y0 slot.
 constexpr int kThreadsA = 256;
-constexpr uint32_t A_RKK = 0;                           // level operands, bf16 [32][kOP] each
-constexpr uint32_t A_RQK = A_RKK + 32 * kOP * 2;
-constexpr uint32_t A_CC = A_RQK + 32 * kOP * 2;
-constexpr uint32_t A_AF = 26624;                        // Akk fp32 [64][kAP] (E blocks in its upper blocks)
-constexpr uint32_t A_TF = A_AF + 64 * kAP * 4;          // T fp32 [64][kAP]
-constexpr uint32_t A_AQK = A_TF + 64 * kAP * 4;         // Aqk bf16 64x64, K-major SW128
-constexpr uint32_t A_TPH = A_AQK + 8192;                // [T; P] hi, 128x64 bf16 K-major SW128
-constexpr uint32_t A_TPL = A_TPH + 16384;               // [T; P] lo
-constexpr uint32_t A_BOP = A_TPL + 16384;               // [v w | b k e^G], four 64-column MN-major blocks
-constexpr uint32_t A_QT = A_BOP + 32768;                // s q e^G bf16 [64][kOP]
-constexpr uint32_t A_X = A_QT + 64 * kOP * 2;           // exchange: fp32 [640]
-constexpr uint32_t A_QKV = 155648;                      // q, k, v tiles (TMA, SW128, two 64-channel boxes each)
-constexpr uint32_t A_BAR = A_QKV + 3 * 16384;           // three mbarriers, TMEM pointer, flag
-constexpr uint32_t A_USED = A_BAR + 32;
-constexpr uint32_t A_QK = A_TPH;                        // q.k per (row, channel), fp32 [64][128], during the scan
+constexpr uint32_t A_QKT = 0;            // q, k tiles (TMA, SW128) [P1-P3]; then [T; P] hi | lo [P5-P8]
+constexpr uint32_t A_TPH = 0, A_TPL = 16384;
+constexpr uint32_t A_AF = 32768;         // q.k fp32 [64][128] [P1-P2]; Akk fp32 [64][kAP] [P3-P4];
+constexpr uint32_t A_TF = A_AF + 64 * kAP * 4;  //   T fp32 [64][kAP] [P4-P5];
+constexpr uint32_t A_BOP = A_AF;         //   [v w | b k e^G], four MN-major SW128 blocks (TMA) [P6-P8]
+constexpr uint32_t A_R = 67584;          // level operands Rkk, Rqk, C, bf16 [32][kOP] each [P3];
+constexpr uint32_t A_RKK = A_R, A_RQK = A_R + 32 * kOP * 2, A_CC = A_R + 64 * kOP * 2;
+constexpr uint32_t A_QT = A_R;           //   s q e^G, two SW128 64-column boxes (TMA) [P4-P9]
+constexpr uint32_t A_AQK = 94208;        // Aqk bf16 64x64, K-major SW128 [P2-P6]
+constexpr uint32_t A_X = A_AQK + 8192;   // exchange: fp32 [640]
+constexpr uint32_t A_BAR = A_X + 640 * 4;  // five mbarriers, TMEM pointer, flag
+constexpr uint32_t A_USED = A_BAR + 48;
 constexpr uint32_t kSmemA = A_USED + 1024;
-static_assert(A_RKK + 3 * 32 * kOP * 2 <= A_AF, "level operands overlap Akk");
-static_assert(A_X + 640 * 4 <= A_QKV && A_QKV % 1024 == 0, "q/k/v tiles misplaced");
-static_assert(A_QK + 64 * 128 * 4 <= A_BOP, "q.k buffer overlaps the B operands");
-static_assert(A_AQK % 1024 == 0 && A_TPH % 1024 == 0 && A_TPL % 1024 == 0 && A_BOP % 1024 == 0,
-              "SW128 tiles must be 1024-byte aligned");
-static_assert(kSmemA <= 232448, "prep kernel over the shared-memory limit");
-constexpr uint32_t TMA_BIG = 0, TMA_P = 256;  // TMEM columns: [U W; Y0 AqkW] (N=256), P = Aqk T (N=64)
+enum BarA { BA_P = 0, BA_BIG, BA_QK, BA_QT, BA_BOP };
+static_assert(A_TF + 64 * kAP * 4 <= A_R && A_AF + 64 * 128 * 4 <= A_R, "Akk / T / q.k overlap the operands");
+static_assert(A_BOP + 32768 <= A_R && A_BOP % 1024 == 0, "B operands misplaced");
+static_assert(A_R + 96 * kOP * 2 <= A_AQK && A_QT + 16384 <= A_AQK && A_QT % 1024 == 0, "level operands misplaced");
+static_assert(A_AQK % 1024 == 0, "SW128 tiles must be 1024-byte aligned");
+static_assert(kSmemA <= 115712, "prep kernel must fit two CTAs per SM");
+constexpr uint32_t TMA_BIG = 0, TMA_P = 0;  // TMEM: P = Aqk T (N=64) first, then [U W; Y0 AqkW] (N=256)
 
 __device__ __forceinline__ void st_bf16(uint8_t *p, float x) {
     *reinterpret_cast<__nv_bfloat16 *>(p) = __float2bfloat16_rn(x);
 }
 
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, uint64_t *bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            ptx::smem_u32(dst)),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(ptx::smem_u32(bar))
+        : "memory");
+}
+
+// Generic-proxy global writes of this thread become visible to later TMA (async-proxy) reads.
+__device__ __forceinline__ void fence_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 // Element (t, d) of the q (which = 0) or k (which = 1) tile.
 __device__ __forceinline__ float qk_tile(const uint8_t *base, int which, int t, int d) {
     return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(
-        base + A_QKV + 16384 * which + (uint32_t)(d >> 6) * 8192u + ptx::sw128(t, d & 63)));
+        base + A_QKT + 16384 * which + (uint32_t)(d >> 6) * 8192u + ptx::sw128(t, d & 63)));
 }
 
 // One bisection level (blocks of s = 2^LS rows): this thread's operand rows, then the warps' MMAs of the
@@ -192,19 +205,19 @@ __device__ __forceinline__ void bisection_level(uint8_t *base, uint32_t sb, floa
 }
 
 template <typename TG>
-__global__ void __launch_bounds__(kThreadsA, 1)
+__global__ void __launch_bounds__(kThreadsA, 2)
     prep_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                const __grid_constant__ CUtensorMap tm_v, const CoreParams p, const SplitWs ws, int *status) {
+                const __grid_constant__ CUtensorMap tm_bop, const __grid_constant__ CUtensorMap tm_qt,
+                const CoreParams p, const SplitWs ws, int *status) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);  // stays a shared pointer
     const uint32_t sb = ptx::smem_u32(base);
     float *Af = reinterpret_cast<float *>(base + A_AF);
     float *Tf = reinterpret_cast<float *>(base + A_TF);
     float *X = reinterpret_cast<float *>(base + A_X);
-    __nv_bfloat16 *QT = reinterpret_cast<__nv_bfloat16 *>(base + A_QT);
     uint64_t *bars = reinterpret_cast<uint64_t *>(base + A_BAR);
-    uint32_t *tmem_ptr = reinterpret_cast<uint32_t *>(base + A_BAR + 24);
-    volatile int *flag = reinterpret_cast<volatile int *>(base + A_BAR + 28);
+    uint32_t *tmem_ptr = reinterpret_cast<uint32_t *>(base + A_BAR + 40);
+    volatile int *flag = reinterpret_cast<volatile int *>(base + A_BAR + 44);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t c = blockIdx.x, bh = blockIdx.y, nch = ws.nch;
@@ -216,27 +229,27 @@ __global__ void __launch_bounds__(kThreadsA, 1)
 
     if (tid == 0) {
         *flag = 0;
-        ptx::mbar_init(&bars[0], 1);
-        ptx::mbar_init(&bars[1], 1);
-        ptx::mbar_init(&bars[2], 1);
+        for (int i = 0; i < 5; ++i) ptx::mbar_init(&bars[i], 1);
         ptx::fence_mbar_init();
-        // The chunk's q, k, v rows (rows past the sequence read as zeros).
-        ptx::mbar_arrive_expect_tx(&bars[2], 3 * 16384);
+        ptx::prefetch_tmap(&tm_bop);
+        ptx::prefetch_tmap(&tm_qt);
+        // The chunk's q and k rows (rows past the sequence read as zeros).
+        ptx::mbar_arrive_expect_tx(&bars[BA_QK], 2 * 16384);
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
-            ptx::tma_load_4d(base + A_QKV + 8192 * x, &tm_q, &bars[2], 64 * x, (int)h, (int)row0, (int)b);
-            ptx::tma_load_4d(base + A_QKV + 16384 + 8192 * x, &tm_k, &bars[2], 64 * x, (int)h, (int)row0, (int)b);
-            ptx::tma_load_4d(base + A_QKV + 32768 + 8192 * x, &tm_v, &bars[2], 64 * x, (int)h, (int)row0, (int)b);
+            ptx::tma_load_4d(base + A_QKT + 8192 * x, &tm_q, &bars[BA_QK], 64 * x, (int)h, (int)row0, (int)b);
+            ptx::tma_load_4d(base + A_QKT + 16384 + 8192 * x, &tm_k, &bars[BA_QK], 64 * x, (int)h, (int)row0, (int)b);
         }
     }
     if (warp == 0) {
-        ptx::tmem_alloc(tmem_ptr, 512);
+        ptx::tmem_alloc(tmem_ptr, 256);
         ptx::tmem_relinquish();
     }
     for (int i = tid; i < 512; i += kThreadsA) ptx::st_shared_v4(sb + A_AQK + 16 * i, 0u, 0u, 0u, 0u);
 
     // One key / value channel per thread, half the chunk's rows each.
     const int d = tid & 127, h2 = tid >> 7;
+    const __nv_bfloat16 *vg = static_cast<const __nv_bfloat16 *>(p.v);
     auto rowidx = [&](int t) -> int64_t { return (b * p.seq + row0 + t) * p.heads + h; };
     auto gate = [&](const void *ptr, int w, int64_t r) -> float {
         return ld(static_cast<const TG *>(ptr) + r * w + (w == 1 ? 0 : d));
@@ -262,22 +275,24 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     float G = h2 ? X[d] : 0.f;
     DC_SPLIT_MARK(1);
 
-    // ---- (1) the scan: G, alpha = e^g, the B operands, s q e^G, Kh, and the level inputs.  q, k, v come
-    //      from the TMA tiles; erase and write are loaded eight rows at a time before any is used. ----
-    const bool tiles_ok = ptx::mbar_wait(&bars[2], 0);
-    const uint32_t cellcol = (uint32_t)(d >> 6) * 8192u;
-    auto tile = [&](int which, int t) -> float { return qk_tile(base, which, t, d); };  // 0 q, 1 k, 2 v
-    float *QK = reinterpret_cast<float *>(base + A_QK);
+    // ---- (1) the scan: G, alpha = e^g, and per row v w, b k e^G, s q e^G (parked in the workspace),
+    //      Kh (to the workspace), q.k (for Aqk's diagonal) and b k (for the bisection).  v, erase and
+    //      write are loaded eight rows at a time before any is used; q and k come from the TMA tiles. ----
+    const bool tiles_ok = ptx::mbar_wait(&bars[BA_QK], 0);
+    float *QK = reinterpret_cast<float *>(base + A_AF);
+    __nv_bfloat16 *park_bop = ws.a6 + bhc * 128 * 128;  // rows 0-63: v w; rows 64-127: b k e^G
+    __nv_bfloat16 *park_qt = ws.y0 + bhc * 64 * 128;    // s q e^G
     uint32_t bk2[16];  // bf16 pairs of consecutive rows of (b k)
 #pragma unroll
     for (int i0 = 0; i0 < 32; i0 += 8) {
-        float ex[8], wx[8];
+        float ex[8], wx[8], vx[8];
 #pragma unroll
         for (int o = 0; o < 8; ++o) {
             const int t = 32 * h2 + i0 + o;
-            ex[o] = wx[o] = 0.f;
+            ex[o] = wx[o] = vx[o] = 0.f;
             if (t < nvalid) {
                 const int64_t r = rowidx(t);
+                vx[o] = __bfloat162float(vg[r * 128 + d]);
                 ex[o] = gate(p.erase, p.ew, r);
                 wx[o] = gate(p.write, p.ww, r);
             }
@@ -286,14 +301,13 @@ __global__ void __launch_bounds__(kThreadsA, 1)
 #pragma unroll
         for (int o = 0; o < 8; ++o) {
             const int i = i0 + o, t = 32 * h2 + i;
-            const float qx = tile(0, t), kx = tile(1, t), vx = tile(2, t);
+            const float qx = qk_tile(base, 0, t, d), kx = qk_tile(base, 1, t, d);
             G += alpha[i];
             alpha[i] = __expf(alpha[i]);
             const float gam = __expf(G);
-            const uint32_t cell = cellcol + ptx::sw128(t, d & 63);
-            st_bf16(base + A_BOP + cell, vx * wx[o]);
-            st_bf16(base + A_BOP + 16384 + cell, ex[o] * kx * gam);
-            QT[t * kOP + d] = __float2bfloat16_rn(scale * qx * gam);
+            park_bop[t * 128 + d] = __float2bfloat16_rn(vx[o] * wx[o]);
+            park_bop[(64 + t) * 128 + d] = __float2bfloat16_rn(ex[o] * kx * gam);
+            park_qt[t * 128 + d] = __float2bfloat16_rn(scale * qx * gam);
             ws.kh[(bhc * 64 + t) * 128 + d] = __float2bfloat16_rn(kx * __expf(G63 - G));
             QK[t * 128 + d] = qx * kx;
             bkx[o] = ex[o] * kx;
@@ -303,6 +317,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     }
     if (h2 == 0) ws.gam[bhc * 128 + d] = __expf(G63);
     if (h2 == 1) X[256 + d] = alpha[0];  // alpha of row 32, the reference of the top level
+    fence_async_global();                 // the parked rows are read back by TMA
     if (!tiles_ok) *flag = 1;
     ptx::named_sync(tc::NB_PAR, kThreadsA);
     // Aqk's diagonal: row t summed over the 128 channels by four threads (rotated reads: no bank conflicts).
@@ -316,6 +331,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         if (part == 0) st_bf16(base + A_AQK + ptx::sw128(t, t), scale * acc);
     }
     const float a32 = X[256 + d];
+    ptx::named_sync(tc::NB_PAR, kThreadsA);  // the q.k buffer is read before Akk overwrites it
     DC_SPLIT_MARK(2);
 
     // ---- (2) Akk (strictly lower) and Aqk (lower) by bisection levels, coarsest first ----
@@ -325,12 +341,18 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     bisection_level<3>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
     bisection_level<2>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
     bisection_level<1>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
+    // The level operands are dead: bring s q e^G back into their place.
+    if (tid == 0) {
+        ptx::mbar_arrive_expect_tx(&bars[BA_QT], 16384);
+        tma_load_2d(base + A_QT, &tm_qt, &bars[BA_QT], 0, (int)(bhc * 64));
+        tma_load_2d(base + A_QT + 8192, &tm_qt, &bars[BA_QT], 64, (int)(bhc * 64));
+    }
     DC_SPLIT_MARK(3);
     // ---- (3) T = (I + Akk)^-1 ----
     tc::solve_unit_lower(Af, Tf, warp, lane, [] {}, [] {});
     DC_SPLIT_MARK(4);
 
-    // ---- (4) T hi + lo: rows 0-63 of the A operand (blocks above the diagonal zero) ----
+    // ---- (4) T hi + lo: rows 0-63 of the A operand (blocks above the diagonal zero), over the q / k tiles ----
     {
         const int i = tid & 63, j0 = (tid >> 6) * 16;
         float t[16];
@@ -369,7 +391,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         return true;
     };
 
-    // ---- (5) P = Aqk T (hi) ----
+    // ---- (5) P = Aqk T (hi); Akk and T are dead: bring [v w | b k e^G] back over them ----
     if (tid == 0) {
         ptx::tc_fence_after();
         const uint32_t id = ptx::idesc_bf16(64, 64, 0, 1);
@@ -377,9 +399,14 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         for (int kk = 0; kk < 4; ++kk)
             ptx::umma_bf16(tmem + TMA_P, ptx::sdesc(sb + A_AQK + kk * 32, 16, 1024),
                            ptx::sdesc(sb + A_TPH + kk * 2048, 16384, 1024), id, kk > 0);
-        ptx::umma_commit(&bars[0]);
+        ptx::umma_commit(&bars[BA_P]);
+        ptx::mbar_arrive_expect_tx(&bars[BA_BOP], 32768);
+        const int prow = (int)(bhc * 128);
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+            tma_load_2d(base + A_BOP + 8192 * x, &tm_bop, &bars[BA_BOP], 64 * (x & 1), prow + 64 * (x >> 1));
     }
-    bool ok = role_wait(0, 0);
+    bool ok = role_wait(BA_P, 0);
     DC_SPLIT_MARK(5);
 
     // ---- (6) P hi + lo: rows 64-127 of the A operand (M=64 accumulator: rows in lanes 0-15) ----
@@ -407,9 +434,11 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         }
         ptx::fence_async_smem();
         ptx::tc_fence_before();
-        ptx::named_sync(tc::NB_PAR, kThreadsA);
+        ok = role_wait(BA_BOP, 0);  // also: every thread's P reads are done before the big MMA overwrites them
+    }
 
-        // ---- (7) [U W; Y0 Aqk W] = [T; P] (hi + lo) [v w | b k e^G] ----
+    // ---- (7) [U W; Y0 Aqk W] = [T; P] (hi + lo) [v w | b k e^G] ----
+    if (ok) {
         if (tid == 0) {
             ptx::tc_fence_after();
             const uint32_t id = ptx::idesc_bf16(128, 256, 0, 1);
@@ -417,10 +446,10 @@ __global__ void __launch_bounds__(kThreadsA, 1)
             for (int kk = 0; kk < 8; ++kk)
                 ptx::umma_bf16(tmem + TMA_BIG, ptx::sdesc(sb + (kk < 4 ? A_TPH : A_TPL) + (kk & 3) * 32, 16, 1024),
                                ptx::sdesc(sb + A_BOP + (kk & 3) * 2048, 8192, 1024), id, kk > 0);
-            ptx::umma_commit(&bars[1]);
+            ptx::umma_commit(&bars[BA_BIG]);
         }
         DC_SPLIT_MARK(6);
-        ok = role_wait(1, 0);
+        ok = role_wait(BA_BIG, 0) && role_wait(BA_QT, 0);
     }
     DC_SPLIT_MARK(7);
 
@@ -455,7 +484,9 @@ __global__ void __launch_bounds__(kThreadsA, 1)
 #pragma unroll
                         for (int o = 0; o < 8; ++o) x[o] = -f[8 * e + o];
                     } else {
-                        const uint4 qv = ptx::ld_shared_v4(sb + A_QT + 2u * ((r - 64) * kOP + col0 + 8 * e));
+                        const int cc = col0 + 8 * e;  // s q e^G, SW128 box (cc >> 6), row r - 64
+                        const uint4 qv = ptx::ld_shared_v4(sb + A_QT + (uint32_t)(cc >> 6) * 8192u +
+                                                           ptx::sw128(r - 64, cc & 63));
                         const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
                         for (int o = 0; o < 4; ++o) {
@@ -473,8 +504,14 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     ptx::tc_fence_before();
     __syncthreads();
     DC_SPLIT_MARK(8);
-    if (*flag && tid == 0) atomicExch(status, kStatusTimeout);
-    if (warp == 0) ptx::tmem_dealloc(tmem, 512);
+    if (*flag && tid == 0) {
+        atomicExch(status, kStatusTimeout);
+        // Let this CTA's own TMA loads land before its shared memory goes away.
+        ptx::mbar_wait(&bars[BA_QT], 0);
+        ptx::mbar_wait(&bars[BA_BOP], 0);
+    }
+    __syncthreads();
+    if (warp == 0) ptx::tmem_dealloc(tmem, 256);
 }
 
 // ---------------------------------------------------------------- scan kernel
@@ -499,14 +536,6 @@ constexpr uint32_t TMB_D = 0, TMB_S = 128;  // TMEM columns
 // Byte offset of 16-byte chunk `chunk` of row `row` in a SW128 tile.
 __device__ __forceinline__ uint32_t sw128c(uint32_t row, uint32_t chunk) {
     return row * 128u + ((chunk ^ (row & 7u)) << 4);
-}
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, uint64_t *bar, int c0, int c1) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            ptx::smem_u32(dst)),
-        "l"(tmap), "r"(c0), "r"(c1), "r"(ptx::smem_u32(bar))
-        : "memory");
 }
 
 template <typename TO>
@@ -859,9 +888,10 @@ int launch_split_typed(const CoreParams &p, void *workspace, cudaStream_t stream
     const split::SplitWs ws = split_carve(p, workspace);
     const int64_t bhn = p.batch * p.heads;
     const uint64_t n = (uint64_t)(bhn * ws.nch);
-    CUtensorMap ma6, mu, my0, mkh, my, mq, mk, mv;
+    CUtensorMap ma6, mu, my0, mkh, my, mq, mk, mbop, mqt;
     if (!encode_rows(&mq, p.q, p.heads, p.seq, p.batch) || !encode_rows(&mk, p.k, p.heads, p.seq, p.batch) ||
-        !encode_rows(&mv, p.v, p.heads, p.seq, p.batch) || !encode_2d(&ma6, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws.a6, 128, n * 128, 64, 128) ||
+        !encode_2d(&mbop, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws.a6, 128, n * 128, 64, 64) ||
+        !encode_2d(&mqt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws.y0, 128, n * 64, 64, 64) || !encode_2d(&ma6, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws.a6, 128, n * 128, 64, 128) ||
         !encode_2d(&mu, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ws.u, 128, n * 64, 32, 64) ||
         !encode_2d(&my0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws.y0, 128, n * 64, 64, 64) ||
         !encode_2d(&mkh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws.kh, 128, n * 64, 64, 64) ||
@@ -880,8 +910,8 @@ int launch_split_typed(const CoreParams &p, void *workspace, cudaStream_t stream
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)split::kSmemB);
     if (e == cudaSuccess) {
-        ka<<<dim3((unsigned)ws.nch, (unsigned)bhn), split::kThreadsA, split::kSmemA, stream>>>(mq, mk, mv, p, ws,
-                                                                                                 status);
+        ka<<<dim3((unsigned)ws.nch, (unsigned)bhn), split::kThreadsA, split::kSmemA, stream>>>(mq, mk, mbop, mqt, p,
+                                                                                                 ws, status);
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) {

@@ -77,22 +77,25 @@ constexpr uint64_t kWsBytesPerChunk = 32768ull + 32768ull + 16384ull + 16384ull 
 constexpr int kThreadsA = 256;
 constexpr uint32_t A_QKT = 0;            // q, k tiles (TMA, SW128) [P1-P3]; then [T; P] hi | lo [P5-P8]
 constexpr uint32_t A_TPH = 0, A_TPL = 16384;
-constexpr uint32_t A_AF = 32768;         // q.k fp32 [64][128] [P1-P2]; Akk fp32 [64][kAP] [P3-P4];
+constexpr uint32_t A_AF = 32768;         // scan staging ring [P1]; Akk fp32 [64][kAP] [P3-P4];
 constexpr uint32_t A_TF = A_AF + 64 * kAP * 4;  //   T fp32 [64][kAP] [P4-P5];
 constexpr uint32_t A_BOP = A_AF;         //   [v w | b k e^G], four MN-major SW128 blocks (TMA) [P6-P8]
 constexpr uint32_t A_R = 67584;          // level operands Rkk, Rqk, C, bf16 [32][kOP] each [P3];
 constexpr uint32_t A_RKK = A_R, A_RQK = A_R + 32 * kOP * 2, A_CC = A_R + 64 * kOP * 2;
 constexpr uint32_t A_QT = A_R;           //   s q e^G, two SW128 64-column boxes (TMA) [P4-P9]
+constexpr uint32_t A_STG = A_AF;         // erase / write / v rows staged by cp.async [P1]: three buffers of
+constexpr uint32_t kStgBytes = 16 * 512 + 16 * 512 + 16 * 256;  // [16 rows] of e, w (up to fp32), v bf16
 constexpr uint32_t A_AQK = 94208;        // Aqk bf16 64x64, K-major SW128 [P2-P6]
 constexpr uint32_t A_X = A_AQK + 8192;   // exchange: fp32 [640]
 constexpr uint32_t A_BAR = A_X + 640 * 4;  // five mbarriers, TMEM pointer, flag
 constexpr uint32_t A_USED = A_BAR + 48;
 constexpr uint32_t kSmemA = A_USED + 1024;
 enum BarA { BA_P = 0, BA_BIG, BA_QK, BA_QT, BA_BOP };
-static_assert(A_TF + 64 * kAP * 4 <= A_R && A_AF + 64 * 128 * 4 <= A_R, "Akk / T / q.k overlap the operands");
+static_assert(A_TF + 64 * kAP * 4 <= A_R, "Akk / T overlap the operands");
 static_assert(A_BOP + 32768 <= A_R && A_BOP % 1024 == 0, "B operands misplaced");
 static_assert(A_R + 96 * kOP * 2 <= A_AQK && A_QT + 16384 <= A_AQK && A_QT % 1024 == 0, "level operands misplaced");
 static_assert(A_AQK % 1024 == 0, "SW128 tiles must be 1024-byte aligned");
+static_assert(A_STG + 3 * kStgBytes <= A_AQK, "scan staging overflows into Aqk");
 static_assert(kSmemA <= 115712, "prep kernel must fit two CTAs per SM");
 constexpr uint32_t TMA_BIG = 0, TMA_P = 0;  // TMEM: P = Aqk T (N=64) first, then [U W; Y0 AqkW] (N=256)
 
@@ -120,11 +123,12 @@ __device__ __forceinline__ float qk_tile(const uint8_t *base, int which, int t, 
 // One bisection level (blocks of s = 2^LS rows): this thread's operand rows, then the warps' MMAs of the
 // packed 32 x 32 product, whose block-diagonal entries are scattered into Akk (fp32) and Aqk (bf16).
 // Thread (d, h2) owns channel d of rows 32 h2 .. 32 h2 + 31; for s <= 32 those rows hold whole blocks.
-template <int LS>
-__device__ __forceinline__ void bisection_level(uint8_t *base, uint32_t sb, float *Af, const uint32_t (&bk2)[16],
-                                                const float (&alpha)[32], float a32, float scale, int d, int h2,
-                                                int warp, int lane) {
-    constexpr int s = 1 << LS, half = s >> 1, lh = LS - 1;
+// One copy of this body serves all six levels (LS at run time, rows unrolled): the kernel's code must
+// stay small enough for the instruction cache with two CTAs per SM.
+__device__ __forceinline__ void bisection_level(int LS, uint8_t *base, uint32_t sb, float *Af,
+                                                const uint32_t (&bk2)[16], const float (&alpha)[32], float a32,
+                                                float scale, int d, int h2, int warp, int lane) {
+    const int s = 1 << LS, half = s >> 1, lh = LS - 1;
     uint8_t *Rkk = base + A_RKK, *Rqk = base + A_RQK, *Cc = base + A_CC;
     auto bk = [&](int i) { return (i & 1) ? ptx::bf16hi(bk2[i / 2]) : ptx::bf16lo(bk2[i / 2]); };
     auto row_side = [&](int i, int m, float P) {
@@ -132,48 +136,32 @@ __device__ __forceinline__ void bisection_level(uint8_t *base, uint32_t sb, floa
         st_bf16(Rqk + 2 * (m * kOP + d), qk_tile(base, 0, 32 * h2 + i, d) * P);
     };
     auto col_side = [&](int i, int n, float Pb) { st_bf16(Cc + 2 * (n * kOP + d), qk_tile(base, 1, 32 * h2 + i, d) * Pb); };
-    if (LS == 6) {
-        if (h2) {  // rows 32-63: the second half, reference row 32
-            float P = 1.f;
+    // Position of row 32 h2 + i inside its block; at the top level (s = 64) the half decides the side.
+    const int hoff = (LS == 6) ? 32 * h2 : 0, pbase = (LS == 6) ? 0 : 16 * h2;
+    float P = 1.f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                P = (i == 0) ? 1.f : P * alpha[i];
-                row_side(i, i, P);
-            }
-        } else {  // rows 0-31: the first half
-            float Pb = a32;
-#pragma unroll
-            for (int i = 31; i >= 0; --i) {
-                if (i < 31) Pb *= alpha[i + 1 < 32 ? i + 1 : 31];
-                col_side(i, i, Pb);
-            }
+    for (int i = 0; i < 32; ++i) {
+        const int pos = (hoff + i) & (s - 1);
+        if (pos >= half) {
+            P = (pos == half) ? 1.f : P * alpha[i];
+            row_side(i, pbase + ((i >> LS) << lh) + (pos - half), P);
         }
-    } else {
-        float P = 1.f;
+    }
+    float Pb = 1.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const int pos = i & (s - 1);
-            if (pos >= half) {
-                P = (pos == half) ? 1.f : P * alpha[i];
-                row_side(i, 16 * h2 + ((i >> LS) << lh) + (pos - half), P);
-            }
-        }
-        float Pb = 1.f;
-#pragma unroll
-        for (int i = 31; i >= 0; --i) {
-            const int pos = i & (s - 1);
-            if (pos < half) {
-                const float an = alpha[i + 1 < 32 ? i + 1 : 31];  // alpha of row t + 1 (inside this half)
-                Pb = (pos == half - 1) ? an : Pb * an;
-                col_side(i, 16 * h2 + ((i >> LS) << lh) + pos, Pb);
-            }
+    for (int i = 31; i >= 0; --i) {
+        const int pos = (hoff + i) & (s - 1);
+        if (pos < half) {
+            const float an = (i == 31) ? a32 : alpha[i + 1 < 32 ? i + 1 : 31];  // alpha of row t + 1
+            Pb = (pos == half - 1) ? an : Pb * an;
+            col_side(i, pbase + ((i >> LS) << lh) + pos, Pb);
         }
     }
     ptx::named_sync(tc::NB_PAR, kThreadsA);
     // Tiles of the packed 32 x 32 product that meet its block diagonal: all eight at the top level,
     // (mt, 2 mt) and (mt, 2 mt + 1) below.  Job = (matrix, m tile, n tile); Akk and Aqk share C.
-    constexpr int njobs = (half == 32) ? 16 : 8;
-#pragma unroll
+    const int njobs = (half == 32) ? 16 : 8;
+#pragma unroll 1
     for (int job0 = 0; job0 < njobs; job0 += kThreadsA / 32) {
         const int job = job0 + warp;
         const int mat = job & 1;
@@ -251,8 +239,12 @@ __global__ void __launch_bounds__(kThreadsA, 2)
     const int d = tid & 127, h2 = tid >> 7;
     const __nv_bfloat16 *vg = static_cast<const __nv_bfloat16 *>(p.v);
     auto rowidx = [&](int t) -> int64_t { return (b * p.seq + row0 + t) * p.heads + h; };
-    auto gate = [&](const void *ptr, int w, int64_t r) -> float {
-        return ld(static_cast<const TG *>(ptr) + r * w + (w == 1 ? 0 : d));
+    auto gate = [&](const void *ptr, int w, int64_t r) -> float {  // inputs are read-only for the kernel
+        const TG *g = static_cast<const TG *>(ptr) + r * w + (w == 1 ? 0 : d);
+        if constexpr (sizeof(TG) == 4)
+            return __ldg(reinterpret_cast<const float *>(g));
+        else
+            return __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16 *>(g)));
     };
 
     DC_SPLIT_MARK(0);
@@ -276,71 +268,117 @@ __global__ void __launch_bounds__(kThreadsA, 2)
     DC_SPLIT_MARK(1);
 
     // ---- (1) the scan: G, alpha = e^g, and per row v w, b k e^G, s q e^G (parked in the workspace),
-    //      Kh (to the workspace), q.k (for Aqk's diagonal) and b k (for the bisection).  v, erase and
-    //      write are loaded eight rows at a time before any is used; q and k come from the TMA tiles. ----
+    //      Kh (to the workspace) and b k (for the bisection).  erase, write (when per channel) and v
+    //      stream through a three-buffer shared-memory ring by cp.async, 8 rows of each half per batch,
+    //      two batches ahead; q and k come from the TMA tiles.  The batch loop is not unrolled (the
+    //      kernel's code must fit the instruction cache), so alpha and bk2 are rotating windows whose
+    //      first slots always hold the current batch. ----
     const bool tiles_ok = ptx::mbar_wait(&bars[BA_QK], 0);
-    float *QK = reinterpret_cast<float *>(base + A_AF);
-    __nv_bfloat16 *park_bop = ws.a6 + bhc * 128 * 128;  // rows 0-63: v w; rows 64-127: b k e^G
-    __nv_bfloat16 *park_qt = ws.y0 + bhc * 64 * 128;    // s q e^G
-    uint32_t bk2[16];  // bf16 pairs of consecutive rows of (b k)
-#pragma unroll
-    for (int i0 = 0; i0 < 32; i0 += 8) {
-        float ex[8], wx[8], vx[8];
-#pragma unroll
-        for (int o = 0; o < 8; ++o) {
-            const int t = 32 * h2 + i0 + o;
-            ex[o] = wx[o] = vx[o] = 0.f;
-            if (t < nvalid) {
-                const int64_t r = rowidx(t);
-                vx[o] = __bfloat162float(vg[r * 128 + d]);
-                ex[o] = gate(p.erase, p.ew, r);
-                wx[o] = gate(p.write, p.ww, r);
-            }
+    constexpr int kRowB = 128 * (int)sizeof(TG);  // bytes of one full-width gate row
+    const bool e_full = p.ew != 1, w_full = p.ww != 1;
+    const int64_t r_first = rowidx(32 * h2), r_step = p.heads;  // rows of this half are r_first + i * r_step
+    __nv_bfloat16 *park_v = ws.a6 + bhc * 128 * 128 + (32 * h2) * 128 + d;   // rows 0-63: v w
+    __nv_bfloat16 *park_k = park_v + 64 * 128;                                 // rows 64-127: b k e^G
+    __nv_bfloat16 *park_q = ws.y0 + bhc * 64 * 128 + (32 * h2) * 128 + d;     // s q e^G
+    __nv_bfloat16 *kh_out = ws.kh + (bhc * 64 + 32 * h2) * 128 + d;
+    auto stage = [&](int k) {  // batch k: rows 8k..8k+7 of each half -> slots 0-7 (half 0), 8-15 (half 1)
+        const uint32_t buf = sb + A_STG + (uint32_t)(k % 3) * kStgBytes;
+        for (int q = tid; q < 16 * (kRowB / 16); q += kThreadsA) {
+            const int slot = q / (kRowB / 16), piece = q % (kRowB / 16);
+            const int t = (slot < 8 ? 0 : 32) + 8 * k + (slot & 7);
+            const int64_t r = t < nvalid ? rowidx(t) : 0;
+            const uint32_t n = t < nvalid ? 16u : 0u;
+            if (e_full)
+                ptx::cp_async16(buf + slot * kRowB + piece * 16,
+                                static_cast<const uint8_t *>(p.erase) + r * kRowB + piece * 16, n);
+            if (w_full)
+                ptx::cp_async16(buf + 8192 + slot * kRowB + piece * 16,
+                                static_cast<const uint8_t *>(p.write) + r * kRowB + piece * 16, n);
         }
+        {
+            const int slot = tid >> 4, piece = tid & 15;
+            const int t = (slot < 8 ? 0 : 32) + 8 * k + (slot & 7);
+            const int64_t r = t < nvalid ? rowidx(t) : 0;
+            ptx::cp_async16(buf + 16384 + slot * 256 + piece * 16, vg + r * 128 + piece * 8, t < nvalid ? 16u : 0u);
+        }
+        ptx::cp_async_commit();
+    };
+    uint32_t bk2[16];  // bf16 pairs of consecutive rows of (b k), rotating with alpha
+    stage(0);
+    stage(1);
+#pragma unroll 1
+    for (int k = 0; k < 4; ++k) {
+        if (k + 2 < 4)
+            stage(k + 2);
+        else
+            ptx::cp_async_commit();  // an empty group keeps the count uniform
+        ptx::cp_async_wait<2>();
+        ptx::named_sync(tc::NB_PAR, kThreadsA);  // every thread's copies of batch k have landed
+        const uint8_t *buf = base + A_STG + (k % 3) * kStgBytes;
+        const TG *se = reinterpret_cast<const TG *>(buf) + (8 * h2) * 128;
+        const TG *sw = reinterpret_cast<const TG *>(buf + 8192) + (8 * h2) * 128;
+        const __nv_bfloat16 *sv = reinterpret_cast<const __nv_bfloat16 *>(buf + 16384) + (8 * h2) * 128 + d;
         float bkx[8];
 #pragma unroll
         for (int o = 0; o < 8; ++o) {
-            const int i = i0 + o, t = 32 * h2 + i;
+            const int i = 8 * k + o, t = 32 * h2 + i;
+            const bool ok_row = t < nvalid;
+            const float ex = e_full ? ld(se + o * 128 + d) : (ok_row ? gate(p.erase, 1, r_first + i * r_step) : 0.f);
+            const float wx = w_full ? ld(sw + o * 128 + d) : (ok_row ? gate(p.write, 1, r_first + i * r_step) : 0.f);
+            const float vx = __bfloat162float(sv[o * 128]);
             const float qx = qk_tile(base, 0, t, d), kx = qk_tile(base, 1, t, d);
-            G += alpha[i];
-            alpha[i] = __expf(alpha[i]);
+            G += alpha[o];
+            alpha[o] = __expf(alpha[o]);
             const float gam = __expf(G);
-            park_bop[t * 128 + d] = __float2bfloat16_rn(vx[o] * wx[o]);
-            park_bop[(64 + t) * 128 + d] = __float2bfloat16_rn(ex[o] * kx * gam);
-            park_qt[t * 128 + d] = __float2bfloat16_rn(scale * qx * gam);
-            ws.kh[(bhc * 64 + t) * 128 + d] = __float2bfloat16_rn(kx * __expf(G63 - G));
-            QK[t * 128 + d] = qx * kx;
-            bkx[o] = ex[o] * kx;
+            park_v[i * 128] = __float2bfloat16_rn(vx * wx);
+            park_k[i * 128] = __float2bfloat16_rn(ex * kx * gam);
+            park_q[i * 128] = __float2bfloat16_rn(scale * qx * gam);
+            kh_out[i * 128] = __float2bfloat16_rn(kx * __expf(G63 - G));
+            bkx[o] = ex * kx;
         }
+        // rotate: the processed batch moves to the back of both windows
+        float a8[8];
 #pragma unroll
-        for (int o = 0; o < 8; o += 2) bk2[(i0 + o) / 2] = ptx::pack_bf16(bkx[o], bkx[o + 1]);
+        for (int o = 0; o < 8; ++o) a8[o] = alpha[o];
+#pragma unroll
+        for (int j = 0; j < 24; ++j) alpha[j] = alpha[j + 8];
+#pragma unroll
+        for (int o = 0; o < 8; ++o) alpha[24 + o] = a8[o];
+#pragma unroll
+        for (int j = 0; j < 12; ++j) bk2[j] = bk2[j + 4];
+#pragma unroll
+        for (int o = 0; o < 8; o += 2) bk2[12 + o / 2] = ptx::pack_bf16(bkx[o], bkx[o + 1]);
+        ptx::named_sync(tc::NB_PAR, kThreadsA);  // batch k's buffer is free for batch k + 3
     }
     if (h2 == 0) ws.gam[bhc * 128 + d] = __expf(G63);
     if (h2 == 1) X[256 + d] = alpha[0];  // alpha of row 32, the reference of the top level
     fence_async_global();                 // the parked rows are read back by TMA
     if (!tiles_ok) *flag = 1;
-    ptx::named_sync(tc::NB_PAR, kThreadsA);
-    // Aqk's diagonal: row t summed over the 128 channels by four threads (rotated reads: no bank conflicts).
+    // Aqk's diagonal: row t's q.k from the tiles, 32 channels per thread, four threads per row.
     {
         const int t = tid >> 2, part = tid & 3;
         float acc = 0.f;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) acc += QK[t * 128 + 32 * part + ((j + t) & 31)];
+        for (int c8 = 0; c8 < 4; ++c8) {
+            const int col = 32 * (part & 1) + 8 * c8;  // channels 64 (part >> 1) + col .. + 7
+            const uint32_t off = (uint32_t)(part >> 1) * 8192u + ptx::sw128(t, col);
+            const uint4 qv = ptx::ld_shared_v4(sb + A_QKT + off), kv = ptx::ld_shared_v4(sb + A_QKT + 16384 + off);
+            const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w}, kw[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                acc += ptx::bf16lo(qw[e]) * ptx::bf16lo(kw[e]) + ptx::bf16hi(qw[e]) * ptx::bf16hi(kw[e]);
+        }
         acc += __shfl_xor_sync(0xffffffffu, acc, 1);
         acc += __shfl_xor_sync(0xffffffffu, acc, 2);
         if (part == 0) st_bf16(base + A_AQK + ptx::sw128(t, t), scale * acc);
     }
     const float a32 = X[256 + d];
-    ptx::named_sync(tc::NB_PAR, kThreadsA);  // the q.k buffer is read before Akk overwrites it
+    ptx::named_sync(tc::NB_PAR, kThreadsA);
     DC_SPLIT_MARK(2);
 
     // ---- (2) Akk (strictly lower) and Aqk (lower) by bisection levels, coarsest first ----
-    bisection_level<6>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
-    bisection_level<5>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
-    bisection_level<4>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
-    bisection_level<3>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
-    bisection_level<2>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
-    bisection_level<1>(base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
+#pragma unroll 1
+    for (int LS = 6; LS >= 1; --LS) bisection_level(LS, base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
     // The level operands are dead: bring s q e^G back into their place.
     if (tid == 0) {
         ptx::mbar_arrive_expect_tx(&bars[BA_QT], 16384);

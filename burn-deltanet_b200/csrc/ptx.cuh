@@ -98,8 +98,6 @@ __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
-// Generic-proxy shared-memory writes become visible to the async proxy
-// (tensor cores, TMA) after this fence plus a thread barrier.
 // Tile store shared -> global through the tensor map (bulk async-group); the
 // shared tile must be made visible to the async proxy (fence_async_smem) and
 // may be overwritten only after bulk_wait_all() or bulk_wait_read().
@@ -112,6 +110,17 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 // Every committed bulk store of this thread has written global memory.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// 16-byte global -> shared copy that bypasses registers; src_bytes = 0 writes zeros.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Every group of this thread but the most recent `n` has landed.
+template <int n>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(n) : "memory"); }
+
+// Generic-proxy shared-memory writes become visible to the async proxy
+// (tensor cores, TMA) after this fence plus a thread barrier.
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // ---------------------------------------------------------------- tcgen05

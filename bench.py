@@ -368,6 +368,7 @@ def run_ours(args):
     dn = importlib.import_module("burn-deltanet_b200")
     hbm_peak, tc_peak, peak_kind = measured_peaks()
     cfg, batch, tokens, u, kind = WORKLOADS[args.workload]
+    batch = args.batch or batch
     x = make_prefill(kind, batch, tokens, u, "cuda", 1000 + rank)
     # One dc_chunk_fwd per step: one kernel, or two (prep + scan) for per-channel gates.
     launches = args.steps * (2 if kind == "gdn2" else 1)
@@ -504,6 +505,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", choices=["prefill", "decode"], default=None,
                     help="time one kernel alone and print a short line (for profiling runs)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per GPU instead of the workload's own (for small profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

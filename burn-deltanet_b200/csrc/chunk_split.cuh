@@ -86,8 +86,9 @@ constexpr uint32_t A_QT = A_R;           //   s q e^G, two SW128 64-column boxes
 constexpr uint32_t A_STG = A_AF;         // erase / write / v rows staged by cp.async [P1]: three buffers of
 constexpr uint32_t kStgBytes = 16 * 512 + 16 * 512 + 16 * 256;  // [16 rows] of e, w (up to fp32), v bf16
 constexpr uint32_t A_AQK = 94208;        // Aqk bf16 64x64, K-major SW128 [P2-P6]
-constexpr uint32_t A_X = A_AQK + 8192;   // exchange: fp32 [640]
-constexpr uint32_t A_BAR = A_X + 640 * 4;  // five mbarriers, TMEM pointer, flag
+constexpr uint32_t A_X = A_AQK + 8192;   // exchange: fp32 [3][4][128] (per quarter: sum of g, first alpha,
+                                         //   product of the other fifteen alphas)
+constexpr uint32_t A_BAR = A_X + 1536 * 4;  // five mbarriers, TMEM pointer, flag
 constexpr uint32_t A_USED = A_BAR + 48;
 constexpr uint32_t kSmemA = A_USED + 1024;
 enum BarA { BA_P = 0, BA_BIG, BA_QK, BA_QT, BA_BOP };
@@ -122,39 +123,76 @@ __device__ __forceinline__ float qk_tile(const uint8_t *base, int which, int t, 
 
 // One bisection level (blocks of s = 2^LS rows): this thread's operand rows, then the warps' MMAs of the
 // packed 32 x 32 product, whose block-diagonal entries are scattered into Akk (fp32) and Aqk (bf16).
-// Thread (d, h2) owns channel d of rows 32 h2 .. 32 h2 + 31; for s <= 32 those rows hold whole blocks.
-// One copy of this body serves all six levels (LS at run time, rows unrolled): the kernel's code must
-// stay small enough for the instruction cache with two CTAs per SM.
+// Thread (cp, q4) owns channels 2 cp, 2 cp + 1 of rows 16 q4 .. 16 q4 + 15 (one quarter); blocks of 16
+// rows or fewer lie inside a quarter, and the coarser two take their starting products from the
+// quarters' published first alphas (af) and products of the other fifteen (ar).  One copy of this body
+// serves all six levels (LS at run time, rows unrolled): the kernel's code must stay small enough for the
+// instruction cache with two CTAs per SM.
 __device__ __forceinline__ void bisection_level(int LS, uint8_t *base, uint32_t sb, float *Af,
-                                                const uint32_t (&bk2)[16], const float (&alpha)[32], float a32,
-                                                float scale, int d, int h2, int warp, int lane) {
+                                                const uint32_t (&bk2)[16], const float (&alpha)[32],
+                                                const float *af, const float *ar, float scale, int cp, int q4,
+                                                int warp, int lane) {
     const int s = 1 << LS, half = s >> 1, lh = LS - 1;
     uint8_t *Rkk = base + A_RKK, *Rqk = base + A_RQK, *Cc = base + A_CC;
-    auto bk = [&](int i) { return (i & 1) ? ptx::bf16hi(bk2[i / 2]) : ptx::bf16lo(bk2[i / 2]); };
-    auto row_side = [&](int i, int m, float P) {
-        st_bf16(Rkk + 2 * (m * kOP + d), bk(i) * P);
-        st_bf16(Rqk + 2 * (m * kOP + d), qk_tile(base, 0, 32 * h2 + i, d) * P);
+    const int ch = 2 * cp;
+    auto tile2 = [&](int which, int i) -> uint32_t {  // q (0) or k (1) of row 16 q4 + i, channels ch, ch + 1
+        return *reinterpret_cast<const uint32_t *>(base + A_QKT + 16384 * which + (uint32_t)(ch >> 6) * 8192u +
+                                                   ptx::sw128(16 * q4 + i, ch & 63));
     };
-    auto col_side = [&](int i, int n, float Pb) { st_bf16(Cc + 2 * (n * kOP + d), qk_tile(base, 1, 32 * h2 + i, d) * Pb); };
-    // Position of row 32 h2 + i inside its block; at the top level (s = 64) the half decides the side.
-    const int hoff = (LS == 6) ? 32 * h2 : 0, pbase = (LS == 6) ? 0 : 16 * h2;
-    float P = 1.f;
+    auto put = [&](uint8_t *buf, int row, float x0, float x1) {
+        *reinterpret_cast<uint32_t *>(buf + 2 * (row * kOP + ch)) = ptx::pack_bf16(x0, x1);
+    };
+    // Which side this quarter's rows are on, where their packed index starts, and the starting products.
+    bool all_row = false, all_col = false;
+    float P0[2] = {1.f, 1.f}, Pb0[2] = {0.f, 0.f};
+    int mbase = 8 * q4;
+    if (LS == 6) {
+        all_row = q4 >= 2;
+        all_col = !all_row;
+        mbase = 16 * (q4 & 1);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        const int pos = (hoff + i) & (s - 1);
-        if (pos >= half) {
-            P = (pos == half) ? 1.f : P * alpha[i];
-            row_side(i, pbase + ((i >> LS) << lh) + (pos - half), P);
+        for (int c = 0; c < 2; ++c) {
+            P0[c] = (q4 == 3) ? ar[2 * 128 + ch + c] * alpha[c] : 1.f;  // product of alphas 33 .. 48
+            Pb0[c] = (q4 == 1) ? af[2 * 128 + ch + c]                   // alpha 32
+                               : af[128 + ch + c] * ar[128 + ch + c] * af[2 * 128 + ch + c];  // alphas 16 .. 32
+        }
+    } else if (LS == 5) {
+        all_row = (q4 & 1) != 0;
+        all_col = !all_row;
+        mbase = 16 * (q4 >> 1);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) Pb0[c] = af[(q4 + 1 < 4 ? q4 + 1 : 3) * 128 + ch + c];  // alpha of the next quarter's first row
+    }
+    float P[2] = {1.f, 1.f};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int pos = i & (s - 1);
+        const bool rs = all_row || (!all_col && pos >= half);
+        if (rs) {
+            const bool start = all_row ? (i == 0) : (pos == half);
+            const int m = all_row ? mbase + i : mbase + ((i >> LS) << lh) + (pos - half);
+            const uint32_t b2 = bk2[i], q2 = tile2(0, i);
+#pragma unroll
+            for (int c = 0; c < 2; ++c) P[c] = start ? (all_row ? P0[c] : 1.f) : P[c] * alpha[2 * i + c];
+            put(Rkk, m, ptx::bf16lo(b2) * P[0], ptx::bf16hi(b2) * P[1]);
+            put(Rqk, m, ptx::bf16lo(q2) * P[0], ptx::bf16hi(q2) * P[1]);
         }
     }
-    float Pb = 1.f;
+    float Pb[2] = {1.f, 1.f};
 #pragma unroll
-    for (int i = 31; i >= 0; --i) {
-        const int pos = (hoff + i) & (s - 1);
-        if (pos < half) {
-            const float an = (i == 31) ? a32 : alpha[i + 1 < 32 ? i + 1 : 31];  // alpha of row t + 1
-            Pb = (pos == half - 1) ? an : Pb * an;
-            col_side(i, pbase + ((i >> LS) << lh) + pos, Pb);
+    for (int i = 15; i >= 0; --i) {
+        const int pos = i & (s - 1);
+        const bool cs = all_col || (!all_row && pos < half);
+        if (cs) {
+            const bool start = all_col ? (i == 15) : (pos == half - 1);
+            const int n = all_col ? mbase + i : mbase + ((i >> LS) << lh) + pos;
+            const uint32_t k2 = tile2(1, i);
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const float an = alpha[2 * (i + 1 < 16 ? i + 1 : 15) + c];  // alpha of the next row (in quarter)
+                Pb[c] = start ? (all_col ? Pb0[c] : an) : Pb[c] * an;
+            }
+            put(Cc, n, ptx::bf16lo(k2) * Pb[0], ptx::bf16hi(k2) * Pb[1]);
         }
     }
     ptx::named_sync(tc::NB_PAR, kThreadsA);
@@ -235,57 +273,84 @@ __global__ void __launch_bounds__(kThreadsA, 2)
     }
     for (int i = tid; i < 512; i += kThreadsA) ptx::st_shared_v4(sb + A_AQK + 16 * i, 0u, 0u, 0u, 0u);
 
-    // One key / value channel per thread, half the chunk's rows each.
-    const int d = tid & 127, h2 = tid >> 7;
+    // Two adjacent key / value channels per thread, a quarter of the chunk's rows each.
+    const int cp = tid & 63, q4 = tid >> 6, ch = 2 * cp;
     const __nv_bfloat16 *vg = static_cast<const __nv_bfloat16 *>(p.v);
     auto rowidx = [&](int t) -> int64_t { return (b * p.seq + row0 + t) * p.heads + h; };
-    auto gate = [&](const void *ptr, int w, int64_t r) -> float {  // inputs are read-only for the kernel
-        const TG *g = static_cast<const TG *>(ptr) + r * w + (w == 1 ? 0 : d);
-        if constexpr (sizeof(TG) == 4)
-            return __ldg(reinterpret_cast<const float *>(g));
-        else
-            return __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16 *>(g)));
+    auto gate2 = [&](const void *ptr, int w, int64_t r, float &x0, float &x1) {  // inputs are read-only here
+        const TG *g = static_cast<const TG *>(ptr) + r * w + (w == 1 ? 0 : ch);
+        if (w == 1) {
+            x0 = x1 = (sizeof(TG) == 4) ? __ldg(reinterpret_cast<const float *>(g))
+                                        : __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16 *>(g)));
+        } else if constexpr (sizeof(TG) == 4) {
+            const float2 v2 = __ldg(reinterpret_cast<const float2 *>(g));
+            x0 = v2.x;
+            x1 = v2.y;
+        } else {
+            const __nv_bfloat162 v2 = __ldg(reinterpret_cast<const __nv_bfloat162 *>(g));
+            x0 = __low2float(v2);
+            x1 = __high2float(v2);
+        }
     };
+    float *Xg = X, *Xaf = X + 512, *Xar = X + 1024;  // [quarter][channel]
 
     DC_SPLIT_MARK(0);
-    // ---- (0) this half's g (all loads in flight at once) and its sum: the chunk-local offsets of G ----
-    float alpha[32];  // g until the scan below turns it into e^g
+    // ---- (0) this quarter's g (all loads in flight at once) and its sum: the chunk-local offsets of G ----
+    float alpha[32];  // [row][channel]; g until the scan turns it into e^g
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        const int t = 32 * h2 + i;
-        alpha[i] = (p.gw > 0 && t < nvalid) ? gate(p.g, p.gw, rowidx(t)) : 0.f;
+    for (int i = 0; i < 16; ++i) {
+        const int t = 16 * q4 + i;
+        alpha[2 * i] = alpha[2 * i + 1] = 0.f;
+        if (p.gw > 0 && t < nvalid) gate2(p.g, p.gw, rowidx(t), alpha[2 * i], alpha[2 * i + 1]);
     }
-    float gsum = 0.f;
+    {
+        float gs0 = 0.f, gs1 = 0.f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) gsum += alpha[i];
-    X[h2 * 128 + d] = gsum;
+        for (int i = 0; i < 16; ++i) {
+            gs0 += alpha[2 * i];
+            gs1 += alpha[2 * i + 1];
+        }
+        Xg[q4 * 128 + ch] = gs0;
+        Xg[q4 * 128 + ch + 1] = gs1;
+    }
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_ptr;
-    const float G63 = X[d] + X[128 + d];
-    float G = h2 ? X[d] : 0.f;
+    float G[2], G63[2];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        float before = 0.f, all = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float x = Xg[q * 128 + ch + c];
+            if (q < q4) before += x;
+            all += x;
+        }
+        G[c] = before;
+        G63[c] = all;
+    }
     DC_SPLIT_MARK(1);
 
     // ---- (1) the scan: G, alpha = e^g, and per row v w, b k e^G, s q e^G (parked in the workspace),
     //      Kh (to the workspace) and b k (for the bisection).  erase, write (when per channel) and v
-    //      stream through a three-buffer shared-memory ring by cp.async, 8 rows of each half per batch,
+    //      stream through a three-buffer shared-memory ring by cp.async, 4 rows of each quarter per batch,
     //      two batches ahead; q and k come from the TMA tiles.  The batch loop is not unrolled (the
     //      kernel's code must fit the instruction cache), so alpha and bk2 are rotating windows whose
     //      first slots always hold the current batch. ----
     const bool tiles_ok = ptx::mbar_wait(&bars[BA_QK], 0);
     constexpr int kRowB = 128 * (int)sizeof(TG);  // bytes of one full-width gate row
     const bool e_full = p.ew != 1, w_full = p.ww != 1;
-    const int64_t r_first = rowidx(32 * h2), r_step = p.heads;  // rows of this half are r_first + i * r_step
-    __nv_bfloat16 *park_v = ws.a6 + bhc * 128 * 128 + (32 * h2) * 128 + d;   // rows 0-63: v w
-    __nv_bfloat16 *park_k = park_v + 64 * 128;                                 // rows 64-127: b k e^G
-    __nv_bfloat16 *park_q = ws.y0 + bhc * 64 * 128 + (32 * h2) * 128 + d;     // s q e^G
-    __nv_bfloat16 *kh_out = ws.kh + (bhc * 64 + 32 * h2) * 128 + d;
-    auto stage = [&](int k) {  // batch k: rows 8k..8k+7 of each half -> slots 0-7 (half 0), 8-15 (half 1)
+    const int64_t r_first = rowidx(16 * q4), r_step = p.heads;  // rows of this quarter: r_first + i * r_step
+    uint32_t *park_v = reinterpret_cast<uint32_t *>(ws.a6 + bhc * 128 * 128 + (16 * q4) * 128 + ch);  // v w
+    uint32_t *park_k = park_v + 64 * 64;                                                          // b k e^G
+    uint32_t *park_q = reinterpret_cast<uint32_t *>(ws.y0 + bhc * 64 * 128 + (16 * q4) * 128 + ch);  // s q e^G
+    uint32_t *kh_out = reinterpret_cast<uint32_t *>(ws.kh + (bhc * 64 + 16 * q4) * 128 + ch);
+    auto stage = [&](int k) {  // batch k: rows 4k..4k+3 of each quarter -> slots 4 q + 0..3
         const uint32_t buf = sb + A_STG + (uint32_t)(k % 3) * kStgBytes;
         for (int q = tid; q < 16 * (kRowB / 16); q += kThreadsA) {
             const int slot = q / (kRowB / 16), piece = q % (kRowB / 16);
-            const int t = (slot < 8 ? 0 : 32) + 8 * k + (slot & 7);
+            const int t = 16 * (slot >> 2) + 4 * k + (slot & 3);
             const int64_t r = t < nvalid ? rowidx(t) : 0;
             const uint32_t n = t < nvalid ? 16u : 0u;
             if (e_full)
@@ -297,13 +362,13 @@ __global__ void __launch_bounds__(kThreadsA, 2)
         }
         {
             const int slot = tid >> 4, piece = tid & 15;
-            const int t = (slot < 8 ? 0 : 32) + 8 * k + (slot & 7);
+            const int t = 16 * (slot >> 2) + 4 * k + (slot & 3);
             const int64_t r = t < nvalid ? rowidx(t) : 0;
             ptx::cp_async16(buf + 16384 + slot * 256 + piece * 16, vg + r * 128 + piece * 8, t < nvalid ? 16u : 0u);
         }
         ptx::cp_async_commit();
     };
-    uint32_t bk2[16];  // bf16 pairs of consecutive rows of (b k), rotating with alpha
+    uint32_t bk2[16];  // per row, (b k) of the two channels as a bf16 pair; rotates with alpha
     stage(0);
     stage(1);
 #pragma unroll 1
@@ -315,26 +380,53 @@ __global__ void __launch_bounds__(kThreadsA, 2)
         ptx::cp_async_wait<2>();
         ptx::named_sync(tc::NB_PAR, kThreadsA);  // every thread's copies of batch k have landed
         const uint8_t *buf = base + A_STG + (k % 3) * kStgBytes;
-        const TG *se = reinterpret_cast<const TG *>(buf) + (8 * h2) * 128;
-        const TG *sw = reinterpret_cast<const TG *>(buf + 8192) + (8 * h2) * 128;
-        const __nv_bfloat16 *sv = reinterpret_cast<const __nv_bfloat16 *>(buf + 16384) + (8 * h2) * 128 + d;
-        float bkx[8];
+        const TG *se = reinterpret_cast<const TG *>(buf) + (4 * q4) * 128 + ch;
+        const TG *sw = reinterpret_cast<const TG *>(buf + 8192) + (4 * q4) * 128 + ch;
+        const uint32_t *sv = reinterpret_cast<const uint32_t *>(buf + 16384 + (4 * q4) * 256 + 2 * ch);
+        uint32_t bkw[4];
 #pragma unroll
-        for (int o = 0; o < 8; ++o) {
-            const int i = 8 * k + o, t = 32 * h2 + i;
+        for (int o = 0; o < 4; ++o) {
+            const int i = 4 * k + o, t = 16 * q4 + i;
             const bool ok_row = t < nvalid;
-            const float ex = e_full ? ld(se + o * 128 + d) : (ok_row ? gate(p.erase, 1, r_first + i * r_step) : 0.f);
-            const float wx = w_full ? ld(sw + o * 128 + d) : (ok_row ? gate(p.write, 1, r_first + i * r_step) : 0.f);
-            const float vx = __bfloat162float(sv[o * 128]);
-            const float qx = qk_tile(base, 0, t, d), kx = qk_tile(base, 1, t, d);
-            G += alpha[o];
-            alpha[o] = __expf(alpha[o]);
-            const float gam = __expf(G);
-            park_v[i * 128] = __float2bfloat16_rn(vx * wx);
-            park_k[i * 128] = __float2bfloat16_rn(ex * kx * gam);
-            park_q[i * 128] = __float2bfloat16_rn(scale * qx * gam);
-            kh_out[i * 128] = __float2bfloat16_rn(kx * __expf(G63 - G));
-            bkx[o] = ex * kx;
+            float ex[2], wx[2];
+            if (e_full) {
+                ex[0] = ld(se + o * 128);
+                ex[1] = ld(se + o * 128 + 1);
+            } else {
+                ex[0] = ex[1] = 0.f;
+                if (ok_row) gate2(p.erase, 1, r_first + i * r_step, ex[0], ex[1]);
+            }
+            if (w_full) {
+                wx[0] = ld(sw + o * 128);
+                wx[1] = ld(sw + o * 128 + 1);
+            } else {
+                wx[0] = wx[1] = 0.f;
+                if (ok_row) gate2(p.write, 1, r_first + i * r_step, wx[0], wx[1]);
+            }
+            const uint32_t v2 = sv[o * 64];
+            const uint32_t q2 = *reinterpret_cast<const uint32_t *>(base + A_QKT + (uint32_t)(ch >> 6) * 8192u +
+                                                                    ptx::sw128(t, ch & 63));
+            const uint32_t k2 = *reinterpret_cast<const uint32_t *>(base + A_QKT + 16384 + (uint32_t)(ch >> 6) * 8192u +
+                                                                    ptx::sw128(t, ch & 63));
+            const float vx[2] = {ptx::bf16lo(v2), ptx::bf16hi(v2)}, qx[2] = {ptx::bf16lo(q2), ptx::bf16hi(q2)};
+            const float kx[2] = {ptx::bf16lo(k2), ptx::bf16hi(k2)};
+            float vw[2], kg[2], qg[2], kh[2], bk[2];
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                G[c] += alpha[2 * o + c];
+                alpha[2 * o + c] = __expf(alpha[2 * o + c]);
+                const float gam = __expf(G[c]);
+                vw[c] = vx[c] * wx[c];
+                kg[c] = ex[c] * kx[c] * gam;
+                qg[c] = scale * qx[c] * gam;
+                kh[c] = kx[c] * __expf(G63[c] - G[c]);
+                bk[c] = ex[c] * kx[c];
+            }
+            park_v[i * 64] = ptx::pack_bf16(vw[0], vw[1]);
+            park_k[i * 64] = ptx::pack_bf16(kg[0], kg[1]);
+            park_q[i * 64] = ptx::pack_bf16(qg[0], qg[1]);
+            kh_out[i * 64] = ptx::pack_bf16(kh[0], kh[1]);
+            bkw[o] = ptx::pack_bf16(bk[0], bk[1]);
         }
         // rotate: the processed batch moves to the back of both windows
         float a8[8];
@@ -347,12 +439,23 @@ __global__ void __launch_bounds__(kThreadsA, 2)
 #pragma unroll
         for (int j = 0; j < 12; ++j) bk2[j] = bk2[j + 4];
 #pragma unroll
-        for (int o = 0; o < 8; o += 2) bk2[12 + o / 2] = ptx::pack_bf16(bkx[o], bkx[o + 1]);
+        for (int o = 0; o < 4; ++o) bk2[12 + o] = bkw[o];
         ptx::named_sync(tc::NB_PAR, kThreadsA);  // batch k's buffer is free for batch k + 3
     }
-    if (h2 == 0) ws.gam[bhc * 128 + d] = __expf(G63);
-    if (h2 == 1) X[256 + d] = alpha[0];  // alpha of row 32, the reference of the top level
-    fence_async_global();                 // the parked rows are read back by TMA
+    if (q4 == 0) {
+        ws.gam[bhc * 128 + ch] = __expf(G63[0]);
+        ws.gam[bhc * 128 + ch + 1] = __expf(G63[1]);
+    }
+    // Publish this quarter's first alpha and the product of its other fifteen (the coarse levels' starts).
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        float rest = 1.f;
+#pragma unroll
+        for (int i = 1; i < 16; ++i) rest *= alpha[2 * i + c];
+        Xaf[q4 * 128 + ch + c] = alpha[c];
+        Xar[q4 * 128 + ch + c] = rest;
+    }
+    fence_async_global();  // the parked rows are read back by TMA
     if (!tiles_ok) *flag = 1;
     // Aqk's diagonal: row t's q.k from the tiles, 32 channels per thread, four threads per row.
     {
@@ -372,13 +475,12 @@ __global__ void __launch_bounds__(kThreadsA, 2)
         acc += __shfl_xor_sync(0xffffffffu, acc, 2);
         if (part == 0) st_bf16(base + A_AQK + ptx::sw128(t, t), scale * acc);
     }
-    const float a32 = X[256 + d];
     ptx::named_sync(tc::NB_PAR, kThreadsA);
     DC_SPLIT_MARK(2);
 
     // ---- (2) Akk (strictly lower) and Aqk (lower) by bisection levels, coarsest first ----
 #pragma unroll 1
-    for (int LS = 6; LS >= 1; --LS) bisection_level(LS, base, sb, Af, bk2, alpha, a32, scale, d, h2, warp, lane);
+    for (int LS = 6; LS >= 1; --LS) bisection_level(LS, base, sb, Af, bk2, alpha, Xaf, Xar, scale, cp, q4, warp, lane);
     // The level operands are dead: bring s q e^G back into their place.
     if (tid == 0) {
         ptx::mbar_arrive_expect_tx(&bars[BA_QT], 16384);

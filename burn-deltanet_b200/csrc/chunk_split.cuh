@@ -87,8 +87,9 @@ constexpr uint32_t A_STG = A_AF;         // erase / write / v rows staged by cp.
 constexpr uint32_t kStgBytes = 16 * 512 + 16 * 512 + 16 * 256;  // [16 rows] of e, w (up to fp32), v bf16
 constexpr uint32_t A_AQK = 94208;        // Aqk bf16 64x64, K-major SW128 [P2-P6]
 constexpr uint32_t A_X = A_AQK + 8192;   // exchange: fp32 [3][4][128] (per quarter: sum of g, first alpha,
-                                         //   product of the other fifteen alphas)
-constexpr uint32_t A_BAR = A_X + 1536 * 4;  // five mbarriers, TMEM pointer, flag
+                                         //   product of the other fifteen alphas), then [4][2][48] partial
+                                         //   sums of the two finest levels
+constexpr uint32_t A_BAR = A_X + 1920 * 4;  // five mbarriers, TMEM pointer, flag
 constexpr uint32_t A_USED = A_BAR + 48;
 constexpr uint32_t kSmemA = A_USED + 1024;
 enum BarA { BA_P = 0, BA_BIG, BA_QK, BA_QT, BA_BOP };
@@ -228,6 +229,95 @@ __device__ __forceinline__ void bisection_level(int LS, uint8_t *base, uint32_t 
         }
     }
     ptx::named_sync(tc::NB_PAR, kThreadsA);
+}
+
+// After the call, v[0] of lane l holds the sum over the warp's lanes of v[l] (32 values, 31 shuffles).
+__device__ __forceinline__ void reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+    for (int w = 16; w >= 1; w >>= 1) {
+        const bool upper = (lane & w) != 0;
+#pragma unroll
+        for (int i = 0; i < w; ++i) {
+            const float send = upper ? v[i] : v[i + w];
+            const float keep = upper ? v[i + w] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+        }
+    }
+}
+
+// The two finest bisection levels (blocks of 2 and 4 rows) without the MMA machinery: each thread forms its
+// quarter's 8 + 16 pairs per matrix for its two channels (at most three alpha factors each), the warp sums
+// them over its 64 channels in registers, and the quarter's two warps add up through shared memory.
+// Element e of the 48: Akk (e < 24) or Aqk, pair u = e mod 24: u < 8 the 2-block pair (2u+1, 2u), else the
+// 4-block b = (u - 8) / 4 pair (4b + 2 + p/2, 4b + p mod 2), p = (u - 8) mod 4.
+__device__ __forceinline__ void finest_levels(uint8_t *base, float *Af, float *Xr, const uint32_t (&bk2)[16],
+                                              const float (&alpha)[32], float scale, int cp, int q4, int tid,
+                                              int lane) {
+    const int ch = 2 * cp;
+    auto tile2 = [&](int which, int i) -> uint32_t {
+        return *reinterpret_cast<const uint32_t *>(base + A_QKT + 16384 * which + (uint32_t)(ch >> 6) * 8192u +
+                                                   ptx::sw128(16 * q4 + i, ch & 63));
+    };
+    float v[48];
+#pragma unroll
+    for (int e = 0; e < 48; ++e) v[e] = 0.f;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        auto a = [&](int i) { return alpha[2 * i + c]; };
+        auto half_of = [&](uint32_t w) { return c ? ptx::bf16hi(w) : ptx::bf16lo(w); };
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {  // 2-blocks: (2m + 1, 2m)
+            const float kj = half_of(tile2(1, 2 * m)) * a(2 * m + 1);
+            v[m] += half_of(bk2[2 * m + 1]) * kj;
+            v[24 + m] += half_of(tile2(0, 2 * m + 1)) * kj;
+        }
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {  // 4-blocks: rows 4bb + {2, 3} with 4bb + {0, 1}
+            const int r0 = 4 * bb;
+            const float a1 = a(r0 + 1), a2 = a(r0 + 2), a3 = a(r0 + 3);
+            const float k0 = half_of(tile2(1, r0)), k1 = half_of(tile2(1, r0 + 1));
+            const float dec[4] = {a1 * a2, a2, a1 * a2 * a3, a2 * a3};  // (2,0), (2,1), (3,0), (3,1)
+#pragma unroll
+            for (int pp = 0; pp < 4; ++pp) {
+                const int i = r0 + 2 + (pp >> 1);
+                const float kd = ((pp & 1) ? k1 : k0) * dec[pp];
+                v[8 + 4 * bb + pp] += half_of(bk2[i]) * kd;
+                v[24 + 8 + 4 * bb + pp] += half_of(tile2(0, i)) * kd;
+            }
+        }
+    }
+    // Sum over the warp's lanes: elements 0-31 by a full reduce-scatter, 32-47 by a half one.
+    float lo[32], hi[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) lo[e] = v[e];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) hi[e] = (e < 16) ? v[32 + e] : 0.f;
+    reduce_scatter32(lo, lane);
+    reduce_scatter32(hi, lane);
+    const int wh = cp >> 5;  // which of the quarter's two warps
+    Xr[(q4 * 2 + wh) * 48 + lane] = lo[0];
+    if (lane < 16) Xr[(q4 * 2 + wh) * 48 + 32 + lane] = hi[0];
+    ptx::named_sync(tc::NB_PAR, kThreadsA);
+    if (cp < 48) {
+        const int e = cp, u = e % 24;
+        const float sum = Xr[(q4 * 2) * 48 + e] + Xr[(q4 * 2 + 1) * 48 + e];
+        int i, j;
+        if (u < 8) {
+            i = 2 * u + 1;
+            j = 2 * u;
+        } else {
+            const int bb = (u - 8) >> 2, pp = (u - 8) & 3;
+            i = 4 * bb + 2 + (pp >> 1);
+            j = 4 * bb + (pp & 1);
+        }
+        i += 16 * q4;
+        j += 16 * q4;
+        if (e < 24)
+            Af[i * kAP + j] = sum;
+        else
+            st_bf16(base + A_AQK + ptx::sw128(i, j), scale * sum);
+    }
+    (void)tid;
 }
 
 template <typename TG>
@@ -480,7 +570,9 @@ __global__ void __launch_bounds__(kThreadsA, 2)
 
     // ---- (2) Akk (strictly lower) and Aqk (lower) by bisection levels, coarsest first ----
 #pragma unroll 1
-    for (int LS = 6; LS >= 1; --LS) bisection_level(LS, base, sb, Af, bk2, alpha, Xaf, Xar, scale, cp, q4, warp, lane);
+    for (int LS = 6; LS >= 3; --LS) bisection_level(LS, base, sb, Af, bk2, alpha, Xaf, Xar, scale, cp, q4, warp, lane);
+    finest_levels(base, Af, X + 1536, bk2, alpha, scale, cp, q4, tid, lane);
+    ptx::named_sync(tc::NB_PAR, kThreadsA);
     // The level operands are dead: bring s q e^G back into their place.
     if (tid == 0) {
         ptx::mbar_arrive_expect_tx(&bars[BA_QT], 16384);

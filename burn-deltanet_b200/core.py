@@ -219,7 +219,7 @@ def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_b
 
 
 def delta_step(q_bhk, k_bhk, v_bhv, erase_bhK, write_bhV, g_bhK, state_bhkv, scale: float, *,
-               n_householder: int = 1, out_dtype: Optional[torch.dtype] = None,
+               n_householder: int = 1, out_dtype: Optional[torch.dtype] = None, force_simt: bool = False,
                y_out: Optional[torch.Tensor] = None, state_out: Optional[torch.Tensor] = None):
     """One delta-rule tick for all heads (src/delta/recurrent.rs:41-99).
 
@@ -265,7 +265,7 @@ def delta_step(q_bhk, k_bhk, v_bhv, erase_bhK, write_bhV, g_bhK, state_bhkv, sca
     a.erase_w, a.write_w = e4.shape[3], w4.shape[3]
     a.g_w = 0 if g_bhK is None else g_bhK.shape[2]
     a.in_dtype, a.gate_dtype, a.out_dtype = in_dt, gate_dt, _dtype_code(y, "y")
-    a.flags = 0
+    a.flags = _abi.DC_FLAG_FORCE_SIMT if force_simt else 0  # the per-tile kernel instead of the streaming one
     a.scale = float(scale)
     a.q, a.k, a.v = q_bhk.data_ptr(), k_bhk.data_ptr(), v_bhv.data_ptr()
     a.erase, a.write = erase_bhK.data_ptr(), write_bhV.data_ptr()

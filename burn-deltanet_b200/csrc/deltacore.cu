@@ -19,6 +19,7 @@
 #include "chunk_tc.cuh"
 #include "common.cuh"
 #include "step.cuh"
+#include "step_stream.cuh"
 
 namespace {
 
@@ -107,8 +108,49 @@ int launch_step_cfg(const dc::CoreParams &p, cudaStream_t stream) {
     return e == cudaSuccess ? DC_OK : cuda_fail(e);
 }
 
+// Multiprocessors of the current device (cached per device).
+int sm_count() {
+    static int count[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!count[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        count[dev] = n;
+    }
+    return count[dev];
+}
+
+// Whether the streaming decode kernel serves this tick: one micro-step, dk = dv = 128, 16-byte-aligned rows.
+bool stream_applies(const dc::CoreParams &p, size_t in_size, size_t gate_size) {
+    if (p.u != 1 || p.dk != 128 || p.dv != 128) return false;
+    if (!aligned(p.state_in, 16) || !aligned(p.state_out, 16) || !aligned(p.q, 16) || !aligned(p.k, 16) ||
+        !aligned(p.v, 16))
+        return false;
+    if ((p.ew != 1 && !aligned(p.erase, 16)) || (p.ww != 1 && !aligned(p.write, 16)) || (p.gw > 1 && !aligned(p.g, 16)))
+        return false;
+    (void)in_size;
+    (void)gate_size;
+    return true;
+}
+
 template <typename TI, typename TG, typename TO>
-int launch_step_typed(const dc::CoreParams &p, cudaStream_t stream) {
+int launch_step_stream(const dc::CoreParams &p, cudaStream_t stream) {
+    int *status = dc::device_status_ptr();
+    if (!status) return cuda_fail(cudaErrorInvalidSymbol);
+    auto kern = dc::stream::step_stream_kernel<TI, TG, TO>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dc::stream::kSmem);
+    if (e != cudaSuccess) return cuda_fail(e);
+    const int64_t bh = p.batch * p.heads;
+    const unsigned grid = (unsigned)(bh < sm_count() ? bh : sm_count());
+    kern<<<grid, dc::stream::kThreads, dc::stream::kSmem, stream>>>(p, status);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? DC_OK : cuda_fail(e);
+}
+
+template <typename TI, typename TG, typename TO>
+int launch_step_typed(const dc::CoreParams &p, cudaStream_t stream, bool allow_stream = true) {
+    if (allow_stream && stream_applies(p, sizeof(TI), sizeof(TG))) return launch_step_stream<TI, TG, TO>(p, stream);
     const bool vec4 = (p.dv % 4 == 0) && aligned(p.state_in, 16) && aligned(p.state_out, 16);
     if (vec4) {
         if (p.dk <= 128) return launch_step_cfg<TI, TG, TO, 4, 64, 16>(p, stream);
@@ -138,7 +180,9 @@ int dispatch_types(int32_t in_dt, int32_t gate_dt, int32_t out_dt, A &&...args) 
 
 template <typename TI, typename TG, typename TO>
 struct StepLauncher {
-    static int run(const dc::CoreParams &p, cudaStream_t s) { return launch_step_typed<TI, TG, TO>(p, s); }
+    static int run(const dc::CoreParams &p, cudaStream_t s, bool allow_stream) {
+        return launch_step_typed<TI, TG, TO>(p, s, allow_stream);
+    }
 };
 
 // ---------------------------------------------------------------------------
@@ -281,7 +325,7 @@ static int run_recurrent(const dc_chunk_args *a, cudaStream_t s) {
                                        a->state_out);
         p.kv_bstride = a->seq * u;
         p.q_bstride = a->seq;
-        const int st = dispatch_types<StepLauncher>(a->in_dtype, a->gate_dtype, a->out_dtype, p, s);
+        const int st = dispatch_types<StepLauncher>(a->in_dtype, a->gate_dtype, a->out_dtype, p, s, true);
         if (st != DC_OK) return st;
     }
     return DC_OK;
@@ -376,7 +420,7 @@ int dc_step(const dc_step_args *a, dc_stream_t stream) {
                                          a->write_w, a->g_w, a->scale, a->q, a->k, a->v, a->erase, a->write, a->g,
                                          a->state_in, a->y, a->state_out);
     return dispatch_types<StepLauncher>(a->in_dtype, a->gate_dtype, a->out_dtype, p,
-                                        reinterpret_cast<cudaStream_t>(stream));
+                                        reinterpret_cast<cudaStream_t>(stream), (a->flags & DC_FLAG_FORCE_SIMT) == 0);
 }
 
 }  // extern "C"

@@ -107,6 +107,21 @@ __device__ __forceinline__ void tma_store_4d(const void *tmap, uint32_t src, int
                  : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Contiguous copy global -> this CTA's shared memory (bytes a multiple of 16, both addresses 16-byte aligned),
+// completing on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst), "l"(src),
+        "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+// Contiguous copy shared -> global in the thread's bulk async-group.
+__device__ __forceinline__ void bulk_store(void *dst, uint32_t src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+                 : "memory");
+}
+// Every committed bulk store of this thread has finished reading its shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // Every committed bulk store of this thread has written global memory.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 

@@ -82,7 +82,8 @@ enum dc_dtype {
 };
 
 /* dc_chunk_args.flags */
-#define DC_FLAG_FORCE_SIMT 0x1u /* run the CUDA-core chunk kernel even where the tensor-core one applies */
+#define DC_FLAG_FORCE_SIMT 0x1u /* dc_chunk_fwd: the CUDA-core chunk kernel even where a tensor-core one applies;
+                                   dc_step: the per-tile kernel even where the streaming one applies */
 #define DC_FLAG_RECURRENT 0x2u  /* DeltaPath::Recurrent: walk the sequence token by token with the fused
                                    decode tick (one launch per token, state updated in state_out) */
 #define DC_FLAG_FORCE_SPLIT 0x4u /* take the two-kernel (workspace) tensor-core path even for per-head gates */

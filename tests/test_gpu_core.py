@@ -20,6 +20,7 @@ from _inputs import config_inputs, constant_raw, random_raw
 
 pytestmark = pytest.mark.gpu
 dn = importlib.import_module("burn-deltanet_b200")
+abi = importlib.import_module("burn-deltanet_b200._abi")
 
 F32_TOL = 1e-4
 
@@ -252,3 +253,34 @@ def test_step_in_place_and_out_of_place_agree():
                           state_out=st2)
     torch.cuda.synchronize()
     assert torch.equal(y0, y1) and torch.equal(s0, st2)
+
+
+@pytest.mark.parametrize("widths,in_dtype,out_dtype", [
+    ((1, 1, 1), torch.bfloat16, torch.float32),
+    ((128, 128, 128), torch.bfloat16, torch.bfloat16),
+    ((1, 128, 0), torch.float32, torch.float32),
+    ((128, 1, 1), torch.float32, torch.bfloat16),
+])
+def test_step_stream_matches_the_per_tile_kernel(widths, in_dtype, out_dtype):
+    """The streaming decode kernel (one CTA per SM walking 256 heads through a three-slot ring) against the
+    per-tile kernel, in place and out of place."""
+    ew, ww, gw = widths
+    rng = np.random.default_rng(15 + ew + gw)
+    b, h, d = 64, 4, 128
+    raw = config_inputs(5, rng, b, 1, h, d, d)
+    raw["erase"], raw["write"] = raw["erase"][..., :ew], raw["write"][..., :ww]
+    raw["g"] = None if gw == 0 else raw["g"][..., :gw]
+    st = to_dev(rng.normal(0, 0.05, (b, h, d, d)))
+    dev = {n: None if raw[n] is None else to_dev(raw[n], in_dtype if n in ("q", "k", "v") else torch.float32)[:, 0]
+           .contiguous() for n in ("q", "k", "v", "erase", "write", "g")}
+    args = (dev["q"], dev["k"], dev["v"], dev["erase"], dev["write"], dev["g"])
+    y0, s0 = dn.delta_step(*args, st, 0.09, out_dtype=out_dtype, force_simt=True)
+    y1, s1 = dn.delta_step(*args, st, 0.09, out_dtype=out_dtype)
+    st2 = st.clone()
+    y2, _ = dn.delta_step(*args, st2, 0.09, out_dtype=out_dtype, state_out=st2)
+    torch.cuda.synchronize()
+    tol = 1e-2 if out_dtype == torch.bfloat16 else 1e-5
+    assert (y0.float() - y1.float()).abs().max().item() < tol
+    assert (s0 - s1).abs().max().item() < 1e-5
+    assert torch.equal(y1, y2) and torch.equal(s1, st2)
+    assert abi.lib().dc_device_status(1) == 0

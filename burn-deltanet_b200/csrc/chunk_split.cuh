@@ -747,46 +747,56 @@ __global__ void __launch_bounds__(kThreadsA, 2)
 }
 
 // ---------------------------------------------------------------- scan kernel
+// One CTA per (batch x head, slice of W = 64 NB value columns): V', y and S restricted to a set of value
+// columns depend only on S's same columns, so the slices of one head run independently (each reads the
+// head's full A6 and Kh, which its sibling slices find in L2).  Narrow slices shorten the per-chunk chain
+// and fill the GPU when there are few heads.
 constexpr int kThreadsB = 128;
-constexpr uint32_t B_A6 = 0;              // A6: two K-major SW128 blocks (channels 0-63, 64-127), 128 rows
-constexpr uint32_t B_KH = 32768;          // Kh: two MN-major SW128 blocks of 64 channels, 64 rows
-constexpr uint32_t B_U = 49152;           // U fp32: four SW128 blocks of 32 columns, 64 rows
-constexpr uint32_t B_Y0 = 81920;          // Y0: two SW128 blocks of 64 columns, 64 rows
-constexpr uint32_t B_VP = 98304;          // V' hi (two 64-column blocks), then lo
-constexpr uint32_t B_S = 131072;          // S bf16, MN-major, two 64-column blocks of 128 rows
-constexpr uint32_t B_Y = 163840;          // y staging for the TMA store (two SW128 boxes)
-constexpr uint32_t B_BAR = 180224;
+template <int NB>
+struct ScanLayout {
+    static constexpr int W = 64 * NB;                           // value columns of the slice
+    static constexpr uint32_t A6 = 0;                           // two K-major SW128 blocks, 128 rows
+    static constexpr uint32_t KH = 32768;                       // two MN-major SW128 blocks, 64 rows
+    static constexpr uint32_t U = KH + 16384;                   // fp32, 2 NB SW128 blocks of 32 columns, 64 rows
+    static constexpr uint32_t Y0 = U + 16384 * NB;              // NB SW128 blocks of 64 columns, 64 rows
+    static constexpr uint32_t VP = Y0 + 8192 * NB;              // V' hi (NB blocks), then lo
+    static constexpr uint32_t S = VP + 16384 * NB;              // S bf16, MN-major, NB blocks of 128 rows
+    static constexpr uint32_t Y = S;                            // y staging (NB SW128 boxes) over S: between
+                                                                //   MMA6's read of S and the tail's rewrite
+    static constexpr uint32_t BAR = S + 16384 * NB;
+    static constexpr uint32_t TMEMPTR = BAR + 8 * 5, FLAG = TMEMPTR + 4, PEND = FLAG + 4;
+    static constexpr uint32_t SMEM = PEND + 12 + 1024;
+    static constexpr uint32_t TM_D = 0, TM_S = W, TM_COLS = 2 * W;  // TMEM: [V'; y] and S
+    static_assert(SMEM <= 232448, "scan kernel over the shared-memory limit");
+};
 enum BarB { BB_A6 = 0, BB_KH, BB_UY, BB_M6, BB_M7, kBarsB };
-constexpr uint32_t B_TMEMPTR = B_BAR + 8 * kBarsB;
-constexpr uint32_t B_FLAG = B_TMEMPTR + 4;
-constexpr uint32_t B_PEND = B_FLAG + 4;  // int[3]: parity of the A6 / Kh / UY load in flight, or -1
-constexpr uint32_t B_USED = B_PEND + 12;
-constexpr uint32_t kSmemB = B_USED + 1024;
-static_assert(kSmemB <= 232448, "scan kernel over the shared-memory limit");
-constexpr uint32_t TMB_D = 0, TMB_S = 128;  // TMEM columns
 
 // Byte offset of 16-byte chunk `chunk` of row `row` in a SW128 tile.
 __device__ __forceinline__ uint32_t sw128c(uint32_t row, uint32_t chunk) {
     return row * 128u + ((chunk ^ (row & 7u)) << 4);
 }
 
-template <typename TO>
+template <typename TO, int NB>
 __global__ void __launch_bounds__(kThreadsB, 1)
     scan_kernel(const __grid_constant__ CUtensorMap tm_a6, const __grid_constant__ CUtensorMap tm_u,
                 const __grid_constant__ CUtensorMap tm_y0, const __grid_constant__ CUtensorMap tm_kh,
                 const __grid_constant__ CUtensorMap tm_y, const CoreParams p, const SplitWs ws, int *status) {
+    using Ly = ScanLayout<NB>;
+    constexpr int W = Ly::W;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);  // stays a shared pointer
     const uint32_t sb = ptx::smem_u32(base);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(base + B_BAR);
-    uint32_t *tmem_ptr = reinterpret_cast<uint32_t *>(base + B_TMEMPTR);
-    volatile int *flag = reinterpret_cast<volatile int *>(base + B_FLAG);
-    volatile int *pend = reinterpret_cast<volatile int *>(base + B_PEND);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(base + Ly::BAR);
+    uint32_t *tmem_ptr = reinterpret_cast<uint32_t *>(base + Ly::TMEMPTR);
+    volatile int *flag = reinterpret_cast<volatile int *>(base + Ly::FLAG);
+    volatile int *pend = reinterpret_cast<volatile int *>(base + Ly::PEND);
     constexpr bool kYTma = sizeof(TO) == 2;
 
     const int tid = threadIdx.x, warp = tid >> 5, r = tid;
     const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-    const int64_t bh = blockIdx.x, b = bh / p.heads, h = bh % p.heads, nch = ws.nch;
+    const int slices = 128 / W;
+    const int64_t bh = blockIdx.x / slices, b = bh / p.heads, h = bh % p.heads, nch = ws.nch;
+    const int col0 = (int)(blockIdx.x % slices) * W;  // first value column of this slice
     const bool leader = tid == 0;
 
     if (leader) {
@@ -801,7 +811,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         if (kYTma) ptx::prefetch_tmap(&tm_y);
     }
     if (warp == 0) {
-        ptx::tmem_alloc(tmem_ptr, 256);
+        ptx::tmem_alloc(tmem_ptr, Ly::TM_COLS);
         ptx::tmem_relinquish();
     }
     ptx::tc_fence_before();
@@ -813,24 +823,24 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         pend[0] = (int)(c & 1);
         ptx::mbar_arrive_expect_tx(&bars[BB_A6], 32768);
         const int row = (int)((bh * nch + c) * 128);
-        tma_load_2d(base + B_A6, &tm_a6, &bars[BB_A6], 0, row);
-        tma_load_2d(base + B_A6 + 16384, &tm_a6, &bars[BB_A6], 64, row);
+        tma_load_2d(base + Ly::A6, &tm_a6, &bars[BB_A6], 0, row);
+        tma_load_2d(base + Ly::A6 + 16384, &tm_a6, &bars[BB_A6], 64, row);
     };
     auto load_kh = [&](int64_t c) {
         pend[1] = (int)(c & 1);
         ptx::mbar_arrive_expect_tx(&bars[BB_KH], 16384);
         const int row = (int)((bh * nch + c) * 64);
-        tma_load_2d(base + B_KH, &tm_kh, &bars[BB_KH], 0, row);
-        tma_load_2d(base + B_KH + 8192, &tm_kh, &bars[BB_KH], 64, row);
+        tma_load_2d(base + Ly::KH, &tm_kh, &bars[BB_KH], 0, row);
+        tma_load_2d(base + Ly::KH + 8192, &tm_kh, &bars[BB_KH], 64, row);
     };
     auto load_uy = [&](int64_t c) {
         pend[2] = (int)(c & 1);
-        ptx::mbar_arrive_expect_tx(&bars[BB_UY], 49152);
+        ptx::mbar_arrive_expect_tx(&bars[BB_UY], 24576 * NB);
         const int row = (int)((bh * nch + c) * 64);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) tma_load_2d(base + B_U + 8192 * j, &tm_u, &bars[BB_UY], 32 * j, row);
-        tma_load_2d(base + B_Y0, &tm_y0, &bars[BB_UY], 0, row);
-        tma_load_2d(base + B_Y0 + 8192, &tm_y0, &bars[BB_UY], 64, row);
+        for (int j = 0; j < 2 * NB; ++j) tma_load_2d(base + Ly::U + 8192 * j, &tm_u, &bars[BB_UY], col0 + 32 * j, row);
+#pragma unroll
+        for (int j = 0; j < NB; ++j) tma_load_2d(base + Ly::Y0 + 8192 * j, &tm_y0, &bars[BB_UY], col0 + 64 * j, row);
     };
     auto role_wait = [&](int bar, uint32_t parity) {
         const bool bad = !ptx::mbar_wait(&bars[bar], parity) || *flag != 0;
@@ -847,12 +857,12 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         load_uy(0);
     }
 
-    // S0 -> TMEM (pre-scaled by chunk 0's decay) and its bf16 copy.
+    // S0 (this slice's columns) -> TMEM (pre-scaled by chunk 0's decay) and its bf16 copy.
     {
         const float g0 = ws.gam[(bh * nch) * 128 + r];
-        const float *src = p.state_in + (bh * 128 + r) * 128;
+        const float *src = p.state_in + (bh * 128 + r) * 128 + col0;
 #pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
+        for (int hh = 0; hh < NB; ++hh) {
 #pragma unroll
             for (int q2 = 0; q2 < 2; ++q2) {
                 uint32_t v[32];
@@ -867,12 +877,12 @@ __global__ void __launch_bounds__(kThreadsB, 1)
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     const float *f = reinterpret_cast<const float *>(v + 8 * q);
-                    ptx::st_shared_v4(sb + B_S + hh * 16384 + ptx::sw128(r, 32 * q2 + 8 * q), ptx::pack_bf16(f[0], f[1]),
+                    ptx::st_shared_v4(sb + Ly::S + hh * 16384 + ptx::sw128(r, 32 * q2 + 8 * q), ptx::pack_bf16(f[0], f[1]),
                                       ptx::pack_bf16(f[2], f[3]), ptx::pack_bf16(f[4], f[5]), ptx::pack_bf16(f[6], f[7]));
                 }
 #pragma unroll
                 for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * g0);
-                ptx::tmem_st32(tmem + lane_base + TMB_S + 64 * hh + 32 * q2, v);
+                ptx::tmem_st32(tmem + lane_base + Ly::TM_S + 64 * hh + 32 * q2, v);
             }
         }
         ptx::tmem_wait_st();
@@ -888,21 +898,20 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         const float gam_next = gnext;
         if (c + 2 < nch) gnext = ws.gam[(bh * nch + c + 2) * 128 + r];
 
-        // ---- D = A6 S ----
+        // ---- D = A6 S[:, slice] ----
         if (leader) {
             if (!ptx::mbar_wait(&bars[BB_A6], par)) {
                 *flag = 1;
             } else {
                 pend[0] = -1;
                 ptx::tc_fence_after();
-                const uint32_t id = ptx::idesc_bf16(128, 128, 0, 1);
+                const uint32_t id = ptx::idesc_bf16(128, W, 0, 1);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    ptx::umma_bf16(tmem + TMB_D, ptx::sdesc(sb + B_A6 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                                   ptx::sdesc(sb + B_S + kk * 2048, 16384, 1024), id, kk > 0);
+                    ptx::umma_bf16(tmem + Ly::TM_D, ptx::sdesc(sb + Ly::A6 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                                   ptx::sdesc(sb + Ly::S + kk * 2048, 16384, 1024), id, kk > 0);
                 ptx::umma_commit(&bars[BB_M6]);
             }
-            if (kYTma) ptx::bulk_wait_all();  // the previous chunk's y tile has been read
         }
         if (!(ok = role_wait(BB_M6, par))) break;
         if (leader && c + 1 < nch) load_a6(c + 1);
@@ -914,18 +923,18 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         {
             const int64_t tok = c * tc::kL + (r - 64);
             const bool write_y = r >= 64 && tok < p.seq;
-            TO *yrow = static_cast<TO *>(p.y) + ((b * p.seq + (write_y ? tok : 0)) * p.heads + h) * 128;
+            TO *yrow = static_cast<TO *>(p.y) + ((b * p.seq + (write_y ? tok : 0)) * p.heads + h) * 128 + col0;
 #pragma unroll 1
-            for (int hh = 0; hh < 2; ++hh) {
+            for (int hh = 0; hh < NB; ++hh) {
                 uint32_t vv[2][32];
-                ptx::tmem_ld32(tmem + lane_base + TMB_D + 64 * hh, vv[0]);
-                ptx::tmem_ld32(tmem + lane_base + TMB_D + 64 * hh + 32, vv[1]);
+                ptx::tmem_ld32(tmem + lane_base + Ly::TM_D + 64 * hh, vv[0]);
+                ptx::tmem_ld32(tmem + lane_base + Ly::TM_D + 64 * hh + 32, vv[1]);
                 ptx::tmem_wait_ld();
 #pragma unroll
                 for (int q2 = 0; q2 < 2; ++q2) {
                     const float *f = reinterpret_cast<const float *>(vv[q2]);
                     if (r < 64) {
-                        const uint32_t ub = sb + B_U + 8192 * (2 * hh + q2);
+                        const uint32_t ub = sb + Ly::U + 8192 * (2 * hh + q2);
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
                             const uint4 u0 = ptx::ld_shared_v4(ub + sw128c(r, 2 * q));
@@ -941,14 +950,14 @@ __global__ void __launch_bounds__(kThreadsB, 1)
                                 lo[e] = ptx::pack_bf16(x[2 * e] - ptx::bf16lo(hi[e]), x[2 * e + 1] - ptx::bf16hi(hi[e]));
                             }
                             const uint32_t off = hh * 8192 + ptx::sw128(r, 32 * q2 + 8 * q);
-                            ptx::st_shared_v4(sb + B_VP + off, hi[0], hi[1], hi[2], hi[3]);
-                            ptx::st_shared_v4(sb + B_VP + 16384 + off, lo[0], lo[1], lo[2], lo[3]);
+                            ptx::st_shared_v4(sb + Ly::VP + off, hi[0], hi[1], hi[2], hi[3]);
+                            ptx::st_shared_v4(sb + Ly::VP + 8192 * NB + off, lo[0], lo[1], lo[2], lo[3]);
                         }
                     } else {
                         float yv[32];
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
-                            const uint4 y0 = ptx::ld_shared_v4(sb + B_Y0 + hh * 8192 + ptx::sw128(r - 64, 32 * q2 + 8 * q));
+                            const uint4 y0 = ptx::ld_shared_v4(sb + Ly::Y0 + hh * 8192 + ptx::sw128(r - 64, 32 * q2 + 8 * q));
                             const uint32_t yw[4] = {y0.x, y0.y, y0.z, y0.w};
 #pragma unroll
                             for (int e = 0; e < 4; ++e) {
@@ -959,7 +968,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
                         if (kYTma) {
 #pragma unroll
                             for (int q = 0; q < 4; ++q)
-                                ptx::st_shared_v4(sb + B_Y + hh * 8192 + ptx::sw128(r - 64, 32 * q2 + 8 * q),
+                                ptx::st_shared_v4(sb + Ly::Y + hh * 8192 + ptx::sw128(r - 64, 32 * q2 + 8 * q),
                                                   ptx::pack_bf16(yv[8 * q], yv[8 * q + 1]),
                                                   ptx::pack_bf16(yv[8 * q + 2], yv[8 * q + 3]),
                                                   ptx::pack_bf16(yv[8 * q + 4], yv[8 * q + 5]),
@@ -976,27 +985,30 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         ptx::named_sync(1, kThreadsB);
         if (leader) {
             if (kYTma) {
-                ptx::tma_store_4d(&tm_y, sb + B_Y, 0, (int)h, (int)(c * tc::kL), (int)b);
-                ptx::tma_store_4d(&tm_y, sb + B_Y + 8192, 64, (int)h, (int)(c * tc::kL), (int)b);
+#pragma unroll
+                for (int j = 0; j < NB; ++j)
+                    ptx::tma_store_4d(&tm_y, sb + Ly::Y + 8192 * j, col0 + 64 * j, (int)h, (int)(c * tc::kL), (int)b);
                 ptx::bulk_commit();
             }
             if (c + 1 < nch) load_uy(c + 1);
         }
 
-        // ---- S <- diag(gam) S + Kh^T (V'hi + V'lo); TMEM S already holds diag(gam) S ----
+        // ---- S[:, slice] <- diag(gam) S + Kh^T (V'hi + V'lo); TMEM S already holds diag(gam) S ----
         if (leader) {
             if (!ptx::mbar_wait(&bars[BB_KH], par)) {
                 *flag = 1;
             } else {
                 pend[1] = -1;
                 ptx::tc_fence_after();
-                const uint32_t id = ptx::idesc_bf16(128, 128, 1, 1);
+                const uint32_t id = ptx::idesc_bf16(128, W, 1, 1);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    ptx::umma_bf16(tmem + TMB_S, ptx::sdesc(sb + B_KH + (kk & 3) * 2048, 8192, 1024),
-                                   ptx::sdesc(sb + B_VP + (kk >= 4 ? 16384 : 0) + (kk & 3) * 2048, 8192, 1024), id, 1);
+                    ptx::umma_bf16(tmem + Ly::TM_S, ptx::sdesc(sb + Ly::KH + (kk & 3) * 2048, 8192, 1024),
+                                   ptx::sdesc(sb + Ly::VP + (kk >= 4 ? 8192 * NB : 0) + (kk & 3) * 2048, 8192, 1024), id,
+                                   1);
                 ptx::umma_commit(&bars[BB_M7]);
             }
+            if (kYTma) ptx::bulk_wait_all();  // the y tile (over S) has been read before the tail rewrites S
         }
         if (!(ok = role_wait(BB_M7, par))) break;
         if (leader && c + 1 < nch) load_kh(c + 1);
@@ -1005,10 +1017,10 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         ptx::tc_fence_after();
         if (c + 1 < nch) {
 #pragma unroll 1
-            for (int hh = 0; hh < 2; ++hh) {
+            for (int hh = 0; hh < NB; ++hh) {
                 uint32_t vv[2][32];
-                ptx::tmem_ld32(tmem + lane_base + TMB_S + 64 * hh, vv[0]);
-                ptx::tmem_ld32(tmem + lane_base + TMB_S + 64 * hh + 32, vv[1]);
+                ptx::tmem_ld32(tmem + lane_base + Ly::TM_S + 64 * hh, vv[0]);
+                ptx::tmem_ld32(tmem + lane_base + Ly::TM_S + 64 * hh + 32, vv[1]);
                 ptx::tmem_wait_ld();
 #pragma unroll
                 for (int q2 = 0; q2 < 2; ++q2) {
@@ -1016,13 +1028,13 @@ __global__ void __launch_bounds__(kThreadsB, 1)
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const float *f = reinterpret_cast<const float *>(v + 8 * q);
-                        ptx::st_shared_v4(sb + B_S + hh * 16384 + ptx::sw128(r, 32 * q2 + 8 * q), ptx::pack_bf16(f[0], f[1]),
+                        ptx::st_shared_v4(sb + Ly::S + hh * 16384 + ptx::sw128(r, 32 * q2 + 8 * q), ptx::pack_bf16(f[0], f[1]),
                                           ptx::pack_bf16(f[2], f[3]), ptx::pack_bf16(f[4], f[5]),
                                           ptx::pack_bf16(f[6], f[7]));
                     }
 #pragma unroll
                     for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * gam_next);
-                    ptx::tmem_st32(tmem + lane_base + TMB_S + 64 * hh + 32 * q2, v);
+                    ptx::tmem_st32(tmem + lane_base + Ly::TM_S + 64 * hh + 32 * q2, v);
                 }
             }
             ptx::tmem_wait_st();
@@ -1030,12 +1042,12 @@ __global__ void __launch_bounds__(kThreadsB, 1)
             ptx::tc_fence_before();
             ptx::named_sync(1, kThreadsB);
         } else {
-            float *dst = p.state_out + (bh * 128 + r) * 128;
+            float *dst = p.state_out + (bh * 128 + r) * 128 + col0;
 #pragma unroll 1
-            for (int hh = 0; hh < 2; ++hh) {
+            for (int hh = 0; hh < NB; ++hh) {
                 uint32_t vv[2][32];
-                ptx::tmem_ld32(tmem + lane_base + TMB_S + 64 * hh, vv[0]);
-                ptx::tmem_ld32(tmem + lane_base + TMB_S + 64 * hh + 32, vv[1]);
+                ptx::tmem_ld32(tmem + lane_base + Ly::TM_S + 64 * hh, vv[0]);
+                ptx::tmem_ld32(tmem + lane_base + Ly::TM_S + 64 * hh + 32, vv[1]);
                 ptx::tmem_wait_ld();
 #pragma unroll
                 for (int q2 = 0; q2 < 2; ++q2)
@@ -1057,7 +1069,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         }
         __syncthreads();
     }
-    if (warp == 0) ptx::tmem_dealloc(tmem, 256);
+    if (warp == 0) ptx::tmem_dealloc(tmem, Ly::TM_COLS);
 }
 
 }  // namespace split
@@ -1136,18 +1148,21 @@ int launch_split_typed(const CoreParams &p, void *workspace, cudaStream_t stream
         g_tc_error = (int)cudaErrorInvalidSymbol;
         return 6;
     }
+    // The scan runs in 64-column value slices: two CTAs per SM and a shorter per-chunk chain than whole heads.
+    constexpr int kNB = 1;
+    using Ly = split::ScanLayout<kNB>;
     auto ka = split::prep_kernel<TG>;
-    auto kb = split::scan_kernel<TO>;
+    auto kb = split::scan_kernel<TO, kNB>;
     cudaError_t e = cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)split::kSmemA);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)split::kSmemB);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly::SMEM);
     if (e == cudaSuccess) {
         ka<<<dim3((unsigned)ws.nch, (unsigned)bhn), split::kThreadsA, split::kSmemA, stream>>>(mq, mk, mbop, mqt, p,
                                                                                                  ws, status);
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) {
-        kb<<<(unsigned)bhn, split::kThreadsB, split::kSmemB, stream>>>(ma6, mu, my0, mkh, my, p, ws, status);
+        kb<<<(unsigned)(bhn * (128 / Ly::W)), split::kThreadsB, Ly::SMEM, stream>>>(ma6, mu, my0, mkh, my, p, ws,
+                                                                                       status);
         e = cudaGetLastError();
     }
     if (e != cudaSuccess) {

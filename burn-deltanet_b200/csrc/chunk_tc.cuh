@@ -68,7 +68,9 @@ namespace tc {
 
 constexpr int kParThreads = 256;  // warps 0-7: the S-independent ("parallel") role
 constexpr int kSerThreads = 128;  // warps 8-11: the S chain ("serial") role
-constexpr int kThreads = kParThreads + kSerThreads;
+constexpr int kIssueWarp = 12;    // warp 12: issues D1 and MMA4 (an issue blocks its thread while the
+                                  // tensor pipe accepts the MMAs, so no role waits on it)
+constexpr int kThreads = kParThreads + kSerThreads + 32;
 constexpr int kL = 64;    // chunk rows
 constexpr int kD = 128;   // dk = dv
 constexpr int kAP = 68;   // row pitch (floats) of the fp32 Akk and T tiles
@@ -78,15 +80,16 @@ constexpr uint32_t kStageBytes = 49152;                 // [K|Q d0-63][K|Q d64-1
 constexpr uint32_t OFF_STAGE = 0;                       // two stages
 constexpr uint32_t OFF_AU = 2 * kStageBytes;            // [Tb; Pb] hi, 128x64 bf16 K-major
 constexpr uint32_t OFF_AW = OFF_AU + 16384;             // [Tw; Pw] hi
-constexpr uint32_t OFF_S = OFF_AW + 16384;              // S bf16, MN-major, two 64-column blocks of 16 KB
+constexpr uint32_t OFF_S = OFF_AW + 16384;              // S bf16, MN-major, two 64-column blocks of 16 KB; once
+                                                        // MMA6 has read it, block h stages y columns 64h..
 constexpr uint32_t OFF_AQK = OFF_S + 32768;             // Aqk bf16 64x64 K-major
-constexpr uint32_t OFF_AF = OFF_AQK + 8192;             // Akk fp32 [64][68]; then [Tb; Pb] lo
+constexpr uint32_t OFF_AF = OFF_AQK + 8192;             // [Tb; Pb] lo
 constexpr uint32_t OFF_TF = OFF_AF + 64 * kAP * 4;      // T fp32 [64][68];   then [Tw; Pw] lo
-constexpr uint32_t OFF_Y = OFF_TF + 64 * kAP * 4;       // y bf16 64x128 (two SW128 64x64 boxes) for the TMA store
-constexpr uint32_t OFF_GATE = OFF_Y + 16384;            // per stage: e[64], w[64], g[64]
+constexpr uint32_t OFF_AK = OFF_TF + 64 * kAP * 4;      // Akk fp32 [64][68]; E blocks above its diagonal
+constexpr uint32_t OFF_GATE = OFF_AK + 64 * kAP * 4;    // per stage: e[64], w[64], g[64]
 constexpr uint32_t OFF_G = OFF_GATE + 2 * 3 * 64 * 4;   // per stage: G[64], gam[64]
 constexpr uint32_t OFF_BAR = OFF_G + 2 * 2 * 64 * 4;    // mbarriers (below)
-constexpr int kBars = 10;
+constexpr int kBars = 12;
 constexpr uint32_t OFF_TMEMPTR = OFF_BAR + kBars * 8;
 constexpr uint32_t OFF_FLAG = OFF_TMEMPTR + 4;
 constexpr uint32_t OFF_PEND = OFF_FLAG + 4;             // int[2]: parity of a stage's TMA load in flight, or -1
@@ -94,21 +97,19 @@ constexpr uint32_t kSmemUsed = OFF_PEND + 8;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;       // alignment slack
 static_assert(OFF_AF % 1024 == 0 && OFF_TF % 1024 == 0 && OFF_AQK % 1024 == 0 && OFF_S % 1024 == 0,
               "operand tiles need 1 KB alignment");
-static_assert(OFF_Y % 1024 == 0, "SW128 staging tile must be 1024-byte aligned");
 static_assert(kSmemBytes <= 232448, "over the 227 KB per-CTA shared-memory limit");
 
-// mbarrier slots
-enum Bar { B_TMA0 = 0, B_TMA1, B_MMA1, B_MMAP, B_MMA4, B_MMA6, B_MMA7, B_UY_FREE, B_GATE0, B_GATE1 };
+// mbarrier slots.  MMA4 commits twice: B_MMA4W once its D_W half (reading [Tw; Pw] and the T buffer) is
+// done, B_MMA4 once all of it is.  B_OPS: the operand role has finished a chunk (TM_A free, MMA4's
+// operands written).
+enum Bar { B_TMA0 = 0, B_TMA1, B_MMA1, B_MMAP, B_MMA4W, B_MMA4, B_MMA6, B_MMA7, B_UY_FREE, B_OPS, B_GATE0, B_GATE1 };
+static_assert(B_GATE1 + 1 == kBars, "barrier count");
 
 // TMEM columns (512 allocated): A = D1 / D_P, W = D_W (then A6), UY = D_UY, S = D_S.
 constexpr uint32_t TM_A = 0, TM_W = 128, TM_UY = 256, TM_S = 384;
 
 // Named barriers of the two roles (id 0 is __syncthreads).
 constexpr uint32_t NB_PAR = 1, NB_SER = 2;
-// Warps 0-6 of the operand role, for the gate phase; warp 7 skips it while it issues the previous chunk's
-// MMA4 (an issue that blocks its thread for as long as the tensor pipe takes to accept 16 MMAs).
-constexpr uint32_t NB_GATE = 3;
-constexpr int kIssueWarp = 7;
 
 __device__ __forceinline__ float gate_at(const float *p) { return *p; }
 __device__ __forceinline__ float gate_at(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
@@ -269,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);  // stays a shared pointer
     const uint32_t sb = ptx::smem_u32(base);
-    float *Af = reinterpret_cast<float *>(base + OFF_AF);
+    float *Ak = reinterpret_cast<float *>(base + OFF_AK);
     float *Tf = reinterpret_cast<float *>(base + OFF_TF);
     float *gates = reinterpret_cast<float *>(base + OFF_GATE);  // [stage][e | w | g][64]
     float *Gs = reinterpret_cast<float *>(base + OFF_G);        // [stage][G | gam][64]
@@ -284,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t nchunks = (P + kL - 1) / kL;
     const bool gated = p.gw > 0;
     const float scale = p.scale;
-    // bf16 y leaves through a staged TMA store (keeps the load/store pipe free for the operand role);
+    // bf16 y leaves through staged TMA stores (keeps the load/store pipe free for the operand role);
     // fp32 y is stored row by row.
     constexpr bool kYTma = sizeof(TO) == 2;
 
@@ -347,7 +348,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
         for (int64_t c = 0; c < nchunks; ++c) {
             const int st = (int)(c & 1);
-            const uint32_t stg = sb + OFF_STAGE + st * kStageBytes;
             const float *ge = gates + (st * 3 + 0) * 64;
             const float *gw = gates + (st * 3 + 1) * 64;
             float *Gc = Gs + st * 128;
@@ -356,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             // ---- chunk c's gates -> G = cumsum(g), gam = e^G; published to the serial role ----
             if (tid < 192) gates[st * 192 + tid] = gnext;
-            if (warp != kIssueWarp) ptx::named_sync(NB_GATE, kParThreads - 32);
+            ptx::named_sync(NB_PAR, kParThreads);
             if (c + 1 < nchunks && tid < 192) gnext = load_gate<TG>(p, b, h, c + 1, tid);
             if (warp == 0) {
                 const float *g = gates + (st * 3 + 2) * 64;
@@ -372,27 +372,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 gam[2 * lane + 1] = __expf(s);
                 gam[2 * lane] = __expf(s - x1);
             }
-            if (warp != kIssueWarp) ptx::named_sync(NB_GATE, kParThreads - 32);
+            ptx::named_sync(NB_PAR, kParThreads);
             if (leader) ptx::mbar_arrive(&bars[B_GATE0 + st]);
-
-            // ---- chunk c's tiles; chunk c-1's MMA4 must be done (it reads the lo operands in Af/Tf) ----
-            if (!par_wait(B_TMA0 + st, (uint32_t)((c >> 1) & 1))) break;
-            if (tid == 0) pend[st] = -1;
-            if (c > 0 && !par_wait(B_MMA4, (uint32_t)((c - 1) & 1))) break;
             DC_TC_MARK(1);
 
-            // ---- D1 = [K; Q] K^T ----
-            if (leader) {
-                ptx::tc_fence_after();
-                const uint32_t id = ptx::idesc_bf16(128, 64, 0, 0);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    const uint64_t d = ptx::sdesc(stg + off, 16, 1024);
-                    ptx::umma_bf16(tmem + TM_A, d, d, id, kk > 0);
-                }
-                ptx::umma_commit(&bars[B_MMA1]);
-            }
+            // ---- D1 = [K; Q] K^T, issued by the issue warp once chunk c's tiles landed ----
             if (!par_wait(B_MMA1, (uint32_t)(c & 1))) break;
             DC_TC_MARK(2);
 
@@ -419,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int q = 0; q < 8; ++q) {
                         const int j = 32 * ch + 4 * q;
-                        *reinterpret_cast<float4 *>(Af + i * kAP + j) =
+                        *reinterpret_cast<float4 *>(Ak + i * kAP + j) =
                             make_float4(j < i ? a[4 * q] : 0.f, j + 1 < i ? a[4 * q + 1] : 0.f,
                                         j + 2 < i ? a[4 * q + 2] : 0.f, j + 3 < i ? a[4 * q + 3] : 0.f);
                     }
@@ -440,11 +424,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::named_sync(NB_PAR, kParThreads);
             DC_TC_MARK(3);
 
-            // ---- T = (I + Akk)^-1 in 16x16 blocks ----
-            solve_unit_lower(Af, Tf, warp, lane, [&] { DC_TC_MARK(14); }, [&] { DC_TC_MARK(15); });
+            // ---- T = (I + Akk)^-1 in 16x16 blocks, into the buffer chunk c-1's [Tw; Pw] lo occupied ----
+            if (c > 0 && !par_wait(B_MMA4W, (uint32_t)((c - 1) & 1))) break;
+            solve_unit_lower(Ak, Tf, warp, lane, [&] { DC_TC_MARK(14); }, [&] { DC_TC_MARK(15); });
             DC_TC_MARK(4);
 
             // ---- Tb = T diag(w), Tw = T diag(e gam) as bf16 hi + lo (blocks above the diagonal masked) ----
+            // Every A operand buffer of chunk c-1's MMA4 is rewritten from here on.
+            if (c > 0 && !par_wait(B_MMA4, (uint32_t)((c - 1) & 1))) break;
             {
                 const int i = tid & 63, j0 = (tid >> 6) * 16;
                 float t[16];
@@ -531,28 +518,71 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::named_sync(NB_PAR, kParThreads);
             DC_TC_MARK(7);
 
-            // ---- D_UY = [Tb; Pb] V, D_W = [Tw; Pw] K, once the serial role released chunk c-1's ----
-            // Issued by warp 7 while warps 0-6 go on with chunk c+1's gates; everyone meets again at the
-            // next chunk's tile wait, where a wait that ran out here is seen by all.
-            if (tid == kIssueWarp * 32) {
-                if (c > 0 && !ptx::mbar_wait(&bars[B_UY_FREE], (uint32_t)((c - 1) & 1))) {
-                    *flag = 1;
-                } else {
-                    ptx::tc_fence_after();
-                    const uint32_t id = ptx::idesc_bf16(128, 128, 0, 1);
+            // ---- chunk c's MMA4 operands are written and TM_A is free: over to the issue warp ----
+            if (leader) ptx::mbar_arrive(&bars[B_OPS]);
+        }
+    } else if (warp == kIssueWarp) {
+        // ================ issue warp: chunk c's D1, then chunk c-1's MMA4 ================
+        // D1 goes first so that chunk c's masks do not queue behind MMA4 in the tensor pipe (unless chunk
+        // c's tiles are still in flight, in which case MMA4 goes first).  MMA4 waits until the serial role
+        // has released chunk c-2's D_UY / D_W.  A wait that runs out sets the flag and ends the warp; the
+        // roles then run into their own bounded waits.
+        if (lane == 0) {
+            auto issue_d1 = [&](int64_t c) {
+                const int st = (int)(c & 1);
+                const uint32_t stg = sb + OFF_STAGE + st * kStageBytes;
+                pend[st] = -1;
+                ptx::tc_fence_after();
+                const uint32_t id = ptx::idesc_bf16(128, 64, 0, 0);
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint32_t au = (kk < 4) ? OFF_AU : OFF_AF, aw = (kk < 4) ? OFF_AW : OFF_TF;
-                        ptx::umma_bf16(tmem + TM_UY, ptx::sdesc(sb + au + (kk & 3) * 32, 16, 1024),
-                                       ptx::sdesc(stg + 32768 + (kk & 3) * 2048, 8192, 1024), id, kk > 0);
-                        ptx::umma_bf16(tmem + TM_W, ptx::sdesc(sb + aw + (kk & 3) * 32, 16, 1024),
-                                       ptx::sdesc(stg + (kk & 3) * 2048, 16384, 1024), id, kk > 0);
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint64_t d = ptx::sdesc(stg + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+                    ptx::umma_bf16(tmem + TM_A, d, d, id, kk > 0);
+                }
+                ptx::umma_commit(&bars[B_MMA1]);
+            };
+            // MMA4 of chunk c in two parts: D_W = [Tw; Pw] K (commit B_MMA4W), D_UY = [Tb; Pb] V (B_MMA4).
+            auto issue_mma4 = [&](int64_t c, bool w_part) {
+                const uint32_t stg = sb + OFF_STAGE + (int)(c & 1) * kStageBytes;
+                ptx::tc_fence_after();
+                const uint32_t id = ptx::idesc_bf16(128, 128, 0, 1);
+                const uint32_t hi = w_part ? OFF_AW : OFF_AU, lo = w_part ? OFF_TF : OFF_AF;
+                const uint32_t bop = w_part ? stg : stg + 32768, lbo = w_part ? 16384 : 8192;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    ptx::umma_bf16(tmem + (w_part ? TM_W : TM_UY), ptx::sdesc(sb + (kk < 4 ? hi : lo) + (kk & 3) * 32, 16, 1024),
+                                   ptx::sdesc(bop + (kk & 3) * 2048, lbo, 1024), id, kk > 0);
+                ptx::umma_commit(&bars[w_part ? B_MMA4W : B_MMA4]);
+            };
+            bool ok = true;
+            for (int64_t c = 0; c <= nchunks && ok; ++c) {
+                const int st = (int)(c & 1);
+                const uint32_t tpar = (uint32_t)((c >> 1) & 1);
+                // chunk c-1's operands are written, and D1's TM_A has been read
+                if (c > 0 && !(ok = ptx::mbar_wait(&bars[B_OPS], (uint32_t)((c - 1) & 1)))) break;
+                // D1 goes ahead of whichever MMA4 part has not been issued when chunk c's tiles land.
+                bool d1 = !(c < nchunks);
+                auto try_d1 = [&] {
+                    if (!d1 && ptx::mbar_test(&bars[B_TMA0 + st], tpar)) {
+                        issue_d1(c);
+                        d1 = true;
                     }
-                    ptx::umma_commit(&bars[B_MMA4]);
+                };
+                try_d1();
+                if (c > 0) {
+                    if (c > 1 && !(ok = ptx::mbar_wait(&bars[B_UY_FREE], (uint32_t)((c - 2) & 1)))) break;
+                    issue_mma4(c - 1, true);
+                    try_d1();
+                    issue_mma4(c - 1, false);
+                }
+                if (!d1) {
+                    if (!(ok = ptx::mbar_wait(&bars[B_TMA0 + st], tpar))) break;
+                    issue_d1(c);
                 }
             }
-            __syncwarp();
+            if (!ok) *flag = 1;
         }
+        __syncwarp();
     } else {
         // =============================== serial role: the S chain of chunk c ===============================
         const int sp = warp - 8;  // TMEM subpartition
@@ -611,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             DC_TC_MARK(8);
 
             // ---- A6 = [-W; s gam Q - Aqk W] into TMEM, over D_W (bf16 pairs, two per column) ----
-            if (!(ok = ser_wait(B_MMA4, (uint32_t)(c & 1)))) break;
+            if (!(ok = ser_wait(B_MMA4W, (uint32_t)(c & 1)))) break;
             DC_TC_MARK(9);
             ptx::tc_fence_after();
             {
@@ -652,7 +682,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ptx::tmem_wait_st();
             }
             ptx::tc_fence_before();
-            ptx::named_sync(NB_SER, kSerThreads);
+            // A6 is in TMEM, and MMA4's D_UY half (accumulated below) is done
+            if (!(ok = ser_wait(B_MMA4, (uint32_t)(c & 1)))) break;
             DC_TC_MARK(10);
 
             // ---- D_UY += A6 S  ->  [V'; y] ----
@@ -704,7 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         } else if (kYTma) {
 #pragma unroll
                             for (int q = 0; q < 4; ++q)
-                                ptx::st_shared_v4(sb + OFF_Y + hh * 8192 + ptx::sw128(r - 64, 32 * q2 + 8 * q),
+                                ptx::st_shared_v4(sb + OFF_S + hh * 16384 + ptx::sw128(r - 64, 32 * q2 + 8 * q),
                                                   ptx::pack_bf16(f[8 * q], f[8 * q + 1]),
                                                   ptx::pack_bf16(f[8 * q + 2], f[8 * q + 3]),
                                                   ptx::pack_bf16(f[8 * q + 4], f[8 * q + 5]),
@@ -723,8 +754,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (kYTma) {
                     // The Q tile's 64 token rows; rows past the sequence are clipped by the tensor map.
                     const int tok0 = (int)q_first(c, p.u);
-                    ptx::tma_store_4d(&tm_y, sb + OFF_Y, 0, (int)h, tok0, (int)b);
-                    ptx::tma_store_4d(&tm_y, sb + OFF_Y + 8192, 64, (int)h, tok0, (int)b);
+                    ptx::tma_store_4d(&tm_y, sb + OFF_S, 0, (int)h, tok0, (int)b);
+                    ptx::tma_store_4d(&tm_y, sb + OFF_S + 16384, 64, (int)h, tok0, (int)b);
                     ptx::bulk_commit();
                 }
             }
@@ -741,6 +772,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ptx::umma_bf16(tmem + TM_S, ptx::sdesc(stg + (kk & 3) * 2048, 16384, 1024), bdesc, id, 1);
                 }
                 ptx::umma_commit(&bars[B_MMA7]);
+                if (kYTma) ptx::bulk_wait_read_all();  // the y tiles have left the S buffer the tail rewrites
             }
             if (!(ok = ser_wait(B_MMA7, (uint32_t)(c & 1)))) break;
             DC_TC_MARK(13);

@@ -30,10 +30,16 @@
 // chunk's own inputs; only the last three lines depend on S.  Warps 0-7
 // (the "parallel" role) build chunk c+1's operands (masks, solve, Tb/Tw,
 // Pb/Pw) while warps 8-11 (the "serial" role) run chunk c's S chain (A6,
-// V'/y, the state update), so the two chains' latencies overlap.  The roles
-// meet on mbarriers: the serial role waits for chunk c's D_UY/D_W, the
-// parallel role for the serial role to release them (after V'/y) before its
-// next D_UY/D_W, and for the chunk's TMA loads.
+// V'/y, the state update), so the two chains' latencies overlap.  Warp 12
+// issues D1 and the D_UY/D_W products ("MMA4"): an MMA issue blocks its
+// thread while the tensor pipe accepts the MMAs, so neither role waits on
+// it.  It puts chunk c+1's D1 ahead of chunk c's MMA4 in the (in-order)
+// tensor pipe once chunk c+1's tiles have landed, so that the next chunk's
+// masks need not wait for MMA4.  The roles meet on mbarriers: the serial role
+// waits for chunk c's D_W (A6) and D_UY (its MMA), the issue warp for the
+// parallel role's operands and for the serial role to release chunk c-1's
+// D_UY/D_W (after V'/y), and the parallel role for MMA4 to have read the
+// buffers it rewrites (the T buffer, then the hi / lo operands).
 //
 // T (through Tb, Tw and their Aqk products) and V' enter their products as
 // two bf16 terms each (hi + lo, the rounding residual of hi), i.e. at ~16
@@ -45,7 +51,9 @@
 // (8 rows x 128 B atoms): tiles written by TMA with CU_TENSOR_MAP_SWIZZLE_128B
 // and tiles written by threads through ptx::sw128 share one pattern, so the
 // same bytes serve as a K-major operand of one MMA and an MN-major operand of
-// another.  V' (hi, lo) is written into the consumed stage's V and Q slots.
+// another.  V' (hi, lo) is written into the consumed stage's V and Q slots,
+// and bf16 y is staged for its TMA store in the S operand buffer, which the
+// state update rewrites only after MMA6 has read it and the store has left.
 //
 // Every mbarrier wait is bounded (ptx::kWaitLimitNs); a wait that runs out
 // sets the library's device status word, the CTA waits (bounded) for its own

@@ -31,6 +31,7 @@ DC_BF16 = 1
 DC_FLAG_FORCE_SIMT = 0x1
 DC_FLAG_RECURRENT = 0x2
 DC_FLAG_FORCE_SPLIT = 0x4
+DC_FLAG_TEST_STALL = 0x100
 
 EXPORTS = (
     "dc_chunk_fwd", "dc_step", "dc_status_string", "dc_last_cuda_error", "dc_device_status",

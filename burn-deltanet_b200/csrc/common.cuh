@@ -24,6 +24,7 @@ struct CoreParams {
     // place) and of q, g, y (1 for one token; seq for a sequence).
     int64_t kv_bstride, q_bstride;
     float scale;
+    int32_t stall;             // test hook (DC_FLAG_TEST_STALL): issue no tile loads
     const void *q, *k, *v, *erase, *write, *g;
     const float *state_in;
     void *y;

@@ -93,6 +93,7 @@ dc::CoreParams make_params(int64_t batch, int64_t seq, int64_t heads, int64_t dk
     p.state_in = s_in; p.y = y; p.state_out = s_out;
     p.kv_bstride = (int64_t)u * seq;
     p.q_bstride = seq;
+    p.stall = 0;
     return p;
 }
 
@@ -273,13 +274,20 @@ dc::CoreParams chunk_params(const dc_chunk_args *a) {
 
 // The chunk kernel a validated call takes: 2 split (workspace), 1 fused tensor-core, 0 CUDA-core,
 // or -DC_EWORKSPACE when the split path is required but the workspace is short.
-int chunk_choice(const dc_chunk_args *a, const dc::CoreParams &p) {
+int chunk_choice_any(const dc_chunk_args *a, const dc::CoreParams &p) {
     if (a->flags & DC_FLAG_RECURRENT) return 0;
     if (dc::split_applies(p, a->in_dtype, a->flags)) {
         if (a->workspace && a->workspace_bytes >= dc::split_workspace_bytes(p)) return 2;
         if (a->workspace || (a->flags & DC_FLAG_FORCE_SPLIT)) return -DC_EWORKSPACE;
     }
     return dc::tc_applies(p, a->in_dtype, a->flags) ? 1 : 0;
+}
+
+// As above; the stall test hook is taken by the tensor-core kernel only.
+int chunk_choice(const dc_chunk_args *a, const dc::CoreParams &p) {
+    const int choice = chunk_choice_any(a, p);
+    if ((a->flags & DC_FLAG_TEST_STALL) && choice != 1) return -DC_EINVAL_ARG;
+    return choice;
 }
 
 }  // namespace
@@ -302,8 +310,10 @@ int dc_chunk_launches(const dc_chunk_args *a) {
     const int st = validate_chunk(a);
     if (st != DC_OK) return -st;
     if (a->batch == 0 || a->heads == 0) return 0;
+    const int choice = chunk_choice(a, chunk_params(a));
+    if (choice < 0) return choice;
     if (a->flags & DC_FLAG_RECURRENT) return (int)a->seq;
-    return chunk_choice(a, chunk_params(a)) == 2 ? 2 : 1;
+    return choice == 2 ? 2 : 1;
 }
 
 // DeltaPath::Recurrent: the fused tick walks the sequence in place, one launch
@@ -340,16 +350,18 @@ int dc_chunk_fwd(const dc_chunk_args *a, dc_stream_t stream) {
                                          a->write_w, a->g_w, a->scale, a->q, a->k, a->v, a->erase, a->write, a->g,
                                          a->state_in, a->y, a->state_out);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (a->flags & DC_FLAG_RECURRENT) return run_recurrent(a, s);
     const int choice = chunk_choice(a, p);
     if (choice < 0) return -choice;
+    if (a->flags & DC_FLAG_RECURRENT) return run_recurrent(a, s);
     if (choice == 2) {
         st = dc::launch_chunk_split(p, a->gate_dtype, a->out_dtype, a->workspace, s);
         if (st == DC_ECUDA) g_last_cuda_error = dc::tc_last_error();
         return st;
     }
     if (choice == 1) {
-        st = dc::launch_chunk_tc(p, a->gate_dtype, a->out_dtype, s);
+        dc::CoreParams pt = p;
+        pt.stall = (a->flags & DC_FLAG_TEST_STALL) ? 1 : 0;
+        st = dc::launch_chunk_tc(pt, a->gate_dtype, a->out_dtype, s);
         if (st == DC_ECUDA) g_last_cuda_error = dc::tc_last_error();
         return st;
     }
@@ -397,7 +409,7 @@ extern "C" {
 int dc_chunk_fwd_noalloc(const dc_chunk_args *a, dc_stream_t stream) {
     int st = validate_chunk(a);
     if (st != DC_OK || a->batch == 0 || a->heads == 0) return st;
-    if (a->flags & (DC_FLAG_FORCE_SIMT | DC_FLAG_RECURRENT)) return DC_EINVAL_ARG;
+    if (a->flags & (DC_FLAG_FORCE_SIMT | DC_FLAG_RECURRENT | DC_FLAG_TEST_STALL)) return DC_EINVAL_ARG;
     int dev = 0;
     st = check_device(&dev);
     if (st != DC_OK) return st;
@@ -416,11 +428,17 @@ int dc_step(const dc_step_args *a, dc_stream_t stream) {
     if (st != DC_OK || a->batch == 0 || a->heads == 0) return st;
     st = check_device(nullptr);
     if (st != DC_OK) return st;
-    const dc::CoreParams p = make_params(a->batch, 1, a->heads, a->dk, a->dv, a->n_householder, a->erase_w,
-                                         a->write_w, a->g_w, a->scale, a->q, a->k, a->v, a->erase, a->write, a->g,
-                                         a->state_in, a->y, a->state_out);
+    dc::CoreParams p = make_params(a->batch, 1, a->heads, a->dk, a->dv, a->n_householder, a->erase_w, a->write_w,
+                                   a->g_w, a->scale, a->q, a->k, a->v, a->erase, a->write, a->g, a->state_in, a->y,
+                                   a->state_out);
+    const bool allow_stream = (a->flags & DC_FLAG_FORCE_SIMT) == 0;
+    if (a->flags & DC_FLAG_TEST_STALL) {  // the streaming kernel is the one that takes the hook
+        const size_t is = a->in_dtype == DC_F32 ? 4 : 2, gs = a->gate_dtype == DC_F32 ? 4 : 2;
+        if (!allow_stream || !stream_applies(p, is, gs)) return DC_EINVAL_ARG;
+        p.stall = 1;
+    }
     return dispatch_types<StepLauncher>(a->in_dtype, a->gate_dtype, a->out_dtype, p,
-                                        reinterpret_cast<cudaStream_t>(stream), (a->flags & DC_FLAG_FORCE_SIMT) == 0);
+                                        reinterpret_cast<cudaStream_t>(stream), allow_stream);
 }
 
 }  // extern "C"

@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_stream_kernel(const CorePara
                 ptx::bulk_commit();
                 return true;
             };
-            bool ok = true;
+            bool ok = !p.stall;  // (the stall test hook issues nothing: the consumers' waits run out)
             int last_parity[kSlots] = {-1, -1, -1};  // of the load last issued into each slot
             for (int64_t m = 0; m < nitems && ok; ++m) {
                 if (m >= kSlots) {  // head m takes the slot of head m - 3: store that one, let the store read it
@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_stream_kernel(const CorePara
                 last_parity[m % kSlots] = (int)((m / kSlots) & 1);
             }
             for (int64_t m = nitems > kSlots ? nitems - kSlots : 0; m < nitems && ok; ++m) ok = store_done(m);
-            if (!ok) {  // an abort: let every load issued into this CTA's shared memory land before it goes away
+            if (!ok && !p.stall) {  // an abort: let every load issued into this CTA's shared memory land before it goes away
                 for (int sl = 0; sl < kSlots; ++sl)
                     if (last_parity[sl] >= 0) ptx::mbar_wait(&full[sl], (uint32_t)last_parity[sl]);
             }

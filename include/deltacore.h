@@ -87,6 +87,13 @@ enum dc_dtype {
 #define DC_FLAG_RECURRENT 0x2u  /* DeltaPath::Recurrent: walk the sequence token by token with the fused
                                    decode tick (one launch per token, state updated in state_out) */
 #define DC_FLAG_FORCE_SPLIT 0x4u /* take the two-kernel (workspace) tensor-core path even for per-head gates */
+/* Test hook for the failure path, no counterpart in the reference: the launched kernel issues none of
+ * its tile loads, so every bounded wait on them runs out (about 2 s) and the kernel returns early with
+ * the device status word set to 1 (dc_device_status); y and the final state are not written.  Nothing
+ * faults and the context stays usable.  Accepted by dc_chunk_fwd when it takes the tensor-core kernel
+ * (dc_chunk_kernel_choice 1) and by dc_step when it takes the streaming decode kernel; any other call
+ * with it returns DC_EINVAL_ARG. */
+#define DC_FLAG_TEST_STALL 0x100u
 
 /*
  * Chunkwise prefill.  Mirrors
@@ -201,7 +208,8 @@ DC_API int dc_chunk_kernel_choice(const dc_chunk_args *args);
  * host logic; about 97 KB per (batch, head, 64-token chunk). */
 DC_API uint64_t dc_chunk_workspace_size(const dc_chunk_args *args);
 
-/* Number of kernels dc_chunk_fwd enqueues for `args` (for launch accounting); dc_step enqueues one. */
+/* Number of kernels dc_chunk_fwd enqueues for `args` (for launch accounting); dc_step enqueues one.
+ * Negative: -dc_status of a call dc_chunk_fwd would reject. */
 DC_API int dc_chunk_launches(const dc_chunk_args *args);
 
 /* ABI version: major * 10000 + minor * 100 + patch. */

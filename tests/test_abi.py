@@ -117,6 +117,16 @@ def test_kernel_choice_is_host_logic():
     assert abi.lib().dc_chunk_kernel_choice(a) == 0
 
 
+def test_stall_hook_is_taken_by_the_tensor_core_kernel_only():
+    a = _args(dk=128, dv=128, in_dtype=abi.DC_BF16, flags=abi.DC_FLAG_TEST_STALL)
+    assert abi.lib().dc_chunk_kernel_choice(a) == 1
+    for flags in (abi.DC_FLAG_TEST_STALL, abi.DC_FLAG_TEST_STALL | abi.DC_FLAG_RECURRENT):
+        assert abi.lib().dc_chunk_kernel_choice(_args(flags=flags)) == -abi.DC_EINVAL_ARG
+        assert abi.lib().dc_chunk_launches(_args(flags=flags)) == -abi.DC_EINVAL_ARG
+    a = _args(dk=128, dv=128, in_dtype=abi.DC_BF16, flags=abi.DC_FLAG_TEST_STALL | abi.DC_FLAG_FORCE_SIMT)
+    assert abi.lib().dc_chunk_kernel_choice(a) == -abi.DC_EINVAL_ARG
+
+
 def test_step_validation():
     s = abi.StepArgs()
     s.batch, s.heads, s.dk, s.dv = 2, 2, 4, 6

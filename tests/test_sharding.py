@@ -74,3 +74,42 @@ def test_sharded_equals_unsharded_gloo(batch, heads):
     results = sorted(q.get(timeout=5) for _ in range(2))
     for _, ey, es in results:
         assert ey == 0.0 and es == 0.0
+
+
+def _failing_worker(rank, world, port, result_q):
+    """Rank 1 raises before the gather (it never joins the collective); rank 0 must get an error from the
+    gather within the short process-group timeout instead of waiting for ever."""
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    shards = sh.plan(2, 2, world)
+    local = torch.full((1, 3, 2, 4), float(rank))
+    if rank == 1:
+        raise RuntimeError("rank 1 fails before the gather")
+    t0 = time.monotonic()
+    try:
+        sh.gather(local, shards)
+        result_q.put(("no error", time.monotonic() - t0))
+    except Exception as e:  # the collective ends with an error
+        result_q.put((type(e).__name__, time.monotonic() - t0))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_a_rank_that_fails_before_the_gather_ends_the_other_ranks_collective_with_an_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert procs[1].exitcode != 0  # the failing rank raised
+    assert procs[0].exitcode == 0  # the surviving rank returned on its own
+    outcome, secs = q.get(timeout=5)
+    assert outcome != "no error", "the gather completed without the failed rank"
+    assert secs < 60, f"the surviving rank waited {secs:.0f} s"

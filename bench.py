@@ -265,29 +265,28 @@ def time_prefill(dn, x, u, steps, warmup):
 
 
 def time_prefill_e2e(dn, x, u, steps, warmup):
-    """Through the public API from pinned host buffers: H2D inputs, the kernel,
-    D2H of y and the final state, every step."""
+    """Through the public host-memory entry point (dc_chunk_fwd_host) from
+    pinned host buffers: every step copies the inputs in, runs the kernels and
+    copies y and the final state back, slice by slice with the transfers
+    overlapping the kernels; timed on the device stream the call drains into."""
     host = {k: (None if t is None else t.cpu().pin_memory()) for k, t in x.items()}
-    dev = {k: (None if t is None else torch.empty_like(t)) for k, t in x.items()}
     b, s = x["q"].shape[0], x["q"].shape[1]
-    y = torch.empty(b, s, H, D, device="cuda", dtype=torch.bfloat16)
-    s_out = torch.empty_like(x["state"])
-    y_host = torch.empty(y.shape, dtype=y.dtype).pin_memory()
-    s_host = torch.empty(s_out.shape, dtype=s_out.dtype).pin_memory()
+    y_host = torch.empty((b, s, H, D), dtype=torch.bfloat16).pin_memory()
+    s_host = torch.empty(tuple(x["state"].shape), dtype=torch.float32).pin_memory()
     h2d = sum(t.numel() * t.element_size() for t in host.values() if t is not None)
     d2h = y_host.numel() * 2 + s_host.numel() * 4
     gated = x["g"] is not None
+    scratch = [None]
 
     def call():
-        for k, t in host.items():
-            if t is not None:
-                dev[k].copy_(t, non_blocking=True)
-        dn.delta_chunk_recalculated(dev["q"], dev["k"], dev["v"], dev["erase"], dev["write"], dev["g"],
-                                    dev["state"], gated, L, 1.0 / math.sqrt(D), n_householder=u,
-                                    y_out=y, state_out=s_out)
-        y_host.copy_(y, non_blocking=True)
-        s_host.copy_(s_out, non_blocking=True)
+        _, _ = dn.delta_chunk_recalculated_host(host["q"], host["k"], host["v"], host["erase"], host["write"],
+                                                host["g"], host["state"], gated, L, 1.0 / math.sqrt(D),
+                                                n_householder=u, scratch=scratch[0], y_out=y_host,
+                                                state_out=s_host, synchronize=False)
 
+    need = dn.delta_chunk_host_scratch_size(host["q"], host["k"], host["v"], host["erase"], host["write"],
+                                            host["g"], host["state"], gated, L, 1.0 / math.sqrt(D), n_householder=u)
+    scratch[0] = torch.empty(need, dtype=torch.uint8, device="cuda")
     for _ in range(warmup):
         call()
     torch.cuda.synchronize()

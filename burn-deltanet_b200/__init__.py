@@ -19,12 +19,16 @@ from .core import (
     TriSolve,
     beta_gates,
     delta_chunk_recalculated,
+    delta_chunk_host_scratch_size,
+    delta_chunk_recalculated_host,
     delta_step,
 )
 
 __all__ = [
     "DeltaCoreError", "DeltaInput", "DeltaPath", "DeltaShapeError", "TriSolve",
-    "beta_gates", "delta_chunk_recalculated", "delta_step", "library_path",
+    "beta_gates", "delta_chunk_recalculated", "delta_chunk_recalculated_host", "delta_chunk_host_scratch_size",
+    "delta_step",
+    "library_path",
 ]
 
 

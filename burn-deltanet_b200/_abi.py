@@ -37,6 +37,8 @@ EXPORTS = (
     "dc_chunk_fwd", "dc_step", "dc_status_string", "dc_last_cuda_error", "dc_device_status",
     "dc_chunk_kernel_choice", "dc_chunk_launches", "dc_version", "dc_chunk_workspace_size",
     "dc_chunk_fwd_noalloc",
+    "dc_chunk_fwd_host_scratch_size",
+    "dc_chunk_fwd_host",
 )
 
 
@@ -104,6 +106,10 @@ def lib() -> ctypes.CDLL:
         L.dc_chunk_workspace_size.restype = ctypes.c_uint64
         L.dc_chunk_fwd_noalloc.argtypes = [ctypes.POINTER(ChunkArgs), ctypes.c_void_p]
         L.dc_chunk_fwd_noalloc.restype = ctypes.c_int
+        L.dc_chunk_fwd_host_scratch_size.argtypes = [ctypes.POINTER(ChunkArgs)]
+        L.dc_chunk_fwd_host_scratch_size.restype = ctypes.c_uint64
+        L.dc_chunk_fwd_host.argtypes = [ctypes.POINTER(ChunkArgs), ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
+        L.dc_chunk_fwd_host.restype = ctypes.c_int
         _lib = L
     return _lib
 

@@ -143,31 +143,16 @@ def beta_gates(beta: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     return gate, gate
 
 
-def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv,
-                             has_gate: bool, chunk_len: int, scale: float, *, n_householder: int = 1,
-                             out_dtype: Optional[torch.dtype] = None, force_simt: bool = False,
-                             recurrent: bool = False, force_split: bool = False,
-                             workspace: Optional[torch.Tensor] = None,
-                             y_out: Optional[torch.Tensor] = None, state_out: Optional[torch.Tensor] = None):
-    """The backend-extension op (chunk_recalculated.rs:115-126) on CUDA tensors.
-
-    Shapes: q [b, s, h, dk]; k [b, s*u, h, dk]; v [b, s*u, h, dv];
-    erase [b, s*u, h, 1|dk]; write [b, s*u, h, 1|dv]; g [b, s, h, 1|dk]
-    (ignored unless ``has_gate``); state [b, h, dk, dv] float32.
-    Returns ``(y [b, s, h, dv], final_state [b, h, dk, dv])`` as new tensors
-    unless ``y_out`` / ``state_out`` are given (``state_out`` may be ``state_bhkv``).
-    ``recurrent=True`` evaluates DeltaPath::Recurrent: the fused decode tick walks
-    the sequence token by token (one launch per token).
-    Per-channel gates (GDN-2) run on the tensor cores through a device workspace
-    of ``dc_chunk_workspace_size`` bytes: pass ``workspace`` (a uint8 CUDA tensor)
-    to reuse one, otherwise this layer allocates it for the call.
-    ``force_split=True`` takes that two-kernel path for per-head gates too.
-    """
+def _chunk_args(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv, has_gate, chunk_len, scale,
+                n_householder, out_dtype, force_simt, recurrent, force_split, y_out, state_out, check, alloc):
+    """dc_chunk_args for one call, after the reference's shape / width asserts
+    (path.rs:177-208); `check` validates each tensor's placement, `alloc`
+    makes the outputs not given."""
     ts = dict(q=q_bshk, k=k_bshk, v=v_bshv, erase=erase_bshK, write=write_bshV, state=state_bhkv)
     if has_gate:
         ts["g"] = g_bshK
     for name, t in ts.items():
-        _check_tensor(t, name)
+        check(t, name)
     if q_bshk.dim() != 4 or v_bshv.dim() != 4 or state_bhkv.dim() != 4:
         raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, "q, v and state must be rank 4")
     b, s, h, dk = q_bshk.shape
@@ -190,8 +175,10 @@ def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_b
     in_dt = _same_dtype((q_bshk, k_bshk, v_bshv), "q, k, v")
     gate_dt = _same_dtype((erase_bshK, write_bshV, g_bshK if has_gate else None), "erase, write, g")
     out_torch = out_dtype or q_bshk.dtype
-    y = y_out if y_out is not None else torch.empty((b, s, h, dv), device=q_bshk.device, dtype=out_torch)
-    s_out = state_out if state_out is not None else torch.empty_like(state_bhkv)
+    y = y_out if y_out is not None else alloc((b, s, h, dv), out_torch)
+    s_out = state_out if state_out is not None else alloc(tuple(state_bhkv.shape), torch.float32)
+    check(y, "y_out")
+    check(s_out, "state_out")
     a = _abi.ChunkArgs()
     a.batch, a.seq, a.heads, a.dk, a.dv = b, s, h, dk, dv
     a.n_householder = u
@@ -206,6 +193,33 @@ def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_b
     a.erase, a.write = erase_bshK.data_ptr(), write_bshV.data_ptr()
     a.g = g_bshK.data_ptr() if has_gate else None
     a.state_in, a.y, a.state_out = state_bhkv.data_ptr(), y.data_ptr(), s_out.data_ptr()
+    return a, y, s_out
+
+
+def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv,
+                             has_gate: bool, chunk_len: int, scale: float, *, n_householder: int = 1,
+                             out_dtype: Optional[torch.dtype] = None, force_simt: bool = False,
+                             recurrent: bool = False, force_split: bool = False,
+                             workspace: Optional[torch.Tensor] = None,
+                             y_out: Optional[torch.Tensor] = None, state_out: Optional[torch.Tensor] = None):
+    """The backend-extension op (chunk_recalculated.rs:115-126) on CUDA tensors.
+
+    Shapes: q [b, s, h, dk]; k [b, s*u, h, dk]; v [b, s*u, h, dv];
+    erase [b, s*u, h, 1|dk]; write [b, s*u, h, 1|dv]; g [b, s, h, 1|dk]
+    (ignored unless ``has_gate``); state [b, h, dk, dv] float32.
+    Returns ``(y [b, s, h, dv], final_state [b, h, dk, dv])`` as new tensors
+    unless ``y_out`` / ``state_out`` are given (``state_out`` may be ``state_bhkv``).
+    ``recurrent=True`` evaluates DeltaPath::Recurrent: the fused decode tick walks
+    the sequence token by token (one launch per token).
+    Per-channel gates (GDN-2) run on the tensor cores through a device workspace
+    of ``dc_chunk_workspace_size`` bytes: pass ``workspace`` (a uint8 CUDA tensor)
+    to reuse one, otherwise this layer allocates it for the call.
+    ``force_split=True`` takes that two-kernel path for per-head gates too.
+    """
+    a, y, s_out = _chunk_args(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv, has_gate,
+                              chunk_len, scale, n_householder, out_dtype, force_simt, recurrent, force_split,
+                              y_out, state_out, _check_tensor,
+                              lambda shape, dt: torch.empty(shape, device=q_bshk.device, dtype=dt))
     need = int(_abi.lib().dc_chunk_workspace_size(a))
     if need > 0:
         if workspace is None:
@@ -215,6 +229,60 @@ def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_b
     with torch.cuda.device(q_bshk.device):
         stream = torch.cuda.current_stream(q_bshk.device).cuda_stream
         _raise(_abi.lib().dc_chunk_fwd(a, stream), "dc_chunk_fwd")
+    return y, s_out
+
+
+def _check_host_tensor(t: torch.Tensor, what: str) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{what} must be a torch.Tensor")
+    if t.device.type != "cpu":
+        raise DeltaCoreError(_abi.DC_EINVAL_ARG, f"{what} is on {t.device}: this entry point takes host tensors")
+    if not t.is_contiguous():
+        raise DeltaCoreError(_abi.DC_EINVAL_ARG, f"{what} must be contiguous")
+
+
+def delta_chunk_host_scratch_size(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv,
+                                  has_gate: bool, chunk_len: int, scale: float, *, n_householder: int = 1,
+                                  out_dtype: Optional[torch.dtype] = None, force_simt: bool = False,
+                                  force_split: bool = False) -> int:
+    """Bytes of device scratch :func:`delta_chunk_recalculated_host` needs for
+    these host tensors (``dc_chunk_fwd_host_scratch_size``)."""
+    a = _chunk_args(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv, has_gate, chunk_len,
+                    scale, n_householder, out_dtype, force_simt, False, force_split, None, None,
+                    _check_host_tensor, lambda shape, dt: torch.empty(shape, dtype=dt))[0]
+    return int(_abi.lib().dc_chunk_fwd_host_scratch_size(a))
+
+
+def delta_chunk_recalculated_host(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv,
+                                  has_gate: bool, chunk_len: int, scale: float, *, n_householder: int = 1,
+                                  out_dtype: Optional[torch.dtype] = None, force_simt: bool = False,
+                                  force_split: bool = False, device=None, scratch: Optional[torch.Tensor] = None,
+                                  y_out: Optional[torch.Tensor] = None, state_out: Optional[torch.Tensor] = None,
+                                  synchronize: bool = True):
+    """:func:`delta_chunk_recalculated` on HOST tensors (pinned for full PCIe
+    speed) through ``dc_chunk_fwd_host``: the batch is streamed through the
+    GPU in slices of whole sequences, copies in both directions overlapping
+    the kernels.  Outputs are host tensors (pinned when allocated here).
+    ``scratch`` is a uint8 CUDA tensor of ``dc_chunk_fwd_host_scratch_size``
+    bytes to reuse (allocated per call otherwise).  With ``synchronize=False``
+    the call returns once the work is queued on the device's current stream;
+    the outputs are complete when that stream has drained.
+    """
+    dev = torch.device(device if device is not None else "cuda")
+    pin = lambda shape, dt: torch.empty(shape, dtype=dt, pin_memory=True)
+    a, y, s_out = _chunk_args(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv, has_gate,
+                              chunk_len, scale, n_householder, out_dtype, force_simt, False, force_split,
+                              y_out, state_out, _check_host_tensor, pin)
+    need = int(_abi.lib().dc_chunk_fwd_host_scratch_size(a))
+    if scratch is None:
+        scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    _check_tensor(scratch, "scratch")
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev)
+        _raise(_abi.lib().dc_chunk_fwd_host(a, scratch.data_ptr(), scratch.numel(), stream.cuda_stream),
+               "dc_chunk_fwd_host")
+        if synchronize:
+            stream.synchronize()
     return y, s_out
 
 

@@ -341,18 +341,17 @@ static int run_recurrent(const dc_chunk_args *a, cudaStream_t s) {
     return DC_OK;
 }
 
-int dc_chunk_fwd(const dc_chunk_args *a, dc_stream_t stream) {
-    int st = validate_chunk(a);
-    if (st != DC_OK || a->batch == 0 || a->heads == 0) return st;
-    st = check_device(nullptr);
-    if (st != DC_OK) return st;
-    const dc::CoreParams p = make_params(a->batch, a->seq, a->heads, a->dk, a->dv, a->n_householder, a->erase_w,
-                                         a->write_w, a->g_w, a->scale, a->q, a->k, a->v, a->erase, a->write, a->g,
-                                         a->state_in, a->y, a->state_out);
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+}  // extern "C"
+
+namespace {
+
+// dc_chunk_fwd after validation and the device check.
+int chunk_fwd_launch(const dc_chunk_args *a, cudaStream_t s) {
+    const dc::CoreParams p = chunk_params(a);
     const int choice = chunk_choice(a, p);
     if (choice < 0) return -choice;
     if (a->flags & DC_FLAG_RECURRENT) return run_recurrent(a, s);
+    int st;
     if (choice == 2) {
         st = dc::launch_chunk_split(p, a->gate_dtype, a->out_dtype, a->workspace, s);
         if (st == DC_ECUDA) g_last_cuda_error = dc::tc_last_error();
@@ -366,6 +365,18 @@ int dc_chunk_fwd(const dc_chunk_args *a, dc_stream_t stream) {
         return st;
     }
     return dispatch_types<SimtLauncher>(a->in_dtype, a->gate_dtype, a->out_dtype, p, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int dc_chunk_fwd(const dc_chunk_args *a, dc_stream_t stream) {
+    int st = validate_chunk(a);
+    if (st != DC_OK || a->batch == 0 || a->heads == 0) return st;
+    st = check_device(nullptr);
+    if (st != DC_OK) return st;
+    return chunk_fwd_launch(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
@@ -439,6 +450,161 @@ int dc_step(const dc_step_args *a, dc_stream_t stream) {
     }
     return dispatch_types<StepLauncher>(a->in_dtype, a->gate_dtype, a->out_dtype, p,
                                         reinterpret_cast<cudaStream_t>(stream), allow_stream);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// dc_chunk_fwd_host: the prefill from host memory, with the PCIe transfers of
+// one slice of sequences overlapping the kernels of the previous one and the
+// copies back of the one before (three streams, two device slots).
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kHostSlices = 8;  // the batch is cut into at most this many slices of whole sequences
+
+struct HostPlan {
+    int64_t per_slice;   // sequences per slice
+    size_t seq_bytes[9]; // bytes of one sequence: q, k, v, erase, write, g, state_in, y, state_out
+    size_t off[9];       // offsets of those regions inside a slot
+    size_t slot;         // bytes of one slot
+    size_t ws;           // the two-kernel path's workspace for one slice (kernels run in order: one is enough)
+    size_t total;
+};
+
+size_t round256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+HostPlan host_plan(const dc_chunk_args *a) {
+    HostPlan hp{};
+    hp.per_slice = (a->batch + kHostSlices - 1) / kHostSlices;
+    const size_t is = dtype_size(a->in_dtype), gs = dtype_size(a->gate_dtype), os = dtype_size(a->out_dtype);
+    const size_t s = (size_t)a->seq, su = s * (size_t)a->n_householder, h = (size_t)a->heads;
+    const size_t dk = (size_t)a->dk, dv = (size_t)a->dv;
+    const size_t per[9] = {s * h * dk * is, su * h * dk * is, su * h * dv * is,
+                           su * h * (size_t)a->erase_w * gs, su * h * (size_t)a->write_w * gs,
+                           a->g_w ? s * h * (size_t)a->g_w * gs : 0, h * dk * dv * 4, s * h * dv * os, h * dk * dv * 4};
+    size_t o = 0;
+    for (int i = 0; i < 9; ++i) {
+        hp.seq_bytes[i] = per[i];
+        hp.off[i] = o;
+        o += round256(per[i] * (size_t)hp.per_slice);
+    }
+    hp.slot = o;
+    // The slice's kernel choice is taken on 256-aligned device pointers: stand-ins suffice for the size.
+    dc_chunk_args sl = *a;
+    sl.batch = a->batch < hp.per_slice ? a->batch : hp.per_slice;
+    const void *fake = reinterpret_cast<const void *>((uintptr_t)4096);
+    sl.q = sl.k = sl.v = sl.erase = sl.write = fake;
+    sl.g = a->g_w ? fake : nullptr;
+    sl.state_in = sl.state_out = reinterpret_cast<float *>((uintptr_t)8192);
+    sl.y = reinterpret_cast<void *>((uintptr_t)12288);
+    const dc::CoreParams p = chunk_params(&sl);
+    hp.ws = dc::split_applies(p, a->in_dtype, a->flags) ? round256(dc::split_workspace_bytes(p)) : 0;
+    hp.total = 2 * hp.slot + hp.ws;
+    return hp;
+}
+
+// Streams and events of one call, released when it returns (CUDA defers the release until their work is done).
+struct HostStreams {
+    cudaStream_t up = nullptr, down = nullptr;
+    cudaEvent_t start = nullptr, up_done[2] = {}, compute_done[2] = {}, down_done[2] = {};
+    ~HostStreams() {
+        for (cudaEvent_t e : {start, up_done[0], up_done[1], compute_done[0], compute_done[1], down_done[0], down_done[1]})
+            if (e) cudaEventDestroy(e);
+        if (up) cudaStreamDestroy(up);
+        if (down) cudaStreamDestroy(down);
+    }
+    cudaError_t create() {
+        cudaError_t e = cudaStreamCreateWithFlags(&up, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&down, cudaStreamNonBlocking);
+        for (cudaEvent_t *ev : {&start, &up_done[0], &up_done[1], &compute_done[0], &compute_done[1], &down_done[0],
+                                &down_done[1]})
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+        return e;
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+uint64_t dc_chunk_fwd_host_scratch_size(const dc_chunk_args *a) {
+    if (validate_chunk(a) != DC_OK || a->batch == 0 || a->heads == 0) return 0;
+    return host_plan(a).total;
+}
+
+int dc_chunk_fwd_host(const dc_chunk_args *a, void *scratch, uint64_t scratch_bytes, dc_stream_t stream) {
+    int st = validate_chunk(a);
+    if (st != DC_OK || a->batch == 0 || a->heads == 0) return st;
+    if (a->flags & DC_FLAG_TEST_STALL) return DC_EINVAL_ARG;
+    if (!scratch || !aligned(scratch, 256)) return DC_EINVAL_ARG;
+    const HostPlan hp = host_plan(a);
+    if (scratch_bytes < hp.total) return DC_EWORKSPACE;
+    st = check_device(nullptr);
+    if (st != DC_OK) return st;
+
+    cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+    HostStreams hs;
+    cudaError_t e = hs.create();
+    // Nothing starts before the work already queued on the caller's stream (it may still use the scratch).
+    if (e == cudaSuccess) e = cudaEventRecord(hs.start, cs);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(hs.up, hs.start, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(hs.down, hs.start, 0);
+    if (e != cudaSuccess) return cuda_fail(e);
+
+    const void *src[7] = {a->q, a->k, a->v, a->erase, a->write, a->g, a->state_in};
+    void *dst_host[2] = {a->y, a->state_out};
+    char *const base = static_cast<char *>(scratch);
+    const int64_t nslices = (a->batch + hp.per_slice - 1) / hp.per_slice;
+    for (int64_t i = 0; i < nslices; ++i) {
+        const int slot = (int)(i & 1);
+        const int64_t b0 = i * hp.per_slice;
+        const int64_t nb = (a->batch - b0) < hp.per_slice ? (a->batch - b0) : hp.per_slice;
+        char *sb = base + (size_t)slot * hp.slot;
+        dc_chunk_args sl = *a;
+        sl.batch = nb;
+        sl.q = sb + hp.off[0];
+        sl.k = sb + hp.off[1];
+        sl.v = sb + hp.off[2];
+        sl.erase = sb + hp.off[3];
+        sl.write = sb + hp.off[4];
+        sl.g = a->g_w ? sb + hp.off[5] : nullptr;
+        sl.state_in = reinterpret_cast<const float *>(sb + hp.off[6]);
+        sl.y = sb + hp.off[7];
+        sl.state_out = reinterpret_cast<float *>(sb + hp.off[8]);
+        sl.workspace = hp.ws ? base + 2 * hp.slot : nullptr;
+        sl.workspace_bytes = hp.ws;
+        const void *dst[7] = {sl.q, sl.k, sl.v, sl.erase, sl.write, sl.g, sl.state_in};
+
+        // in: once the kernels of slice i-2 (the slot's last reader) are done
+        if (i >= 2) e = cudaStreamWaitEvent(hs.up, hs.compute_done[slot], 0);
+        for (int r = 0; r < 7 && e == cudaSuccess; ++r)
+            if (hp.seq_bytes[r])
+                e = cudaMemcpyAsync(const_cast<void *>(dst[r]), static_cast<const char *>(src[r]) + b0 * hp.seq_bytes[r],
+                                    (size_t)nb * hp.seq_bytes[r], cudaMemcpyHostToDevice, hs.up);
+        if (e == cudaSuccess) e = cudaEventRecord(hs.up_done[slot], hs.up);
+        // compute on the caller's stream: after the slice landed and slice i-2's results left the slot
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, hs.up_done[slot], 0);
+        if (e == cudaSuccess && i >= 2) e = cudaStreamWaitEvent(cs, hs.down_done[slot], 0);
+        if (e != cudaSuccess) return cuda_fail(e);
+        st = chunk_fwd_launch(&sl, cs);
+        if (st != DC_OK) return st;
+        e = cudaEventRecord(hs.compute_done[slot], cs);
+        // out
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(hs.down, hs.compute_done[slot], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(static_cast<char *>(dst_host[0]) + b0 * hp.seq_bytes[7], sl.y, (size_t)nb * hp.seq_bytes[7],
+                                cudaMemcpyDeviceToHost, hs.down);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(static_cast<char *>(dst_host[1]) + b0 * hp.seq_bytes[8], sl.state_out,
+                                (size_t)nb * hp.seq_bytes[8], cudaMemcpyDeviceToHost, hs.down);
+        if (e == cudaSuccess) e = cudaEventRecord(hs.down_done[slot], hs.down);
+        if (e != cudaSuccess) return cuda_fail(e);
+    }
+    // The caller's stream drains only after the last results reached the host.
+    e = cudaStreamWaitEvent(cs, hs.down_done[0], 0);
+    if (e == cudaSuccess && nslices > 1) e = cudaStreamWaitEvent(cs, hs.down_done[1], 0);
+    return e == cudaSuccess ? DC_OK : cuda_fail(e);
 }
 
 }  // extern "C"

@@ -185,6 +185,21 @@ DC_API int dc_step(const dc_step_args *args, dc_stream_t stream);
 #define DC_NOALLOC_SCRATCH_BYTES (64ull << 20)
 DC_API int dc_chunk_fwd_noalloc(const dc_chunk_args *args, dc_stream_t stream);
 
+/*
+ * dc_chunk_fwd from host memory: args' q, k, v, erase, write, g and state_in are read from, and y and
+ * state_out written to, HOST memory (page-locked for full PCIe speed).  No counterpart in the reference,
+ * whose tensors already live on the backend's device.  The batch is cut into up to 8 slices of whole
+ * sequences; each slice is copied in on one stream, computed on `stream` and copied out on another, two
+ * slices in flight, so the transfers in both directions overlap each other and the kernels.  `scratch`
+ * is device memory of at least dc_chunk_fwd_host_scratch_size(args) bytes, 256-byte aligned (both
+ * slices' device copies, plus the two-kernel path's workspace); a smaller one is DC_EWORKSPACE.  The
+ * work is ordered after everything already queued on `stream`, and `stream` is made to wait for all of
+ * it: once `stream` has drained, y and state_out hold the results.  Creates (and releases) two streams
+ * and seven events per call; allocates no memory.
+ */
+DC_API uint64_t dc_chunk_fwd_host_scratch_size(const dc_chunk_args *args);
+DC_API int dc_chunk_fwd_host(const dc_chunk_args *args, void *scratch, uint64_t scratch_bytes, dc_stream_t stream);
+
 /* Human-readable name of a dc_status. */
 DC_API const char *dc_status_string(int status);
 

@@ -161,3 +161,17 @@ def test_python_mirror_sanity_mirrors_the_reference_asserts():
     assert dn.DeltaPath.default().resolved_chunk_len() == 64
     assert dn.DeltaPath.Recurrent().resolved_chunk_len() == 1
     assert dn.DeltaPath.with_chunk_len(16).resolved_chunk_len() == 16
+
+
+def test_host_entry_point_scratch_is_host_logic():
+    a = _args(batch=10)
+    need = abi.lib().dc_chunk_fwd_host_scratch_size(a)
+    # two slots of 2 sequences each (10 sequences in up to 8 slices), every region 256-byte aligned
+    seq = [9 * 2 * 4 * 4, 9 * 2 * 4 * 4, 9 * 2 * 6 * 4, 9 * 2 * 1 * 4, 9 * 2 * 1 * 4, 9 * 2 * 1 * 4,
+           2 * 4 * 6 * 4, 9 * 2 * 6 * 4, 2 * 4 * 6 * 4]
+    slot = sum(-(-2 * n // 256) * 256 for n in seq)
+    assert need == 2 * slot
+    assert abi.lib().dc_chunk_fwd_host(a, 0x100000, need - 1, None) == abi.DC_EWORKSPACE
+    assert abi.lib().dc_chunk_fwd_host(a, 0x100010, need, None) == abi.DC_EINVAL_ARG  # scratch not 256-aligned
+    assert abi.lib().dc_chunk_fwd_host(_args(flags=abi.DC_FLAG_TEST_STALL), 0x100000, need, None) == abi.DC_EINVAL_ARG
+    assert abi.lib().dc_chunk_fwd_host_scratch_size(_args(seq=0)) == 0

@@ -122,18 +122,17 @@ __device__ __forceinline__ float qk_tile(const uint8_t *base, int which, int t, 
         base + A_QKT + 16384 * which + (uint32_t)(d >> 6) * 8192u + ptx::sw128(t, d & 63)));
 }
 
-// One bisection level (blocks of s = 2^LS rows): this thread's operand rows, then the warps' MMAs of the
-// packed 32 x 32 product, whose block-diagonal entries are scattered into Akk (fp32) and Aqk (bf16).
-// Thread (cp, q4) owns channels 2 cp, 2 cp + 1 of rows 16 q4 .. 16 q4 + 15 (one quarter); blocks of 16
-// rows or fewer lie inside a quarter, and the coarser two take their starting products from the
-// quarters' published first alphas (af) and products of the other fifteen (ar).  One copy of this body
-// serves all six levels (LS at run time, rows unrolled): the kernel's code must stay small enough for the
-// instruction cache with two CTAs per SM.
-__device__ __forceinline__ void bisection_level(int LS, uint8_t *base, uint32_t sb, float *Af,
-                                                const uint32_t (&bk2)[16], const float (&alpha)[32],
-                                                const float *af, const float *ar, float scale, int cp, int q4,
-                                                int warp, int lane) {
-    const int s = 1 << LS, half = s >> 1, lh = LS - 1;
+// One bisection level (blocks of s = 2^LS rows), part 1: this thread's operand rows.  Thread (cp, q4) owns
+// channels 2 cp, 2 cp + 1 of rows 16 q4 .. 16 q4 + 15 (one quarter).  Blocks of 16 rows or fewer lie inside a
+// quarter; at the two coarser levels a quarter lies wholly on one side of its block, and the quarters'
+// published first alphas (af) and products of the other fifteen (ar) give the starting products.  Each level
+// is its own unrolled body (LS at compile time): which rows are on which side, where their packed index
+// lands and where a running product starts are all constants, leaving a few multiplies, a pack and a store
+// per row.
+template <int LS>
+__device__ __forceinline__ void level_build(uint8_t *base, const uint32_t (&bk2)[16], const float (&alpha)[32],
+                                            const float *af, const float *ar, int cp, int q4) {
+    constexpr int s = 1 << LS, half = s >> 1, lh = LS - 1;
     uint8_t *Rkk = base + A_RKK, *Rqk = base + A_RQK, *Cc = base + A_CC;
     const int ch = 2 * cp;
     auto tile2 = [&](int which, int i) -> uint32_t {  // q (0) or k (1) of row 16 q4 + i, channels ch, ch + 1
@@ -143,60 +142,75 @@ __device__ __forceinline__ void bisection_level(int LS, uint8_t *base, uint32_t 
     auto put = [&](uint8_t *buf, int row, float x0, float x1) {
         *reinterpret_cast<uint32_t *>(buf + 2 * (row * kOP + ch)) = ptx::pack_bf16(x0, x1);
     };
-    // Which side this quarter's rows are on, where their packed index starts, and the starting products.
-    bool all_row = false, all_col = false;
-    float P0[2] = {1.f, 1.f}, Pb0[2] = {0.f, 0.f};
-    int mbase = 8 * q4;
-    if (LS == 6) {
-        all_row = q4 >= 2;
-        all_col = !all_row;
-        mbase = 16 * (q4 & 1);
+    auto row_side = [&](int i, int m, float (&P)[2], bool start, const float (&P0)[2]) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) P[c] = start ? P0[c] : P[c] * alpha[2 * i + c];
+        const uint32_t b2 = bk2[i], q2 = tile2(0, i);
+        put(Rkk, m, ptx::bf16lo(b2) * P[0], ptx::bf16hi(b2) * P[1]);
+        put(Rqk, m, ptx::bf16lo(q2) * P[0], ptx::bf16hi(q2) * P[1]);
+    };
+    auto col_side = [&](int i, int n, float (&Pb)[2], bool start, const float (&Pb0)[2]) {
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-            P0[c] = (q4 == 3) ? ar[2 * 128 + ch + c] * alpha[c] : 1.f;  // product of alphas 33 .. 48
-            Pb0[c] = (q4 == 1) ? af[2 * 128 + ch + c]                   // alpha 32
-                               : af[128 + ch + c] * ar[128 + ch + c] * af[2 * 128 + ch + c];  // alphas 16 .. 32
+            const float an = alpha[2 * (i + 1 < 16 ? i + 1 : 15) + c];  // alpha of the next row (in quarter)
+            Pb[c] = start ? Pb0[c] : Pb[c] * an;
         }
-    } else if (LS == 5) {
-        all_row = (q4 & 1) != 0;
-        all_col = !all_row;
-        mbase = 16 * (q4 >> 1);
+        const uint32_t k2 = tile2(1, i);
+        put(Cc, n, ptx::bf16lo(k2) * Pb[0], ptx::bf16hi(k2) * Pb[1]);
+    };
+    float P[2] = {1.f, 1.f}, Pb[2] = {1.f, 1.f};
+    if constexpr (LS >= 5) {
+        // The quarter is wholly a row side or a column side of its 2^LS block.
+        const bool all_row = (LS == 6) ? (q4 >= 2) : ((q4 & 1) != 0);
+        const int mbase = (LS == 6) ? 16 * (q4 & 1) : 16 * (q4 >> 1);
+        if (all_row) {
+            float P0[2] = {1.f, 1.f};
+            if (LS == 6 && q4 == 3) {
 #pragma unroll
-        for (int c = 0; c < 2; ++c) Pb0[c] = af[(q4 + 1 < 4 ? q4 + 1 : 3) * 128 + ch + c];  // alpha of the next quarter's first row
-    }
-    float P[2] = {1.f, 1.f};
+                for (int c = 0; c < 2; ++c) P0[c] = ar[2 * 128 + ch + c] * alpha[c];  // product of alphas 33 .. 48
+            }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const int pos = i & (s - 1);
-        const bool rs = all_row || (!all_col && pos >= half);
-        if (rs) {
-            const bool start = all_row ? (i == 0) : (pos == half);
-            const int m = all_row ? mbase + i : mbase + ((i >> LS) << lh) + (pos - half);
-            const uint32_t b2 = bk2[i], q2 = tile2(0, i);
-#pragma unroll
-            for (int c = 0; c < 2; ++c) P[c] = start ? (all_row ? P0[c] : 1.f) : P[c] * alpha[2 * i + c];
-            put(Rkk, m, ptx::bf16lo(b2) * P[0], ptx::bf16hi(b2) * P[1]);
-            put(Rqk, m, ptx::bf16lo(q2) * P[0], ptx::bf16hi(q2) * P[1]);
-        }
-    }
-    float Pb[2] = {1.f, 1.f};
-#pragma unroll
-    for (int i = 15; i >= 0; --i) {
-        const int pos = i & (s - 1);
-        const bool cs = all_col || (!all_row && pos < half);
-        if (cs) {
-            const bool start = all_col ? (i == 15) : (pos == half - 1);
-            const int n = all_col ? mbase + i : mbase + ((i >> LS) << lh) + pos;
-            const uint32_t k2 = tile2(1, i);
+            for (int i = 0; i < 16; ++i) row_side(i, mbase + i, P, i == 0, P0);
+        } else {
+            float Pb0[2];
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-                const float an = alpha[2 * (i + 1 < 16 ? i + 1 : 15) + c];  // alpha of the next row (in quarter)
-                Pb[c] = start ? (all_col ? Pb0[c] : an) : Pb[c] * an;
+                if (LS == 6)
+                    Pb0[c] = (q4 == 1) ? af[2 * 128 + ch + c]                                  // alpha 32
+                                       : af[128 + ch + c] * ar[128 + ch + c] * af[2 * 128 + ch + c];  // alphas 16 .. 32
+                else
+                    Pb0[c] = af[(q4 + 1 < 4 ? q4 + 1 : 3) * 128 + ch + c];  // alpha of the next quarter's first row
             }
-            put(Cc, n, ptx::bf16lo(k2) * Pb[0], ptx::bf16hi(k2) * Pb[1]);
+#pragma unroll
+            for (int i = 15; i >= 0; --i) col_side(i, mbase + i, Pb, i == 15, Pb0);
+        }
+    } else {
+        const int mbase = 8 * q4;
+        const float one[2] = {1.f, 1.f};
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int pos = i & (s - 1);
+            if (pos >= half) row_side(i, mbase + ((i >> LS) << lh) + (pos - half), P, pos == half, one);
+        }
+#pragma unroll
+        for (int i = 15; i >= 0; --i) {
+            const int pos = i & (s - 1);
+            if (pos < half) {
+                float an[2];
+#pragma unroll
+                for (int c = 0; c < 2; ++c) an[c] = alpha[2 * (i + 1 < 16 ? i + 1 : 15) + c];
+                col_side(i, mbase + ((i >> LS) << lh) + pos, Pb, pos == half - 1, an);
+            }
         }
     }
-    ptx::named_sync(tc::NB_PAR, kThreadsA);
+}
+
+// Part 2: the warps' MMAs of the packed 32 x 32 product, whose block-diagonal entries are scattered into Akk
+// (fp32) and Aqk (bf16).  One copy serves every level (LS at run time).
+__device__ __forceinline__ void level_mma(int LS, uint8_t *base, uint32_t sb, float *Af, float scale, int warp,
+                                          int lane) {
+    const int s = 1 << LS, half = s >> 1, lh = LS - 1;
+    (void)s;
     // Tiles of the packed 32 x 32 product that meet its block diagonal: all eight at the top level,
     // (mt, 2 mt) and (mt, 2 mt + 1) below.  Job = (matrix, m tile, n tile); Akk and Aqk share C.
     const int njobs = (half == 32) ? 16 : 8;
@@ -228,7 +242,6 @@ __device__ __forceinline__ void bisection_level(int LS, uint8_t *base, uint32_t 
                 st_bf16(base + A_AQK + ptx::sw128(i, j), scale * acc[e]);
         }
     }
-    ptx::named_sync(tc::NB_PAR, kThreadsA);
 }
 
 // After the call, v[0] of lane l holds the sum over the warp's lanes of v[l] (32 values, 31 shuffles).
@@ -570,7 +583,17 @@ __global__ void __launch_bounds__(kThreadsA, 2)
 
     // ---- (2) Akk (strictly lower) and Aqk (lower) by bisection levels, coarsest first ----
 #pragma unroll 1
-    for (int LS = 6; LS >= 3; --LS) bisection_level(LS, base, sb, Af, bk2, alpha, Xaf, Xar, scale, cp, q4, warp, lane);
+    for (int LS = 6; LS >= 3; --LS) {
+        switch (LS) {
+            case 6: level_build<6>(base, bk2, alpha, Xaf, Xar, cp, q4); break;
+            case 5: level_build<5>(base, bk2, alpha, Xaf, Xar, cp, q4); break;
+            case 4: level_build<4>(base, bk2, alpha, Xaf, Xar, cp, q4); break;
+            default: level_build<3>(base, bk2, alpha, Xaf, Xar, cp, q4); break;
+        }
+        ptx::named_sync(tc::NB_PAR, kThreadsA);
+        level_mma(LS, base, sb, Af, scale, warp, lane);
+        ptx::named_sync(tc::NB_PAR, kThreadsA);
+    }
     finest_levels(base, Af, X + 1536, bk2, alpha, scale, cp, q4, tid, lane);
     ptx::named_sync(tc::NB_PAR, kThreadsA);
     // The level operands are dead: bring s q e^G back into their place.

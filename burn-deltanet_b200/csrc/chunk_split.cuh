@@ -397,6 +397,38 @@ __global__ void __launch_bounds__(kThreadsA, 2)
     };
     float *Xg = X, *Xaf = X + 512, *Xar = X + 1024;  // [quarter][channel]
 
+    constexpr int kRowB = 128 * (int)sizeof(TG);  // bytes of one full-width gate row
+    const bool e_full = p.ew != 1, w_full = p.ww != 1;
+    const int64_t r_first = rowidx(16 * q4), r_step = p.heads;  // rows of this quarter: r_first + i * r_step
+    uint32_t *park_v = reinterpret_cast<uint32_t *>(ws.a6 + bhc * 128 * 128 + (16 * q4) * 128 + ch);  // v w
+    uint32_t *park_k = park_v + 64 * 64;                                                          // b k e^G
+    uint32_t *park_q = reinterpret_cast<uint32_t *>(ws.y0 + bhc * 64 * 128 + (16 * q4) * 128 + ch);  // s q e^G
+    uint32_t *kh_out = reinterpret_cast<uint32_t *>(ws.kh + (bhc * 64 + 16 * q4) * 128 + ch);
+    auto stage = [&](int k) {  // batch k: rows 4k..4k+3 of each quarter -> slots 4 q + 0..3
+        const uint32_t buf = sb + A_STG + (uint32_t)(k % 3) * kStgBytes;
+        for (int q = tid; q < 16 * (kRowB / 16); q += kThreadsA) {
+            const int slot = q / (kRowB / 16), piece = q % (kRowB / 16);
+            const int t = 16 * (slot >> 2) + 4 * k + (slot & 3);
+            const int64_t r = t < nvalid ? rowidx(t) : 0;
+            const uint32_t n = t < nvalid ? 16u : 0u;
+            if (e_full)
+                ptx::cp_async16(buf + slot * kRowB + piece * 16,
+                                static_cast<const uint8_t *>(p.erase) + r * kRowB + piece * 16, n);
+            if (w_full)
+                ptx::cp_async16(buf + 8192 + slot * kRowB + piece * 16,
+                                static_cast<const uint8_t *>(p.write) + r * kRowB + piece * 16, n);
+        }
+        {
+            const int slot = tid >> 4, piece = tid & 15;
+            const int t = 16 * (slot >> 2) + 4 * k + (slot & 3);
+            const int64_t r = t < nvalid ? rowidx(t) : 0;
+            ptx::cp_async16(buf + 16384 + slot * 256 + piece * 16, vg + r * 128 + piece * 8, t < nvalid ? 16u : 0u);
+        }
+        ptx::cp_async_commit();
+    };
+    // The scan's first two batches of erase / write / v are in flight while g loads.
+    stage(0);
+    stage(1);
     DC_SPLIT_MARK(0);
     // ---- (0) this quarter's g (all loads in flight at once) and its sum: the chunk-local offsets of G ----
     float alpha[32];  // [row][channel]; g until the scan turns it into e^g
@@ -442,38 +474,7 @@ __global__ void __launch_bounds__(kThreadsA, 2)
     //      kernel's code must fit the instruction cache), so alpha and bk2 are rotating windows whose
     //      first slots always hold the current batch. ----
     const bool tiles_ok = ptx::mbar_wait(&bars[BA_QK], 0);
-    constexpr int kRowB = 128 * (int)sizeof(TG);  // bytes of one full-width gate row
-    const bool e_full = p.ew != 1, w_full = p.ww != 1;
-    const int64_t r_first = rowidx(16 * q4), r_step = p.heads;  // rows of this quarter: r_first + i * r_step
-    uint32_t *park_v = reinterpret_cast<uint32_t *>(ws.a6 + bhc * 128 * 128 + (16 * q4) * 128 + ch);  // v w
-    uint32_t *park_k = park_v + 64 * 64;                                                          // b k e^G
-    uint32_t *park_q = reinterpret_cast<uint32_t *>(ws.y0 + bhc * 64 * 128 + (16 * q4) * 128 + ch);  // s q e^G
-    uint32_t *kh_out = reinterpret_cast<uint32_t *>(ws.kh + (bhc * 64 + 16 * q4) * 128 + ch);
-    auto stage = [&](int k) {  // batch k: rows 4k..4k+3 of each quarter -> slots 4 q + 0..3
-        const uint32_t buf = sb + A_STG + (uint32_t)(k % 3) * kStgBytes;
-        for (int q = tid; q < 16 * (kRowB / 16); q += kThreadsA) {
-            const int slot = q / (kRowB / 16), piece = q % (kRowB / 16);
-            const int t = 16 * (slot >> 2) + 4 * k + (slot & 3);
-            const int64_t r = t < nvalid ? rowidx(t) : 0;
-            const uint32_t n = t < nvalid ? 16u : 0u;
-            if (e_full)
-                ptx::cp_async16(buf + slot * kRowB + piece * 16,
-                                static_cast<const uint8_t *>(p.erase) + r * kRowB + piece * 16, n);
-            if (w_full)
-                ptx::cp_async16(buf + 8192 + slot * kRowB + piece * 16,
-                                static_cast<const uint8_t *>(p.write) + r * kRowB + piece * 16, n);
-        }
-        {
-            const int slot = tid >> 4, piece = tid & 15;
-            const int t = 16 * (slot >> 2) + 4 * k + (slot & 3);
-            const int64_t r = t < nvalid ? rowidx(t) : 0;
-            ptx::cp_async16(buf + 16384 + slot * 256 + piece * 16, vg + r * 128 + piece * 8, t < nvalid ? 16u : 0u);
-        }
-        ptx::cp_async_commit();
-    };
     uint32_t bk2[16];  // per row, (b k) of the two channels as a bf16 pair; rotates with alpha
-    stage(0);
-    stage(1);
 #pragma unroll 1
     for (int k = 0; k < 4; ++k) {
         if (k + 2 < 4)
@@ -712,13 +713,7 @@ __global__ void __launch_bounds__(kThreadsA, 2)
     if (ok) {
         ptx::tc_fence_after();
         const int sp = warp & 3, ch = warp >> 2, r = 32 * sp + lane;
-#pragma unroll 1
-        for (int qq = 0; qq < 4; ++qq) {
-            uint32_t v[32];
-            ptx::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + TMA_BIG + 128 * ch + 32 * qq, v);
-            ptx::tmem_wait_ld();
-            const float *f = reinterpret_cast<const float *>(v);
-            const int col0 = 32 * qq;
+        auto store32 = [&](const float *f, int col0) {  // this row's 32 columns from col0
             if (ch == 0 && r < 64) {
                 float4 *dst = reinterpret_cast<float4 *>(ws.u + (bhc * 64 + r) * 128 + col0);
 #pragma unroll
@@ -753,6 +748,15 @@ __global__ void __launch_bounds__(kThreadsA, 2)
                                         ptx::pack_bf16(x[6], x[7]));
                 }
             }
+        };
+#pragma unroll 1
+        for (int q2 = 0; q2 < 2; ++q2) {  // two 32-column TMEM loads per wait
+            uint32_t vv[2][32];
+            ptx::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + TMA_BIG + 128 * ch + 64 * q2, vv[0]);
+            ptx::tmem_ld32(tmem + ((uint32_t)(32 * sp) << 16) + TMA_BIG + 128 * ch + 64 * q2 + 32, vv[1]);
+            ptx::tmem_wait_ld();
+            store32(reinterpret_cast<const float *>(vv[0]), 64 * q2);
+            store32(reinterpret_cast<const float *>(vv[1]), 64 * q2 + 32);
         }
     }
 

@@ -316,6 +316,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_ptr;
 
+    // One chunk's q/k/v tiles pulled into L2 ahead of their load into a stage.
+    auto prefetch_tiles = [&](int64_t c) {
+        const int row = (int)(c * kL), qrow = (int)q_first(c, p.u);
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+            ptx::tma_prefetch_4d(&tm_k, 64 * x, (int)h, row, (int)b);
+            ptx::tma_prefetch_4d(&tm_q, 64 * x, (int)h, qrow, (int)b);
+            ptx::tma_prefetch_4d(&tm_v, 64 * x, (int)h, row, (int)b);
+        }
+    };
     // One chunk's q/k/v tiles into stage `st`, completing on its mbarrier.
     auto issue_tma = [&](int64_t c, int st) {
         uint64_t *bar = &bars[B_TMA0 + st];
@@ -587,6 +597,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!(ok = ptx::mbar_wait(&bars[B_TMA0 + st], tpar))) break;
                     issue_d1(c);
                 }
+                // Chunk c+2 loads into chunk c's stage once chunk c's MMA7 is done, more than a chunk from
+                // now: pull its tiles into L2 already, so that its load (and D1) does not wait on HBM.
+                if (c + 2 < nchunks && !p.stall) prefetch_tiles(c + 2);
             }
             if (!ok) *flag = 1;
         }

@@ -107,6 +107,14 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const void *tmap, uint64_
         : "memory");
 }
 
+// 4-D tile of a tensor map prefetched into L2 only (no shared memory, no completion to wait for): a later
+// tma_load_4d of the same tile then reads L2 instead of HBM.
+__device__ __forceinline__ void tma_prefetch_4d(const void *tmap, int c0, int c1, int c2, int c3) {
+    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(tmap), "r"(c0),
+                 "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

@@ -94,10 +94,14 @@ constexpr uint32_t OFF_AQK = OFF_S + 32768;             // Aqk bf16 64x64 K-majo
 constexpr uint32_t OFF_AF = OFF_AQK + 8192;             // [Tb; Pb] lo
 constexpr uint32_t OFF_TF = OFF_AF + 64 * kAP * 4;      // T fp32 [64][68];   then [Tw; Pw] lo
 constexpr uint32_t OFF_AK = OFF_TF + 64 * kAP * 4;      // Akk fp32 [64][68]; E blocks above its diagonal
-constexpr uint32_t OFF_GATE = OFF_AK + 64 * kAP * 4;    // per stage: e[64], w[64], g[64]
-constexpr uint32_t OFF_G = OFF_GATE + 2 * 3 * 64 * 4;   // per stage: G[64], gam[64]
-constexpr uint32_t OFF_BAR = OFF_G + 2 * 2 * 64 * 4;    // mbarriers (below)
-constexpr int kBars = 12;
+// Gate slots: chunk c's gates live in slot c % 3.  Three, not two: the operand role writes chunk c+2's
+// gates as soon as it finishes chunk c+1, which can be before the state role has read chunk c's (A6, V'/y);
+// it can only start chunk c+3 after chunk c+1's MMA4, which waits for the state role to release chunk c.
+constexpr int kGateSlots = 3;
+constexpr uint32_t OFF_GATE = OFF_AK + 64 * kAP * 4;             // per slot: e[64], w[64], g[64]
+constexpr uint32_t OFF_G = OFF_GATE + kGateSlots * 3 * 64 * 4;   // per slot: G[64], gam[64]
+constexpr uint32_t OFF_BAR = OFF_G + kGateSlots * 2 * 64 * 4;    // mbarriers (below)
+constexpr int kBars = 13;
 constexpr uint32_t OFF_TMEMPTR = OFF_BAR + kBars * 8;
 constexpr uint32_t OFF_FLAG = OFF_TMEMPTR + 4;
 constexpr uint32_t OFF_PEND = OFF_FLAG + 4;             // int[2]: parity of a stage's TMA load in flight, or -1
@@ -110,8 +114,8 @@ static_assert(kSmemBytes <= 232448, "over the 227 KB per-CTA shared-memory limit
 // mbarrier slots.  MMA4 commits twice: B_MMA4W once its D_W half (reading [Tw; Pw] and the T buffer) is
 // done, B_MMA4 once all of it is.  B_OPS: the operand role has finished a chunk (TM_A free, MMA4's
 // operands written).
-enum Bar { B_TMA0 = 0, B_TMA1, B_MMA1, B_MMAP, B_MMA4W, B_MMA4, B_MMA6, B_MMA7, B_UY_FREE, B_OPS, B_GATE0, B_GATE1 };
-static_assert(B_GATE1 + 1 == kBars, "barrier count");
+enum Bar { B_TMA0 = 0, B_TMA1, B_MMA1, B_MMAP, B_MMA4W, B_MMA4, B_MMA6, B_MMA7, B_UY_FREE, B_OPS, B_GATE0 };
+static_assert(B_GATE0 + kGateSlots == kBars, "barrier count");
 
 // TMEM columns (512 allocated): A = D1 / D_P, W = D_W (then A6), UY = D_UY, S = D_S.
 constexpr uint32_t TM_A = 0, TM_W = 128, TM_UY = 256, TM_S = 384;
@@ -280,8 +284,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sb = ptx::smem_u32(base);
     float *Ak = reinterpret_cast<float *>(base + OFF_AK);
     float *Tf = reinterpret_cast<float *>(base + OFF_TF);
-    float *gates = reinterpret_cast<float *>(base + OFF_GATE);  // [stage][e | w | g][64]
-    float *Gs = reinterpret_cast<float *>(base + OFF_G);        // [stage][G | gam][64]
+    float *gates = reinterpret_cast<float *>(base + OFF_GATE);  // [slot][e | w | g][64]
+    float *Gs = reinterpret_cast<float *>(base + OFF_G);        // [slot][G | gam][64]
     uint64_t *bars = reinterpret_cast<uint64_t *>(base + OFF_BAR);
     uint32_t *tmem_ptr = reinterpret_cast<uint32_t *>(base + OFF_TMEMPTR);
     volatile int *flag = reinterpret_cast<volatile int *>(base + OFF_FLAG);
@@ -365,19 +369,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         float gnext = (tid < 192) ? load_gate<TG>(p, b, h, 0, tid) : 0.f;
 
         for (int64_t c = 0; c < nchunks; ++c) {
-            const int st = (int)(c & 1);
-            const float *ge = gates + (st * 3 + 0) * 64;
-            const float *gw = gates + (st * 3 + 1) * 64;
-            float *Gc = Gs + st * 128;
+            const int gsl = (int)(c % kGateSlots);
+            const float *ge = gates + (gsl * 3 + 0) * 64;
+            const float *gw = gates + (gsl * 3 + 1) * 64;
+            float *Gc = Gs + gsl * 128;
             float *gam = Gc + 64;
             DC_TC_MARK(0);
 
             // ---- chunk c's gates -> G = cumsum(g), gam = e^G; published to the serial role ----
-            if (tid < 192) gates[st * 192 + tid] = gnext;
+            if (tid < 192) gates[gsl * 192 + tid] = gnext;
             ptx::named_sync(NB_PAR, kParThreads);
             if (c + 1 < nchunks && tid < 192) gnext = load_gate<TG>(p, b, h, c + 1, tid);
             if (warp == 0) {
-                const float *g = gates + (st * 3 + 2) * 64;
+                const float *g = gates + (gsl * 3 + 2) * 64;
                 const float x0 = g[2 * lane], x1 = g[2 * lane + 1];
                 float s = x0 + x1;
 #pragma unroll
@@ -391,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 gam[2 * lane] = __expf(s - x1);
             }
             ptx::named_sync(NB_PAR, kParThreads);
-            if (leader) ptx::mbar_arrive(&bars[B_GATE0 + st]);
+            if (leader) ptx::mbar_arrive(&bars[B_GATE0 + gsl]);
             DC_TC_MARK(1);
 
             // ---- D1 = [K; Q] K^T, issued by the issue warp once chunk c's tiles landed ----
@@ -657,7 +661,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int64_t c = 0; c < nchunks && ok; ++c) {
             const int st = (int)(c & 1);
             const uint32_t stg = sb + OFF_STAGE + st * kStageBytes;
-            const float *Gc = Gs + st * 128;
+            const float *Gc = Gs + (int)(c % kGateSlots) * 128;
             const float *gam = Gc + 64;
             DC_TC_MARK(8);
 
@@ -801,8 +805,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             // ---- S -> bf16 operand and the accumulator pre-scaled by the next chunk's decay ----
             if (c + 1 < nchunks) {
-                if (!(ok = ser_wait(B_GATE0 + (st ^ 1), (uint32_t)(((c + 1) >> 1) & 1)))) break;
-                const float Gam = Gs[(st ^ 1) * 128 + 64 + 63];
+                const int gnx = (int)((c + 1) % kGateSlots);
+                if (!(ok = ser_wait(B_GATE0 + gnx, (uint32_t)(((c + 1) / kGateSlots) & 1)))) break;
+                const float Gam = Gs[gnx * 128 + 64 + 63];
                 ptx::tc_fence_after();
 #pragma unroll 1
                 for (int hh = 0; hh < 2; ++hh) {

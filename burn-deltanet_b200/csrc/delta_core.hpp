@@ -140,7 +140,7 @@ struct DeltaInput {
     // per-channel gates (GDN-2) a workspace of this size lets the tensor cores
     // take the prefill; without one it runs on the CUDA cores.
     uint64_t workspace_size(const DeltaPath &path, DType y_dtype) const {
-        const dc_chunk_args a = args(path, nullptr, y_dtype, nullptr, nullptr, 0);
+        const dc_chunk_args a = args(path, placeholder_y(), y_dtype, placeholder_state(), nullptr, 0);
         return dc_chunk_workspace_size(&a);
     }
 
@@ -155,7 +155,32 @@ struct DeltaInput {
         check_status(dc_chunk_fwd(&a, stream), "DeltaInput::run");
     }
 
+    // Bytes of device scratch run_from_host() needs for `path`.
+    uint64_t host_scratch_size(const DeltaPath &path, DType y_dtype) const {
+        const dc_chunk_args a = args(path, placeholder_y(), y_dtype, placeholder_state(), nullptr, 0);
+        return dc_chunk_fwd_host_scratch_size(&a);
+    }
+
+    // run() for a caller whose tensors are in HOST memory (every view, y and
+    // final_state; page-locked for full PCIe speed): the library streams the
+    // batch through the GPU in slices of whole sequences, the copies in both
+    // directions overlapping the kernels, over `scratch` (device memory of
+    // host_scratch_size() bytes, 256-byte aligned).  Returns once the work is
+    // queued; the results are on the host when `stream` has drained.
+    void run_from_host(const DeltaPath &path, void *y, DType y_dtype, float *final_state, void *scratch,
+                       uint64_t scratch_bytes, dc_stream_t stream = nullptr) const {
+        sanity();
+        const dc_chunk_args a = args(path, y, y_dtype, final_state, nullptr, 0);
+        check_status(dc_chunk_fwd_host(&a, scratch, scratch_bytes, stream), "DeltaInput::run_from_host");
+    }
+
   private:
+    // Size queries depend on the shapes and on whether the outputs are 16-byte aligned, not on where they
+    // are: they pass these stand-ins (aligned, distinct, never dereferenced), i.e. assume aligned outputs
+    // such as any device allocation.
+    static void *placeholder_y() { return reinterpret_cast<void *>(uintptr_t{1} << 12); }
+    static float *placeholder_state() { return reinterpret_cast<float *>(uintptr_t{1} << 13); }
+
     dc_chunk_args args(const DeltaPath &path, void *y, DType y_dtype, float *final_state, void *workspace,
                        uint64_t workspace_bytes) const {
         const Dims d = dims();

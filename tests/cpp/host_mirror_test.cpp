@@ -198,8 +198,66 @@ int main() {
         std::vector<double> yd(y.begin(), y.end()), sd(s.begin(), s.end());
         const double e = std::fmax(max_abs(yd, y0), max_abs(sd, s0));
         expect(e < 2e-2, "bf16 tensor-core chunk path (d = 128)", e);
+
+        // The same call from host memory (pinned): bit-identical to the device call.
+        DeltaInput hin = in;
+        uint16_t *hq, *hk, *hv;
+        float *hb, *hg, *hs, *hy, *hso;
+        cudaMallocHost(&hq, qb.size() * 2);
+        cudaMallocHost(&hk, kb.size() * 2);
+        cudaMallocHost(&hv, vb.size() * 2);
+        cudaMallocHost(&hb, bf.size() * 4);
+        cudaMallocHost(&hg, gf.size() * 4);
+        cudaMallocHost(&hs, sf.size() * 4);
+        cudaMallocHost(&hy, y.size() * 4);
+        cudaMallocHost(&hso, s.size() * 4);
+        std::memcpy(hq, qb.data(), qb.size() * 2);
+        std::memcpy(hk, kb.data(), kb.size() * 2);
+        std::memcpy(hv, vb.data(), vb.size() * 2);
+        std::memcpy(hb, bf.data(), bf.size() * 4);
+        std::memcpy(hg, gf.data(), gf.size() * 4);
+        std::memcpy(hs, sf.data(), sf.size() * 4);
+        hin.q_bshk = view4(hq, 2, 200, 2, 128, DType::BF16);
+        hin.k_bshk = view4(hk, 2, 200, 2, 128, DType::BF16);
+        hin.v_bshv = view4(hv, 2, 200, 2, 128, DType::BF16);
+        hin.erase_bshK = view4(hb, 2, 200, 2, 1, DType::F32);
+        hin.write_bshV = view4(hb, 2, 200, 2, 1, DType::F32);
+        hin.g_bshK = view4(hg, 2, 200, 2, 1, DType::F32);
+        hin.state_bhkv = hs;
+        const uint64_t need = hin.host_scratch_size(DeltaPath::chunk(), DType::F32);
+        void *scratch = nullptr;
+        cudaMalloc(&scratch, need);
+        hin.run_from_host(DeltaPath::chunk(), hy, DType::F32, hso, scratch, need);
+        cudaDeviceSynchronize();
+        const bool same = std::memcmp(hy, y.data(), y.size() * 4) == 0 && std::memcmp(hso, s.data(), s.size() * 4) == 0;
+        expect(same, "run_from_host == run (bit-identical)", 0.0);
+        for (void *ptr : {(void *)hq, (void *)hk, (void *)hv, (void *)hb, (void *)hg, (void *)hs, (void *)hy, (void *)hso})
+            cudaFreeHost(ptr);
+        cudaFree(scratch);
         for (void *ptr : {(void *)dq, (void *)dk, (void *)dv, (void *)db, (void *)dg, (void *)ds, (void *)dy, (void *)dso})
             cudaFree(ptr);
+    }
+
+    // Size queries are host logic: per-channel gates need a workspace (the two-kernel tensor-core path),
+    // per-head gates do not; the host entry point always needs its scratch.
+    {
+        auto fake = [](int i) { return reinterpret_cast<const void *>(uintptr_t{1} << (20 + i)); };
+        DeltaInput in;
+        in.q_bshk = view4(fake(0), 1, 128, 2, 128, DType::BF16);
+        in.k_bshk = view4(fake(1), 1, 128, 2, 128, DType::BF16);
+        in.v_bshv = view4(fake(2), 1, 128, 2, 128, DType::BF16);
+        in.erase_bshK = view4(fake(3), 1, 128, 2, 128, DType::F32);
+        in.write_bshV = view4(fake(4), 1, 128, 2, 128, DType::F32);
+        TensorView g = view4(fake(5), 1, 128, 2, 128, DType::F32);
+        in.g_bshK = g;
+        in.state_bhkv = reinterpret_cast<const float *>(fake(6));
+        const uint64_t ws = in.workspace_size(DeltaPath::chunk(), DType::F32);
+        expect(ws == 2ull * 2 * 98816, "workspace_size: per-channel gates, 2 chunks x 2 heads", (double)ws);
+        in.erase_bshK = view4(fake(3), 1, 128, 2, 1, DType::F32);
+        in.write_bshV = view4(fake(4), 1, 128, 2, 1, DType::F32);
+        in.g_bshK = view4(fake(5), 1, 128, 2, 1, DType::F32);
+        expect(in.workspace_size(DeltaPath::chunk(), DType::F32) == 0, "workspace_size: per-head gates need none", 0.0);
+        expect(in.host_scratch_size(DeltaPath::chunk(), DType::F32) > 0, "host_scratch_size > 0", 0.0);
     }
 
     // The reference's panics as exceptions.

@@ -147,3 +147,33 @@ def test_deltaproduct_fold_ungated():
     raw["g"] = None
     y, s, y0, s0 = run_tc_fold(raw, 2)
     assert np.abs(y - y0).max() < BF16_TOL and np.abs(s - s0).max() < BF16_TOL
+
+
+@pytest.mark.parametrize("cfg,u,out_dtype", [(3, 1, torch.float32), (4, 2, torch.float32), (4, 3, torch.bfloat16),
+                                             (3, 1, torch.bfloat16)])
+def test_repeat_calls_are_bit_identical(cfg, u, out_dtype):
+    """The kernel's roles hand buffers to each other through mbarriers only; a buffer reused too early shows
+    up as run-to-run differences.  Gated inputs (the gate slots are read by both roles), several chunks,
+    five calls, and a one-sequence call against its rows of the batched one."""
+    raw = config_inputs(cfg, np.random.default_rng(31 + u), 3, 200, 2, 128, 128, u=u)
+    raw["state"] = np.random.default_rng(32).normal(0, 0.02, raw["state"].shape)
+    q, k, v = (dev(raw[n], torch.bfloat16) for n in ("q", "k", "v"))
+    e, w, g, st = (dev(raw[n]) for n in ("erase", "write", "g", "state"))
+
+    def call(sl=slice(None)):
+        y, s = dn.delta_chunk_recalculated(q[sl].contiguous(), k[sl].contiguous(), v[sl].contiguous(),
+                                           e[sl].contiguous(), w[sl].contiguous(), g[sl].contiguous(),
+                                           st[sl].contiguous(), True, 64, 1 / np.sqrt(128), n_householder=u,
+                                           out_dtype=out_dtype)
+        torch.cuda.synchronize()
+        return y, s
+
+    assert abi.lib().dc_chunk_kernel_choice is not None
+    y0, s0 = call()
+    for _ in range(4):
+        y, s = call()
+        assert torch.equal(y, y0) and torch.equal(s, s0)
+    for b in range(3):
+        y, s = call(slice(b, b + 1))
+        assert torch.equal(y, y0[b:b + 1]) and torch.equal(s, s0[b:b + 1])
+    assert abi.lib().dc_device_status(1) == 0

@@ -284,3 +284,24 @@ def test_step_stream_matches_the_per_tile_kernel(widths, in_dtype, out_dtype):
     assert (s0 - s1).abs().max().item() < 1e-5
     assert torch.equal(y1, y2) and torch.equal(s1, st2)
     assert abi.lib().dc_device_status(1) == 0
+
+
+def test_step_stream_repeat_calls_are_bit_identical():
+    """The streaming decode kernel's producer and consumers share a three-slot ring: repeated ticks from the
+    same state, and a subset of the heads, must agree bit for bit."""
+    rng = np.random.default_rng(51)
+    b, h, d = 300, 4, 128  # 1200 heads: every CTA walks several heads through the ring
+    raw = config_inputs(5, rng, b, 1, h, d, d)
+    st = to_dev(rng.normal(0, 0.05, (b, h, d, d)))
+    dv = {n: to_dev(raw[n], torch.bfloat16 if n in ("q", "k", "v") else torch.float32)[:, 0].contiguous()
+          for n in ("q", "k", "v", "erase", "write", "g")}
+    args = (dv["q"], dv["k"], dv["v"], dv["erase"], dv["write"], dv["g"])
+    y0, s0 = dn.delta_step(*args, st, 0.09, out_dtype=torch.float32)
+    for _ in range(4):
+        y, s = dn.delta_step(*args, st, 0.09, out_dtype=torch.float32)
+        assert torch.equal(y, y0) and torch.equal(s, s0)
+    sub = slice(7, 9)
+    y, s = dn.delta_step(*(t[sub].contiguous() for t in args), st[sub].contiguous(), 0.09, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y0[sub]) and torch.equal(s, s0[sub])
+    assert abi.lib().dc_device_status(1) == 0

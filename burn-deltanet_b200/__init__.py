@@ -12,23 +12,24 @@ The package directory name is not a Python identifier; import it with
 """
 from . import _abi
 from .core import (
+    DeltaChunkFunction,
     DeltaCoreError,
     DeltaInput,
     DeltaPath,
     DeltaShapeError,
     TriSolve,
     beta_gates,
-    delta_chunk_recalculated,
     delta_chunk_host_scratch_size,
+    delta_chunk_recalculated,
+    delta_chunk_recalculated_backward,
     delta_chunk_recalculated_host,
     delta_step,
 )
 
 __all__ = [
-    "DeltaCoreError", "DeltaInput", "DeltaPath", "DeltaShapeError", "TriSolve",
-    "beta_gates", "delta_chunk_recalculated", "delta_chunk_recalculated_host", "delta_chunk_host_scratch_size",
-    "delta_step",
-    "library_path",
+    "DeltaChunkFunction", "DeltaCoreError", "DeltaInput", "DeltaPath", "DeltaShapeError", "TriSolve",
+    "beta_gates", "delta_chunk_host_scratch_size", "delta_chunk_recalculated", "delta_chunk_recalculated_backward",
+    "delta_chunk_recalculated_host", "delta_step", "library_path",
 ]
 
 

@@ -39,6 +39,8 @@ EXPORTS = (
     "dc_chunk_fwd_noalloc",
     "dc_chunk_fwd_host_scratch_size",
     "dc_chunk_fwd_host",
+    "dc_chunk_bwd_workspace_size",
+    "dc_chunk_bwd",
 )
 
 
@@ -56,6 +58,18 @@ class ChunkArgs(ctypes.Structure):
         ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
         ("erase", ctypes.c_void_p), ("write", ctypes.c_void_p), ("g", ctypes.c_void_p),
         ("state_in", ctypes.c_void_p), ("y", ctypes.c_void_p), ("state_out", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
+    ]
+
+
+class ChunkBwdArgs(ctypes.Structure):
+    """struct dc_chunk_bwd_args."""
+    _fields_ = [
+        ("fwd", ChunkArgs),
+        ("d_y", ctypes.c_void_p), ("d_state_final", ctypes.c_void_p),
+        ("d_q", ctypes.c_void_p), ("d_k", ctypes.c_void_p), ("d_v", ctypes.c_void_p),
+        ("d_erase", ctypes.c_void_p), ("d_write", ctypes.c_void_p), ("d_g", ctypes.c_void_p),
+        ("d_state", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
     ]
 
@@ -110,6 +124,10 @@ def lib() -> ctypes.CDLL:
         L.dc_chunk_fwd_host_scratch_size.restype = ctypes.c_uint64
         L.dc_chunk_fwd_host.argtypes = [ctypes.POINTER(ChunkArgs), ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
         L.dc_chunk_fwd_host.restype = ctypes.c_int
+        L.dc_chunk_bwd_workspace_size.argtypes = [ctypes.POINTER(ChunkBwdArgs)]
+        L.dc_chunk_bwd_workspace_size.restype = ctypes.c_uint64
+        L.dc_chunk_bwd.argtypes = [ctypes.POINTER(ChunkBwdArgs), ctypes.c_void_p]
+        L.dc_chunk_bwd.restype = ctypes.c_int
         _lib = L
     return _lib
 

@@ -232,6 +232,80 @@ def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_b
     return y, s_out
 
 
+def delta_chunk_recalculated_backward(d_y_bshv, d_final_state_bhkv, q_bshk, k_bshk, v_bshv, erase_bshK,
+                                      write_bshV, g_bshK, state_bhkv, has_gate: bool, chunk_len: int,
+                                      scale: float, *, n_householder: int = 1,
+                                      workspace: Optional[torch.Tensor] = None):
+    """The backward of :func:`delta_chunk_recalculated` (``dc_chunk_bwd``): the
+    reference's ``combined_backward`` (src/delta/chunk_recalculated/
+    combined_backward.rs:72-84) on CUDA tensors.
+
+    Returns ``(d_q, d_k, d_v, d_erase, d_write, d_g, d_state)`` (float32, each
+    shaped like its input; ``d_g`` is ``None`` unless ``has_gate``): the
+    derivatives of ``<y, d_y> + <final_state, d_final_state>`` through the
+    forward call with the given inputs.  ``d_final_state_bhkv`` may be
+    ``None`` (zero).  dk, dv <= 128.
+    """
+    # (the forward's y / final state are not used: one-element stand-ins)
+    a, _, _ = _chunk_args(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv, has_gate,
+                          chunk_len, scale, n_householder, torch.float32, False, False, False, None, None,
+                          _check_tensor, lambda shape, dt: torch.empty(1, device=q_bshk.device, dtype=dt))
+    _check_tensor(d_y_bshv, "d_y")
+    if d_y_bshv.dtype != torch.float32 or tuple(d_y_bshv.shape) != (a.batch, a.seq, a.heads, a.dv):
+        raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, f"d_y must be float32 [{a.batch}, {a.seq}, {a.heads}, {a.dv}]")
+    if d_final_state_bhkv is not None:
+        _check_tensor(d_final_state_bhkv, "d_final_state")
+        if d_final_state_bhkv.dtype != torch.float32 or d_final_state_bhkv.shape != state_bhkv.shape:
+            raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, "d_final_state must be float32 shaped like the state")
+    new = lambda t: torch.empty(t.shape, device=t.device, dtype=torch.float32)
+    grads = dict(d_q=new(q_bshk), d_k=new(k_bshk), d_v=new(v_bshv), d_erase=new(erase_bshK),
+                 d_write=new(write_bshV), d_g=new(g_bshK) if has_gate else None, d_state=new(state_bhkv))
+    bw = _abi.ChunkBwdArgs()
+    bw.fwd = a
+    bw.d_y = d_y_bshv.data_ptr()
+    bw.d_state_final = None if d_final_state_bhkv is None else d_final_state_bhkv.data_ptr()
+    for name, t in grads.items():
+        setattr(bw, name, None if t is None else t.data_ptr())
+    need = int(_abi.lib().dc_chunk_bwd_workspace_size(bw))
+    if workspace is None:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=q_bshk.device)
+    _check_tensor(workspace, "workspace")
+    bw.workspace, bw.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    with torch.cuda.device(q_bshk.device):
+        _raise(_abi.lib().dc_chunk_bwd(bw, torch.cuda.current_stream(q_bshk.device).cuda_stream), "dc_chunk_bwd")
+    return (grads["d_q"], grads["d_k"], grads["d_v"], grads["d_erase"], grads["d_write"], grads["d_g"],
+            grads["d_state"])
+
+
+class DeltaChunkFunction(torch.autograd.Function):
+    """The custom autodiff node (src/delta/chunk_recalculated/backward.rs:30-265): the forward
+    keeps only its leaf inputs, and the backward recomputes what it needs from them.
+
+    ``y, final_state = DeltaChunkFunction.apply(q, k, v, erase, write, g, state, has_gate,
+    chunk_len, scale, n_householder)``; gradients flow to every tensor input (``g`` when
+    ``has_gate``).  y is float32."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, erase, write, g, state, has_gate, chunk_len, scale, n_householder=1):
+        y, s_out = delta_chunk_recalculated(q, k, v, erase, write, g, state, has_gate, chunk_len, scale,
+                                            n_householder=n_householder, out_dtype=torch.float32)
+        ctx.save_for_backward(q, k, v, erase, write, g if has_gate else None, state)
+        ctx.cfg = (has_gate, chunk_len, scale, n_householder)
+        return y, s_out
+
+    @staticmethod
+    def backward(ctx, d_y, d_state):
+        q, k, v, erase, write, g, state = ctx.saved_tensors
+        has_gate, chunk_len, scale, u = ctx.cfg
+        d_y = torch.zeros_like(v[:, :q.shape[1]], dtype=torch.float32) if d_y is None else d_y.float().contiguous()
+        d_state = None if d_state is None else d_state.float().contiguous()
+        dq, dk, dv, de, dw, dg, ds = delta_chunk_recalculated_backward(
+            d_y, d_state, q, k, v, erase, write, g, state, has_gate, chunk_len, scale, n_householder=u)
+        cast = lambda grad, like: None if grad is None else grad.to(like.dtype)
+        return (cast(dq, q), cast(dk, k), cast(dv, v), cast(de, erase), cast(dw, write),
+                cast(dg, g) if has_gate else None, cast(ds, state), None, None, None, None)
+
+
 def _check_host_tensor(t: torch.Tensor, what: str) -> None:
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{what} must be a torch.Tensor")

@@ -16,6 +16,7 @@
 #include "../../include/deltacore.h"
 #include "chunk_simt.cuh"
 #include "chunk_split.cuh"
+#include "bwd_recurrent.cuh"
 #include "chunk_tc.cuh"
 #include "common.cuh"
 #include "step.cuh"
@@ -605,6 +606,95 @@ int dc_chunk_fwd_host(const dc_chunk_args *a, void *scratch, uint64_t scratch_by
     e = cudaStreamWaitEvent(cs, hs.down_done[0], 0);
     if (e == cudaSuccess && nslices > 1) e = cudaStreamWaitEvent(cs, hs.down_done[1], 0);
     return e == cudaSuccess ? DC_OK : cuda_fail(e);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// dc_chunk_bwd: the backward, token by token on the CUDA cores (bwd_recurrent.cuh).
+// ---------------------------------------------------------------------------
+namespace {
+
+int validate_bwd(const dc_chunk_bwd_args *a) {
+    if (!a) return DC_EINVAL_ARG;
+    const dc_chunk_args &f = a->fwd;
+    // The forward's own checks, with stand-ins for the outputs this call does not use.
+    dc_chunk_args chk = f;
+    chk.y = reinterpret_cast<void *>((uintptr_t)1 << 12);
+    chk.state_out = reinterpret_cast<float *>((uintptr_t)1 << 13);
+    chk.out_dtype = DC_F32;
+    chk.workspace = nullptr;
+    chk.workspace_bytes = 0;
+    chk.flags = 0;
+    int st = validate_chunk(&chk);
+    if (st != DC_OK) return st;
+    if (f.dk > dc::bwd::kMaxD || f.dv > dc::bwd::kMaxD) return DC_EUNSUPPORTED;
+    if (!a->d_y || !a->d_q || !a->d_k || !a->d_v || !a->d_erase || !a->d_write || !a->d_state) return DC_EINVAL_ARG;
+    if (f.g_w > 0 && !a->d_g) return DC_EINVAL_ARG;
+    if (a->workspace && !aligned(a->workspace, 16)) return DC_EINVAL_ARG;
+    return DC_OK;
+}
+
+uint64_t bwd_workspace_bytes(const dc_chunk_args &f) {
+    const int64_t n = f.seq * f.n_householder;
+    const int64_t nblk = (n + dc::bwd::kBlk - 1) / dc::bwd::kBlk;
+    const uint64_t per = (uint64_t)f.dk * (uint64_t)f.dv * 4ull;
+    return (uint64_t)(f.batch * f.heads) * (uint64_t)(nblk + dc::bwd::kBlk) * per;
+}
+
+template <typename TI, typename TG>
+int launch_bwd_typed(const dc::bwd::Params &p, cudaStream_t s) {
+    const dc::bwd::Layout L((int)p.f.dk, (int)p.f.dv);
+    const size_t smem = (size_t)L.total * sizeof(float);
+    auto kern = dc::bwd::bwd_recurrent_kernel<TI, TG>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e);
+    kern<<<(unsigned)(p.f.batch * p.f.heads), dc::bwd::kThreads, smem, s>>>(p);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? DC_OK : cuda_fail(e);
+}
+
+}  // namespace
+
+extern "C" {
+
+uint64_t dc_chunk_bwd_workspace_size(const dc_chunk_bwd_args *a) {
+    if (validate_bwd(a) != DC_OK) return 0;
+    return bwd_workspace_bytes(a->fwd);
+}
+
+int dc_chunk_bwd(const dc_chunk_bwd_args *a, dc_stream_t stream) {
+    int st = validate_bwd(a);
+    if (st != DC_OK) return st;
+    const dc_chunk_args &f = a->fwd;
+    if (f.batch == 0 || f.heads == 0) return DC_OK;
+    if (!a->workspace || a->workspace_bytes < bwd_workspace_bytes(f)) return DC_EWORKSPACE;
+    st = check_device(nullptr);
+    if (st != DC_OK) return st;
+    dc::bwd::Params p{};
+    p.f = chunk_params(&f);
+    p.dy = a->d_y;
+    p.dS_final = a->d_state_final;
+    p.dq = a->d_q;
+    p.dk = a->d_k;
+    p.dv = a->d_v;
+    p.de = a->d_erase;
+    p.dw = a->d_write;
+    p.dg = a->d_g;
+    p.dS0 = a->d_state;
+    const int64_t n = f.seq * f.n_householder;
+    p.nblk = (n + dc::bwd::kBlk - 1) / dc::bwd::kBlk;
+    p.ckpt = static_cast<float *>(a->workspace);
+    p.scratch = p.ckpt + (size_t)(f.batch * f.heads) * (size_t)p.nblk * (size_t)(f.dk * f.dv);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int key = f.in_dtype * 2 + f.gate_dtype;
+    switch (key) {
+        case 0: return launch_bwd_typed<float, float>(p, s);
+        case 1: return launch_bwd_typed<float, __nv_bfloat16>(p, s);
+        case 2: return launch_bwd_typed<__nv_bfloat16, float>(p, s);
+        case 3: return launch_bwd_typed<__nv_bfloat16, __nv_bfloat16>(p, s);
+    }
+    return DC_EUNSUPPORTED_DTYPE;
 }
 
 }  // extern "C"

@@ -200,6 +200,37 @@ DC_API int dc_chunk_fwd_noalloc(const dc_chunk_args *args, dc_stream_t stream);
 DC_API uint64_t dc_chunk_fwd_host_scratch_size(const dc_chunk_args *args);
 DC_API int dc_chunk_fwd_host(const dc_chunk_args *args, void *scratch, uint64_t scratch_bytes, dc_stream_t stream);
 
+/*
+ * The backward of dc_chunk_fwd: the gradients the reference's custom autodiff node returns.  Mirrors
+ *   fn combined_backward(d_y_bshv, d_final_state_bhkv, q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV,
+ *                        g_bshK: Option<_>, state_bhkv, chunk_len, scale) -> DeltaChunkGrads
+ * (src/delta/chunk_recalculated/combined_backward.rs:72-84), i.e. the derivatives of
+ * L = <y, d_y> + <final_state, d_state_final> with respect to every input of the forward call
+ * described by `fwd` (its y, state_out and workspace fields are not used).  Gradients are float32 in
+ * the layouts of their inputs, gate gradients at the gate's own width (summed over a broadcast axis);
+ * d_g is written when fwd.g_w > 0.  d_state_final may be NULL (zero).  Needs dk, dv <= 128 and a device
+ * workspace of dc_chunk_bwd_workspace_size(args) bytes (16-byte aligned): per (batch, head) the state at
+ * every 16th micro-step and a 16-step replay buffer.  This first implementation walks the recurrence
+ * back token by token on the CUDA cores in fp32, one CTA per (batch, head).
+ */
+typedef struct dc_chunk_bwd_args {
+    dc_chunk_args fwd;
+    const float *d_y;           /* [batch, seq, heads, dv] */
+    const float *d_state_final; /* [batch, heads, dk, dv], or NULL */
+    float *d_q;                 /* [batch, seq, heads, dk] */
+    float *d_k;                 /* [batch, seq*u, heads, dk] */
+    float *d_v;                 /* [batch, seq*u, heads, dv] */
+    float *d_erase;             /* [batch, seq*u, heads, erase_w] */
+    float *d_write;             /* [batch, seq*u, heads, write_w] */
+    float *d_g;                 /* [batch, seq, heads, g_w], or NULL when g_w == 0 */
+    float *d_state;             /* [batch, heads, dk, dv] */
+    void *workspace;
+    uint64_t workspace_bytes;
+} dc_chunk_bwd_args;
+
+DC_API uint64_t dc_chunk_bwd_workspace_size(const dc_chunk_bwd_args *args);
+DC_API int dc_chunk_bwd(const dc_chunk_bwd_args *args, dc_stream_t stream);
+
 /* Human-readable name of a dc_status. */
 DC_API const char *dc_status_string(int status);
 

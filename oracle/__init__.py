@@ -12,7 +12,10 @@ It wraps ``liboracle.so`` (``oracle_core.c``, built by ``oracle/Makefile``):
   tri.rs:72-136 (the reference's chunkwise WY forward);
 * ``fold`` / ``unfold`` — the DeltaProduct / GDN-2 micro-step fold of
   src/delta_product/delta_product.rs:178-228 (q on the last micro-step, the
-  forget gate on the first, the output of the last micro-step kept).
+  forget gate on the first, the output of the last micro-step kept);
+* ``recurrent_backward`` (``oracle/backward.py``, numpy) — the gradients of
+  the custom backward (src/delta/chunk_recalculated/combined_backward.rs:
+  72-190) as the derivative of the recurrence, float64.
 
 Arrays use the reference's layouts: per-token ``[batch, seq, heads, width]``,
 state ``[batch, heads, dk, dv]``.
@@ -180,3 +183,6 @@ def householder(kind, q, k, v, erase, write, g, state, u, chunk_len=64, scale=No
     else:
         y, s = chunk(qf, k, v, erase, write, gf, state, chunk_len, scale, dtype, threads)
     return unfold(y, u), s
+
+
+from .backward import recurrent_backward  # noqa: E402  (numpy only)

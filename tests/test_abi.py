@@ -47,6 +47,7 @@ def test_struct_layout_matches_the_header(tmp_path):
     fields = {
         "dc_chunk_args": [f for f, _ in abi.ChunkArgs._fields_],
         "dc_step_args": [f for f, _ in abi.StepArgs._fields_],
+        "dc_chunk_bwd_args": [f for f, _ in abi.ChunkBwdArgs._fields_],
     }
     lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "deltacore.h"', "int main(void) {"]
     for st, names in fields.items():
@@ -60,7 +61,8 @@ def test_struct_layout_matches_the_header(tmp_path):
     subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
     want = {tuple(l.split()[:2]): int(l.split()[2]) for l in out if l}
-    for st, cls in (("dc_chunk_args", abi.ChunkArgs), ("dc_step_args", abi.StepArgs)):
+    for st, cls in (("dc_chunk_args", abi.ChunkArgs), ("dc_step_args", abi.StepArgs),
+                    ("dc_chunk_bwd_args", abi.ChunkBwdArgs)):
         assert want[(st, "sizeof")] == ctypes.sizeof(cls)
         for n, _ in cls._fields_:
             assert want[(st, n)] == getattr(cls, n).offset, (st, n)
@@ -175,3 +177,20 @@ def test_host_entry_point_scratch_is_host_logic():
     assert abi.lib().dc_chunk_fwd_host(a, 0x100010, need, None) == abi.DC_EINVAL_ARG  # scratch not 256-aligned
     assert abi.lib().dc_chunk_fwd_host(_args(flags=abi.DC_FLAG_TEST_STALL), 0x100000, need, None) == abi.DC_EINVAL_ARG
     assert abi.lib().dc_chunk_fwd_host_scratch_size(_args(seq=0)) == 0
+
+
+def test_backward_validation_and_workspace_are_host_logic():
+    bw = abi.ChunkBwdArgs()
+    bw.fwd = _args(dk=8, dv=8, seq=40)
+    fake = 0x200000
+    bw.d_y, bw.d_q, bw.d_k, bw.d_v = fake, fake + 4096, fake + 8192, fake + 12288
+    bw.d_erase, bw.d_write, bw.d_g, bw.d_state = fake + 16384, fake + 20480, fake + 24576, fake + 28672
+    # per (batch, head): the state at every 16th micro-step (ceil(40 / 16) = 3) and a 16-step buffer
+    assert abi.lib().dc_chunk_bwd_workspace_size(bw) == 2 * 2 * (3 + 16) * 8 * 8 * 4
+    assert abi.lib().dc_chunk_bwd(bw, None) == abi.DC_EWORKSPACE  # no workspace given
+    bw.d_g = None
+    assert abi.lib().dc_chunk_bwd(bw, None) == abi.DC_EINVAL_ARG  # gated forward needs d_g
+    big = abi.ChunkBwdArgs()
+    big.fwd = _args(dk=256, dv=8, erase_w=1)
+    big.d_y = big.d_q = big.d_k = big.d_v = big.d_erase = big.d_write = big.d_g = big.d_state = fake
+    assert abi.lib().dc_chunk_bwd(big, None) == abi.DC_EUNSUPPORTED

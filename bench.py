@@ -300,6 +300,39 @@ def time_prefill_e2e(dn, x, u, steps, warmup):
     return e0.elapsed_time(e1) / steps, h2d, d2h
 
 
+def time_backward(dn, steps, warmup, batch=8, tokens=4096):
+    """The backward (dc_chunk_bwd) at config 2's shapes: d_y and d_final_state in, every input's
+    gradient out.  Returns (ms per step, algorithmic bytes per launch)."""
+    x = make_prefill("deltanet", batch, tokens, 1, "cuda", 7)
+    g = torch.Generator(device="cuda").manual_seed(8)
+    dy = torch.randn(batch, tokens, H, D, device="cuda", generator=g)
+    dsf = torch.randn(tuple(x["state"].shape), device="cuda", generator=g)
+    ws = [None]
+
+    def call():
+        out = dn.delta_chunk_recalculated_backward(dy, dsf, x["q"], x["k"], x["v"], x["erase"], x["write"], None,
+                                                   x["state"], False, L, 1.0 / math.sqrt(D), workspace=ws[0])
+        return out
+
+    from importlib import import_module
+    abi = import_module("burn-deltanet_b200._abi")
+    for _ in range(max(1, warmup)):
+        call()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        call()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    assert abi.lib().dc_device_status(0) == 0
+    nb = lambda t: t.numel() * t.element_size()
+    read = sum(nb(x[n]) for n in ("q", "k", "v", "erase", "write", "state")) + nb(dy) + nb(dsf)
+    written = 4 * (3 * x["q"].numel() + x["erase"].numel() + x["write"].numel() + x["state"].numel())
+    return e0.elapsed_time(e1) / steps, read + written
+
+
 def time_decode(dn, steps, warmup):
     """Config 3's decode: one fused tick for 256 sequences x 16 heads per step,
     the state updated in place; the K ticks replay from one CUDA graph."""
@@ -386,6 +419,11 @@ def run_ours(args):
         if rank == 0:
             print(json.dumps({"prefill_ms_per_step": ms, "tok_s": batch * tokens * world / (ms / 1e3)}))
         return
+    if args.only == "backward":
+        bw_ms, bw_bytes = time_backward(dn, 2, 1)
+        if rank == 0:
+            print(json.dumps({"backward_ms_per_step": bw_ms, "backward_gbs": bw_bytes / (bw_ms / 1e3) / 1e9}))
+        return
     ms = max_over_ranks(ms, world)
     tok_per_rank = batch * tokens
     value = tok_per_rank * world / (ms / 1e3)
@@ -396,6 +434,8 @@ def run_ours(args):
     flops = 2 * (5 * L * D + 3 * D * D) * batch * tokens * u * H
     dec_ms, dec_bytes = time_decode(dn, 256, args.warmup)
     dec_ms = max_over_ranks(dec_ms, world)
+    bw_ms, bw_bytes = time_backward(dn, 2, 1)
+    bw_ms = max_over_ranks(bw_ms, world)
     dec_tok = DECODE["batch"] * world / (dec_ms / 1e3)
     traffic = profiled_traffic(args.workload)
     gather_info = None
@@ -422,6 +462,13 @@ def run_ours(args):
                    "roofline": {"bound": "hbm", "achieved": dec_bytes / (dec_ms / 1e3) / 1e9, "peak": hbm_peak,
                                 "unit": "GB/s", "frac": dec_bytes / (dec_ms / 1e3) / 1e9 / hbm_peak},
                    "gpu_launches": 256},
+        "backward": {"metric": "backward tok/s (dc_chunk_bwd at config 2's shapes: every input's gradient; "
+                               "first version, recurrence on the CUDA cores)",
+                     "value": 8 * 4096 * world / (bw_ms / 1e3), "unit": "tok/s", "ms_per_step": bw_ms, "steps": 2,
+                     "roofline": {"bound": "hbm", "achieved": bw_bytes / (bw_ms / 1e3) / 1e9, "peak": hbm_peak,
+                                  "unit": "GB/s", "frac": bw_bytes / (bw_ms / 1e3) / 1e9 / hbm_peak,
+                                  "algorithmic_bytes_per_launch": bw_bytes},
+                     "gpu_launches": 2},
         "clocks": clocks.summary(),
     }
     if gather_info is not None:
@@ -502,7 +549,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="deltanet")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["prefill", "decode"], default=None,
+    ap.add_argument("--only", choices=["prefill", "decode", "backward"], default=None,
                     help="time one kernel alone and print a short line (for profiling runs)")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU instead of the workload's own (for small profiling captures)")

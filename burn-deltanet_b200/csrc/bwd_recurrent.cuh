@@ -95,6 +95,9 @@ __global__ void __launch_bounds__(kThreads) bwd_recurrent_kernel(const Params p)
     const int64_t N = f.seq * u;  // micro-steps
     const int64_t elems = (int64_t)dk * dv;
     const bool gated = f.gw > 0;
+    // Element sweeps over a [dk][dv] matrix: thread (er, ec) takes column ec of rows er, er + rstep, ...
+    const int rstep = kThreads / dv, er = tid / dv, ec = tid - er * dv;
+    const bool sweeper = er < rstep;
 
     const TI *Q = static_cast<const TI *>(f.q), *K = static_cast<const TI *>(f.k), *V = static_cast<const TI *>(f.v);
     const TG *E = static_cast<const TG *>(f.erase), *W = static_cast<const TG *>(f.write), *G = static_cast<const TG *>(f.g);
@@ -146,17 +149,15 @@ __global__ void __launch_bounds__(kThreads) bwd_recurrent_kernel(const Params p)
     };
     // M[i][j] += sign a[i] b[j]
     auto rank1 = [&](float *M, const float *a, const float *bvec, float sign) {
-        for (int64_t e = tid; e < elems; e += kThreads) {
-            const int i = (int)(e / dv), j = (int)(e % dv);
-            M[i * P + j] = fmaf(sign * a[i], bvec[j], M[i * P + j]);
+        if (sweeper) {
+            const float bj = sign * bvec[ec];
+            for (int i = er; i < dk; i += rstep) M[i * P + ec] = fmaf(a[i], bj, M[i * P + ec]);
         }
         __syncthreads();
     };
     auto scale_rows = [&](float *M, const float *a) {
-        for (int64_t e = tid; e < elems; e += kThreads) {
-            const int i = (int)(e / dv), j = (int)(e % dv);
-            M[i * P + j] *= a[i];
-        }
+        if (sweeper)
+            for (int i = er; i < dk; i += rstep) M[i * P + ec] *= a[i];
         __syncthreads();
     };
     // sum over the block of one value per thread (threads beyond `n` pass 0)
@@ -171,12 +172,14 @@ __global__ void __launch_bounds__(kThreads) bwd_recurrent_kernel(const Params p)
         __syncthreads();
         return s;
     };
-    // global <-> shared state copies
+    // global <-> shared state copies ([dk][dv] contiguous in global memory)
     auto store_state = [&](const float *M, float *dst) {
-        for (int64_t e = tid; e < elems; e += kThreads) dst[e] = M[(e / dv) * P + e % dv];
+        if (sweeper)
+            for (int i = er; i < dk; i += rstep) dst[i * dv + ec] = M[i * P + ec];
     };
     auto load_state = [&](float *M, const float *src) {
-        for (int64_t e = tid; e < elems; e += kThreads) M[(e / dv) * P + e % dv] = src ? src[e] : 0.f;
+        if (sweeper)
+            for (int i = er; i < dk; i += rstep) M[i * P + ec] = src ? src[i * dv + ec] : 0.f;
         __syncthreads();
     };
 

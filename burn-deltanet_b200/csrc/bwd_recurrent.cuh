@@ -26,8 +26,9 @@
 // The reverse walk needs S-_n at every step, and running the recurrence backwards would divide by
 // alpha.  So the kernel stores the state at the start of every block of kBlk micro-steps (a forward
 // pass), then for each block from the last: replays the block forward from its checkpoint, keeping
-// each step's S- in a per-(batch, head) scratch, and walks the block back.  S and dS live in shared
-// memory; one CTA (256 threads) per (batch, head); dk, dv <= 128.
+// each step's S- in a scratch, and walks the block back.  One CTA (256 threads) per (batch, head,
+// slice of 32 value columns), its slices of S and dS in shared memory (~42 KB at dk = 128: several
+// CTAs per SM hide each other's latency); dk, dv <= 128.
 #pragma once
 
 #include "common.cuh"
@@ -38,26 +39,34 @@ namespace bwd {
 constexpr int kThreads = 256;
 constexpr int kBlk = 16;    // micro-steps per checkpoint block
 constexpr int kMaxD = 128;  // dk, dv
+constexpr int kSlice = 32;  // value columns per CTA
 
+// The value columns of S evolve independently (recurrent.rs:41-99 acts on S column by column); only
+// the gradients that sum over them (dq, dk, d_erase, d_g, and d_write at width 1) couple the slices.
+// With several slices each CTA writes its share of those into a partial buffer [slice][...], and
+// reduce_partials adds the slices up in a fixed order (deterministic); with one slice they go straight
+// to the outputs.
 struct Params {
     CoreParams f;           // the forward call: dims, widths, scale, q, k, v, erase, write, g, state_in
     const float *dy;        // [batch, seq, heads, dv]
     const float *dS_final;  // [batch, heads, dk, dv] or null (zero)
-    float *dq, *dk, *dv;    // [batch, seq, heads, dk]; [batch, seq*u, heads, dk]; [batch, seq*u, heads, dv]
-    float *de, *dw;         // [batch, seq*u, heads, erase_w]; [batch, seq*u, heads, write_w]
-    float *dg;              // [batch, seq, heads, g_w] (g_w > 0)
+    float *dv, *dw_full;    // [batch, seq*u, heads, dv]: dv, and d_write when write_w == dv
     float *dS0;             // [batch, heads, dk, dv]
-    float *ckpt;            // [batch*heads][nblk][dk][dv]
-    float *scratch;         // [batch*heads][kBlk][dk][dv]
+    // column-summed gradients: base and the stride between slices (0 with one slice)
+    float *dq, *dk, *de, *dg, *dw1;
+    int64_t sq, sk, se, sg, sw1;
+    float *ckpt;            // [batch*heads][nslice][nblk][dk][kSlice]
+    float *scratch;         // [batch*heads][nslice][kBlk][dk][kSlice]
     int64_t nblk;
+    int32_t nslice;
 };
 
-// Shared-memory layout (floats): S and dS with a row pitch of dv + 1 (row and column sweeps both
-// conflict-free), then the step's vectors and two rows of partial sums.
+// Shared-memory layout (floats): S and dS ([dk][kSlice + 1]), then the step's vectors and the partial
+// sums of the reductions.
 struct Layout {
-    int dk, dv, P;
+    int dk, P;
     int S, dS, kx, bk, ex, al, qs, r1, r2, vx, wx, uu, du, dy, red, scal, total;
-    __host__ __device__ Layout(int dk_, int dv_) : dk(dk_), dv(dv_), P(dv_ + 1) {
+    __host__ __device__ explicit Layout(int dk_) : dk(dk_), P(kSlice + 1) {
         S = 0;
         dS = S + dk * P;
         kx = dS + dk * P;
@@ -68,13 +77,13 @@ struct Layout {
         r1 = qs + kMaxD;
         r2 = r1 + kMaxD;
         vx = r2 + kMaxD;
-        wx = vx + kMaxD;
-        uu = wx + kMaxD;
-        du = uu + kMaxD;
-        dy = du + kMaxD;
-        red = dy + kMaxD;         // [2][kMaxD]
-        scal = red + 2 * kMaxD;   // [8] block-reduction slots
-        total = scal + 8 * 32;
+        wx = vx + kSlice;
+        uu = wx + kSlice;
+        du = uu + kSlice;
+        dy = du + kSlice;
+        red = dy + kSlice;        // [kThreads]
+        scal = red + kThreads;    // [8] block-reduction slots
+        total = scal + 32;
     }
 };
 
@@ -83,7 +92,7 @@ __global__ void __launch_bounds__(kThreads) bwd_recurrent_kernel(const Params p)
     extern __shared__ float sm[];
     const CoreParams &f = p.f;
     const int dk = (int)f.dk, dv = (int)f.dv, u = f.u;
-    const Layout L(dk, dv);
+    const Layout L(dk);
     const int P = L.P;
     float *S = sm + L.S, *dS = sm + L.dS;
     float *kx = sm + L.kx, *bk = sm + L.bk, *ex = sm + L.ex, *al = sm + L.al, *qs = sm + L.qs;
@@ -92,12 +101,14 @@ __global__ void __launch_bounds__(kThreads) bwd_recurrent_kernel(const Params p)
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t bh = blockIdx.x, b = bh / f.heads, h = bh % f.heads;
+    const int sl = blockIdx.y, c0 = sl * kSlice, ws = (dv - c0) < kSlice ? (dv - c0) : kSlice;  // this slice's columns
     const int64_t N = f.seq * u;  // micro-steps
-    const int64_t elems = (int64_t)dk * dv;
+    const int64_t selems = (int64_t)dk * kSlice;
     const bool gated = f.gw > 0;
-    // Element sweeps over a [dk][dv] matrix: thread (er, ec) takes column ec of rows er, er + rstep, ...
-    const int rstep = kThreads / dv, er = tid / dv, ec = tid - er * dv;
-    const bool sweeper = er < rstep;
+    // Element sweeps over a [dk][ws] matrix: thread (er, ec) takes column ec of rows er, er + kRows, ...
+    constexpr int kRows = kThreads / kSlice;
+    const int er = tid / kSlice, ec = tid % kSlice;
+    const bool sweeper = ec < ws;
 
     const TI *Q = static_cast<const TI *>(f.q), *K = static_cast<const TI *>(f.k), *V = static_cast<const TI *>(f.v);
     const TG *E = static_cast<const TG *>(f.erase), *W = static_cast<const TG *>(f.write), *G = static_cast<const TG *>(f.g);
@@ -105,41 +116,46 @@ __global__ void __launch_bounds__(kThreads) bwd_recurrent_kernel(const Params p)
     auto row_t = [&](int64_t t) { return (b * f.seq + t) * f.heads + h; };   // token rows
 
     // ---- block-wide helpers (all threads; each ends with a barrier) ----
-    // out[j] = sum_i M[i][j] x[i]
+    // out[j] = sum_i M[i][j] x[i], j < ws: kRows row groups, then their partial sums added
     auto col_product = [&](const float *M, const float *x, float *out) {
-        const int j = tid & 127, half = tid >> 7, h0 = half * ((dk + 1) >> 1), h1 = half ? dk : ((dk + 1) >> 1);
-        if (j < dv) {
-            float a0 = 0.f, a1 = 0.f;
-            int i = h0;
-            for (; i + 1 < h1; i += 2) {
-                a0 = fmaf(M[i * P + j], x[i], a0);
-                a1 = fmaf(M[(i + 1) * P + j], x[i + 1], a1);
+        float a0 = 0.f, a1 = 0.f;
+        if (sweeper) {
+            int i = er;
+            for (; i + kRows < dk; i += 2 * kRows) {
+                a0 = fmaf(M[i * P + ec], x[i], a0);
+                a1 = fmaf(M[(i + kRows) * P + ec], x[i + kRows], a1);
             }
-            if (i < h1) a0 = fmaf(M[i * P + j], x[i], a0);
-            red[half * kMaxD + j] = a0 + a1;
+            if (i < dk) a0 = fmaf(M[i * P + ec], x[i], a0);
+        }
+        red[tid] = a0 + a1;
+        __syncthreads();
+        if (tid < ws) {
+            float sum = 0.f;
+#pragma unroll
+            for (int g = 0; g < kRows; ++g) sum += red[g * kSlice + tid];
+            out[tid] = sum;
         }
         __syncthreads();
-        if (tid < dv) out[tid] = red[tid] + red[kMaxD + tid];
-        __syncthreads();
     };
-    // out[i] = sum_j M[i][j] x[j]   (x == nullptr: out[i] = sum_j M[i][j] N2[i][j])
+    // out[i] = sum_{j < ws} M[i][j] x[j]   (x == nullptr: sum_j M[i][j] M2[i][j])
     auto row_product = [&](const float *M, const float *x, const float *M2, float *out) {
-        const int i = tid & 127, half = tid >> 7, c0 = half * ((dv + 1) >> 1), c1 = half ? dv : ((dv + 1) >> 1);
+        const int i = tid & 127, half = tid >> 7, hc = (ws + 1) >> 1;
+        const int c0h = half * hc, c1h = half ? ws : hc;
         if (i < dk) {
             float a0 = 0.f, a1 = 0.f;
-            int j = c0;
+            int j = c0h;
             if (x) {
-                for (; j + 1 < c1; j += 2) {
+                for (; j + 1 < c1h; j += 2) {
                     a0 = fmaf(M[i * P + j], x[j], a0);
                     a1 = fmaf(M[i * P + j + 1], x[j + 1], a1);
                 }
-                if (j < c1) a0 = fmaf(M[i * P + j], x[j], a0);
+                if (j < c1h) a0 = fmaf(M[i * P + j], x[j], a0);
             } else {
-                for (; j + 1 < c1; j += 2) {
+                for (; j + 1 < c1h; j += 2) {
                     a0 = fmaf(M[i * P + j], M2[i * P + j], a0);
                     a1 = fmaf(M[i * P + j + 1], M2[i * P + j + 1], a1);
                 }
-                if (j < c1) a0 = fmaf(M[i * P + j], M2[i * P + j], a0);
+                if (j < c1h) a0 = fmaf(M[i * P + j], M2[i * P + j], a0);
             }
             red[half * kMaxD + i] = a0 + a1;
         }
@@ -151,16 +167,16 @@ __global__ void __launch_bounds__(kThreads) bwd_recurrent_kernel(const Params p)
     auto rank1 = [&](float *M, const float *a, const float *bvec, float sign) {
         if (sweeper) {
             const float bj = sign * bvec[ec];
-            for (int i = er; i < dk; i += rstep) M[i * P + ec] = fmaf(a[i], bj, M[i * P + ec]);
+            for (int i = er; i < dk; i += kRows) M[i * P + ec] = fmaf(a[i], bj, M[i * P + ec]);
         }
         __syncthreads();
     };
     auto scale_rows = [&](float *M, const float *a) {
         if (sweeper)
-            for (int i = er; i < dk; i += rstep) M[i * P + ec] *= a[i];
+            for (int i = er; i < dk; i += kRows) M[i * P + ec] *= a[i];
         __syncthreads();
     };
-    // sum over the block of one value per thread (threads beyond `n` pass 0)
+    // sum over the block of one value per thread
     auto block_sum = [&](float v) {
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -172,19 +188,28 @@ __global__ void __launch_bounds__(kThreads) bwd_recurrent_kernel(const Params p)
         __syncthreads();
         return s;
     };
-    // global <-> shared state copies ([dk][dv] contiguous in global memory)
-    auto store_state = [&](const float *M, float *dst) {
+    // this slice of a [dk][dv] state in global memory <-> shared; checkpoints are [dk][kSlice]
+    auto store_full = [&](const float *M, float *dst) {
         if (sweeper)
-            for (int i = er; i < dk; i += rstep) dst[i * dv + ec] = M[i * P + ec];
+            for (int i = er; i < dk; i += kRows) dst[i * dv + c0 + ec] = M[i * P + ec];
     };
-    auto load_state = [&](float *M, const float *src) {
+    auto load_full = [&](float *M, const float *src) {
         if (sweeper)
-            for (int i = er; i < dk; i += rstep) M[i * P + ec] = src ? src[i * dv + ec] : 0.f;
+            for (int i = er; i < dk; i += kRows) M[i * P + ec] = src ? src[i * dv + c0 + ec] : 0.f;
+        __syncthreads();
+    };
+    auto store_local = [&](const float *M, float *dst) {
+        if (sweeper)
+            for (int i = er; i < dk; i += kRows) dst[i * kSlice + ec] = M[i * P + ec];
+    };
+    auto load_local = [&](float *M, const float *src) {
+        if (sweeper)
+            for (int i = er; i < dk; i += kRows) M[i * P + ec] = src[i * kSlice + ec];
         __syncthreads();
     };
 
     // The inputs of micro-step n into the shared vectors: k, b (.) k, the erase row (width-expanded),
-    // the decay alpha (1 unless micro-step 0 of a gated token), v, w.
+    // the decay alpha (1 unless micro-step 0 of a gated token), and this slice's v, w.
     auto load_step = [&](int64_t n) {
         const int64_t t = n / u, m = n % u;
         const int64_t rn = row_n(n);
@@ -196,10 +221,10 @@ __global__ void __launch_bounds__(kThreads) bwd_recurrent_kernel(const Params p)
             ex[tid] = e;
             bk[tid] = e * kk;
             al[tid] = decay ? __expf(ld(G + row_t(t) * f.gw + (f.gw == 1 ? 0 : tid))) : 1.f;
-        }
-        if (tid < dv) {
-            vx[tid] = ld(V + rn * dv + tid);
-            wx[tid] = ld(W + rn * f.ww + (f.ww == 1 ? 0 : tid));
+        } else if (tid >= 128 && tid - 128 < ws) {
+            const int j = tid - 128;
+            vx[j] = ld(V + rn * dv + c0 + j);
+            wx[j] = ld(W + rn * f.ww + (f.ww == 1 ? 0 : c0 + j));
         }
         __syncthreads();
         return decay;
@@ -208,85 +233,97 @@ __global__ void __launch_bounds__(kThreads) bwd_recurrent_kernel(const Params p)
     // `keep` (if not null) receives S-.
     auto forward_step = [&](bool decay, float *keep) {
         if (decay) scale_rows(S, al);
-        if (keep) store_state(S, keep);
+        if (keep) store_local(S, keep);
         col_product(S, bk, uu);
-        if (tid < dv) uu[tid] = wx[tid] * vx[tid] - uu[tid];
+        if (tid < ws) uu[tid] = wx[tid] * vx[tid] - uu[tid];
         __syncthreads();
         rank1(S, kx, uu, 1.f);
     };
 
-    float *ckpt = p.ckpt + bh * p.nblk * elems;
-    float *scratch = p.scratch + bh * (int64_t)kBlk * elems;
+    const int64_t cta = bh * p.nslice + sl;
+    float *ckpt = p.ckpt + cta * p.nblk * selems;
+    float *scratch = p.scratch + cta * (int64_t)kBlk * selems;
+    float *dq = p.dq + sl * p.sq, *dkp = p.dk + sl * p.sk, *dep = p.de + sl * p.se;
+    float *dgp = gated ? p.dg + sl * p.sg : nullptr, *dw1 = p.dw1 ? p.dw1 + sl * p.sw1 : nullptr;
 
     // ---- pass 1: the state at the start of every block ----
-    load_state(S, f.state_in + bh * elems);
+    load_full(S, f.state_in + bh * (int64_t)dk * dv);
     for (int64_t blk = 0; blk < p.nblk; ++blk) {
-        store_state(S, ckpt + blk * elems);
+        store_local(S, ckpt + blk * selems);
         const int64_t n1 = (blk + 1) * kBlk < N ? (blk + 1) * kBlk : N;
         for (int64_t n = blk * kBlk; n < n1; ++n) forward_step(load_step(n), nullptr);
     }
 
     // ---- pass 2: block by block from the last, replay forward (keeping S-) and walk back ----
-    load_state(dS, p.dS_final ? p.dS_final + bh * elems : nullptr);
+    load_full(dS, p.dS_final ? p.dS_final + bh * (int64_t)dk * dv : nullptr);
     for (int64_t blk = p.nblk - 1; blk >= 0; --blk) {
         const int64_t n0 = blk * kBlk, n1 = (n0 + kBlk) < N ? (n0 + kBlk) : N;
         __syncthreads();
-        load_state(S, ckpt + blk * elems);
+        load_local(S, ckpt + blk * selems);
         for (int64_t n = n0; n < n1; ++n) {
             const bool decay = load_step(n);
-            forward_step(decay, scratch + (n - n0) * elems);
+            forward_step(decay, scratch + (n - n0) * selems);
         }
         __syncthreads();
         for (int64_t n = n1 - 1; n >= n0; --n) {
             const int64_t t = n / u, m = n % u, rn = row_n(n);
             const bool decay = load_step(n);
-            load_state(S, scratch + (n - n0) * elems);  // S-_n
-            col_product(S, bk, uu);                    // u_n = w v - S-^T bk
-            if (tid < dv) uu[tid] = wx[tid] * vx[tid] - uu[tid];
+            load_local(S, scratch + (n - n0) * selems);  // S-_n
+            col_product(S, bk, uu);                     // u_n = w v - S-^T bk (this slice)
+            if (tid < ws) uu[tid] = wx[tid] * vx[tid] - uu[tid];
             __syncthreads();
             if (m == u - 1) {  // the read-out step of token t
                 const int64_t rt = row_t(t);
                 if (tid < dk) qs[tid] = f.scale * ld(Q + rt * dk + tid);
-                if (tid < dv) dyv[tid] = p.dy[rt * dv + tid];
+                if (tid < ws) dyv[tid] = p.dy[rt * dv + c0 + tid];
                 __syncthreads();
                 row_product(S, dyv, nullptr, r1);  // S- dy
-                const float udy = block_sum(tid < dv ? uu[tid] * dyv[tid] : 0.f);
-                if (tid < dk) p.dq[rt * dk + tid] = f.scale * (r1[tid] + kx[tid] * udy);
+                const float udy = block_sum(tid < ws ? uu[tid] * dyv[tid] : 0.f);
+                if (tid < dk) dq[rt * dk + tid] = f.scale * (r1[tid] + kx[tid] * udy);
                 rank1(dS, qs, dyv, 1.f);
             }
             col_product(dS, kx, du);            // du = dS^T k
             row_product(S, du, nullptr, r1);    // S- du
             row_product(dS, uu, nullptr, r2);   // dS u
-            if (tid < dk) p.dk[rn * dk + tid] = r2[tid] - ex[tid] * r1[tid];
+            if (tid < dk) dkp[rn * dk + tid] = r2[tid] - ex[tid] * r1[tid];
             if (f.ew != 1) {
-                if (tid < dk) p.de[rn * dk + tid] = -kx[tid] * r1[tid];
+                if (tid < dk) dep[rn * dk + tid] = -kx[tid] * r1[tid];
             } else {
                 const float s = block_sum(tid < dk ? -kx[tid] * r1[tid] : 0.f);
-                if (tid == 0) p.de[rn] = s;
+                if (tid == 0) dep[rn] = s;
             }
-            if (tid < dv) p.dv[rn * dv + tid] = wx[tid] * du[tid];
+            if (tid < ws) p.dv[rn * dv + c0 + tid] = wx[tid] * du[tid];
             if (f.ww != 1) {
-                if (tid < dv) p.dw[rn * dv + tid] = vx[tid] * du[tid];
+                if (tid < ws) p.dw_full[rn * dv + c0 + tid] = vx[tid] * du[tid];
             } else {
-                const float s = block_sum(tid < dv ? vx[tid] * du[tid] : 0.f);
-                if (tid == 0) p.dw[rn] = s;
+                const float s = block_sum(tid < ws ? vx[tid] * du[tid] : 0.f);
+                if (tid == 0) dw1[rn] = s;
             }
             rank1(dS, bk, du, -1.f);            // dS-
             if (decay) {
                 row_product(dS, nullptr, S, r1);  // sum_j dS-_ij S-_ij
                 const int64_t rt = row_t(t);
                 if (f.gw != 1) {
-                    if (tid < dk) p.dg[rt * dk + tid] = r1[tid];
+                    if (tid < dk) dgp[rt * dk + tid] = r1[tid];
                 } else {
                     const float s = block_sum(tid < dk ? r1[tid] : 0.f);
-                    if (tid == 0) p.dg[rt] = s;
+                    if (tid == 0) dgp[rt] = s;
                 }
                 scale_rows(dS, al);
             }
         }
     }
     __syncthreads();
-    store_state(dS, p.dS0 + bh * elems);
+    store_full(dS, p.dS0 + bh * (int64_t)dk * dv);
+}
+
+// out[e] = sum over `nslice` slices (stride `stride`) of part[e], in slice order.
+__global__ void reduce_partials(const float *part, int64_t stride, int nslice, float *out, int64_t n) {
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        float s = part[e];
+        for (int k = 1; k < nslice; ++k) s += part[k * stride + e];
+        out[e] = s;
+    }
 }
 
 }  // namespace bwd

@@ -635,21 +635,43 @@ int validate_bwd(const dc_chunk_bwd_args *a) {
     return DC_OK;
 }
 
-uint64_t bwd_workspace_bytes(const dc_chunk_args &f) {
-    const int64_t n = f.seq * f.n_householder;
-    const int64_t nblk = (n + dc::bwd::kBlk - 1) / dc::bwd::kBlk;
-    const uint64_t per = (uint64_t)f.dk * (uint64_t)f.dv * 4ull;
-    return (uint64_t)(f.batch * f.heads) * (uint64_t)(nblk + dc::bwd::kBlk) * per;
+// The backward's workspace: checkpoints and the replay scratch per (batch, head, slice), then, with more
+// than one value slice, the slices' partial sums of the column-summed gradients.
+struct BwdPlan {
+    int32_t nslice;
+    int64_t nblk;
+    uint64_t ckpt, scratch, pq, pk, pe, pg, pw1, total;  // element counts (floats) / total bytes
+};
+
+BwdPlan bwd_plan(const dc_chunk_args &f) {
+    BwdPlan pl{};
+    const int64_t n = f.seq * f.n_householder, bh = f.batch * f.heads;
+    pl.nslice = (int32_t)((f.dv + dc::bwd::kSlice - 1) / dc::bwd::kSlice);
+    pl.nblk = (n + dc::bwd::kBlk - 1) / dc::bwd::kBlk;
+    const uint64_t st = (uint64_t)f.dk * dc::bwd::kSlice;
+    pl.ckpt = (uint64_t)(bh * pl.nslice * pl.nblk) * st;
+    pl.scratch = (uint64_t)(bh * pl.nslice * dc::bwd::kBlk) * st;
+    if (pl.nslice > 1) {
+        pl.pq = (uint64_t)(f.batch * f.seq * f.heads * f.dk);
+        pl.pk = (uint64_t)(f.batch * n * f.heads * f.dk);
+        pl.pe = (uint64_t)(f.batch * n * f.heads * f.erase_w);
+        pl.pg = (uint64_t)(f.batch * f.seq * f.heads * f.g_w);
+        pl.pw1 = f.write_w == 1 ? (uint64_t)(f.batch * n * f.heads) : 0;
+    }
+    pl.total = 4ull * (pl.ckpt + pl.scratch + (uint64_t)pl.nslice * (pl.pq + pl.pk + pl.pe + pl.pg + pl.pw1));
+    return pl;
 }
+
+uint64_t bwd_workspace_bytes(const dc_chunk_args &f) { return bwd_plan(f).total; }
 
 template <typename TI, typename TG>
 int launch_bwd_typed(const dc::bwd::Params &p, cudaStream_t s) {
-    const dc::bwd::Layout L((int)p.f.dk, (int)p.f.dv);
+    const dc::bwd::Layout L((int)p.f.dk);
     const size_t smem = (size_t)L.total * sizeof(float);
     auto kern = dc::bwd::bwd_recurrent_kernel<TI, TG>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_fail(e);
-    kern<<<(unsigned)(p.f.batch * p.f.heads), dc::bwd::kThreads, smem, s>>>(p);
+    kern<<<dim3((unsigned)(p.f.batch * p.f.heads), (unsigned)p.nslice), dc::bwd::kThreads, smem, s>>>(p);
     e = cudaGetLastError();
     return e == cudaSuccess ? DC_OK : cuda_fail(e);
 }
@@ -671,30 +693,62 @@ int dc_chunk_bwd(const dc_chunk_bwd_args *a, dc_stream_t stream) {
     if (!a->workspace || a->workspace_bytes < bwd_workspace_bytes(f)) return DC_EWORKSPACE;
     st = check_device(nullptr);
     if (st != DC_OK) return st;
+    const BwdPlan pl = bwd_plan(f);
     dc::bwd::Params p{};
     p.f = chunk_params(&f);
     p.dy = a->d_y;
     p.dS_final = a->d_state_final;
-    p.dq = a->d_q;
-    p.dk = a->d_k;
     p.dv = a->d_v;
-    p.de = a->d_erase;
-    p.dw = a->d_write;
-    p.dg = a->d_g;
+    p.dw_full = f.write_w == 1 ? nullptr : a->d_write;
     p.dS0 = a->d_state;
-    const int64_t n = f.seq * f.n_householder;
-    p.nblk = (n + dc::bwd::kBlk - 1) / dc::bwd::kBlk;
-    p.ckpt = static_cast<float *>(a->workspace);
-    p.scratch = p.ckpt + (size_t)(f.batch * f.heads) * (size_t)p.nblk * (size_t)(f.dk * f.dv);
+    p.nblk = pl.nblk;
+    p.nslice = pl.nslice;
+    float *ws = static_cast<float *>(a->workspace);
+    p.ckpt = ws;
+    p.scratch = ws + pl.ckpt;
+    float *part = p.scratch + pl.scratch;
+    if (pl.nslice > 1) {  // column-summed gradients go to per-slice partials first
+        p.dq = part;
+        p.dk = p.dq + pl.nslice * pl.pq;
+        p.de = p.dk + pl.nslice * pl.pk;
+        p.dg = p.de + pl.nslice * pl.pe;
+        p.dw1 = f.write_w == 1 ? p.dg + pl.nslice * pl.pg : nullptr;
+        p.sq = (int64_t)pl.pq;
+        p.sk = (int64_t)pl.pk;
+        p.se = (int64_t)pl.pe;
+        p.sg = (int64_t)pl.pg;
+        p.sw1 = (int64_t)pl.pw1;
+    } else {
+        p.dq = a->d_q;
+        p.dk = a->d_k;
+        p.de = a->d_erase;
+        p.dg = a->d_g;
+        p.dw1 = f.write_w == 1 ? a->d_write : nullptr;
+    }
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const int key = f.in_dtype * 2 + f.gate_dtype;
     switch (key) {
-        case 0: return launch_bwd_typed<float, float>(p, s);
-        case 1: return launch_bwd_typed<float, __nv_bfloat16>(p, s);
-        case 2: return launch_bwd_typed<__nv_bfloat16, float>(p, s);
-        case 3: return launch_bwd_typed<__nv_bfloat16, __nv_bfloat16>(p, s);
+        case 0: st = launch_bwd_typed<float, float>(p, s); break;
+        case 1: st = launch_bwd_typed<float, __nv_bfloat16>(p, s); break;
+        case 2: st = launch_bwd_typed<__nv_bfloat16, float>(p, s); break;
+        case 3: st = launch_bwd_typed<__nv_bfloat16, __nv_bfloat16>(p, s); break;
+        default: return DC_EUNSUPPORTED_DTYPE;
     }
-    return DC_EUNSUPPORTED_DTYPE;
+    if (st != DC_OK || pl.nslice == 1) return st;
+    // add the slices' partial sums up (in slice order: deterministic)
+    auto reduce = [&](const float *src, uint64_t n, float *dst) -> int {
+        if (!n) return DC_OK;
+        const unsigned blocks = (unsigned)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+        dc::bwd::reduce_partials<<<blocks, 256, 0, s>>>(src, (int64_t)n, pl.nslice, dst, (int64_t)n);
+        const cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? DC_OK : cuda_fail(e);
+    };
+    if ((st = reduce(p.dq, pl.pq, a->d_q)) != DC_OK) return st;
+    if ((st = reduce(p.dk, pl.pk, a->d_k)) != DC_OK) return st;
+    if ((st = reduce(p.de, pl.pe, a->d_erase)) != DC_OK) return st;
+    if (f.g_w > 0 && (st = reduce(p.dg, pl.pg, a->d_g)) != DC_OK) return st;
+    if (f.write_w == 1 && (st = reduce(p.dw1, pl.pw1, a->d_write)) != DC_OK) return st;
+    return DC_OK;
 }
 
 }  // extern "C"

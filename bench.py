@@ -446,10 +446,7 @@ def run_ours(args):
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (seeded, BASELINE config recipes)",
-        "config": {"workload": f"config {cfg}: {kind} prefill B={batch} per GPU, T={tokens}, H={H}, "
-                               f"dk=dv={D}" + (f", u={u}" if u > 1 else ""),
-                   "global_batch": batch * world, "seq_len": tokens, "parallelism": f"batch x head over {world} GPU",
-                   "l2": "inputs larger than L2 (no flush needed)"},
+        "config": arm_config(cfg, kind, batch, tokens, u, world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": traffic,
                      "algorithmic_bytes_per_launch": nbytes,
@@ -493,6 +490,15 @@ def profiled_traffic(workload):
     return None
 
 
+def arm_config(cfg, kind, batch, tokens, u, world):
+    """The workload both arms report (the reference arm times a bounded sample of it, described in its
+    cpu_baseline)."""
+    return {"workload": f"config {cfg}: {kind} prefill B={batch} per GPU, T={tokens}, H={H}, dk=dv={D}"
+                        + (f", u={u}" if u > 1 else ""),
+            "global_batch": batch * world, "seq_len": tokens, "parallelism": f"batch x head over {world} GPU",
+            "l2": "inputs larger than L2 (no flush needed)"}
+
+
 def run_reference(args):
     """The reference's algorithm on the host cores: this build cannot compile
     the Rust reference (no cargo, Burn deps not vendored), so the arm times its
@@ -530,12 +536,11 @@ def run_reference(args):
         "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded, BASELINE config recipes)",
-        "config": {"workload": f"config {cfg}: {kind} prefill, sample B={sample_batch} T={sample_tokens} H={H} "
-                               f"dk=dv={D}",
-                   "global_batch": sample_batch, "seq_len": sample_tokens, "parallelism": "host threads"},
+        "config": arm_config(cfg, kind, batch, tokens, u, args.gpus),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": min(threads, sample_batch * H), "kind": "port",
-                         "sample": f"oracle chunk path fp32 (the reference algorithm restated in C, OpenMP), "
-                                   f"B={sample_batch} T={sample_tokens} H={H} per step"},
+                         "sample": f"oracle chunk path fp32 (the reference algorithm restated in C, OpenMP over "
+                                   f"(batch, head)), a bounded sample of the workload per step: "
+                                   f"B={sample_batch} T={sample_tokens} H={H}"},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -262,11 +262,11 @@ def test_step_in_place_and_out_of_place_agree():
     ((128, 1, 1), torch.float32, torch.bfloat16),
 ])
 def test_step_stream_matches_the_per_tile_kernel(widths, in_dtype, out_dtype):
-    """The streaming decode kernel (one CTA per SM walking 256 heads through a three-slot ring) against the
-    per-tile kernel, in place and out of place."""
+    """The streaming decode kernel (one CTA per SM walking 1024 heads through a three-slot ring; it serves
+    ticks of at least 1024 heads) against the per-tile kernel, in place and out of place."""
     ew, ww, gw = widths
     rng = np.random.default_rng(15 + ew + gw)
-    b, h, d = 64, 4, 128
+    b, h, d = 256, 4, 128
     raw = config_inputs(5, rng, b, 1, h, d, d)
     raw["erase"], raw["write"] = raw["erase"][..., :ew], raw["write"][..., :ww]
     raw["g"] = None if gw == 0 else raw["g"][..., :gw]
@@ -300,7 +300,7 @@ def test_step_stream_repeat_calls_are_bit_identical():
     for _ in range(4):
         y, s = dn.delta_step(*args, st, 0.09, out_dtype=torch.float32)
         assert torch.equal(y, y0) and torch.equal(s, s0)
-    sub = slice(7, 9)
+    sub = slice(7, 263)  # 1024 heads: still the streaming kernel (it serves ticks of at least 1024 heads)
     y, s = dn.delta_step(*(t[sub].contiguous() for t in args), st[sub].contiguous(), 0.09, out_dtype=torch.float32)
     torch.cuda.synchronize()
     assert torch.equal(y, y0[sub]) and torch.equal(s, s0[sub])

@@ -2,7 +2,7 @@
 """Benchmark of the delta-rule core on B200: prefill and decode tokens/s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload deltanet|gdn-decode|deltaproduct2|deltaproduct3|gdn2]
+                    [--workload deltanet|deltaproduct2|deltaproduct3|gdn2]
 
 One JSON line on rank 0.  The default workload is BASELINE config 2 (the
 DeltaNet prefill in bf16, B=8 T=4096 H=16 dk=dv=128, chunk 64, fp32 state):
@@ -11,7 +11,12 @@ rank per GPU) every rank owns its own batch of 8 sequences — batch x head
 sharding with no collective on the data path — so the work per GPU is fixed
 ("scaling": "weak") and ``value`` counts the tokens of all ranks.  The decode
 of BASELINE config 3 (256 sequences, H=16, fp32 state, one fused tick per
-step) is measured in the same run and reported under "decode".
+step) is measured in the same run and reported under "decode", and the
+backward (dc_chunk_bwd at config 2's shapes) under "backward".
+
+``--workload gdn2`` is BASELINE config 5: one batch of 16 sequences sharded
+over the N GPUs ("scaling": "strong"), and its decode is config 5's own: 512
+GDN-2 step() tokens from each rank's prefill final state.
 
 Inputs are synthetic (seeded, the configs' recipes) and larger than L2; every
 number is device time from CUDA events on the launching stream, max over ranks.
@@ -37,12 +42,16 @@ import torch  # noqa: E402
 
 H, D, L = 16, 128, 64
 WORKLOADS = {
-    # name: (config index, batch per GPU, tokens, n_householder, gates)
+    # name: (config index, batch per GPU (or in all, for STRONG), tokens, n_householder, gates)
     "deltanet": (2, 8, 4096, 1, "deltanet"),
     "deltaproduct2": (4, 4, 8192, 2, "deltaproduct"),
     "deltaproduct3": (4, 4, 8192, 3, "deltaproduct"),
     "gdn2": (5, 16, 16384, 1, "gdn2"),
 }
+# Config 5 is one batch of 16 sequences sharded over the GPUs (strong scaling); the others keep their
+# batch per GPU (weak scaling).
+STRONG = {"gdn2"}
+CFG5_DECODE_STEPS = 512
 DECODE = dict(batch=256, heads=16, d=128)
 
 
@@ -333,6 +342,49 @@ def time_backward(dn, steps, warmup, batch=8, tokens=4096):
     return e0.elapsed_time(e1) / steps, read + written
 
 
+def time_decode_cfg5(dn, state, steps, warmup, seed):
+    """Config 5's decode: `steps` GDN-2 step() tokens (per-channel erase, write and log-decay) from the
+    prefill's final state, for this rank's sequences x 16 heads, the state updated in place; the ticks
+    replay from one CUDA graph.  Returns (ms per step, bytes per step)."""
+    b = state.shape[0]
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    rn = lambda *s: torch.randn(*s, device="cuda", generator=g)
+    bf = torch.bfloat16
+    a = torch.rand(1, 1, H, D, device="cuda", generator=g) * math.log(16.0)
+    q, k, v = l2n(rn(steps, b, H, D)).to(bf), l2n(rn(steps, b, H, D)).to(bf), rn(steps, b, H, D).to(bf)
+    e, w = torch.sigmoid(rn(steps, b, H, D)), torch.sigmoid(rn(steps, b, H, D))
+    gg = -torch.exp(a) * torch.nn.functional.softplus(rn(steps, b, H, D))
+    y = torch.empty(steps, b, H, D, device="cuda", dtype=bf)
+    st = state.clone()
+
+    def tick(t):
+        dn.delta_step(q[t], k[t], v[t], e[t], w[t], gg[t], st, 1.0 / math.sqrt(D), y_out=y[t], state_out=st)
+
+    for t in range(max(3, warmup)):
+        tick(t)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            for t in range(steps):
+                tick(t)
+    torch.cuda.current_stream().wait_stream(side)
+    st.copy_(state)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    step_bytes = b * H * (2 * D * D * 4 + 3 * D * 2 + 3 * D * 4 + D * 2)
+    del graph
+    return ms, step_bytes
+
+
 def time_decode(dn, steps, warmup):
     """Config 3's decode: one fused tick for 256 sequences x 16 heads per step,
     the state updated in place; the K ticks replay from one CUDA graph."""
@@ -400,6 +452,11 @@ def run_ours(args):
     dn = importlib.import_module("burn-deltanet_b200")
     hbm_peak, tc_peak, peak_kind = measured_peaks()
     cfg, batch, tokens, u, kind = WORKLOADS[args.workload]
+    strong = args.workload in STRONG and not args.batch
+    if strong:
+        if batch % world:
+            raise SystemExit(f"{args.workload}: {batch} sequences do not split over {world} GPUs")
+        batch //= world  # this rank's share of the one batch
     batch = args.batch or batch
     x = make_prefill(kind, batch, tokens, u, "cuda", 1000 + rank)
     # One dc_chunk_fwd per step: one kernel, or two (prep + scan) for per-channel gates.
@@ -432,11 +489,25 @@ def run_ours(args):
     ms_e2e, h2d, d2h = time_prefill_e2e(dn, x, u, max(1, min(args.steps, 5)), 1)
     ms_e2e = max_over_ranks(ms_e2e, world)
     flops = 2 * (5 * L * D + 3 * D * D) * batch * tokens * u * H
-    dec_ms, dec_bytes = time_decode(dn, 256, args.warmup)
+    if kind == "gdn2":  # config 5: decode from this rank's prefill final state
+        y_p, s_final = dn.delta_chunk_recalculated(x["q"], x["k"], x["v"], x["erase"], x["write"], x["g"],
+                                                   x["state"], True, L, 1.0 / math.sqrt(D))
+        del y_p
+        dec_steps = CFG5_DECODE_STEPS
+        dec_ms, dec_bytes = time_decode_cfg5(dn, s_final, dec_steps, args.warmup, 2000 + rank)
+        dec_seq = batch
+        dec_metric = (f"decode tok/s (config 5: GDN-2 step, {batch * world} sequences x {H} heads, {dec_steps} "
+                      f"steps from the prefill's final state, fp32 state)")
+        del s_final
+    else:
+        dec_steps = 256
+        dec_ms, dec_bytes = time_decode(dn, dec_steps, args.warmup)
+        dec_seq = DECODE["batch"]
+        dec_metric = "decode tok/s (config 3: GDN step, 256 sequences x 16 heads, fp32 state)"
     dec_ms = max_over_ranks(dec_ms, world)
     bw_ms, bw_bytes = time_backward(dn, 2, 1)
     bw_ms = max_over_ranks(bw_ms, world)
-    dec_tok = DECODE["batch"] * world / (dec_ms / 1e3)
+    dec_tok = dec_seq * world / (dec_ms / 1e3)
     traffic = profiled_traffic(args.workload)
     gather_info = None
     if world > 1:
@@ -444,9 +515,9 @@ def run_ours(args):
     line = {
         "metric": f"prefill tok/s ({kind}, bf16 in, fp32 state, H={H} dk=dv={D}, chunk {L})",
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic (seeded, BASELINE config recipes)",
-        "config": arm_config(cfg, kind, batch, tokens, u, world),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong" if strong else "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, BASELINE config recipes)",
+        "config": arm_config(cfg, kind, batch, tokens, u, world, strong),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": traffic,
                      "algorithmic_bytes_per_launch": nbytes,
@@ -454,11 +525,11 @@ def run_ours(args):
         "e2e": {"value": tok_per_rank * world / (ms_e2e / 1e3), "unit": "tok/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
         "gpu_launches": launches,
-        "decode": {"metric": "decode tok/s (config 3: GDN step, 256 sequences x 16 heads, fp32 state)",
-                   "value": dec_tok, "unit": "tok/s", "ms_per_step": dec_ms, "steps": 256,
+        "decode": {"metric": dec_metric,
+                   "value": dec_tok, "unit": "tok/s", "ms_per_step": dec_ms, "steps": dec_steps,
                    "roofline": {"bound": "hbm", "achieved": dec_bytes / (dec_ms / 1e3) / 1e9, "peak": hbm_peak,
                                 "unit": "GB/s", "frac": dec_bytes / (dec_ms / 1e3) / 1e9 / hbm_peak},
-                   "gpu_launches": 256},
+                   "gpu_launches": dec_steps},
         "backward": {"metric": "backward tok/s (dc_chunk_bwd at config 2's shapes: every input's gradient; "
                                "first version, recurrence on the CUDA cores)",
                      "value": 8 * 4096 * world / (bw_ms / 1e3), "unit": "tok/s", "ms_per_step": bw_ms, "steps": 2,
@@ -490,10 +561,11 @@ def profiled_traffic(workload):
     return None
 
 
-def arm_config(cfg, kind, batch, tokens, u, world):
+def arm_config(cfg, kind, batch, tokens, u, world, strong=False):
     """The workload both arms report (the reference arm times a bounded sample of it, described in its
-    cpu_baseline)."""
-    return {"workload": f"config {cfg}: {kind} prefill B={batch} per GPU, T={tokens}, H={H}, dk=dv={D}"
+    cpu_baseline).  `batch` is per GPU."""
+    per = f"B={batch * world} over {world} GPU" if strong else f"B={batch} per GPU"
+    return {"workload": f"config {cfg}: {kind} prefill {per}, T={tokens}, H={H}, dk=dv={D}"
                         + (f", u={u}" if u > 1 else ""),
             "global_batch": batch * world, "seq_len": tokens, "parallelism": f"batch x head over {world} GPU",
             "l2": "inputs larger than L2 (no flush needed)"}
@@ -534,9 +606,11 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": f"prefill tok/s ({kind}, bf16 in, fp32 state, H={H} dk=dv={D}, chunk {L})",
         "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "strong" if args.workload in STRONG else "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded, BASELINE config recipes)",
-        "config": arm_config(cfg, kind, batch, tokens, u, args.gpus),
+        "config": arm_config(cfg, kind, batch // args.gpus if args.workload in STRONG else batch, tokens, u,
+                             args.gpus, args.workload in STRONG),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": min(threads, sample_batch * H), "kind": "port",
                          "sample": f"oracle chunk path fp32 (the reference algorithm restated in C, OpenMP over "
                                    f"(batch, head)), a bounded sample of the workload per step: "

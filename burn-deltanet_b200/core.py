@@ -235,7 +235,7 @@ def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_b
 def delta_chunk_recalculated_backward(d_y_bshv, d_final_state_bhkv, q_bshk, k_bshk, v_bshv, erase_bshK,
                                       write_bshV, g_bshK, state_bhkv, has_gate: bool, chunk_len: int,
                                       scale: float, *, n_householder: int = 1,
-                                      workspace: Optional[torch.Tensor] = None):
+                                      workspace: Optional[torch.Tensor] = None, recurrent: bool = False):
     """The backward of :func:`delta_chunk_recalculated` (``dc_chunk_bwd``): the
     reference's ``combined_backward`` (src/delta/chunk_recalculated/
     combined_backward.rs:72-84) on CUDA tensors.
@@ -244,11 +244,13 @@ def delta_chunk_recalculated_backward(d_y_bshv, d_final_state_bhkv, q_bshk, k_bs
     shaped like its input; ``d_g`` is ``None`` unless ``has_gate``): the
     derivatives of ``<y, d_y> + <final_state, d_final_state>`` through the
     forward call with the given inputs.  ``d_final_state_bhkv`` may be
-    ``None`` (zero).  dk, dv <= 128.
+    ``None`` (zero).  dk, dv <= 128.  A log-decay per head (or none) takes the
+    chunked backward; per-channel log-decays, or ``recurrent=True``, the
+    token-by-token one.
     """
     # (the forward's y / final state are not used: one-element stand-ins)
     a, _, _ = _chunk_args(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv, has_gate,
-                          chunk_len, scale, n_householder, torch.float32, False, False, False, None, None,
+                          chunk_len, scale, n_householder, torch.float32, False, recurrent, False, None, None,
                           _check_tensor, lambda shape, dt: torch.empty(1, device=q_bshk.device, dtype=dt))
     _check_tensor(d_y_bshv, "d_y")
     if d_y_bshv.dtype != torch.float32 or tuple(d_y_bshv.shape) != (a.batch, a.seq, a.heads, a.dv):

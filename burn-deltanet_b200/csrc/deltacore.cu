@@ -16,6 +16,7 @@
 #include "../../include/deltacore.h"
 #include "chunk_simt.cuh"
 #include "chunk_split.cuh"
+#include "bwd_chunk.cuh"
 #include "bwd_recurrent.cuh"
 #include "chunk_tc.cuh"
 #include "common.cuh"
@@ -617,7 +618,8 @@ int dc_chunk_fwd_host(const dc_chunk_args *a, void *scratch, uint64_t scratch_by
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
-// dc_chunk_bwd: the backward, token by token on the CUDA cores (bwd_recurrent.cuh).
+// dc_chunk_bwd: the backward, chunk by chunk (bwd_chunk.cuh) for a log-decay per head or none, token by
+// token (bwd_recurrent.cuh) for per-channel log-decays or with DC_FLAG_RECURRENT.
 // ---------------------------------------------------------------------------
 namespace {
 
@@ -668,7 +670,96 @@ BwdPlan bwd_plan(const dc_chunk_args &f) {
     return pl;
 }
 
-uint64_t bwd_workspace_bytes(const dc_chunk_args &f) { return bwd_plan(f).total; }
+// The chunked backward's workspace (floats; every region a multiple of 4 floats, so 16-byte aligned).
+struct ChunkBwdPlan {
+    int64_t nc, nch;
+    int32_t dkp, dvp, nslice;
+    uint64_t w, uv, sq, gl, st, total;  // element counts per array / total bytes
+};
+
+bool chunk_bwd_applies(const dc_chunk_args &f) { return f.g_w <= 1 && (f.flags & DC_FLAG_RECURRENT) == 0; }
+
+ChunkBwdPlan chunk_bwd_plan(const dc_chunk_args &f) {
+    using namespace dc::bwdc;
+    ChunkBwdPlan pl{};
+    const int64_t n = f.seq * f.n_householder;
+    pl.nc = (n + kBL - 1) / kBL;
+    pl.nch = f.batch * f.heads * pl.nc;
+    pl.dkp = (int32_t)((f.dk + 3) / 4 * 4);
+    pl.dvp = (int32_t)((f.dv + 3) / 4 * 4);
+    pl.nslice = (pl.dvp + kSlice - 1) / kSlice;
+    pl.w = (uint64_t)pl.nch * kBL * pl.dkp;
+    pl.uv = (uint64_t)pl.nch * kBL * pl.dvp;
+    pl.sq = (uint64_t)pl.nch * kBL * kBL;
+    pl.gl = ((uint64_t)pl.nch + 3) / 4 * 4;
+    pl.st = (uint64_t)pl.nch * pl.dvp * pl.dkp;
+    pl.total = 4ull * (3 * pl.w + 3 * pl.uv + 3 * pl.sq + pl.gl + 2 * pl.st);
+    return pl;
+}
+
+uint64_t bwd_workspace_bytes(const dc_chunk_args &f) {
+    return chunk_bwd_applies(f) ? chunk_bwd_plan(f).total : bwd_plan(f).total;
+}
+
+template <typename TI, typename TG>
+int launch_chunk_bwd_typed(const dc::bwdc::Params &p, int64_t bh, cudaStream_t s) {
+    using namespace dc::bwdc;
+    const int64_t nch = bh * p.nc;
+    const size_t sp = kPrepSmemFloats * sizeof(float), ss = kScanSmemFloats * sizeof(float),
+                 sg = kGradSmemFloats * sizeof(float);
+    cudaError_t e = cudaFuncSetAttribute(prep_kernel<TI, TG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ss);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(grad_kernel<TI, TG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sg);
+    if (e != cudaSuccess) return cuda_fail(e);
+    prep_kernel<TI, TG><<<(unsigned)nch, kThreads, sp, s>>>(p);
+    scan_kernel<<<dim3((unsigned)bh, (unsigned)p.nslice), kThreads, ss, s>>>(p);
+    grad_kernel<TI, TG><<<(unsigned)nch, kThreads, sg, s>>>(p);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? DC_OK : cuda_fail(e);
+}
+
+int run_chunk_bwd(const dc_chunk_bwd_args *a, cudaStream_t s) {
+    const dc_chunk_args &f = a->fwd;
+    const ChunkBwdPlan pl = chunk_bwd_plan(f);
+    if (pl.nch > 0x7fffffffLL || f.batch * f.heads > 0x7fffffffLL) return DC_EUNSUPPORTED;
+    dc::bwdc::Params p{};
+    p.f = chunk_params(&f);
+    p.dy = a->d_y;
+    p.dS_final = a->d_state_final;
+    p.dq = a->d_q;
+    p.dk = a->d_k;
+    p.dv = a->d_v;
+    p.de = a->d_erase;
+    p.dw = a->d_write;
+    p.dg = a->d_g;
+    p.dS0 = a->d_state;
+    float *ws = static_cast<float *>(a->workspace);
+    p.W = ws;
+    p.Kh = p.W + pl.w;
+    p.Qp = p.Kh + pl.w;
+    p.U = p.Qp + pl.w;
+    p.Vp = p.U + pl.uv;
+    p.dVp = p.Vp + pl.uv;
+    p.att = p.dVp + pl.uv;
+    p.T = p.att + pl.sq;
+    p.A = p.T + pl.sq;
+    p.gl = p.A + pl.sq;
+    p.ST = p.gl + pl.gl;
+    p.dSnT = p.ST + pl.st;
+    p.nc = pl.nc;
+    p.dkp = pl.dkp;
+    p.dvp = pl.dvp;
+    p.nslice = pl.nslice;
+    const int64_t bh = f.batch * f.heads;
+    switch (f.in_dtype * 2 + f.gate_dtype) {
+        case 0: return launch_chunk_bwd_typed<float, float>(p, bh, s);
+        case 1: return launch_chunk_bwd_typed<float, __nv_bfloat16>(p, bh, s);
+        case 2: return launch_chunk_bwd_typed<__nv_bfloat16, float>(p, bh, s);
+        case 3: return launch_chunk_bwd_typed<__nv_bfloat16, __nv_bfloat16>(p, bh, s);
+        default: return DC_EUNSUPPORTED_DTYPE;
+    }
+}
 
 template <typename TI, typename TG>
 int launch_bwd_typed(const dc::bwd::Params &p, cudaStream_t s) {
@@ -699,6 +790,7 @@ int dc_chunk_bwd(const dc_chunk_bwd_args *a, dc_stream_t stream) {
     if (!a->workspace || a->workspace_bytes < bwd_workspace_bytes(f)) return DC_EWORKSPACE;
     st = check_device(nullptr);
     if (st != DC_OK) return st;
+    if (chunk_bwd_applies(f)) return run_chunk_bwd(a, reinterpret_cast<cudaStream_t>(stream));
     const BwdPlan pl = bwd_plan(f);
     dc::bwd::Params p{};
     p.f = chunk_params(&f);

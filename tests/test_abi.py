@@ -185,9 +185,18 @@ def test_backward_validation_and_workspace_are_host_logic():
     fake = 0x200000
     bw.d_y, bw.d_q, bw.d_k, bw.d_v = fake, fake + 4096, fake + 8192, fake + 12288
     bw.d_erase, bw.d_write, bw.d_g, bw.d_state = fake + 16384, fake + 20480, fake + 24576, fake + 28672
-    # per (batch, head, 32-column slice): the slice of the state at every 16th micro-step
-    # (ceil(40 / 16) = 3) and a 16-step buffer; one slice (dv = 8): no partial sums
-    assert abi.lib().dc_chunk_bwd_workspace_size(bw) == 2 * 2 * (3 + 16) * 8 * 32 * 4
+    # a log-decay per head takes the chunked backward: per 32-micro-step chunk (2 per (batch, head), 8 in
+    # all; dk = dv = 8) W, K^, Q', U, V', dV' [32][8], att, T, A [32][32], gam_L, S and dS_next [8][8]
+    nch = 2 * 2 * 2
+    assert abi.lib().dc_chunk_bwd_workspace_size(bw) == 4 * (6 * nch * 32 * 8 + 3 * nch * 32 * 32 + nch + 2 * nch * 64)
+    # the token-by-token one (DC_FLAG_RECURRENT, or per-channel log-decays): per (batch, head, 32-column
+    # slice) the slice of the state at every 16th micro-step (ceil(40 / 16) = 3) and a 16-step buffer;
+    # one slice (dv = 8): no partial sums
+    rec = abi.ChunkBwdArgs.from_buffer_copy(bw)
+    rec.fwd.flags = abi.DC_FLAG_RECURRENT
+    assert abi.lib().dc_chunk_bwd_workspace_size(rec) == 2 * 2 * (3 + 16) * 8 * 32 * 4
+    rec.fwd.flags, rec.fwd.g_w = 0, 8
+    assert abi.lib().dc_chunk_bwd_workspace_size(rec) == 2 * 2 * (3 + 16) * 8 * 32 * 4
     assert abi.lib().dc_chunk_bwd(bw, None) == abi.DC_EWORKSPACE  # no workspace given
     bw.d_g = None
     assert abi.lib().dc_chunk_bwd(bw, None) == abi.DC_EINVAL_ARG  # gated forward needs d_g

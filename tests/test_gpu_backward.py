@@ -36,21 +36,22 @@ def make(seed, b, t, h, dk, dv, u, gates, beta_max):
                 dsf=rng.standard_normal((b, h, dk, dv)))
 
 
-def gpu_grads(x, u, in_dtype=torch.float32, with_dsf=True):
+def gpu_grads(x, u, in_dtype=torch.float32, with_dsf=True, recurrent=False):
     dev = lambda a, dt=torch.float32: None if a is None else torch.tensor(a, dtype=dt, device="cuda")
     q, k, v = (dev(x[n], in_dtype) for n in ("q", "k", "v"))
     dk = q.shape[3]
     out = dn.delta_chunk_recalculated_backward(dev(x["dy"]), dev(x["dsf"]) if with_dsf else None, q, k, v,
                                                dev(x["e"]), dev(x["w"]), dev(x["g"]), dev(x["s0"]),
-                                               x["g"] is not None, 64, 1 / np.sqrt(dk), n_householder=u)
+                                               x["g"] is not None, 64, 1 / np.sqrt(dk), n_householder=u,
+                                               recurrent=recurrent)
     torch.cuda.synchronize()
     assert abi.lib().dc_device_status(1) == 0
     rounded = {n: (t.double().cpu().numpy() if t is not None else None) for n, t in zip(("q", "k", "v"), (q, k, v))}
     return dict(zip(NAMES, (None if t is None else t.double().cpu().numpy() for t in out))), rounded
 
 
-def check(x, u, in_dtype=torch.float32, tol=1e-4, with_dsf=True):
-    got, r = gpu_grads(x, u, in_dtype, with_dsf)
+def check(x, u, in_dtype=torch.float32, tol=1e-4, with_dsf=True, recurrent=False):
+    got, r = gpu_grads(x, u, in_dtype, with_dsf, recurrent)
     dk = x["q"].shape[3]
     ref = oracle.recurrent_backward(r["q"], r["k"], r["v"], x["e"], x["w"], x["g"], x["s0"], x["dy"],
                                     x["dsf"] if with_dsf else None, 1 / np.sqrt(dk), u)
@@ -123,3 +124,73 @@ def test_backward_is_deterministic():
         b, _ = gpu_grads(x, 1)
         for n in NAMES:
             assert np.array_equal(a[n], b[n]), n
+
+
+def make_widths(seed, b, t, h, dk, dv, u, gates, beta_max, ew, ww):
+    """`make` with the erase / write gates at the given widths (1 or full) and g per head or none."""
+    x = make(seed, b, t, h, dk, dv, u, gates, beta_max)
+    rng = np.random.default_rng(seed + 1)
+    x["e"] = rng.uniform(0.05, beta_max, (b, t * u, h, ew))
+    x["w"] = rng.uniform(0.05, 1.0, (b, t * u, h, ww))
+    return x
+
+
+@pytest.mark.parametrize("gates,u,beta_max,dims", [
+    ("none", 1, 0.95, (2, 16, 3, 8, 8)),
+    ("head", 1, 1.95, (2, 12, 2, 8, 8)),
+    ("head", 2, 1.95, (2, 9, 2, 8, 8)),
+    ("head", 1, 0.95, (2, 16, 2, 8, 16)),
+])
+def test_recurrent_backward_still_serves_per_head_gates(gates, u, beta_max, dims):
+    """DC_FLAG_RECURRENT sends a per-head (or no) log-decay down the token-by-token backward too."""
+    x = make(zlib.crc32(repr(("rec", gates, u, dims)).encode()), *dims, u, gates, beta_max)
+    check(x, u, recurrent=True)
+
+
+@pytest.mark.parametrize("t,u", [(31, 1), (32, 1), (33, 1), (64, 1), (65, 1), (16, 2), (17, 2), (11, 3)])
+def test_chunked_backward_at_chunk_boundaries(t, u):
+    """Sequences ending just before, on and after a 32-micro-step chunk boundary."""
+    x = make(zlib.crc32(repr(("edge", t, u)).encode()), 2, t, 2, 16, 16, u, "head", 1.95)
+    check(x, u)
+
+
+@pytest.mark.parametrize("dk,dv,ew,ww", [
+    (8, 40, 1, 1),      # two value slices, the second one partial
+    (12, 100, 12, 100),  # full-width erase and write, dk and dv not powers of two
+    (128, 64, 1, 64),
+    (64, 128, 64, 1),   # four value slices
+    (5, 7, 5, 7),       # widths that are not multiples of 4 (zero-padded columns)
+])
+def test_chunked_backward_head_sizes_and_gate_widths(dk, dv, ew, ww):
+    x = make_widths(zlib.crc32(repr(("dims", dk, dv, ew, ww)).encode()), 2, 45, 2, dk, dv, 1, "head", 0.95, ew, ww)
+    x["s0"] *= 0.3
+    check(x, 1)
+
+
+@pytest.mark.parametrize("u", [1, 2])
+def test_chunked_backward_d128_long(u):
+    """dk = dv = 128, 300 tokens (ten chunks at u = 1), per-head gates, bf16 q/k/v."""
+    x = make(21 + u, 2, 300, 2, 128, 128, u, "head", 0.95)
+    x["s0"] *= 0.1
+    print(f"worst relative error {check(x, u, torch.bfloat16):.2e}")
+
+
+def test_chunked_backward_is_deterministic():
+    x = make(12, 3, 70, 2, 32, 48, 1, "head", 0.95)
+    a, _ = gpu_grads(x, 1)
+    for _ in range(2):
+        b, _ = gpu_grads(x, 1)
+        for n in NAMES:
+            if a[n] is not None:
+                assert np.array_equal(a[n], b[n]), n
+
+
+def test_chunked_and_recurrent_backward_agree():
+    """The two CUDA backwards on the same inputs (ungated DeltaNet at d = 128, the benchmark's head size)."""
+    x = make(13, 1, 200, 2, 128, 128, 1, "none", 0.95)
+    a, _ = gpu_grads(x, 1)
+    b, _ = gpu_grads(x, 1, recurrent=True)
+    for n in NAMES:
+        if a[n] is not None:
+            err = np.abs(a[n] - b[n]).max() / max(1.0, np.abs(b[n]).max())
+            assert err < 1e-4, (n, err)

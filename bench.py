@@ -494,7 +494,7 @@ def run_ours(args):
             print(json.dumps({"prefill_ms_per_step": ms, "tok_s": batch * tokens * world / (ms / 1e3)}))
         return
     if args.only == "backward":
-        bw_ms, bw_bytes = time_backward(dn, 2, 1)
+        bw_ms, bw_bytes = time_backward(dn, 2, 1, batch=args.batch or 8)
         if rank == 0:
             print(json.dumps({"backward_ms_per_step": bw_ms, "backward_gbs": bw_bytes / (bw_ms / 1e3) / 1e9}))
         return

@@ -685,8 +685,8 @@ ChunkBwdPlan chunk_bwd_plan(const dc_chunk_args &f) {
     const int64_t n = f.seq * f.n_householder;
     pl.nc = (n + kBL - 1) / kBL;
     pl.nch = f.batch * f.heads * pl.nc;
-    pl.dkp = (int32_t)((f.dk + 3) / 4 * 4);
-    pl.dvp = (int32_t)((f.dv + 3) / 4 * 4);
+    pl.dkp = (int32_t)((f.dk + 7) / 8 * 8);
+    pl.dvp = (int32_t)((f.dv + 7) / 8 * 8);
     pl.nslice = (pl.dvp + kSlice - 1) / kSlice;
     pl.w = (uint64_t)pl.nch * kBL * pl.dkp;
     pl.uv = (uint64_t)pl.nch * kBL * pl.dvp;
@@ -751,6 +751,7 @@ int run_chunk_bwd(const dc_chunk_bwd_args *a, cudaStream_t s) {
     p.dkp = pl.dkp;
     p.dvp = pl.dvp;
     p.nslice = pl.nslice;
+    p.dy_vec = (f.dv % 4 == 0 && aligned(a->d_y, 16)) ? 1 : 0;
     const int64_t bh = f.batch * f.heads;
     switch (f.in_dtype * 2 + f.gate_dtype) {
         case 0: return launch_chunk_bwd_typed<float, float>(p, bh, s);

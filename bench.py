@@ -52,6 +52,11 @@ WORKLOADS = {
 # batch per GPU (weak scaling).
 STRONG = {"gdn2"}
 CFG5_DECODE_STEPS = 512
+# Flop (2 x multiply-adds) of the chunked backward per token-head, d = 128 and its chunks of L = 32:
+# prep 4 L d (A, att, W, U); the scans 2 d^2 forward (V', S) and L d + 3 d^2 back (dV', dS); the gradients
+# 3 d^2 + L d (the S products, datt), 2 L d (dT), 2 L d (d(wv), dKg), 2 L^2 (X, dA), 4 L d (F, Fa products).
+BWD_L = 32
+BWD_FLOP = 2 * (14 * BWD_L * D + 8 * D * D + 2 * BWD_L * BWD_L)
 DECODE = dict(batch=256, heads=16, d=128)
 
 
@@ -548,12 +553,14 @@ def run_ours(args):
                                 "unit": "GB/s", "frac": dec_bytes / (dec_ms / 1e3) / 1e9 / hbm_peak},
                    "gpu_launches": dec_steps},
         "backward": {"metric": "backward tok/s (dc_chunk_bwd at config 2's shapes: every input's gradient; "
-                               "first version, recurrence on the CUDA cores)",
+                               "chunked, fp32-accurate tf32 products on the tensor cores)",
                      "value": 8 * 4096 * world / (bw_ms / 1e3), "unit": "tok/s", "ms_per_step": bw_ms, "steps": 2,
-                     "roofline": {"bound": "hbm", "achieved": bw_bytes / (bw_ms / 1e3) / 1e9, "peak": hbm_peak,
-                                  "unit": "GB/s", "frac": bw_bytes / (bw_ms / 1e3) / 1e9 / hbm_peak,
-                                  "algorithmic_bytes_per_launch": bw_bytes},
-                     "gpu_launches": 2},
+                     "roofline": {"bound": "tensor", "achieved": BWD_FLOP * 8 * 4096 * H / (bw_ms / 1e3) / 1e12,
+                                  "peak": tc_peak, "unit": "TFLOP/s",
+                                  "frac": BWD_FLOP * 8 * 4096 * H / (bw_ms / 1e3) / 1e12 / tc_peak,
+                                  "flop_per_token_head": BWD_FLOP,
+                                  "hbm_gbs_of_inputs_and_gradients": bw_bytes / (bw_ms / 1e3) / 1e9},
+                     "gpu_launches": 3 * 2},
         "clocks": clocks.summary(),
     }
     if gather_info is not None:

@@ -209,11 +209,16 @@ DC_API int dc_chunk_fwd_host(const dc_chunk_args *args, void *scratch, uint64_t 
  * described by `fwd` (its y, state_out and workspace fields are not used).  Gradients are float32 in
  * the layouts of their inputs, gate gradients at the gate's own width (summed over a broadcast axis);
  * d_g is written when fwd.g_w > 0.  d_state_final may be NULL (zero).  Needs dk, dv <= 128 and a device
- * workspace of dc_chunk_bwd_workspace_size(args) bytes (16-byte aligned): per (batch, head, 32 value
- * columns) the state at every 16th micro-step and a 16-step replay buffer, and with dv > 32 the slices'
- * partial sums of the gradients that sum over value columns.  This first implementation walks the
- * recurrence back token by token on the CUDA cores in fp32, one CTA per (batch, head, 32 value columns);
- * results are deterministic.
+ * workspace of dc_chunk_bwd_workspace_size(args) bytes (16-byte aligned).  Two implementations, both
+ * deterministic (every gradient element written once):
+ *   - a log-decay per head or none (fwd.g_w <= 1): chunked, chunks of 32 micro-steps, three kernels
+ *     (the chunks' WY factors, a forward and reverse scan over the chunks per 32 value columns, the
+ *     chunks' gradients), fp32-accurate tf32 products on the tensor cores.  Workspace per chunk: its WY
+ *     factors, V' and dV', and the state and state gradient at its boundary (about 240 KB at dk = dv = 128);
+ *   - per-channel log-decays (fwd.g_w == dk), or DC_FLAG_RECURRENT in fwd.flags: the recurrence walked
+ *     back token by token on the CUDA cores, one CTA per (batch, head, 32 value columns).  Workspace: per
+ *     (batch, head, 32 value columns) the state at every 16th micro-step and a 16-step replay buffer, and
+ *     with dv > 32 the slices' partial sums of the gradients that sum over value columns.
  */
 typedef struct dc_chunk_bwd_args {
     dc_chunk_args fwd;

@@ -364,6 +364,50 @@ def time_backward(dn, steps, warmup, batch=8, tokens=4096):
     return e0.elapsed_time(e1) / steps, read + written
 
 
+def time_out_norm(dn, steps, warmup, batch=8, tokens=4096):
+    """The gated output norm (dc_out_norm) on config 2's read-out: y and gate bf16 [B, T, 16, 128] in,
+    bf16 out; inputs (268 MB) larger than L2.  Returns (ms per call, algorithmic bytes per call)."""
+    g = torch.Generator(device="cuda").manual_seed(11)
+    y = torch.randn(batch, tokens, H, D, device="cuda", generator=g).to(torch.bfloat16)
+    gate = torch.randn(batch, tokens, H, D, device="cuda", generator=g).to(torch.bfloat16)
+    w = torch.rand(D, device="cuda", generator=g) + 0.5
+    out = torch.empty_like(y)
+    for _ in range(max(3, warmup)):
+        dn.out_norm(y, gate, w, out=out)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        dn.out_norm(y, gate, w, out=out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps, 3 * y.numel() * 2 + w.numel() * 4
+
+
+def time_prologue(dn, steps, warmup, batch=8, tokens=4096):
+    """The front-end prologue (dc_qkv_prologue) on config 2's projection: x bf16 [B, T, 3 H D] (the
+    [q | k | v] channels), short convolution K = 4 with SiLU, q / k L2 norm, q, k, v bf16 out; inputs
+    (403 MB) larger than L2.  Returns (ms per call, algorithmic bytes per call)."""
+    g = torch.Generator(device="cuda").manual_seed(12)
+    c = 3 * H * D
+    x = torch.randn(batch, tokens, c, device="cuda", generator=g).to(torch.bfloat16)
+    w = torch.randn(c, 4, device="cuda", generator=g) * 0.5
+    win = torch.randn(batch, c, 4, device="cuda", generator=g)
+    for _ in range(max(3, warmup)):
+        out = dn.qkv_prologue(x, H, D, D, w, None, win)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        out = dn.qkv_prologue(x, H, D, D, w, None, win)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    del out
+    return e0.elapsed_time(e1) / steps, 2 * x.numel() * 2 + 2 * win.numel() * 4 + w.numel() * 4
+
+
 def time_decode_cfg5(dn, state, steps, warmup, seed):
     """Config 5's decode: `steps` GDN-2 step() tokens (per-channel erase, write and log-decay) from the
     prefill's final state, for this rank's sequences x 16 heads, the state updated in place; the ticks
@@ -498,6 +542,16 @@ def run_ours(args):
         if rank == 0:
             print(json.dumps({"prefill_ms_per_step": ms, "tok_s": batch * tokens * world / (ms / 1e3)}))
         return
+    if args.only == "prologue":
+        pr_ms, pr_bytes = time_prologue(dn, 20, 3, batch=args.batch or 8)
+        if rank == 0:
+            print(json.dumps({"prologue_ms": pr_ms, "prologue_gbs": pr_bytes / (pr_ms / 1e3) / 1e9}))
+        return
+    if args.only == "out_norm":
+        on_ms, on_bytes = time_out_norm(dn, 20, 3, batch=args.batch or 8)
+        if rank == 0:
+            print(json.dumps({"out_norm_ms": on_ms, "out_norm_gbs": on_bytes / (on_ms / 1e3) / 1e9}))
+        return
     if args.only == "backward":
         bw_ms, bw_bytes = time_backward(dn, 2, 1, batch=args.batch or 8)
         if rank == 0:
@@ -529,6 +583,10 @@ def run_ours(args):
     dec_ms = max_over_ranks(dec_ms, world)
     bw_ms, bw_bytes = time_backward(dn, 2, 1)
     bw_ms = max_over_ranks(bw_ms, world)
+    on_ms, on_bytes = time_out_norm(dn, 20, 3)
+    on_ms = max_over_ranks(on_ms, world)
+    pr_ms, pr_bytes = time_prologue(dn, 20, 3)
+    pr_ms = max_over_ranks(pr_ms, world)
     dec_tok = dec_seq * world / (dec_ms / 1e3)
     traffic = profiled_traffic(args.workload)
     gather_info = None
@@ -561,6 +619,20 @@ def run_ours(args):
                                   "flop_per_token_head": BWD_FLOP,
                                   "hbm_gbs_of_inputs_and_gradients": bw_bytes / (bw_ms / 1e3) / 1e9},
                      "gpu_launches": 3 * 2},
+        "out_norm": {"metric": "out-norm tok/s (gated per-head RMSNorm after the read-out, config 2's output: "
+                               "bf16 y and gate in, bf16 out)",
+                     "value": 8 * 4096 * world / (on_ms / 1e3), "unit": "tok/s", "ms_per_step": on_ms, "steps": 20,
+                     "roofline": {"bound": "hbm", "achieved": on_bytes / (on_ms / 1e3) / 1e9, "peak": hbm_peak,
+                                  "unit": "GB/s", "frac": on_bytes / (on_ms / 1e3) / 1e9 / hbm_peak,
+                                  "algorithmic_bytes_per_launch": on_bytes},
+                     "gpu_launches": 20},
+        "prologue": {"metric": "prologue tok/s (front-end after the input projection, config 2: short "
+                               "convolution K=4 + SiLU + q/k L2 norm, bf16 in and out)",
+                     "value": 8 * 4096 * world / (pr_ms / 1e3), "unit": "tok/s", "ms_per_step": pr_ms, "steps": 20,
+                     "roofline": {"bound": "hbm", "achieved": pr_bytes / (pr_ms / 1e3) / 1e9, "peak": hbm_peak,
+                                  "unit": "GB/s", "frac": pr_bytes / (pr_ms / 1e3) / 1e9 / hbm_peak,
+                                  "algorithmic_bytes_per_launch": pr_bytes},
+                     "gpu_launches": 20},
         "clocks": clocks.summary(),
     }
     if gather_info is not None:
@@ -652,7 +724,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="deltanet")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["prefill", "decode", "backward"], default=None,
+    ap.add_argument("--only", choices=["prefill", "decode", "backward", "out_norm", "prologue"], default=None,
                     help="time one kernel alone and print a short line (for profiling runs)")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU instead of the workload's own (for small profiling captures)")

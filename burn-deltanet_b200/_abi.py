@@ -41,6 +41,8 @@ EXPORTS = (
     "dc_chunk_fwd_host",
     "dc_chunk_bwd_workspace_size",
     "dc_chunk_bwd",
+    "dc_out_norm",
+    "dc_qkv_prologue",
 )
 
 
@@ -89,6 +91,36 @@ class StepArgs(ctypes.Structure):
     ]
 
 
+class OutNormArgs(ctypes.Structure):
+    """struct dc_out_norm_args."""
+    _fields_ = [
+        ("rows", ctypes.c_int64), ("dv", ctypes.c_int64),
+        ("in_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("y", ctypes.c_void_p), ("gate", ctypes.c_void_p), ("weight", ctypes.c_void_p), ("out", ctypes.c_void_p),
+    ]
+
+
+DC_PROLOGUE_CONV_SILU = 0x1
+DC_PROLOGUE_QK_SILU = 0x2
+DC_PROLOGUE_L2 = 0x4
+
+
+class PrologueArgs(ctypes.Structure):
+    """struct dc_qkv_prologue_args."""
+    _fields_ = [
+        ("batch", ctypes.c_int64), ("seq", ctypes.c_int64), ("heads", ctypes.c_int64),
+        ("dk", ctypes.c_int64), ("dv", ctypes.c_int64),
+        ("n_householder", ctypes.c_int32), ("conv_kernel", ctypes.c_int32),
+        ("in_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32),
+        ("flags", ctypes.c_uint32),
+        ("x_stride", ctypes.c_int64),
+        ("x", ctypes.c_void_p), ("conv_weight", ctypes.c_void_p), ("conv_bias", ctypes.c_void_p),
+        ("window_in", ctypes.c_void_p), ("window_out", ctypes.c_void_p),
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+    ]
+
+
 _lib = None
 
 
@@ -128,6 +160,10 @@ def lib() -> ctypes.CDLL:
         L.dc_chunk_bwd_workspace_size.restype = ctypes.c_uint64
         L.dc_chunk_bwd.argtypes = [ctypes.POINTER(ChunkBwdArgs), ctypes.c_void_p]
         L.dc_chunk_bwd.restype = ctypes.c_int
+        L.dc_out_norm.argtypes = [ctypes.POINTER(OutNormArgs), ctypes.c_void_p]
+        L.dc_out_norm.restype = ctypes.c_int
+        L.dc_qkv_prologue.argtypes = [ctypes.POINTER(PrologueArgs), ctypes.c_void_p]
+        L.dc_qkv_prologue.restype = ctypes.c_int
         _lib = L
     return _lib
 

@@ -279,6 +279,99 @@ def delta_chunk_recalculated_backward(d_y_bshv, d_final_state_bhkv, q_bshk, k_bs
             grads["d_state"])
 
 
+def out_norm(y_bshv: torch.Tensor, gate_bshv: Optional[torch.Tensor], weight: torch.Tensor, eps: float = 1e-5, *,
+             out_dtype: Optional[torch.dtype] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The per-head output normalisation after the read-out, ``OutNorm::forward``
+    (src/common/norm.rs:129-135), through ``dc_out_norm``: over the last axis
+    (one head's ``head_v_dim`` values) of ``y``,
+    ``y / sqrt(mean(y^2) + eps) * weight``, times ``silu(gate)`` when a gate is
+    given (the gated form, burn-stack ``RmsNormGated``).  ``y`` and ``gate``
+    share a dtype (float32 / bfloat16); ``weight`` is float32 ``[head_v_dim]``.
+    Returns ``out`` (``y``'s shape, ``out_dtype`` or ``y``'s dtype); it may be
+    ``y`` itself.  ``eps`` defaults to 1e-5 (Burn's RMSNorm default).
+    """
+    _check_tensor(y_bshv, "y")
+    dv = y_bshv.shape[-1]
+    if gate_bshv is not None:
+        _check_tensor(gate_bshv, "gate")
+        if gate_bshv.shape != y_bshv.shape:
+            raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, f"gate has shape {tuple(gate_bshv.shape)}, want {tuple(y_bshv.shape)}")
+    _check_tensor(weight, "weight")
+    if weight.dtype != torch.float32 or tuple(weight.shape) != (dv,):
+        raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, f"weight must be float32 [{dv}]")
+    in_code = _same_dtype((y_bshv, gate_bshv), "y and gate")
+    if out is None:
+        out = torch.empty(y_bshv.shape, device=y_bshv.device, dtype=out_dtype or y_bshv.dtype)
+    _check_tensor(out, "out")
+    if out.shape != y_bshv.shape:
+        raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, "out must be shaped like y")
+    a = _abi.OutNormArgs()
+    a.rows, a.dv = y_bshv.numel() // max(dv, 1), dv
+    a.in_dtype, a.out_dtype, a.eps = in_code, _dtype_code(out, "out"), float(eps)
+    a.y, a.weight, a.out = y_bshv.data_ptr(), weight.data_ptr(), out.data_ptr()
+    a.gate = None if gate_bshv is None else gate_bshv.data_ptr()
+    with torch.cuda.device(y_bshv.device):
+        _raise(_abi.lib().dc_out_norm(a, torch.cuda.current_stream(y_bshv.device).cuda_stream), "dc_out_norm")
+    return out
+
+
+def qkv_prologue(x_bsw: torch.Tensor, heads: int, dk: int, dv: int, conv_weight: torch.Tensor,
+                 conv_bias: Optional[torch.Tensor] = None, window_bwc: Optional[torch.Tensor] = None, *,
+                 n_householder: int = 1, conv_silu: bool = True, qk_silu: bool = False, l2: bool = True,
+                 out_dtype: Optional[torch.dtype] = None):
+    """The front-end between the input projection and the core (``QkvProjection::forward`` / ``step``
+    after ``in_proj``, src/common/qkv.rs:373-500) through ``dc_qkv_prologue``.
+
+    ``x_bsw`` ``[B, S, >= C]`` holds the projection's ``[q | u k | u v]`` channels first (C = heads dk
+    (1 + u) + u heads dv; a column slice of the whole projection is fine).  The causal depthwise short
+    convolution (``conv_weight [C, K]``, ``conv_bias [C]`` or None) runs over its channels with the
+    rolling window ``window_bwc [B, C, K]`` (None: zeros; src/common/conv.rs:81-160), then SiLU
+    (``conv_silu``; else SiLU on v and, with ``qk_silu``, on q and k), then the L2 norm of q and k over
+    each head (``l2``).  Returns ``(q [B, S, H, dk], k [B, S u, H, dk], v [B, S u, H, dv], next window)``;
+    a single-token ``step`` is ``S = 1``.
+    """
+    _check_tensor(conv_weight, "conv_weight")
+    if not isinstance(x_bsw, torch.Tensor) or not x_bsw.is_cuda:
+        raise DeltaCoreError(_abi.DC_EDEVICE, "x must be a CUDA tensor")
+    if x_bsw.dim() != 3 or x_bsw.stride(2) != 1 or x_bsw.stride(0) != x_bsw.shape[1] * x_bsw.stride(1):
+        raise DeltaCoreError(_abi.DC_EINVAL_ARG, "x must be [B, S, W] with contiguous channels and tokens")
+    b, s, _ = x_bsw.shape
+    u = int(n_householder)
+    c = heads * dk * (1 + u) + u * heads * dv
+    if conv_weight.dtype != torch.float32 or conv_weight.dim() != 2 or conv_weight.shape[0] != c:
+        raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, f"conv_weight must be float32 [{c}, K]")
+    kk = conv_weight.shape[1]
+    if conv_bias is not None:
+        _check_tensor(conv_bias, "conv_bias")
+        if conv_bias.dtype != torch.float32 or tuple(conv_bias.shape) != (c,):
+            raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, f"conv_bias must be float32 [{c}]")
+    if window_bwc is not None:
+        _check_tensor(window_bwc, "window")
+        if window_bwc.dtype != torch.float32 or tuple(window_bwc.shape) != (b, c, kk):
+            raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, f"window must be float32 [{b}, {c}, {kk}]")
+    odt = out_dtype or x_bsw.dtype
+    dev = x_bsw.device
+    q = torch.empty(b, s, heads, dk, device=dev, dtype=odt)
+    k = torch.empty(b, s * u, heads, dk, device=dev, dtype=odt)
+    v = torch.empty(b, s * u, heads, dv, device=dev, dtype=odt)
+    nxt = torch.empty(b, c, kk, device=dev, dtype=torch.float32)
+    a = _abi.PrologueArgs()
+    a.batch, a.seq, a.heads, a.dk, a.dv = b, s, heads, dk, dv
+    a.n_householder, a.conv_kernel = u, kk
+    a.in_dtype, a.out_dtype = _dtype_code(x_bsw, "x"), _dtype_code(q, "out")
+    a.flags = ((_abi.DC_PROLOGUE_CONV_SILU if conv_silu else 0) | (_abi.DC_PROLOGUE_QK_SILU if qk_silu else 0)
+               | (_abi.DC_PROLOGUE_L2 if l2 else 0))
+    a.x_stride = x_bsw.stride(1)
+    a.x, a.conv_weight = x_bsw.data_ptr(), conv_weight.data_ptr()
+    a.conv_bias = None if conv_bias is None else conv_bias.data_ptr()
+    a.window_in = None if window_bwc is None else window_bwc.data_ptr()
+    a.window_out = nxt.data_ptr()
+    a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+    with torch.cuda.device(dev):
+        _raise(_abi.lib().dc_qkv_prologue(a, torch.cuda.current_stream(dev).cuda_stream), "dc_qkv_prologue")
+    return q, k, v, nxt
+
+
 class DeltaChunkFunction(torch.autograd.Function):
     """The custom autodiff node (src/delta/chunk_recalculated/backward.rs:30-265): the forward
     keeps only its leaf inputs, and the backward recomputes what it needs from them.

@@ -19,6 +19,8 @@
 #include "bwd_chunk.cuh"
 #include "bwd_recurrent.cuh"
 #include "chunk_tc.cuh"
+#include "out_norm.cuh"
+#include "prologue.cuh"
 #include "common.cuh"
 #include "step.cuh"
 #include "step_stream.cuh"
@@ -848,6 +850,138 @@ int dc_chunk_bwd(const dc_chunk_bwd_args *a, dc_stream_t stream) {
     if (f.g_w > 0 && (st = reduce(p.dg, pl.pg, a->d_g)) != DC_OK) return st;
     if (f.write_w == 1 && (st = reduce(p.dw1, pl.pw1, a->d_write)) != DC_OK) return st;
     return DC_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// dc_out_norm: the per-head output normalisation (out_norm.cuh).
+// ---------------------------------------------------------------------------
+namespace {
+
+int validate_out_norm(const dc_out_norm_args *a) {
+    if (!a) return DC_EINVAL_ARG;
+    if (a->rows < 0 || a->dv < 1) return DC_EINVAL_SHAPE;
+    if (a->dv > 32 * dc::onorm::kMaxPer) return DC_EUNSUPPORTED;
+    if (!(a->eps >= 0.f) || !isfinite(a->eps)) return DC_EINVAL_ARG;
+    if ((a->in_dtype != DC_F32 && a->in_dtype != DC_BF16) || (a->out_dtype != DC_F32 && a->out_dtype != DC_BF16))
+        return DC_EUNSUPPORTED_DTYPE;
+    if (a->rows > 0 && (!a->y || !a->weight || !a->out)) return DC_EINVAL_ARG;
+    return DC_OK;
+}
+
+template <typename TI, typename TO>
+int launch_out_norm(const dc::onorm::Params &p, cudaStream_t s) {
+    using namespace dc::onorm;
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    const int64_t per_cta = (kThreads / 32) * kRowsPerWarp;
+    int64_t blocks = (p.rows + per_cta - 1) / per_cta;
+    const int64_t cap = (int64_t)sms * 16;  // grid-stride beyond 16 CTAs per SM
+    if (blocks > cap) blocks = cap;
+    if (p.dv <= 128) out_norm_kernel<TI, TO, 4><<<(unsigned)blocks, kThreads, 0, s>>>(p);
+    else out_norm_kernel<TI, TO, kMaxPer><<<(unsigned)blocks, kThreads, 0, s>>>(p);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? DC_OK : cuda_fail(e);
+}
+
+}  // namespace
+
+extern "C" {
+
+int dc_out_norm(const dc_out_norm_args *a, dc_stream_t stream) {
+    int st = validate_out_norm(a);
+    if (st != DC_OK) return st;
+    if (a->rows == 0) return DC_OK;
+    st = check_device(nullptr);
+    if (st != DC_OK) return st;
+    dc::onorm::Params p{};
+    p.rows = a->rows;
+    p.dv = (int32_t)a->dv;
+    p.eps = a->eps;
+    p.y = a->y;
+    p.gate = a->gate;
+    p.weight = a->weight;
+    p.out = a->out;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (a->in_dtype * 2 + a->out_dtype) {
+        case 0: return launch_out_norm<float, float>(p, s);
+        case 1: return launch_out_norm<float, __nv_bfloat16>(p, s);
+        case 2: return launch_out_norm<__nv_bfloat16, float>(p, s);
+        default: return launch_out_norm<__nv_bfloat16, __nv_bfloat16>(p, s);
+    }
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// dc_qkv_prologue: the front-end after the input projection (prologue.cuh).
+// ---------------------------------------------------------------------------
+namespace {
+
+int validate_prologue(const dc_qkv_prologue_args *a) {
+    if (!a) return DC_EINVAL_ARG;
+    if (a->batch < 1 || a->seq < 1 || a->heads < 1 || a->dk < 1 || a->dv < 1 || a->n_householder < 1)
+        return DC_EINVAL_SHAPE;
+    if (a->conv_kernel < 1) return DC_EINVAL_ARG;
+    if (a->conv_kernel > dc::pro::kMaxK || a->dk > dc::pro::kThreads || a->dv > dc::pro::kThreads)
+        return DC_EUNSUPPORTED;
+    if (a->batch > 65535 || (a->seq + dc::pro::kTile - 1) / dc::pro::kTile > 65535) return DC_EUNSUPPORTED;
+    if ((a->in_dtype != DC_F32 && a->in_dtype != DC_BF16) || (a->out_dtype != DC_F32 && a->out_dtype != DC_BF16))
+        return DC_EUNSUPPORTED_DTYPE;
+    if (a->flags & ~(DC_PROLOGUE_CONV_SILU | DC_PROLOGUE_QK_SILU | DC_PROLOGUE_L2)) return DC_EINVAL_ARG;
+    const int64_t channels = a->heads * a->dk * (1 + a->n_householder) + a->n_householder * a->heads * a->dv;
+    if (a->x_stride < channels) return DC_EINVAL_SHAPE;
+    if (!a->x || !a->conv_weight || !a->q || !a->k || !a->v) return DC_EINVAL_ARG;
+    if (a->window_out && a->window_in) {  // the next window must not overwrite the one being read
+        const char *i0 = reinterpret_cast<const char *>(a->window_in), *o0 = reinterpret_cast<const char *>(a->window_out);
+        const int64_t bytes = a->batch * channels * a->conv_kernel * (int64_t)sizeof(float);
+        if (o0 < i0 + bytes && i0 < o0 + bytes) return DC_EINVAL_ARG;
+    }
+    return DC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dc_qkv_prologue(const dc_qkv_prologue_args *a, dc_stream_t stream) {
+    int st = validate_prologue(a);
+    if (st != DC_OK) return st;
+    st = check_device(nullptr);
+    if (st != DC_OK) return st;
+    dc::pro::Params p{};
+    p.batch = a->batch;
+    p.seq = a->seq;
+    p.heads = a->heads;
+    p.dk = a->dk;
+    p.dv = a->dv;
+    p.u = a->n_householder;
+    p.K = a->conv_kernel;
+    p.channels = a->heads * a->dk * (1 + a->n_householder) + a->n_householder * a->heads * a->dv;
+    p.x_stride = a->x_stride;
+    p.conv_silu = (a->flags & DC_PROLOGUE_CONV_SILU) ? 1 : 0;
+    p.qk_silu = (a->flags & DC_PROLOGUE_QK_SILU) ? 1 : 0;
+    p.l2 = (a->flags & DC_PROLOGUE_L2) ? 1 : 0;
+    p.x = a->x;
+    p.weight = a->conv_weight;
+    p.bias = a->conv_bias;
+    p.window_in = a->window_in;
+    p.window_out = a->window_out;
+    p.q = a->q;
+    p.k = a->k;
+    p.v = a->v;
+    const dim3 grid((unsigned)(a->heads * (1 + 2 * (int64_t)a->n_householder)),
+                    (unsigned)((a->seq + dc::pro::kTile - 1) / dc::pro::kTile), (unsigned)a->batch);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (a->in_dtype * 2 + a->out_dtype) {
+        case 0: dc::pro::prologue_kernel<float, float><<<grid, dc::pro::kThreads, 0, s>>>(p); break;
+        case 1: dc::pro::prologue_kernel<float, __nv_bfloat16><<<grid, dc::pro::kThreads, 0, s>>>(p); break;
+        case 2: dc::pro::prologue_kernel<__nv_bfloat16, float><<<grid, dc::pro::kThreads, 0, s>>>(p); break;
+        default: dc::pro::prologue_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, dc::pro::kThreads, 0, s>>>(p); break;
+    }
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? DC_OK : cuda_fail(e);
 }
 
 }  // extern "C"

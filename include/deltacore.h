@@ -238,6 +238,67 @@ typedef struct dc_chunk_bwd_args {
 DC_API uint64_t dc_chunk_bwd_workspace_size(const dc_chunk_bwd_args *args);
 DC_API int dc_chunk_bwd(const dc_chunk_bwd_args *args, dc_stream_t stream);
 
+/*
+ * The per-head output normalisation after the read-out.  Mirrors OutNorm::forward
+ * (src/common/norm.rs:129-135): over each row of y [rows, dv] (rows = batch * seq * heads; one head's
+ * dv values),
+ *   gate != NULL (OutNorm::Gated, burn-stack RmsNormGated):  out = y / sqrt(mean(y^2) + eps) * weight * silu(gate)
+ *   gate == NULL (OutNorm::Plain, burn-stack RmsNorm):       out = y / sqrt(mean(y^2) + eps) * weight
+ * with silu(x) = x / (1 + e^-x), fp32 arithmetic.  y and gate share in_dtype, out has out_dtype
+ * (DC_F32 or DC_BF16); weight is float32 [dv].  1 <= dv <= 256; rows may be 0.  out may alias y.
+ * The reference panics on a gate / norm mismatch; here the presence of gate selects the form.
+ */
+typedef struct dc_out_norm_args {
+    int64_t rows;
+    int64_t dv;
+    int32_t in_dtype, out_dtype;
+    float eps;
+    const void *y;
+    const void *gate;
+    const float *weight;
+    void *out;
+} dc_out_norm_args;
+
+DC_API int dc_out_norm(const dc_out_norm_args *args, dc_stream_t stream);
+
+/*
+ * The front-end between the fused input projection and the core, on the projection's [q | u k | u v]
+ * channel segment (QkvProjection::forward / step after in_proj, src/common/qkv.rs:373-500):
+ *   the causal depthwise short convolution with its rolling window (src/common/conv.rs:81-160): x is
+ *   left-padded with window_in's newest conv_kernel - 1 columns (zeros when NULL), y[c, t] = bias[c] +
+ *   sum_j weight[c, j] x_pad[c, t + j], and window_out receives the padded input's last conv_kernel
+ *   columns (the next call's window; not written when NULL; must not overlap window_in);
+ *   then SiLU on every channel (DC_PROLOGUE_CONV_SILU), or else SiLU on v and, with
+ *   DC_PROLOGUE_QK_SILU, on q and k (qkv.rs:405-413);
+ *   then, with DC_PROLOGUE_L2, q and k over each head: x / sqrt(sum x^2 + 1e-6) (norm.rs:83-90).
+ * Outputs: q [batch, seq, heads, dk], k [batch, seq*u, heads, dk], v [batch, seq*u, heads, dv] (micro-step
+ * m of token t is row t*u + m), in out_dtype.  x holds channel c of token t at (b*seq + t)*x_stride + c
+ * (x_stride >= channels = heads*dk*(1 + u) + u*heads*dv, so x may be a column slice of the whole
+ * projection), in in_dtype; conv_weight [channels, conv_kernel], conv_bias [channels] or NULL, windows
+ * [batch, channels, conv_kernel], all float32.  seq >= 1 (conv.rs asserts it); a single-token step() is
+ * seq = 1.  1 <= conv_kernel <= 8, dk, dv <= 128.  No GQA expansion (value heads = heads).
+ */
+#define DC_PROLOGUE_CONV_SILU 0x1u
+#define DC_PROLOGUE_QK_SILU 0x2u
+#define DC_PROLOGUE_L2 0x4u
+
+typedef struct dc_qkv_prologue_args {
+    int64_t batch, seq, heads, dk, dv;
+    int32_t n_householder;
+    int32_t conv_kernel;
+    int32_t in_dtype, out_dtype;
+    uint32_t flags;
+    int64_t x_stride;
+    const void *x;
+    const float *conv_weight;
+    const float *conv_bias;
+    const float *window_in;
+    float *window_out;
+    void *q, *k, *v;
+} dc_qkv_prologue_args;
+
+DC_API int dc_qkv_prologue(const dc_qkv_prologue_args *args, dc_stream_t stream);
+
 /* Human-readable name of a dc_status. */
 DC_API const char *dc_status_string(int status);
 

@@ -15,7 +15,12 @@ It wraps ``liboracle.so`` (``oracle_core.c``, built by ``oracle/Makefile``):
   forget gate on the first, the output of the last micro-step kept);
 * ``recurrent_backward`` (``oracle/backward.py``, numpy) — the gradients of
   the custom backward (src/delta/chunk_recalculated/combined_backward.rs:
-  72-190) as the derivative of the recurrence, float64.
+  72-190) as the derivative of the recurrence, float64;
+* ``out_norm`` (``oracle/out_norm.py``, numpy) — the per-head output
+  normalisation OutNorm (src/common/norm.rs:106-144);
+* ``qkv_prologue`` (``oracle/prologue.py``, numpy) — the front-end after the
+  input projection: short convolution, activations, q/k L2 norm
+  (src/common/conv.rs, src/common/qkv.rs:373-500).
 
 Arrays use the reference's layouts: per-token ``[batch, seq, heads, width]``,
 state ``[batch, heads, dk, dv]``.
@@ -186,3 +191,5 @@ def householder(kind, q, k, v, erase, write, g, state, u, chunk_len=64, scale=No
 
 
 from .backward import recurrent_backward  # noqa: E402  (numpy only)
+from .out_norm import out_norm  # noqa: E402  (numpy only)
+from .prologue import qkv_prologue  # noqa: E402  (numpy only)

@@ -48,6 +48,8 @@ def test_struct_layout_matches_the_header(tmp_path):
         "dc_chunk_args": [f for f, _ in abi.ChunkArgs._fields_],
         "dc_step_args": [f for f, _ in abi.StepArgs._fields_],
         "dc_chunk_bwd_args": [f for f, _ in abi.ChunkBwdArgs._fields_],
+        "dc_out_norm_args": [f for f, _ in abi.OutNormArgs._fields_],
+        "dc_qkv_prologue_args": [f for f, _ in abi.PrologueArgs._fields_],
     }
     lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "deltacore.h"', "int main(void) {"]
     for st, names in fields.items():
@@ -62,7 +64,8 @@ def test_struct_layout_matches_the_header(tmp_path):
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
     want = {tuple(l.split()[:2]): int(l.split()[2]) for l in out if l}
     for st, cls in (("dc_chunk_args", abi.ChunkArgs), ("dc_step_args", abi.StepArgs),
-                    ("dc_chunk_bwd_args", abi.ChunkBwdArgs)):
+                    ("dc_chunk_bwd_args", abi.ChunkBwdArgs), ("dc_out_norm_args", abi.OutNormArgs),
+                    ("dc_qkv_prologue_args", abi.PrologueArgs)):
         assert want[(st, "sizeof")] == ctypes.sizeof(cls)
         for n, _ in cls._fields_:
             assert want[(st, n)] == getattr(cls, n).offset, (st, n)
@@ -204,3 +207,45 @@ def test_backward_validation_and_workspace_are_host_logic():
     big.fwd = _args(dk=256, dv=8, erase_w=1)
     big.d_y = big.d_q = big.d_k = big.d_v = big.d_erase = big.d_write = big.d_g = big.d_state = fake
     assert abi.lib().dc_chunk_bwd(big, None) == abi.DC_EUNSUPPORTED
+
+
+def test_out_norm_validation_is_host_logic():
+    """dc_out_norm rejects bad arguments before any device work (OutNorm's shape asserts become codes)."""
+    a = abi.OutNormArgs()
+    a.rows, a.dv, a.in_dtype, a.out_dtype, a.eps = 4, 128, abi.DC_BF16, abi.DC_BF16, 1e-5
+    a.y, a.gate, a.weight, a.out = 0x10000, 0x20000, 0x30000, 0x40000
+    lib = abi.lib()
+    bad = [("dv", 0, abi.DC_EINVAL_SHAPE), ("rows", -1, abi.DC_EINVAL_SHAPE), ("dv", 257, abi.DC_EUNSUPPORTED),
+           ("eps", float("nan"), abi.DC_EINVAL_ARG), ("eps", -1.0, abi.DC_EINVAL_ARG),
+           ("in_dtype", 5, abi.DC_EUNSUPPORTED_DTYPE), ("out_dtype", 5, abi.DC_EUNSUPPORTED_DTYPE),
+           ("y", None, abi.DC_EINVAL_ARG), ("weight", None, abi.DC_EINVAL_ARG), ("out", None, abi.DC_EINVAL_ARG)]
+    for name, value, code in bad:
+        b = abi.OutNormArgs.from_buffer_copy(a)
+        setattr(b, name, value)
+        assert lib.dc_out_norm(b, None) == code, name
+    empty = abi.OutNormArgs.from_buffer_copy(a)
+    empty.rows, empty.y, empty.weight, empty.out = 0, None, None, None
+    assert lib.dc_out_norm(empty, None) == abi.DC_OK  # nothing to do: no device touched
+    assert lib.dc_out_norm(None, None) == abi.DC_EINVAL_ARG
+
+
+def test_prologue_validation_is_host_logic():
+    """dc_qkv_prologue rejects bad arguments before any device work (conv.rs / qkv.rs asserts as codes)."""
+    a = abi.PrologueArgs()
+    a.batch, a.seq, a.heads, a.dk, a.dv, a.n_householder, a.conv_kernel = 2, 9, 2, 8, 8, 1, 4
+    a.in_dtype = a.out_dtype = abi.DC_F32
+    a.flags = abi.DC_PROLOGUE_CONV_SILU | abi.DC_PROLOGUE_L2
+    a.x_stride = 2 * 8 * 2 + 2 * 8
+    a.x, a.conv_weight, a.q, a.k, a.v = 0x10000, 0x20000, 0x30000, 0x40000, 0x50000
+    a.window_in, a.window_out = 0x60000, 0x70000
+    lib = abi.lib()
+    bad = [("seq", 0, abi.DC_EINVAL_SHAPE), ("dk", 0, abi.DC_EINVAL_SHAPE), ("n_householder", 0, abi.DC_EINVAL_SHAPE),
+           ("conv_kernel", 0, abi.DC_EINVAL_ARG), ("conv_kernel", 9, abi.DC_EUNSUPPORTED), ("dv", 129, abi.DC_EUNSUPPORTED),
+           ("x_stride", 47, abi.DC_EINVAL_SHAPE), ("in_dtype", 7, abi.DC_EUNSUPPORTED_DTYPE), ("flags", 0x8, abi.DC_EINVAL_ARG),
+           ("x", None, abi.DC_EINVAL_ARG), ("conv_weight", None, abi.DC_EINVAL_ARG), ("v", None, abi.DC_EINVAL_ARG),
+           ("window_out", 0x60010, abi.DC_EINVAL_ARG)]  # the next window may not overlap the one being read
+    for name, value, code in bad:
+        b = abi.PrologueArgs.from_buffer_copy(a)
+        setattr(b, name, value)
+        assert lib.dc_qkv_prologue(b, None) == code, name
+    assert lib.dc_qkv_prologue(None, None) == abi.DC_EINVAL_ARG

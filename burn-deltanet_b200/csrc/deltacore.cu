@@ -875,12 +875,30 @@ int launch_out_norm(const dc::onorm::Params &p, cudaStream_t s) {
     using namespace dc::onorm;
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-    const int64_t per_cta = (kThreads / 32) * kRowsPerWarp;
-    int64_t blocks = (p.rows + per_cta - 1) / per_cta;
     const int64_t cap = (int64_t)sms * 16;  // grid-stride beyond 16 CTAs per SM
-    if (blocks > cap) blocks = cap;
-    if (p.dv <= 128) out_norm_kernel<TI, TO, 4><<<(unsigned)blocks, kThreads, 0, s>>>(p);
-    else out_norm_kernel<TI, TO, kMaxPer><<<(unsigned)blocks, kThreads, 0, s>>>(p);
+    auto grid = [&](int64_t rows_per_cta) {
+        const int64_t blocks = (p.rows + rows_per_cta - 1) / rows_per_cta;
+        return (unsigned)(blocks < cap ? blocks : cap);
+    };
+    // 16-byte rows: a power-of-two number of 16-byte chunks per row, every row start 16-byte aligned
+    constexpr int64_t vec = 16 / sizeof(TI);
+    const int64_t lpr = p.dv / vec;
+    const bool rows16 = p.dv % vec == 0 && (lpr & (lpr - 1)) == 0 && lpr >= 4 && lpr <= 32 &&
+                        aligned(p.y, 16) && aligned(p.out, 16) && (!p.gate || aligned(p.gate, 16)) &&
+                        (p.dv * (int64_t)sizeof(TO)) % 16 == 0;
+    if (rows16) {
+        const int64_t rows_per_cta = (kThreads / 32) * (32 / lpr) * kSlots;
+        switch (lpr) {
+            case 4: out_norm_vec_kernel<TI, TO, 4><<<grid(rows_per_cta), kThreads, 0, s>>>(p); break;
+            case 8: out_norm_vec_kernel<TI, TO, 8><<<grid(rows_per_cta), kThreads, 0, s>>>(p); break;
+            case 16: out_norm_vec_kernel<TI, TO, 16><<<grid(rows_per_cta), kThreads, 0, s>>>(p); break;
+            default: out_norm_vec_kernel<TI, TO, 32><<<grid(rows_per_cta), kThreads, 0, s>>>(p); break;
+        }
+    } else if (p.dv <= 128) {
+        out_norm_kernel<TI, TO, 4><<<grid((kThreads / 32) * kRowsPerWarp), kThreads, 0, s>>>(p);
+    } else {
+        out_norm_kernel<TI, TO, kMaxPer><<<grid((kThreads / 32) * kRowsPerWarp), kThreads, 0, s>>>(p);
+    }
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? DC_OK : cuda_fail(e);
 }
@@ -941,6 +959,12 @@ int validate_prologue(const dc_qkv_prologue_args *a) {
     return DC_OK;
 }
 
+template <typename TI, typename TO>
+void launch_prologue(bool k4, dim3 grid, const dc::pro::Params &p, cudaStream_t s) {
+    if (k4) dc::pro::prologue_kernel<TI, TO, 4><<<grid, dc::pro::kThreads, 0, s>>>(p);
+    else dc::pro::prologue_kernel<TI, TO, dc::pro::kMaxK><<<grid, dc::pro::kThreads, 0, s>>>(p);
+}
+
 }  // namespace
 
 extern "C" {
@@ -963,6 +987,10 @@ int dc_qkv_prologue(const dc_qkv_prologue_args *a, dc_stream_t stream) {
     p.conv_silu = (a->flags & DC_PROLOGUE_CONV_SILU) ? 1 : 0;
     p.qk_silu = (a->flags & DC_PROLOGUE_QK_SILU) ? 1 : 0;
     p.l2 = (a->flags & DC_PROLOGUE_L2) ? 1 : 0;
+    {
+        const int64_t esz = a->in_dtype == DC_BF16 ? 2 : 4;
+        p.vec_rows = (aligned(a->x, 16) && (a->x_stride * esz) % 16 == 0) ? 1 : 0;
+    }
     p.x = a->x;
     p.weight = a->conv_weight;
     p.bias = a->conv_bias;
@@ -974,11 +1002,12 @@ int dc_qkv_prologue(const dc_qkv_prologue_args *a, dc_stream_t stream) {
     const dim3 grid((unsigned)(a->heads * (1 + 2 * (int64_t)a->n_householder)),
                     (unsigned)((a->seq + dc::pro::kTile - 1) / dc::pro::kTile), (unsigned)a->batch);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const bool k4 = a->conv_kernel == 4;
     switch (a->in_dtype * 2 + a->out_dtype) {
-        case 0: dc::pro::prologue_kernel<float, float><<<grid, dc::pro::kThreads, 0, s>>>(p); break;
-        case 1: dc::pro::prologue_kernel<float, __nv_bfloat16><<<grid, dc::pro::kThreads, 0, s>>>(p); break;
-        case 2: dc::pro::prologue_kernel<__nv_bfloat16, float><<<grid, dc::pro::kThreads, 0, s>>>(p); break;
-        default: dc::pro::prologue_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, dc::pro::kThreads, 0, s>>>(p); break;
+        case 0: launch_prologue<float, float>(k4, grid, p, s); break;
+        case 1: launch_prologue<float, __nv_bfloat16>(k4, grid, p, s); break;
+        case 2: launch_prologue<__nv_bfloat16, float>(k4, grid, p, s); break;
+        default: launch_prologue<__nv_bfloat16, __nv_bfloat16>(k4, grid, p, s); break;
     }
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? DC_OK : cuda_fail(e);

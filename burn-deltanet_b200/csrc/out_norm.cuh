@@ -1,7 +1,8 @@
 // out_norm.cuh — the per-head output normalisation that follows the delta rule's read-out
 // (src/common/norm.rs:106-144, OutNorm): over each (batch, token, head) row of y [.., dv],
 //
-//   gated:  out = y / sqrt(mean(y^2) + eps) * w (.) silu(gate),   silu(x) = x sigma(x)
+//   gated:  out = y / sqrt(mean(y^2) + eps) * w (.) silu(gate),   silu(x) = x sigma(x) (fast exponential
+//           and division intrinsics: a few ulp)
 //   plain:  out = y / sqrt(mean(y^2) + eps) * w
 //
 // the RmsNormGated / RmsNorm modules of burn-stack (rev 984d42d3, not vendored in the reference tree; the
@@ -74,10 +75,89 @@ __global__ void __launch_bounds__(kThreads) out_norm_kernel(const Params p) {
                 const int d = lane + 32 * e;
                 if (e < per && d < dv) {
                     float v = y[q][e] * inv * w[e];
-                    if (Gt) v *= g[q][e] / (1.f + expf(-g[q][e]));
+                    if (Gt) v *= __fdividef(g[q][e], 1.f + __expf(-g[q][e]));
                     st(O + r * dv + d, v);
                 }
             }
+        }
+    }
+}
+
+// 16-byte vector access: VEC = 16 / sizeof(T) elements.
+__device__ __forceinline__ void load16(const float *p, float (&v)[4]) {
+    const float4 t = *reinterpret_cast<const float4 *>(p);
+    v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+}
+__device__ __forceinline__ void load16(const __nv_bfloat16 *p, float (&v)[8]) {
+    const uint4 t = *reinterpret_cast<const uint4 *>(p);
+    const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
+        v[2 * i] = f.x, v[2 * i + 1] = f.y;
+    }
+}
+template <int N>
+__device__ __forceinline__ void store_vec(float *p, const float (&v)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) *reinterpret_cast<float4 *>(p + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+}
+template <int N>
+__device__ __forceinline__ void store_vec(__nv_bfloat16 *p, const float (&v)[N]) {
+    uint32_t w[N / 2];
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+        const __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t *>(&b);
+    }
+    if constexpr (N == 8) *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    else *reinterpret_cast<uint2 *>(p) = make_uint2(w[0], w[1]);
+}
+
+// The same normalisation with 16-byte loads and stores: a row is LPR lanes of VEC = 16 / sizeof(TI)
+// consecutive elements each (dv = LPR VEC, LPR a power of two <= 32), a warp holds 32 / LPR rows per slot
+// and kSlots slots per iteration, all of them loaded before the first use.  Needs 16-byte-aligned rows.
+constexpr int kSlots = 4;
+
+template <typename TI, typename TO, int LPR>
+__global__ void __launch_bounds__(kThreads) out_norm_vec_kernel(const Params p) {
+    constexpr int VEC = 16 / sizeof(TI), RPS = 32 / LPR;
+    const int lane = threadIdx.x & 31, sub = lane % LPR, srow = lane / LPR, col = sub * VEC;
+    const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
+    const int dv = p.dv;
+    const TI *Y = static_cast<const TI *>(p.y), *Gt = static_cast<const TI *>(p.gate);
+    const TI *Gb = Gt ? Gt : Y;  // the gate's loads read y when there is no gate (and are not used)
+    TO *O = static_cast<TO *>(p.out);
+    float w[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) w[e] = p.weight[col + e];
+    const float inv_dv = 1.f / (float)dv;
+    for (int64_t r0 = ((int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * (RPS * kSlots); r0 < p.rows;
+         r0 += warps * (RPS * kSlots)) {
+        float y[kSlots][VEC], g[kSlots][VEC];
+#pragma unroll
+        for (int q = 0; q < kSlots; ++q) {
+            const int64_t r = r0 + q * RPS + srow;
+            const int64_t o = (r < p.rows ? r : 0) * dv + col;
+            load16(Y + o, y[q]);
+            load16(Gb + o, g[q]);
+        }
+#pragma unroll
+        for (int q = 0; q < kSlots; ++q) {
+            const int64_t r = r0 + q * RPS + srow;
+            float ss = 0.f;
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) ss = fmaf(y[q][e], y[q][e], ss);
+#pragma unroll
+            for (int o = LPR / 2; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float inv = rsqrtf(fmaf(ss, inv_dv, p.eps));
+            float v[VEC];
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) {
+                v[e] = y[q][e] * inv * w[e];
+                if (Gt) v[e] *= __fdividef(g[q][e], 1.f + __expf(-g[q][e]));
+            }
+            if (r < p.rows) store_vec(O + r * dv + col, v);
         }
     }
 }

@@ -11,13 +11,15 @@
 //   * q, k over the head axis: x / sqrt(sum x^2 + 1e-6) (src/common/norm.rs:83-90), or none.
 //
 // One CTA (128 threads, one per channel of a head segment) per (segment, 32-token tile, batch), the
-// segments being the H q heads, the u H k heads and the u H v heads.  Each thread loads its channel's
-// 32 + K - 1 inputs at once (the window supplies the ones before the sequence), convolves, and the
-// q / k norms reduce over the segment (a warp-level transpose reduction, then the four warps).  HBM-bound:
-// each input read once, each output written once.
+// segments being the H q heads, the u H k heads and the u H v heads.  The tile's inputs (32 + K - 1
+// tokens; the window supplies the ones before the sequence) are staged in shared memory by 16-byte
+// asynchronous copies, each thread slides its channel's K taps down them, and the q / k norms reduce
+// over the segment (a warp-level transpose reduction, then the four warps).  HBM-bound: each input read
+// once (plus the K - 1 halo rows), each output written once.
 #pragma once
 
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace dc {
 namespace pro {
@@ -29,6 +31,7 @@ constexpr int kMaxK = 8;       // short-convolution width
 struct Params {
     int64_t batch, seq, heads, dk, dv, channels, x_stride;
     int32_t u, K, conv_silu, qk_silu, l2;
+    int32_t vec_rows;          // x rows 16-byte aligned (x and x_stride): tiles staged by cp.async
     const void *x;             // [B, S, x_stride]: channel c of token t at (b S + t) x_stride + c
     const float *weight;       // [channels, K]
     const float *bias;         // [channels] or null
@@ -37,10 +40,15 @@ struct Params {
     void *q, *k, *v;
 };
 
-__device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
+// x sigma(x) with the fast exponential and division intrinsics (a few ulp; x -> -inf gives 0)
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
-template <typename TI, typename TO>
+// KT: the taps compiled in (4, the reference's width, or kMaxK with the unused taps zero)
+template <typename TI, typename TO, int KT>
 __global__ void __launch_bounds__(kThreads) prologue_kernel(const Params p) {
+    constexpr int kRows = kTile + KT - 1;           // the tile's inputs: tokens t0 - K + 1 .. t0 + kTile - 1
+    __shared__ __align__(16) TI tile[kRows][kThreads];
+    __shared__ float head[KT][kThreads];  // rows before the sequence (the window, float32)
     __shared__ float red[kThreads / 32][kTile];
     __shared__ float inv[kTile];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -58,43 +66,65 @@ __global__ void __launch_bounds__(kThreads) prologue_kernel(const Params p) {
         const int64_t s = seg - H - p.u * H;
         kind = 2, width = (int)p.dv, m = s / H, h = s - m * H, base = kd * (1 + p.u) + m * H * p.dv + h * p.dv;
     }
-    const bool on = tid < width;
-    const int64_t c = base + (on ? tid : 0);
     const int K = p.K;
     const TI *X = static_cast<const TI *>(p.x);
+    const int64_t tfirst = t0 - (KT - 1);  // token of tile row 0 (rows before KT - K hold zero taps)
 
-    // inputs of tokens t0 - K + 1 .. t0 + kTile - 1 (the window before the sequence, zero past its end),
-    // every load issued before the first use
-    constexpr int kHalo = kTile + kMaxK - 1;
-    float xs[kHalo];
-    const float *win = p.window_in ? p.window_in + (b * p.channels + c) * K : nullptr;
-#pragma unroll
-    for (int i = 0; i < kHalo; ++i) {
-        const int64_t t = t0 - K + 1 + i;
-        const bool in_seq = i < kTile + K - 1 && t >= 0 && t < p.seq;
-        const bool in_win = i < kTile + K - 1 && t < 0 && win != nullptr;
-        const float xv = ld(X + (in_seq ? (b * p.seq + t) * p.x_stride + c : 0));
-        const float wv = in_win ? win[K + t] : 0.f;
-        xs[i] = in_seq ? xv : wv;
+    // ---- stage the inputs: 16-byte copies of the in-sequence rows (or scalar loads when the rows are not
+    // 16-byte aligned), the window's float32 values for the rows before the sequence, zeros after it ----
+    constexpr int kVec = 16 / sizeof(TI);
+    const bool vec = p.vec_rows && (base % kVec) == 0 && (width % kVec) == 0;
+    const int r_lo = tfirst < 0 ? (int)(-tfirst) : 0;                                   // rows before the sequence
+    const int r_hi = p.seq - tfirst < kRows ? (int)(p.seq - tfirst) : kRows;            // rows from r_hi: past it
+    const TI *xrow = X + (b * p.seq + tfirst) * p.x_stride + base;                       // row r at r * x_stride
+    if (vec) {
+        const int per_row = width / kVec, rstep = kThreads / per_row;
+        const int q = tid % per_row;
+        for (int r = r_lo + tid / per_row; r < r_hi; r += rstep)
+            ptx::cp_async16(ptx::smem_u32(&tile[r][q * kVec]), xrow + r * p.x_stride + q * kVec, 16u);
+        ptx::cp_async_commit();
+    } else if (tid < width) {
+        for (int r = r_lo; r < r_hi; ++r) tile[r][tid] = xrow[r * p.x_stride + tid];
     }
-    float w[kMaxK];
+    if (tid < width) {
+        const float *win = p.window_in ? p.window_in + (b * p.channels + base + tid) * K : nullptr;
+        for (int r = 0; r < r_lo; ++r) {  // token tfirst + r < 0: window column K + t (zero before it)
+            const int64_t t = tfirst + r;
+            if (r < KT) head[r][tid] = (t >= -(int64_t)(K - 1) && win) ? win[K + t] : 0.f;
+        }
+        for (int r = r_hi; r < kRows; ++r) st(&tile[r][tid], 0.f);
+    }
+    if (vec) ptx::cp_async_wait<0>();
+    __syncthreads();
+
+    // ---- convolve (taps j < K; the first KT - K rows are never read), activation ----
+    const bool on = tid < width;
+    const int cch = on ? tid : 0;
+    const int64_t c = base + cch;
+    // taps shifted to the tile rows they read: ws[j] = w[j - (KT - K)] (zero below)
+    float ws[KT];
 #pragma unroll
-    for (int j = 0; j < kMaxK; ++j) w[j] = j < K ? p.weight[c * K + j] : 0.f;
+    for (int j = 0; j < KT; ++j) ws[j] = j >= KT - K ? p.weight[c * K + j - (KT - K)] : 0.f;
     const float bias = p.bias ? p.bias[c] : 0.f;
-    // output token t0 + i reads the inputs of tokens t0 + i - K + 1 + j (j < K), i.e. xs[i + j]; the taps
-    // j >= K have w = 0 and read zeros inside xs
     const bool act = p.conv_silu || kind == 2 || p.qk_silu;  // the conv's SiLU, or v's, or q / k's
+    // output token t0 + i reads tokens t0 + i - K + 1 + j (j < K): tile rows i + (KT - K) + j; the rows
+    // before the sequence come from `head` (they only enter the first KT - 1 history values)
+    float hist[KT];
+#pragma unroll
+    for (int j = 0; j < KT - 1; ++j) hist[j + 1] = tfirst + j < 0 ? head[j][cch] : ld(&tile[j][cch]);
     float y[kTile];
 #pragma unroll
     for (int i = 0; i < kTile; ++i) {
+#pragma unroll
+        for (int j = 0; j < KT - 1; ++j) hist[j] = hist[j + 1];
+        hist[KT - 1] = ld(&tile[i + KT - 1][cch]);
         float a = bias;
 #pragma unroll
-        for (int j = 0; j < kMaxK; ++j) a = fmaf(w[j], xs[i + j], a);
+        for (int j = 0; j < KT; ++j) a = fmaf(ws[j], hist[j], a);
         if (act) a = silu(a);
         y[i] = on ? a : 0.f;
     }
-    const bool norm = p.l2 && kind < 2;
-    if (norm) {
+    if (p.l2 && kind < 2) {
         // sum over the segment of y^2 per token: a transpose reduction leaves token `lane`'s warp sum in
         // s[0] (31 shuffles for 32 tokens), then the warps add up
         float s[kTile];
@@ -122,22 +152,23 @@ __global__ void __launch_bounds__(kThreads) prologue_kernel(const Params p) {
 #pragma unroll
         for (int i = 0; i < kTile; ++i) y[i] *= inv[i];
     }
-    // outputs: row (b, t) of q, row (b, t u + m) of k / v
+    // ---- outputs: row (b, t) of q, row (b, t u + m) of k / v ----
     TO *out = static_cast<TO *>(kind == 0 ? p.q : kind == 1 ? p.k : p.v);
     const int64_t rows_per_b = kind == 0 ? p.seq : p.seq * p.u, step = kind == 0 ? 1 : p.u;
+    const int64_t pitch = step * H * width;  // elements between consecutive tokens' rows
+    const int n = p.seq - t0 < kTile ? (int)(p.seq - t0) : kTile;
     if (on) {
+        TO *o = out + ((b * rows_per_b + t0 * step + m) * H + h) * width + tid;
 #pragma unroll
-        for (int i = 0; i < kTile; ++i) {
-            const int64_t t = t0 + i;
-            if (t < p.seq) st(out + ((b * rows_per_b + t * step + m) * H + h) * width + tid, y[i]);
-        }
+        for (int i = 0; i < kTile; ++i, o += pitch)
+            if (i < n) st(o, y[i]);
     }
-    // the next window: the padded input's last K columns, from the CTA holding the last token
+    // ---- the next window: the padded input's last K columns, from the CTA holding the last token ----
     if (p.window_out && on && t0 <= p.seq - 1 && p.seq - 1 < t0 + kTile) {
         float *wo = p.window_out + (b * p.channels + c) * K;
         for (int j = 0; j < K; ++j) {
-            const int64_t t = p.seq - K + j;  // token of padded column S - 1 + j
-            wo[j] = t >= 0 ? ld(X + (b * p.seq + t) * p.x_stride + c) : (win ? win[K + t] : 0.f);
+            const int r = (int)(p.seq - K + j - tfirst);
+            wo[j] = p.seq - K + j < 0 ? head[r][cch] : ld(&tile[r][cch]);
         }
     }
 }

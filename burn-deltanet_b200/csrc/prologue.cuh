@@ -173,5 +173,167 @@ __global__ void __launch_bounds__(kThreads) prologue_kernel(const Params p) {
     }
 }
 
+// ---------------------------------------------------------------------------------------------------
+// The same computation two channels per thread (even dk and dv): a CTA of 128 threads serves two head
+// segments, 64 threads each, so shared-memory reads and output stores move channel pairs (bf16x2 or
+// float2) and each thread's share of the norm's reduction halves.  Both halves reach every barrier (the
+// second half of the last CTA may have no segment, and a q / k half may sit beside a v half).
+// ---------------------------------------------------------------------------------------------------
+constexpr int kHalf = kThreads / 2;  // threads per segment
+
+__device__ __forceinline__ float2 to_f2(float2 v) { return v; }
+__device__ __forceinline__ float2 to_f2(__nv_bfloat162 v) { return __bfloat1622float2(v); }
+__device__ __forceinline__ void st2(float *o, float a, float b) { *reinterpret_cast<float2 *>(o) = make_float2(a, b); }
+__device__ __forceinline__ void st2(__nv_bfloat16 *o, float a, float b) {
+    *reinterpret_cast<__nv_bfloat162 *>(o) = __floats2bfloat162_rn(a, b);
+}
+template <typename T> struct PairOf;
+template <> struct PairOf<float> { using type = float2; };
+template <> struct PairOf<__nv_bfloat16> { using type = __nv_bfloat162; };
+
+template <typename TI, typename TO, int KT>
+__global__ void __launch_bounds__(kThreads) prologue_pair_kernel(const Params p) {
+    using TI2 = typename PairOf<TI>::type;
+    constexpr int kRows = kTile + KT - 1;
+    __shared__ __align__(16) TI tile[2][kRows][kThreads];
+    __shared__ float2 head[2][KT][kHalf];  // rows before the sequence (the window, float32)
+    __shared__ float red[kThreads / 32][kTile];
+    __shared__ float inv[2][kTile];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, half = tid / kHalf, lt = tid % kHalf;
+    const int64_t H = p.heads, kd = H * p.dk, nseg = H * (1 + 2 * (int64_t)p.u);
+    const int64_t seg = 2 * (int64_t)blockIdx.x + half, b = blockIdx.z, t0 = (int64_t)blockIdx.y * kTile;
+    const bool live = seg < nseg;
+    int kind, width;  // 0 q, 1 k, 2 v
+    int64_t h, m, base;
+    if (seg < H) {
+        kind = 0, width = (int)p.dk, h = seg, m = 0, base = seg * p.dk;
+    } else if (seg < H + p.u * H) {
+        const int64_t sq = seg - H;
+        kind = 1, width = (int)p.dk, m = sq / H, h = sq - m * H, base = kd + m * kd + h * p.dk;
+    } else {
+        const int64_t sq = live ? seg - H - p.u * H : 0;
+        kind = 2, width = live ? (int)p.dv : 0, m = sq / H, h = sq - m * H,
+        base = kd * (1 + p.u) + m * H * p.dv + h * p.dv;
+    }
+    const int K = p.K;
+    const TI *X = static_cast<const TI *>(p.x);
+    const int64_t tfirst = t0 - (KT - 1);
+    TI(*tl)[kThreads] = tile[half];
+
+    // ---- stage this half's segment ----
+    constexpr int kVec = 16 / sizeof(TI);
+    const bool vec = p.vec_rows && (base % kVec) == 0 && (width % kVec) == 0;
+    const int r_lo = tfirst < 0 ? (int)(-tfirst) : 0;
+    const int r_hi = p.seq - tfirst < kRows ? (int)(p.seq - tfirst) : kRows;
+    const TI *xrow = X + (b * p.seq + tfirst) * p.x_stride + base;
+    const bool on = 2 * lt < width;  // this thread's channel pair 2 lt, 2 lt + 1
+    if (live && vec) {
+        const int per_row = width / kVec, rstep = kHalf / per_row;
+        const int q = lt % per_row;
+        for (int r = r_lo + lt / per_row; r < r_hi; r += rstep)
+            ptx::cp_async16(ptx::smem_u32(&tl[r][q * kVec]), xrow + r * p.x_stride + q * kVec, 16u);
+    } else if (live && on) {
+        for (int r = r_lo; r < r_hi; ++r) {
+            tl[r][2 * lt] = xrow[r * p.x_stride + 2 * lt];
+            tl[r][2 * lt + 1] = xrow[r * p.x_stride + 2 * lt + 1];
+        }
+    }
+    ptx::cp_async_commit();
+    if (live && on) {
+        const float *win = p.window_in ? p.window_in + (b * p.channels + base + 2 * lt) * K : nullptr;
+        for (int r = 0; r < r_lo; ++r) {  // token tfirst + r < 0: window column K + t (zero before it)
+            const int64_t t = tfirst + r;
+            const bool w_ok = t >= -(int64_t)(K - 1) && win;
+            if (r < KT) head[half][r][lt] = w_ok ? make_float2(win[K + t], win[K + K + t]) : make_float2(0.f, 0.f);
+        }
+        for (int r = r_hi; r < kRows; ++r) {
+            st(&tl[r][2 * lt], 0.f);
+            st(&tl[r][2 * lt + 1], 0.f);
+        }
+    }
+    ptx::cp_async_wait<0>();
+    __syncthreads();
+
+    // ---- convolve both channels, activation ----
+    const int cch = on ? 2 * lt : 0;
+    const int64_t c = base + cch;
+    float w0[KT], w1[KT];
+#pragma unroll
+    for (int j = 0; j < KT; ++j) {
+        w0[j] = (live && j >= KT - K) ? p.weight[c * K + j - (KT - K)] : 0.f;
+        w1[j] = (live && j >= KT - K) ? p.weight[(c + 1) * K + j - (KT - K)] : 0.f;
+    }
+    const float b0 = (live && p.bias) ? p.bias[c] : 0.f, b1 = (live && p.bias) ? p.bias[c + 1] : 0.f;
+    const bool act = p.conv_silu || kind == 2 || p.qk_silu;
+    float2 hist[KT];
+#pragma unroll
+    for (int j = 0; j < KT - 1; ++j)
+        hist[j + 1] = tfirst + j < 0 ? head[half][j][lt] : to_f2(*reinterpret_cast<const TI2 *>(&tl[j][cch]));
+    float y0[kTile], y1[kTile];
+#pragma unroll
+    for (int i = 0; i < kTile; ++i) {
+#pragma unroll
+        for (int j = 0; j < KT - 1; ++j) hist[j] = hist[j + 1];
+        hist[KT - 1] = to_f2(*reinterpret_cast<const TI2 *>(&tl[i + KT - 1][cch]));
+        float a0 = b0, a1 = b1;
+#pragma unroll
+        for (int j = 0; j < KT; ++j) {
+            a0 = fmaf(w0[j], hist[j].x, a0);
+            a1 = fmaf(w1[j], hist[j].y, a1);
+        }
+        if (act) a0 = silu(a0), a1 = silu(a1);
+        y0[i] = (live && on) ? a0 : 0.f;
+        y1[i] = (live && on) ? a1 : 0.f;
+    }
+    if (p.l2) {  // uniform over the CTA: every thread reaches the barriers, q / k halves apply the result
+        float sm[kTile];
+#pragma unroll
+        for (int i = 0; i < kTile; ++i) sm[i] = fmaf(y0[i], y0[i], y1[i] * y1[i]);
+#pragma unroll
+        for (int wd = kTile / 2; wd >= 1; wd >>= 1) {
+            const bool upper = (lane & wd) != 0;
+#pragma unroll
+            for (int i = 0; i < wd; ++i) {
+                const float send = upper ? sm[i] : sm[i + wd];
+                const float keep = upper ? sm[i + wd] : sm[i];
+                sm[i] = keep + __shfl_xor_sync(0xffffffffu, send, wd);
+            }
+        }
+        red[warp][lane] = sm[0];
+        __syncthreads();
+        if (tid < 2 * kTile) {
+            const int hf = tid / kTile, i = tid % kTile;
+            inv[hf][i] = rsqrtf(red[2 * hf][i] + red[2 * hf + 1][i] + 1e-6f);
+        }
+        __syncthreads();
+        if (kind < 2) {
+#pragma unroll
+            for (int i = 0; i < kTile; ++i) y0[i] *= inv[half][i], y1[i] *= inv[half][i];
+        }
+    }
+    // ---- outputs ----
+    if (live && on) {
+        TO *out = static_cast<TO *>(kind == 0 ? p.q : kind == 1 ? p.k : p.v);
+        const int64_t rows_per_b = kind == 0 ? p.seq : p.seq * p.u, step = kind == 0 ? 1 : p.u;
+        const int64_t pitch = step * H * width;
+        const int n = p.seq - t0 < kTile ? (int)(p.seq - t0) : kTile;
+        TO *o = out + ((b * rows_per_b + t0 * step + m) * H + h) * width + 2 * lt;
+#pragma unroll
+        for (int i = 0; i < kTile; ++i, o += pitch)
+            if (i < n) st2(o, y0[i], y1[i]);
+        if (p.window_out && t0 <= p.seq - 1 && p.seq - 1 < t0 + kTile) {
+            float *wo = p.window_out + (b * p.channels + c) * K;
+            for (int j = 0; j < K; ++j) {
+                const int r = (int)(p.seq - K + j - tfirst);
+                float2 v;
+                if (p.seq - K + j < 0) v = head[half][r][lt];
+                else v = to_f2(*reinterpret_cast<const TI2 *>(&tl[r][cch]));
+                wo[j] = v.x;
+                wo[K + j] = v.y;
+            }
+        }
+    }
+}
+
 }  // namespace pro
 }  // namespace dc

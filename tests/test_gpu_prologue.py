@@ -1,7 +1,8 @@
 """GPU parity of the front-end prologue (dc_qkv_prologue) against the float64 oracle (oracle/prologue.py).
 
 The short convolution with its window, the activations, the q / k L2 norm and the micro-step reshape
-(src/common/conv.rs, src/common/qkv.rs:373-500), over: the benchmark head size (dk = dv = 128), sequences
+(src/common/conv.rs, src/common/qkv.rs:373-500), over both kernels (two channels per thread for even
+head widths, one for odd), the benchmark head size (dk = dv = 128), sequences
 that end inside and on a 32-token tile, a single-token step from a window, DeltaProduct micro-steps
 (u = 2, 3), K = 1 (no window), SiLU not fused into the convolution, no norm, x as a column slice of a wider
 projection, bf16 and float32.  Split calls carrying the window equal one call, and token-by-token steps
@@ -54,7 +55,8 @@ def test_prologue_benchmark_heads(s, dtype):
     check(x, 2, 128, 128, 1, w, bias, win)
 
 
-@pytest.mark.parametrize("u,dk,dv,k", [(2, 64, 32, 3), (3, 16, 24, 4), (1, 40, 8, 1), (2, 8, 8, 8)])
+@pytest.mark.parametrize("u,dk,dv,k", [(2, 64, 32, 3), (3, 16, 24, 4), (1, 40, 8, 1), (2, 8, 8, 8),
+                                      (1, 9, 7, 4), (2, 5, 6, 3)])  # odd widths: one channel per thread
 def test_prologue_micro_steps_and_widths(u, dk, dv, k):
     x, w, bias, win = make(u * 100 + dk, 2, 37, 3, dk, dv, u, k, torch.float32, window=k > 1)
     check(x, 3, dk, dv, u, w, bias, win)

@@ -408,6 +408,26 @@ def time_prologue(dn, steps, warmup, batch=8, tokens=4096):
     return e0.elapsed_time(e1) / steps, 2 * x.numel() * 2 + 2 * win.numel() * 4 + w.numel() * 4
 
 
+def time_gates(dn, steps, warmup):
+    """The front-end's gate producers at config 5's sizes (B=16, T=16384, H=16, dk=128): the per-channel
+    log-decay over bf16 [B, T, H dk] (the up projection's output) and the doubled erase gate over bf16
+    [B, T, H dk], each float32 out.  Returns (ms per pair of calls, algorithmic bytes per pair)."""
+    g = torch.Generator(device="cuda").manual_seed(13)
+    x = torch.randn(16, 16384, H * D, device="cuda", generator=g).to(torch.bfloat16)
+    bias, a = torch.randn(H * D, device="cuda", generator=g), torch.rand(H, device="cuda", generator=g)
+    for _ in range(max(3, warmup)):
+        dn.channel_log_decay(x, bias, a, D, -5.0), dn.write_gate(x, doubled=True)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        dn.channel_log_decay(x, bias, a, D, -5.0), dn.write_gate(x, doubled=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps, 2 * (x.numel() * 2 + x.numel() * 4)
+
+
 def time_decode_cfg5(dn, state, steps, warmup, seed):
     """Config 5's decode: `steps` GDN-2 step() tokens (per-channel erase, write and log-decay) from the
     prefill's final state, for this rank's sequences x 16 heads, the state updated in place; the ticks
@@ -541,6 +561,11 @@ def run_ours(args):
     if args.only == "prefill":
         if rank == 0:
             print(json.dumps({"prefill_ms_per_step": ms, "tok_s": batch * tokens * world / (ms / 1e3)}))
+        return
+    if args.only == "gates":
+        gt_ms, gt_bytes = time_gates(dn, 10, 3)
+        if rank == 0:
+            print(json.dumps({"gates_ms": gt_ms, "gates_gbs": gt_bytes / (gt_ms / 1e3) / 1e9}))
         return
     if args.only == "prologue":
         pr_ms, pr_bytes = time_prologue(dn, 20, 3, batch=args.batch or 8)
@@ -724,7 +749,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="deltanet")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["prefill", "decode", "backward", "out_norm", "prologue"], default=None,
+    ap.add_argument("--only", choices=["prefill", "decode", "backward", "out_norm", "prologue", "gates"], default=None,
                     help="time one kernel alone and print a short line (for profiling runs)")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU instead of the workload's own (for small profiling captures)")

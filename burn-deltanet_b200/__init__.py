@@ -26,12 +26,15 @@ from .core import (
     delta_step,
     out_norm,
     qkv_prologue,
+    write_gate,
+    head_log_decay,
+    channel_log_decay,
 )
 
 __all__ = [
     "DeltaChunkFunction", "DeltaCoreError", "DeltaInput", "DeltaPath", "DeltaShapeError", "TriSolve",
     "beta_gates", "delta_chunk_host_scratch_size", "delta_chunk_recalculated", "delta_chunk_recalculated_backward",
-    "delta_chunk_recalculated_host", "delta_step", "library_path", "out_norm", "qkv_prologue",
+    "delta_chunk_recalculated_host", "delta_step", "library_path", "out_norm", "qkv_prologue", "write_gate", "head_log_decay", "channel_log_decay",
 ]
 
 

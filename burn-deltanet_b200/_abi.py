@@ -43,6 +43,7 @@ EXPORTS = (
     "dc_chunk_bwd",
     "dc_out_norm",
     "dc_qkv_prologue",
+    "dc_gates",
 )
 
 
@@ -121,6 +122,21 @@ class PrologueArgs(ctypes.Structure):
     ]
 
 
+DC_GATE_WRITE = 0
+DC_GATE_HEAD_DECAY = 1
+DC_GATE_CHANNEL_DECAY = 2
+
+
+class GateArgs(ctypes.Structure):
+    """struct dc_gate_args."""
+    _fields_ = [
+        ("rows", ctypes.c_int64), ("cols", ctypes.c_int64), ("x_stride", ctypes.c_int64),
+        ("kind", ctypes.c_int32), ("in_dtype", ctypes.c_int32), ("group", ctypes.c_int32),
+        ("scale", ctypes.c_float), ("lo", ctypes.c_float), ("hi", ctypes.c_float),
+        ("x", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("a_log", ctypes.c_void_p), ("out", ctypes.c_void_p),
+    ]
+
+
 _lib = None
 
 
@@ -164,6 +180,8 @@ def lib() -> ctypes.CDLL:
         L.dc_out_norm.restype = ctypes.c_int
         L.dc_qkv_prologue.argtypes = [ctypes.POINTER(PrologueArgs), ctypes.c_void_p]
         L.dc_qkv_prologue.restype = ctypes.c_int
+        L.dc_gates.argtypes = [ctypes.POINTER(GateArgs), ctypes.c_void_p]
+        L.dc_gates.restype = ctypes.c_int
         _lib = L
     return _lib
 

@@ -372,6 +372,63 @@ def qkv_prologue(x_bsw: torch.Tensor, heads: int, dk: int, dv: int, conv_weight:
     return q, k, v, nxt
 
 
+def _gates(x: torch.Tensor, kind: int, cols_out, group=1, scale=1.0, lo=0.0, hi=0.0, bias=None, a_log=None):
+    """dc_gates over the last axis of x (a [.., cols] column slice; rows contiguous in the leading axes)."""
+    if not isinstance(x, torch.Tensor) or not x.is_cuda:
+        raise DeltaCoreError(_abi.DC_EDEVICE, "x must be a CUDA tensor")
+    cols = x.shape[-1]
+    rows = x.numel() // max(cols, 1)
+    x2 = x.reshape(rows, cols) if x.dim() != 2 else x
+    if x2.stride(1) != 1 or (rows > 1 and x2.stride(0) < cols):
+        raise DeltaCoreError(_abi.DC_EINVAL_ARG, "x must have contiguous columns and one row stride")
+    for t, name in ((bias, "bias"), (a_log, "a_log")):
+        if t is not None:
+            _check_tensor(t, name)
+            if t.dtype != torch.float32:
+                raise DeltaCoreError(_abi.DC_EUNSUPPORTED_DTYPE, f"{name} must be float32")
+    out = torch.empty(tuple(x.shape[:-1]) + tuple(cols_out), device=x.device, dtype=torch.float32)
+    a = _abi.GateArgs()
+    a.rows, a.cols, a.x_stride = rows, cols, x2.stride(0) if rows > 1 else cols
+    a.kind, a.in_dtype, a.group = kind, _dtype_code(x, "x"), group
+    a.scale, a.lo, a.hi = scale, lo, hi
+    a.x, a.out = x2.data_ptr(), out.data_ptr()
+    a.bias = None if bias is None else bias.data_ptr()
+    a.a_log = None if a_log is None else a_log.data_ptr()
+    with torch.cuda.device(x.device):
+        _raise(_abi.lib().dc_gates(a, torch.cuda.current_stream(x.device).cuda_stream), "dc_gates")
+    return out
+
+
+def write_gate(raw: torch.Tensor, doubled: bool = False) -> torch.Tensor:
+    """The write gates of ``squash_write`` (src/common/qkv.rs:333-368) through ``dc_gates``:
+    ``sigmoid(raw)``, times 2 for the erase gate under ``allow_neg_eigval``.  ``raw`` may be a column
+    slice of the projection; returns float32 of ``raw``'s shape."""
+    return _gates(raw, _abi.DC_GATE_WRITE, (raw.shape[-1],), scale=2.0 if doubled else 1.0)
+
+
+def head_log_decay(dt_raw: torch.Tensor, dt_bias: torch.Tensor, a_log: torch.Tensor,
+                   dt_limit=(0.0, 6.5504e4)) -> torch.Tensor:
+    """``ForgetGate::log_decay`` (src/common/gate.rs:51-59) through ``dc_gates``:
+    ``clamp(softplus(dt_raw + dt_bias), *dt_limit) * -exp(a_log)`` over the last axis (heads)."""
+    h = dt_raw.shape[-1]
+    if tuple(dt_bias.shape) != (h,) or tuple(a_log.shape) != (h,):
+        raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, f"dt_bias and a_log must be [{h}]")
+    return _gates(dt_raw, _abi.DC_GATE_HEAD_DECAY, (h,), lo=float(dt_limit[0]), hi=float(dt_limit[1]),
+                  bias=dt_bias, a_log=a_log)
+
+
+def channel_log_decay(dt: torch.Tensor, dt_bias: torch.Tensor, a_log: torch.Tensor, head_k_dim: int,
+                      lower_bound: float) -> torch.Tensor:
+    """``ChannelForgetGate::log_decay`` (src/common/gate.rs:178-196) through ``dc_gates``, on its ``up``
+    projection's output ``dt [.., heads * head_k_dim]``: ``lower_bound * sigmoid((dt + dt_bias) *
+    exp(a_log[head]))``, returned as float32 ``[.., heads, head_k_dim]``."""
+    c = dt.shape[-1]
+    if c % head_k_dim or tuple(dt_bias.shape) != (c,) or tuple(a_log.shape) != (c // head_k_dim,):
+        raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, "dt_bias must be [heads * head_k_dim], a_log [heads]")
+    return _gates(dt, _abi.DC_GATE_CHANNEL_DECAY, (c // head_k_dim, head_k_dim), group=head_k_dim,
+                  scale=float(lower_bound), bias=dt_bias, a_log=a_log)
+
+
 class DeltaChunkFunction(torch.autograd.Function):
     """The custom autodiff node (src/delta/chunk_recalculated/backward.rs:30-265): the forward
     keeps only its leaf inputs, and the backward recomputes what it needs from them.

@@ -1022,3 +1022,50 @@ int dc_qkv_prologue(const dc_qkv_prologue_args *a, dc_stream_t stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// dc_gates: the front-end's gate producers (prologue.cuh).
+// ---------------------------------------------------------------------------
+extern "C" {
+
+int dc_gates(const dc_gate_args *a, dc_stream_t stream) {
+    if (!a) return DC_EINVAL_ARG;
+    if (a->rows < 0 || a->cols < 1 || a->x_stride < a->cols) return DC_EINVAL_SHAPE;
+    if (a->kind < DC_GATE_WRITE || a->kind > DC_GATE_CHANNEL_DECAY) return DC_EINVAL_ARG;
+    if (a->in_dtype != DC_F32 && a->in_dtype != DC_BF16) return DC_EUNSUPPORTED_DTYPE;
+    if (!isfinite(a->scale) || (a->kind == DC_GATE_HEAD_DECAY && !(a->lo <= a->hi))) return DC_EINVAL_ARG;
+    if (a->kind == DC_GATE_CHANNEL_DECAY && (a->group < 1 || a->cols % a->group != 0)) return DC_EINVAL_SHAPE;
+    if (a->rows == 0) return DC_OK;
+    if (!a->x || !a->out || (a->kind != DC_GATE_WRITE && (!a->bias || !a->a_log))) return DC_EINVAL_ARG;
+    const int st = check_device(nullptr);
+    if (st != DC_OK) return st;
+    dc::pro::GateParams p{};
+    p.rows = a->rows;
+    p.cols = a->cols;
+    p.x_stride = a->x_stride;
+    p.kind = a->kind;
+    p.group = a->group;
+    p.scale = a->scale;
+    p.lo = a->lo;
+    p.hi = a->hi;
+    p.x = a->x;
+    p.bias = a->bias;
+    p.a_log = a->a_log;
+    p.out = a->out;
+    if (a->cols > 0x7fffffffLL) return DC_EUNSUPPORTED;
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    const int64_t cap = (int64_t)sms * 16;
+    const int64_t blocks = a->rows < cap ? a->rows : cap;  // one row per CTA at a time
+    // four columns per thread: whole 4-column groups whose loads (8 or 16 bytes) and stores (16) are aligned
+    const int64_t esz = a->in_dtype == DC_BF16 ? 2 : 4;
+    const int vec4 = (a->cols % 4 == 0 && (a->x_stride * esz) % (4 * esz) == 0 && aligned(a->x, 4 * esz) &&
+                      aligned(a->out, 16)) ? 1 : 0;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (a->in_dtype == DC_BF16) dc::pro::gates_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, s>>>(p, vec4);
+    else dc::pro::gates_kernel<float><<<(unsigned)blocks, 256, 0, s>>>(p, vec4);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? DC_OK : cuda_fail(e);
+}
+
+}  // extern "C"

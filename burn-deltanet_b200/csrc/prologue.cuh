@@ -335,5 +335,76 @@ __global__ void __launch_bounds__(kThreads) prologue_pair_kernel(const Params p)
     }
 }
 
+// ---------------------------------------------------------------------------------------------------
+// The front-end's gate producers, one elementwise map over a [rows, cols] column slice of the projection
+// (row stride x_stride) into a contiguous float32 [rows, cols]:
+//   kind 0  scale sigma(x)                                          the write gates (qkv.rs:333-368)
+//   kind 1  -e^{a[c]} clamp(softplus(x + bias[c]), lo, hi)          ForgetGate::log_decay (gate.rs:51-59)
+//   kind 2  scale sigma((x + bias[c]) e^{a[c / group]})             ChannelForgetGate::log_decay
+//                                                                  (gate.rs:178-196), scale = lower bound
+// softplus(x) = max(x, 0) + log1p(e^-|x|) at full precision; the sigmoids use the fast exponential and
+// division intrinsics (a few ulp).
+// ---------------------------------------------------------------------------------------------------
+struct GateParams {
+    int64_t rows, cols, x_stride;
+    int32_t kind, group;
+    float scale, lo, hi;
+    const void *x;
+    const float *bias, *a_log;
+    float *out;
+};
+
+// sigma(z) * scale with the fast exponential and division intrinsics (a few ulp; z -> -inf gives 0)
+__device__ __forceinline__ float scaled_sigmoid(float scale, float z) { return __fdividef(scale, 1.f + __expf(-z)); }
+
+// kind 0 / 1 at column c; kind 2 with the column's per-head slope e^{a[c / group]} given
+__device__ __forceinline__ float gate_map(const GateParams &p, float x, int c, float slope) {
+    if (p.kind == 0) return scaled_sigmoid(p.scale, x);
+    if (p.kind == 1) {
+        const float z = x + p.bias[c];
+        const float sp = fmaxf(z, 0.f) + log1pf(expf(-fabsf(z)));
+        return -expf(p.a_log[c]) * fminf(fmaxf(sp, p.lo), p.hi);
+    }
+    return scaled_sigmoid(p.scale, (x + p.bias[c]) * slope);
+}
+__device__ __forceinline__ float gate_slope(const GateParams &p, int c) {
+    return p.kind == 2 ? expf(p.a_log[c / p.group]) : 0.f;
+}
+
+// One CTA per row at a time (rows blockIdx.x, + gridDim.x, ...), its threads along the columns: four
+// consecutive columns per thread (8- or 16-byte loads, 16-byte stores) when `vec4`, else one.
+template <typename TI>
+__global__ void __launch_bounds__(256) gates_kernel(const GateParams p, int vec4) {
+    const TI *X = static_cast<const TI *>(p.x);
+    const int cols = (int)p.cols;
+    for (int64_t r = blockIdx.x; r < p.rows; r += gridDim.x) {
+        const TI *xr = X + r * p.x_stride;
+        float *o = p.out + r * p.cols;
+        if (vec4) {
+            for (int c = 4 * threadIdx.x; c < cols; c += 4 * blockDim.x) {
+                float x4[4];
+                if constexpr (sizeof(TI) == 2) {
+                    const uint2 t = *reinterpret_cast<const uint2 *>(xr + c);
+                    const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&t.x));
+                    const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&t.y));
+                    x4[0] = lo.x, x4[1] = lo.y, x4[2] = hi.x, x4[3] = hi.y;
+                } else {
+                    const float4 t = *reinterpret_cast<const float4 *>(xr + c);
+                    x4[0] = t.x, x4[1] = t.y, x4[2] = t.z, x4[3] = t.w;
+                }
+                // the four columns share a head when the group is a multiple of 4 (one slope)
+                const bool one = p.group % 4 == 0;
+                const float s0 = gate_slope(p, c);
+                const float s1 = one ? s0 : gate_slope(p, c + 1), s2 = one ? s0 : gate_slope(p, c + 2),
+                            s3 = one ? s0 : gate_slope(p, c + 3);
+                *reinterpret_cast<float4 *>(o + c) = make_float4(gate_map(p, x4[0], c, s0), gate_map(p, x4[1], c + 1, s1),
+                                                                 gate_map(p, x4[2], c + 2, s2), gate_map(p, x4[3], c + 3, s3));
+            }
+        } else {
+            for (int c = threadIdx.x; c < cols; c += blockDim.x) o[c] = gate_map(p, ld(xr + c), c, gate_slope(p, c));
+        }
+    }
+}
+
 }  // namespace pro
 }  // namespace dc

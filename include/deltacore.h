@@ -299,6 +299,35 @@ typedef struct dc_qkv_prologue_args {
 
 DC_API int dc_qkv_prologue(const dc_qkv_prologue_args *args, dc_stream_t stream);
 
+/*
+ * The front-end's gate producers: one elementwise map from a [rows, cols] column slice of the input
+ * projection (x: element (r, c) at r*x_stride + c, in_dtype) to a contiguous float32 out [rows, cols]:
+ *   DC_GATE_WRITE          out = scale * sigma(x): squash_write (src/common/qkv.rs:333-368), scale 2 for
+ *                          the erase gate under allow_neg_eigval, else 1 (rows = batch*seq*u, cols = the
+ *                          gate's heads, or heads*head_dim for WriteGate::Channel)
+ *   DC_GATE_HEAD_DECAY     out = -exp(a_log[c]) * clamp(softplus(x + bias[c]), lo, hi): ForgetGate::log_decay
+ *                          (src/common/gate.rs:51-59), cols = heads (rows = batch*seq)
+ *   DC_GATE_CHANNEL_DECAY  out = scale * sigma((x + bias[c]) * exp(a_log[c / group])): ChannelForgetGate::
+ *                          log_decay (gate.rs:178-196) applied to its `up` projection's output, cols =
+ *                          heads*group (group = head_k_dim), scale = the lower bound
+ * softplus(x) = log(1 + e^x).  bias and a_log are float32 (unused ones may be NULL).  rows may be 0.
+ */
+#define DC_GATE_WRITE 0
+#define DC_GATE_HEAD_DECAY 1
+#define DC_GATE_CHANNEL_DECAY 2
+
+typedef struct dc_gate_args {
+    int64_t rows, cols, x_stride;
+    int32_t kind, in_dtype, group;
+    float scale, lo, hi;
+    const void *x;
+    const float *bias;
+    const float *a_log;
+    float *out;
+} dc_gate_args;
+
+DC_API int dc_gates(const dc_gate_args *args, dc_stream_t stream);
+
 /* Human-readable name of a dc_status. */
 DC_API const char *dc_status_string(int status);
 

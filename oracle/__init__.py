@@ -20,7 +20,9 @@ It wraps ``liboracle.so`` (``oracle_core.c``, built by ``oracle/Makefile``):
   normalisation OutNorm (src/common/norm.rs:106-144);
 * ``qkv_prologue`` (``oracle/prologue.py``, numpy) — the front-end after the
   input projection: short convolution, activations, q/k L2 norm
-  (src/common/conv.rs, src/common/qkv.rs:373-500).
+  (src/common/conv.rs, src/common/qkv.rs:373-500), and its gate producers
+  ``write_gate`` / ``head_log_decay`` / ``channel_log_decay``
+  (qkv.rs:333-368, src/common/gate.rs:51-59, 178-196).
 
 Arrays use the reference's layouts: per-token ``[batch, seq, heads, width]``,
 state ``[batch, heads, dk, dv]``.
@@ -192,4 +194,4 @@ def householder(kind, q, k, v, erase, write, g, state, u, chunk_len=64, scale=No
 
 from .backward import recurrent_backward  # noqa: E402  (numpy only)
 from .out_norm import out_norm  # noqa: E402  (numpy only)
-from .prologue import qkv_prologue  # noqa: E402  (numpy only)
+from .prologue import channel_log_decay, head_log_decay, qkv_prologue, softplus, write_gate  # noqa: E402

@@ -65,3 +65,38 @@ def qkv_prologue(x, heads, dk, dv, u, weight, bias, window, conv_silu=True, qk_s
         q = q / np.sqrt((q * q).sum(-1, keepdims=True) + L2_EPS)
         k = k / np.sqrt((k * k).sum(-1, keepdims=True) + L2_EPS)
     return q, k, v, nxt
+
+
+# ---------------------------------------------------------------------------------------------------
+# The gate producers of the front-end (float64).
+# ---------------------------------------------------------------------------------------------------
+def softplus(x):
+    """log(1 + e^x), in the overflow-free form max(x, 0) + log1p(e^-|x|) (burn-stack's ``softplus``,
+    rev 984d42d3, is not vendored in the reference tree; this is the function's definition)."""
+    x = np.asarray(x, dtype=np.float64)
+    return np.maximum(x, 0.0) + np.log1p(np.exp(-np.abs(x)))
+
+
+def write_gate(raw, doubled):
+    """``squash_write`` (src/common/qkv.rs:333-368): sigma(raw), times 2 for the erase gate under
+    ``allow_neg_eigval`` (``doubled``)."""
+    raw = np.asarray(raw, dtype=np.float64)
+    return (2.0 if doubled else 1.0) / (1.0 + np.exp(-raw))
+
+
+def head_log_decay(dt_raw, dt_bias, a_log, dt_limit=(0.0, 6.5504e4)):
+    """``ForgetGate::log_decay`` (src/common/gate.rs:51-59): g = clamp(softplus(dt + b), lo, hi) * -e^a,
+    the per-head parameters broadcast over the last axis (heads)."""
+    dt = softplus(np.asarray(dt_raw, dtype=np.float64) + np.asarray(dt_bias, dtype=np.float64))
+    return np.clip(dt, dt_limit[0], dt_limit[1]) * -np.exp(np.asarray(a_log, dtype=np.float64))
+
+
+def channel_log_decay(dt, dt_bias, a_log, head_k_dim, lower_bound):
+    """``ChannelForgetGate::log_decay`` (src/common/gate.rs:178-196) after its ``up`` projection: the
+    channels [.., heads * head_k_dim] plus the bias, split per head, g = lower_bound *
+    sigmoid(dt * e^{a_h}).  Returns [.., heads, head_k_dim]."""
+    dt = np.asarray(dt, dtype=np.float64) + np.asarray(dt_bias, dtype=np.float64)
+    shape = dt.shape[:-1] + (-1, head_k_dim)
+    dt = dt.reshape(shape)
+    slope = np.exp(np.asarray(a_log, dtype=np.float64))[:, None]
+    return float(lower_bound) / (1.0 + np.exp(-dt * slope))

@@ -50,6 +50,7 @@ def test_struct_layout_matches_the_header(tmp_path):
         "dc_chunk_bwd_args": [f for f, _ in abi.ChunkBwdArgs._fields_],
         "dc_out_norm_args": [f for f, _ in abi.OutNormArgs._fields_],
         "dc_qkv_prologue_args": [f for f, _ in abi.PrologueArgs._fields_],
+        "dc_gate_args": [f for f, _ in abi.GateArgs._fields_],
     }
     lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "deltacore.h"', "int main(void) {"]
     for st, names in fields.items():
@@ -65,7 +66,7 @@ def test_struct_layout_matches_the_header(tmp_path):
     want = {tuple(l.split()[:2]): int(l.split()[2]) for l in out if l}
     for st, cls in (("dc_chunk_args", abi.ChunkArgs), ("dc_step_args", abi.StepArgs),
                     ("dc_chunk_bwd_args", abi.ChunkBwdArgs), ("dc_out_norm_args", abi.OutNormArgs),
-                    ("dc_qkv_prologue_args", abi.PrologueArgs)):
+                    ("dc_qkv_prologue_args", abi.PrologueArgs), ("dc_gate_args", abi.GateArgs)):
         assert want[(st, "sizeof")] == ctypes.sizeof(cls)
         for n, _ in cls._fields_:
             assert want[(st, n)] == getattr(cls, n).offset, (st, n)
@@ -249,3 +250,24 @@ def test_prologue_validation_is_host_logic():
         setattr(b, name, value)
         assert lib.dc_qkv_prologue(b, None) == code, name
     assert lib.dc_qkv_prologue(None, None) == abi.DC_EINVAL_ARG
+
+
+def test_gates_validation_is_host_logic():
+    a = abi.GateArgs()
+    a.rows, a.cols, a.x_stride, a.kind, a.in_dtype, a.group = 8, 16, 40, abi.DC_GATE_CHANNEL_DECAY, abi.DC_F32, 4
+    a.scale, a.lo, a.hi = -5.0, 0.0, 1.0
+    a.x, a.bias, a.a_log, a.out = 0x10000, 0x20000, 0x30000, 0x40000
+    lib = abi.lib()
+    bad = [("cols", 0, abi.DC_EINVAL_SHAPE), ("x_stride", 15, abi.DC_EINVAL_SHAPE), ("kind", 3, abi.DC_EINVAL_ARG),
+           ("in_dtype", 4, abi.DC_EUNSUPPORTED_DTYPE), ("group", 3, abi.DC_EINVAL_SHAPE), ("scale", float("inf"), abi.DC_EINVAL_ARG),
+           ("x", None, abi.DC_EINVAL_ARG), ("bias", None, abi.DC_EINVAL_ARG), ("a_log", None, abi.DC_EINVAL_ARG)]
+    for name, value, code in bad:
+        b = abi.GateArgs.from_buffer_copy(a)
+        setattr(b, name, value)
+        assert lib.dc_gates(b, None) == code, name
+    b = abi.GateArgs.from_buffer_copy(a)
+    b.kind, b.lo, b.hi = abi.DC_GATE_HEAD_DECAY, 2.0, 1.0
+    assert lib.dc_gates(b, None) == abi.DC_EINVAL_ARG  # clamp range upside down
+    b = abi.GateArgs.from_buffer_copy(a)
+    b.rows, b.x, b.out = 0, None, None
+    assert lib.dc_gates(b, None) == abi.DC_OK

@@ -51,3 +51,18 @@ def test_steps_equal_the_forward():
     for i in range(3):
         assert np.abs(np.concatenate([o[i] for o in outs], 1) - full[i]).max() < 1e-12
     assert np.array_equal(window, full[3])
+
+
+def test_gate_producers_match_torch():
+    """softplus, the sigma / 2 sigma write gates and both log-decays against torch's own functions."""
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((5, 12)) * 30  # large arguments: the overflow-free softplus
+    assert np.abs(oracle.softplus(x) - torch.nn.functional.softplus(torch.from_numpy(x), threshold=1e9).numpy()).max() < 1e-12
+    assert np.abs(oracle.write_gate(x, True) - 2 * torch.sigmoid(torch.from_numpy(x)).numpy()).max() < 1e-15
+    dt, bias, a = rng.standard_normal((3, 7, 4)), rng.standard_normal(4), rng.uniform(0, 2.7, 4)
+    ref = torch.clamp(torch.nn.functional.softplus(torch.from_numpy(dt + bias)), 0.0, 1.5) * -torch.exp(torch.from_numpy(a))
+    assert np.abs(oracle.head_log_decay(dt, bias, a, (0.0, 1.5)) - ref.numpy()).max() < 1e-12
+    dt = rng.standard_normal((3, 7, 4 * 5))
+    bias = rng.standard_normal(20)
+    ref = torch.sigmoid(torch.from_numpy(dt + bias).reshape(3, 7, 4, 5) * torch.exp(torch.from_numpy(a))[:, None]) * -5.0
+    assert np.abs(oracle.channel_log_decay(dt, bias, a, 5, -5.0) - ref.numpy()).max() < 1e-12

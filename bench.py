@@ -11,8 +11,9 @@ rank per GPU) every rank owns its own batch of 8 sequences — batch x head
 sharding with no collective on the data path — so the work per GPU is fixed
 ("scaling": "weak") and ``value`` counts the tokens of all ranks.  The decode
 of BASELINE config 3 (256 sequences, H=16, fp32 state, one fused tick per
-step) is measured in the same run and reported under "decode", and the
-backward (dc_chunk_bwd at config 2's shapes) under "backward".
+step) is measured in the same run and reported under "decode", the backward
+(dc_chunk_bwd at config 2's shapes) under "backward", and the front-end and
+epilogue kernels under "prologue", "gates" and "out_norm".
 
 ``--workload gdn2`` is BASELINE config 5: one batch of 16 sequences sharded
 over the N GPUs ("scaling": "strong"), and its decode is config 5's own: 512
@@ -612,6 +613,8 @@ def run_ours(args):
     on_ms = max_over_ranks(on_ms, world)
     pr_ms, pr_bytes = time_prologue(dn, 20, 3)
     pr_ms = max_over_ranks(pr_ms, world)
+    gt_ms, gt_bytes = time_gates(dn, 10, 3)
+    gt_ms = max_over_ranks(gt_ms, world)
     dec_tok = dec_seq * world / (dec_ms / 1e3)
     traffic = profiled_traffic(args.workload)
     gather_info = None
@@ -658,6 +661,13 @@ def run_ours(args):
                                   "unit": "GB/s", "frac": pr_bytes / (pr_ms / 1e3) / 1e9 / hbm_peak,
                                   "algorithmic_bytes_per_launch": pr_bytes},
                      "gpu_launches": 20},
+        "gates": {"metric": "gate producers tok/s (config 5: per-channel log-decay and doubled erase gate, bf16 "
+                            "[16, 16384, 16 x 128] in, float32 out)",
+                  "value": 16 * 16384 * world / (gt_ms / 1e3), "unit": "tok/s", "ms_per_step": gt_ms, "steps": 10,
+                  "roofline": {"bound": "hbm", "achieved": gt_bytes / (gt_ms / 1e3) / 1e9, "peak": hbm_peak,
+                               "unit": "GB/s", "frac": gt_bytes / (gt_ms / 1e3) / 1e9 / hbm_peak,
+                               "algorithmic_bytes_per_launch": gt_bytes},
+                  "gpu_launches": 20},
         "clocks": clocks.summary(),
     }
     if gather_info is not None:

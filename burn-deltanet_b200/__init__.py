@@ -7,7 +7,10 @@ The package directory name is not a Python identifier; import it with
 * ``libdeltacore.so`` — the CUDA kernels behind the C ABI of include/deltacore.h
   (built in-tree by ``build.py``);
 * :mod:`.core`     — the reference's interface (DeltaInput, DeltaPath, delta_step, ...)
-  over that ABI;
+  over that ABI, the custom backward (delta_chunk_recalculated_backward,
+  DeltaChunkFunction), and the block's kernels on either side of the core: the
+  front-end after the input projection (qkv_prologue, write_gate,
+  head_log_decay, channel_log_decay) and the output norm (out_norm);
 * :mod:`.sharding` — batch x head partitioning across the GPUs of one node.
 """
 from . import _abi

@@ -959,11 +959,13 @@ int validate_prologue(const dc_qkv_prologue_args *a) {
     return DC_OK;
 }
 
-// Even head widths take the two-channels-per-thread kernel (two segments per CTA), others one channel per
-// thread (one segment per CTA).
+// The kernel by head width and output alignment: even widths take two channels per thread (two segments
+// per CTA; channel-pair stores, so the outputs must be aligned), odd widths or outputs that are not
+// 16-byte aligned one channel per thread (one segment per CTA).
 template <typename TI, typename TO>
 void launch_prologue(bool k4, dim3 grid, const dc::pro::Params &p, cudaStream_t s) {
-    if (p.dk % 2 == 0 && p.dv % 2 == 0) {
+    const bool out16 = aligned(p.q, 16) && aligned(p.k, 16) && aligned(p.v, 16);
+    if (out16 && p.dk % 2 == 0 && p.dv % 2 == 0) {
         grid.x = (grid.x + 1) / 2;
         if (k4) dc::pro::prologue_pair_kernel<TI, TO, 4><<<grid, dc::pro::kThreads, 0, s>>>(p);
         else dc::pro::prologue_pair_kernel<TI, TO, dc::pro::kMaxK><<<grid, dc::pro::kThreads, 0, s>>>(p);

@@ -1,8 +1,9 @@
 """GPU parity of the front-end prologue (dc_qkv_prologue) against the float64 oracle (oracle/prologue.py).
 
 The short convolution with its window, the activations, the q / k L2 norm and the micro-step reshape
-(src/common/conv.rs, src/common/qkv.rs:373-500), over both kernels (two channels per thread for even
-head widths, one for odd), the benchmark head size (dk = dv = 128), sequences
+(src/common/conv.rs, src/common/qkv.rs:373-500), over both kernels (two channels per thread for even head
+widths, one for odd widths or outputs that are not 16-byte aligned), the benchmark head size
+(dk = dv = 128), sequences
 that end inside and on a 32-token tile, a single-token step from a window, DeltaProduct micro-steps
 (u = 2, 3), K = 1 (no window), SiLU not fused into the convolution, no norm, x as a column slice of a wider
 projection, bf16 and float32.  Split calls carrying the window equal one call, and token-by-token steps
@@ -91,3 +92,26 @@ def test_split_calls_and_steps_equal_one_call():
     for i in range(3):
         assert torch.allclose(torch.cat([o[i] for o in outs], 1), full[i][:, :6], rtol=1e-6, atol=1e-6)
     assert abi.lib().dc_device_status(0) == 0
+
+
+def test_prologue_outputs_not_16_byte_aligned():
+    """Outputs at an odd element offset take the one-channel kernel (the paired one stores channel pairs)."""
+    x, w, bias, win = make(8, 1, 40, 2, 32, 32, 1, 4, torch.float32)
+    want = dn.qkv_prologue(x, 2, 32, 32, w, bias, win)
+    a = abi.PrologueArgs()
+    b_, s_ = x.shape[0], x.shape[1]
+    c = 2 * 32 * 2 + 2 * 32
+    store = torch.empty(3 * b_ * s_ * 2 * 32 + 3, device="cuda")
+    q, k, v = (store[1 + i * b_ * s_ * 64:1 + (i + 1) * b_ * s_ * 64].view(b_, s_, 2, 32) for i in range(3))
+    nxt = torch.empty(b_, c, 4, device="cuda")
+    a.batch, a.seq, a.heads, a.dk, a.dv, a.n_householder, a.conv_kernel = b_, s_, 2, 32, 32, 1, 4
+    a.in_dtype = a.out_dtype = abi.DC_F32
+    a.flags = abi.DC_PROLOGUE_CONV_SILU | abi.DC_PROLOGUE_L2
+    a.x_stride = x.stride(1)
+    a.x, a.conv_weight, a.conv_bias, a.window_in, a.window_out = x.data_ptr(), w.data_ptr(), bias.data_ptr(), win.data_ptr(), nxt.data_ptr()
+    a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+    assert q.data_ptr() % 16 != 0
+    assert abi.lib().dc_qkv_prologue(a, torch.cuda.current_stream().cuda_stream) == abi.DC_OK
+    torch.cuda.synchronize()
+    for got, ref in zip((q, k, v, nxt), want):
+        assert torch.allclose(got, ref, rtol=1e-6, atol=1e-6)

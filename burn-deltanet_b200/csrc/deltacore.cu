@@ -887,7 +887,7 @@ int launch_out_norm(const dc::onorm::Params &p, cudaStream_t s) {
                         aligned(p.y, 16) && aligned(p.out, 16) && (!p.gate || aligned(p.gate, 16)) &&
                         (p.dv * (int64_t)sizeof(TO)) % 16 == 0;
     if (rows16) {
-        const int64_t rows_per_cta = (kThreads / 32) * (32 / lpr) * kSlots;
+        const int64_t rows_per_cta = (kThreads / 32) * (32 / lpr) * slots_for<TI>();
         switch (lpr) {
             case 4: out_norm_vec_kernel<TI, TO, 4><<<grid(rows_per_cta), kThreads, 0, s>>>(p); break;
             case 8: out_norm_vec_kernel<TI, TO, 8><<<grid(rows_per_cta), kThreads, 0, s>>>(p); break;

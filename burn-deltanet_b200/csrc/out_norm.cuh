@@ -118,10 +118,13 @@ __device__ __forceinline__ void store_vec(__nv_bfloat16 *p, const float (&v)[N])
 // consecutive elements each (dv = LPR VEC, LPR a power of two <= 32), a warp holds 32 / LPR rows per slot
 // and kSlots slots per iteration, all of them loaded before the first use.  Needs 16-byte-aligned rows.
 constexpr int kSlots = 4;
+// slots per warp iteration by input width: 2-byte inputs hold twice the elements per 16 bytes, so two
+// slots keep their registers (and occupancy) in line with 4-byte inputs at four
+template <typename TI> __host__ __device__ constexpr int slots_for() { return sizeof(TI) == 2 ? 2 : kSlots; }
 
 template <typename TI, typename TO, int LPR>
 __global__ void __launch_bounds__(kThreads) out_norm_vec_kernel(const Params p) {
-    constexpr int VEC = 16 / sizeof(TI), RPS = 32 / LPR;
+    constexpr int VEC = 16 / sizeof(TI), RPS = 32 / LPR, NS = slots_for<TI>();
     const int lane = threadIdx.x & 31, sub = lane % LPR, srow = lane / LPR, col = sub * VEC;
     const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
     const int dv = p.dv;
@@ -132,18 +135,18 @@ __global__ void __launch_bounds__(kThreads) out_norm_vec_kernel(const Params p) 
 #pragma unroll
     for (int e = 0; e < VEC; ++e) w[e] = p.weight[col + e];
     const float inv_dv = 1.f / (float)dv;
-    for (int64_t r0 = ((int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * (RPS * kSlots); r0 < p.rows;
-         r0 += warps * (RPS * kSlots)) {
-        float y[kSlots][VEC], g[kSlots][VEC];
+    for (int64_t r0 = ((int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * (RPS * NS); r0 < p.rows;
+         r0 += warps * (RPS * NS)) {
+        float y[NS][VEC], g[NS][VEC];
 #pragma unroll
-        for (int q = 0; q < kSlots; ++q) {
+        for (int q = 0; q < NS; ++q) {
             const int64_t r = r0 + q * RPS + srow;
             const int64_t o = (r < p.rows ? r : 0) * dv + col;
             load16(Y + o, y[q]);
             load16(Gb + o, g[q]);
         }
 #pragma unroll
-        for (int q = 0; q < kSlots; ++q) {
+        for (int q = 0; q < NS; ++q) {
             const int64_t r = r0 + q * RPS + srow;
             float ss = 0.f;
 #pragma unroll

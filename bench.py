@@ -53,6 +53,7 @@ WORKLOADS = {
 # batch per GPU (weak scaling).
 STRONG = {"gdn2"}
 CFG5_DECODE_STEPS = 512
+DECODE_STEPS = 1024  # config 3: 1024 consecutive step() calls
 # Flop (2 x multiply-adds) of the chunked backward per token-head, d = 128 and its chunks of L = 32:
 # prep 4 L d (A, att, W, U); the scans 2 d^2 forward (V', S) and L d + 3 d^2 back (dV', dS); the gradients
 # 3 d^2 + L d (the S products, datt), 2 L d (dT), 2 L d (d(wv), dKg), 2 L^2 (X, dA), 4 L d (F, Fa products).
@@ -257,7 +258,7 @@ def cpu_baseline(workload, budget_s=12.0):
         total += time.perf_counter() - t0
         reps += 1
     return {"value": reps * batch * tokens / total, "unit": "tok/s", "cores": min(threads, batch * H),
-            "kind": "port",
+            "kind": "port", "cpu_model": cpu_model(), "host_threads": threads,
             "sample": f"oracle chunk path fp32 (chunk 64, OpenMP over heads), B={batch} T={tokens} H={H} d={D}"
                       f"{' u=' + str(u) if u > 1 else ''}, {reps} call(s) in {total:.2f} s"}
 
@@ -292,6 +293,54 @@ def time_prefill(dn, x, u, steps, warmup):
     for _ in range(steps):
         call()
     e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def time_prefill_gathered(dn, x, u, steps, warmup, world):
+    """Each step: the prefill of this rank's batch, then the all-gather of its y
+    (bf16) into every rank's global output [world x batch, T, H, dv] -- the
+    north star's one collective.  The gather of step i runs on a side stream
+    while step i+1 computes (y and the global output double-buffered); the
+    timed region ends when the last gather has landed on this rank.  Returns ms
+    per step on this rank (the caller takes the max over ranks).  At one GPU
+    there is nothing to gather and this is the plain prefill."""
+    if world == 1:
+        return time_prefill(dn, x, u, steps, warmup)
+    sh = importlib.import_module("burn-deltanet_b200.sharding")
+    b, s = x["q"].shape[0], x["q"].shape[1]
+    shards = sh.plan(b * world, H, world)
+    ys = [torch.empty(b, s, H, D, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    outs = [torch.empty(world * b, s, H, D, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    s_out = torch.empty_like(x["state"])
+    gated = x["g"] is not None
+    compute, comm = torch.cuda.current_stream(), torch.cuda.Stream()
+    done_c = [torch.cuda.Event() for _ in range(2)]
+    done_g = [torch.cuda.Event() for _ in range(2)]
+
+    def step(i):
+        j = i & 1
+        if i >= 2:
+            compute.wait_event(done_g[j])  # the gather of step i-2 has read ys[j]
+        dn.delta_chunk_recalculated(x["q"], x["k"], x["v"], x["erase"], x["write"], x["g"], x["state"],
+                                    gated, L, 1.0 / math.sqrt(D), n_householder=u, y_out=ys[j], state_out=s_out)
+        done_c[j].record(compute)
+        with torch.cuda.stream(comm):
+            comm.wait_event(done_c[j])
+            sh.gather_into(outs[j], ys[j], shards)
+            done_g[j].record(comm)
+
+    for i in range(warmup):
+        step(i)
+    compute.wait_stream(comm)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(compute)
+    for i in range(steps):
+        step(i)
+    compute.wait_stream(comm)
+    e1.record(compute)
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / steps
 
@@ -509,29 +558,110 @@ def time_decode(dn, steps, warmup):
     return ms, step_bytes
 
 
-def time_allgather(batch, tokens, world):
-    """The one collective of the sharded path: all-gather every rank's y
-    (bf16 [batch, T, H, dv]) into the global output on every rank (NCCL).
-    Timed on its own, after the data path; not part of `value`."""
-    sh = importlib.import_module("burn-deltanet_b200.sharding")
-    shards = sh.plan(batch * world, H, world)
-    y = torch.randn(batch, tokens, H, D, device="cuda").to(torch.bfloat16)
-    for _ in range(2):
-        sh.gather(y, shards)
-    torch.cuda.synchronize()
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 3
-    e0.record()
-    for _ in range(reps):
-        out = sh.gather(y, shards)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1) / reps, world)
-    nbytes = out.numel() * out.element_size()
-    del out
-    return {"ms": ms, "bytes_per_rank_out": nbytes,
-            "bus_gbs": nbytes * (world - 1) / world / (ms / 1e3) / 1e9, "collective": "nccl all_gather_into_tensor"}
+def cpu_model():
+    """The host CPU's model name, for the CPU baseline's record."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def hbm_roofline(nbytes, ms, hbm_peak, peak_kind, traffic=None):
+    achieved = nbytes / (ms / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+            "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes_per_launch": nbytes}
+
+
+def measure_cfg4(dn, args, rank, world, hbm_peak, peak_kind):
+    """Config 4 (DeltaProduct, u = 2 and 3, B=4 T=8192 per GPU, weak scaling): one dc_chunk_fwd per step
+    with the micro-steps folded in-kernel; at N > 1 the value counts the all-gather of y, pipelined as in the
+    headline; `kernel_ms` is the prefill alone."""
+    out = {}
+    for u in (2, 3):
+        batch, tokens = 4, 8192
+        x = make_prefill("deltaproduct", batch, tokens, u, "cuda", 4000 + 10 * u + rank)
+        k_ms = max_over_ranks(time_prefill(dn, x, u, args.steps, args.warmup), world)
+        ms = max_over_ranks(time_prefill_gathered(dn, x, u, args.steps, args.warmup, world), world) \
+            if world > 1 else k_ms
+        nbytes = algorithmic_bytes(x, batch * tokens)
+        flops = 2 * (5 * L * D + 3 * D * D) * batch * tokens * u * H
+        out[f"u{u}"] = {
+            "metric": f"prefill tok/s (config 4: DeltaProduct u={u}, bf16 in, fp32 state, B={batch} per GPU, "
+                      f"T={tokens}, H={H}, dk=dv={D}; real tokens, not micro-steps)",
+            "value": batch * tokens * world / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms,
+            "kernel_ms": k_ms, "kernel_value": batch * tokens * world / (k_ms / 1e3), "steps": args.steps,
+            "scaling": "weak", "roofline": dict(hbm_roofline(nbytes, k_ms, hbm_peak, peak_kind),
+                                                tensor_tflops=flops / (k_ms / 1e3) / 1e12),
+            "gpu_launches": args.steps}
+        del x
+        torch.cuda.empty_cache()
+    return out
+
+
+def measure_cfg5(dn, args, rank, world, hbm_peak, peak_kind):
+    """Config 5 as the north star runs it: one batch of 16 GDN-2 sequences (T=16384) sharded batch-major over
+    the N GPUs (strong scaling), the prefill of each rank's sequences (two launches: prep + scan), the
+    all-gather of y into every rank's [16, T, H, dv] output inside the timed step (pipelined: the gather of
+    step i overlaps step i+1), then 512 GDN-2 step() tokens from each rank's own final state.  At N > 1 every
+    rank also runs the whole unsharded batch and checks the gathered y and final state against it bit for
+    bit."""
+    B5, T5 = 16, 16384
+    if B5 % world:
+        return {"unavailable": f"16 sequences do not split over {world} GPUs"}
+    per = B5 // world
+    full = make_prefill("gdn2", B5, T5, 1, "cuda", 5000)  # the same global batch on every rank
+    x = {k: (None if t is None else t[rank * per:(rank + 1) * per].contiguous()) for k, t in full.items()}
+    steps = max(3, min(args.steps, 10))
+    k_ms = max_over_ranks(time_prefill(dn, x, 1, steps, args.warmup), world)
+    ms = max_over_ranks(time_prefill_gathered(dn, x, 1, steps, args.warmup, world), world) if world > 1 else k_ms
+    nbytes = algorithmic_bytes(x, per * T5)
+    flops = 2 * (5 * L * D + 3 * D * D) * per * T5 * H
+    traffic = profiled_traffic("gdn2")
+    rec = {
+        "metric": f"prefill tok/s (config 5: GDN-2, per-channel gates, bf16 in, fp32 state, B={B5} over {world} GPU, "
+                  f"T={T5}, H={H}, dk=dv={D}; y all-gathered to every rank inside the step)",
+        "value": B5 * T5 / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms, "kernel_ms": k_ms,
+        "kernel_value": B5 * T5 / (k_ms / 1e3), "steps": steps, "scaling": "strong",
+        "roofline": dict(hbm_roofline(nbytes, k_ms, hbm_peak, peak_kind,
+                                      None if traffic is None else traffic * per / B5),
+                         tensor_tflops=flops / (k_ms / 1e3) / 1e12, per_gpu=True),
+        "gpu_launches": 2 * steps,
+    }
+    # Sharded == unsharded: this rank's shard, gathered, against the whole batch run on this GPU.
+    y_loc, s_loc = dn.delta_chunk_recalculated(x["q"], x["k"], x["v"], x["erase"], x["write"], x["g"], x["state"],
+                                               True, L, 1.0 / math.sqrt(D))
+    if world > 1:
+        sh = importlib.import_module("burn-deltanet_b200.sharding")
+        shards = sh.plan(B5, H, world)
+        y_all, s_all = sh.gather(y_loc, shards), sh.gather(s_loc, shards, head_axis=1)
+        y_full, s_full = dn.delta_chunk_recalculated(full["q"], full["k"], full["v"], full["erase"], full["write"],
+                                                     full["g"], full["state"], True, L, 1.0 / math.sqrt(D))
+        ok = float(torch.equal(y_all, y_full) and torch.equal(s_all, s_full))
+        worst = max_over_ranks(-ok, world)  # -1 when every rank matched
+        rec["sharded_equals_unsharded"] = worst < 0
+        del y_all, s_all, y_full, s_full
+    del full, y_loc
+    torch.cuda.empty_cache()
+    dec_ms, dec_bytes = time_decode_cfg5(dn, s_loc, CFG5_DECODE_STEPS, args.warmup, 2000 + rank)
+    dec_ms = max_over_ranks(dec_ms, world)
+    rec["decode"] = {
+        "metric": f"decode tok/s (config 5: GDN-2 step, {B5} sequences x {H} heads over {world} GPU, "
+                  f"{CFG5_DECODE_STEPS} steps from the prefill's final state, fp32 state)",
+        "value": B5 / (dec_ms / 1e3), "unit": "tok/s", "ms_per_step": dec_ms, "steps": CFG5_DECODE_STEPS,
+        "roofline": hbm_roofline(dec_bytes, dec_ms, hbm_peak, peak_kind), "gpu_launches": CFG5_DECODE_STEPS}
+    del s_loc
+    ms_e2e, h2d, d2h = time_prefill_e2e(dn, x, 1, 1, 1)
+    ms_e2e = max_over_ranks(ms_e2e, world)
+    rec["e2e"] = {"value": B5 * T5 / (ms_e2e / 1e3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                  "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
+                  "note": "each rank's shard from and back to its own host memory (no gather)"}
+    del x
+    torch.cuda.empty_cache()
+    return rec
 
 
 def run_ours(args):
@@ -552,16 +682,16 @@ def run_ours(args):
     barrier(world)
     torch.cuda.synchronize()
     if args.only == "decode":
-        dec_ms, dec_bytes = time_decode(dn, 256, args.warmup)
+        dec_ms, dec_bytes = time_decode(dn, DECODE_STEPS, args.warmup)
         if rank == 0:
             print(json.dumps({"decode_ms_per_step": dec_ms, "decode_gbs": dec_bytes / (dec_ms / 1e3) / 1e9}))
         return
     with clocks:
-        ms = time_prefill(dn, x, u, args.steps, args.warmup)
+        k_ms = time_prefill(dn, x, u, args.steps, args.warmup)
     barrier(world)
     if args.only == "prefill":
         if rank == 0:
-            print(json.dumps({"prefill_ms_per_step": ms, "tok_s": batch * tokens * world / (ms / 1e3)}))
+            print(json.dumps({"prefill_ms_per_step": k_ms, "tok_s": batch * tokens * world / (k_ms / 1e3)}))
         return
     if args.only == "gates":
         gt_ms, gt_bytes = time_gates(dn, 10, 3)
@@ -583,29 +713,29 @@ def run_ours(args):
         if rank == 0:
             print(json.dumps({"backward_ms_per_step": bw_ms, "backward_gbs": bw_bytes / (bw_ms / 1e3) / 1e9}))
         return
-    ms = max_over_ranks(ms, world)
+    if args.only == "cfg5":
+        rec = measure_cfg5(dn, args, rank, world, hbm_peak, peak_kind)
+        if rank == 0:
+            print(json.dumps(rec))
+        return
+    if args.only == "cfg4":
+        rec = measure_cfg4(dn, args, rank, world, hbm_peak, peak_kind)
+        if rank == 0:
+            print(json.dumps(rec))
+        return
+    k_ms = max_over_ranks(k_ms, world)
     tok_per_rank = batch * tokens
+    # The step at N > 1 includes the all-gather of y to every rank (pipelined with the next step's kernels).
+    ms = max_over_ranks(time_prefill_gathered(dn, x, u, args.steps, args.warmup, world), world) \
+        if world > 1 else k_ms
     value = tok_per_rank * world / (ms / 1e3)
     nbytes = algorithmic_bytes(x, batch * tokens)
-    achieved = nbytes / (ms / 1e3) / 1e9
     ms_e2e, h2d, d2h = time_prefill_e2e(dn, x, u, max(1, min(args.steps, 5)), 1)
     ms_e2e = max_over_ranks(ms_e2e, world)
     flops = 2 * (5 * L * D + 3 * D * D) * batch * tokens * u * H
-    if kind == "gdn2":  # config 5: decode from this rank's prefill final state
-        y_p, s_final = dn.delta_chunk_recalculated(x["q"], x["k"], x["v"], x["erase"], x["write"], x["g"],
-                                                   x["state"], True, L, 1.0 / math.sqrt(D))
-        del y_p
-        dec_steps = CFG5_DECODE_STEPS
-        dec_ms, dec_bytes = time_decode_cfg5(dn, s_final, dec_steps, args.warmup, 2000 + rank)
-        dec_seq = batch
-        dec_metric = (f"decode tok/s (config 5: GDN-2 step, {batch * world} sequences x {H} heads, {dec_steps} "
-                      f"steps from the prefill's final state, fp32 state)")
-        del s_final
-    else:
-        dec_steps = 256
-        dec_ms, dec_bytes = time_decode(dn, dec_steps, args.warmup)
-        dec_seq = DECODE["batch"]
-        dec_metric = "decode tok/s (config 3: GDN step, 256 sequences x 16 heads, fp32 state)"
+    del x
+    torch.cuda.empty_cache()
+    dec_ms, dec_bytes = time_decode(dn, DECODE_STEPS, args.warmup)
     dec_ms = max_over_ranks(dec_ms, world)
     bw_ms, bw_bytes = time_backward(dn, 2, 1)
     bw_ms = max_over_ranks(bw_ms, world)
@@ -615,29 +745,29 @@ def run_ours(args):
     pr_ms = max_over_ranks(pr_ms, world)
     gt_ms, gt_bytes = time_gates(dn, 10, 3)
     gt_ms = max_over_ranks(gt_ms, world)
-    dec_tok = dec_seq * world / (dec_ms / 1e3)
+    torch.cuda.empty_cache()
+    cfg4 = measure_cfg4(dn, args, rank, world, hbm_peak, peak_kind) if args.workload == "deltanet" else None
+    cfg5 = measure_cfg5(dn, args, rank, world, hbm_peak, peak_kind) if args.workload == "deltanet" else None
+    dec_tok = DECODE["batch"] * world / (dec_ms / 1e3)
     traffic = profiled_traffic(args.workload)
-    gather_info = None
-    if world > 1:
-        gather_info = time_allgather(batch, tokens, world)
     line = {
         "metric": f"prefill tok/s ({kind}, bf16 in, fp32 state, H={H} dk=dv={D}, chunk {L})",
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong" if strong else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, BASELINE config recipes)",
         "config": arm_config(cfg, kind, batch, tokens, u, world, strong),
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "peak_kind": peak_kind, "traffic": traffic,
-                     "algorithmic_bytes_per_launch": nbytes,
-                     "tensor_tflops": flops / (ms / 1e3) / 1e12, "tensor_peak": tc_peak},
+        "roofline": dict(hbm_roofline(nbytes, k_ms, hbm_peak, peak_kind, traffic),
+                         tensor_tflops=flops / (k_ms / 1e3) / 1e12, tensor_peak=tc_peak),
+        "kernel_only": {"value": tok_per_rank * world / (k_ms / 1e3), "unit": "tok/s", "ms_per_step": k_ms,
+                        "note": "the prefill alone, without the all-gather of y (identical to value at N=1)"},
         "e2e": {"value": tok_per_rank * world / (ms_e2e / 1e3), "unit": "tok/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e},
         "gpu_launches": launches,
-        "decode": {"metric": dec_metric,
-                   "value": dec_tok, "unit": "tok/s", "ms_per_step": dec_ms, "steps": dec_steps,
-                   "roofline": {"bound": "hbm", "achieved": dec_bytes / (dec_ms / 1e3) / 1e9, "peak": hbm_peak,
-                                "unit": "GB/s", "frac": dec_bytes / (dec_ms / 1e3) / 1e9 / hbm_peak},
-                   "gpu_launches": dec_steps},
+        "decode": {"metric": f"decode tok/s (config 3: GDN step, 256 sequences x 16 heads, fp32 state, "
+                             f"{DECODE_STEPS} consecutive ticks)",
+                   "value": dec_tok, "unit": "tok/s", "ms_per_step": dec_ms, "steps": DECODE_STEPS,
+                   "roofline": hbm_roofline(dec_bytes, dec_ms, hbm_peak, peak_kind),
+                   "gpu_launches": DECODE_STEPS},
         "backward": {"metric": "backward tok/s (dc_chunk_bwd at config 2's shapes: every input's gradient; "
                                "chunked, fp32-accurate tf32 products on the tensor cores)",
                      "value": 8 * 4096 * world / (bw_ms / 1e3), "unit": "tok/s", "ms_per_step": bw_ms, "steps": 2,
@@ -650,28 +780,29 @@ def run_ours(args):
         "out_norm": {"metric": "out-norm tok/s (gated per-head RMSNorm after the read-out, config 2's output: "
                                "bf16 y and gate in, bf16 out)",
                      "value": 8 * 4096 * world / (on_ms / 1e3), "unit": "tok/s", "ms_per_step": on_ms, "steps": 20,
-                     "roofline": {"bound": "hbm", "achieved": on_bytes / (on_ms / 1e3) / 1e9, "peak": hbm_peak,
-                                  "unit": "GB/s", "frac": on_bytes / (on_ms / 1e3) / 1e9 / hbm_peak,
-                                  "algorithmic_bytes_per_launch": on_bytes},
+                     "roofline": hbm_roofline(on_bytes, on_ms, hbm_peak, peak_kind),
                      "gpu_launches": 20},
         "prologue": {"metric": "prologue tok/s (front-end after the input projection, config 2: short "
                                "convolution K=4 + SiLU + q/k L2 norm, bf16 in and out)",
                      "value": 8 * 4096 * world / (pr_ms / 1e3), "unit": "tok/s", "ms_per_step": pr_ms, "steps": 20,
-                     "roofline": {"bound": "hbm", "achieved": pr_bytes / (pr_ms / 1e3) / 1e9, "peak": hbm_peak,
-                                  "unit": "GB/s", "frac": pr_bytes / (pr_ms / 1e3) / 1e9 / hbm_peak,
-                                  "algorithmic_bytes_per_launch": pr_bytes},
+                     "roofline": hbm_roofline(pr_bytes, pr_ms, hbm_peak, peak_kind),
                      "gpu_launches": 20},
         "gates": {"metric": "gate producers tok/s (config 5: per-channel log-decay and doubled erase gate, bf16 "
                             "[16, 16384, 16 x 128] in, float32 out)",
                   "value": 16 * 16384 * world / (gt_ms / 1e3), "unit": "tok/s", "ms_per_step": gt_ms, "steps": 10,
-                  "roofline": {"bound": "hbm", "achieved": gt_bytes / (gt_ms / 1e3) / 1e9, "peak": hbm_peak,
-                               "unit": "GB/s", "frac": gt_bytes / (gt_ms / 1e3) / 1e9 / hbm_peak,
-                               "algorithmic_bytes_per_launch": gt_bytes},
+                  "roofline": hbm_roofline(gt_bytes, gt_ms, hbm_peak, peak_kind),
                   "gpu_launches": 20},
         "clocks": clocks.summary(),
     }
-    if gather_info is not None:
-        line["allgather"] = gather_info
+    if cfg4 is not None:
+        line["cfg4"] = cfg4
+    if cfg5 is not None:
+        line["cfg5"] = cfg5
+    if world > 1:
+        line["allgather"] = {"collective": "nccl all_gather_into_tensor of y (bf16), on a side stream, the gather "
+                                           "of step i overlapping the prefill of step i+1",
+                             "bytes_per_rank_out": world * tok_per_rank * H * D * 2,
+                             "ms_per_step_with_gather": ms, "ms_per_step_kernel_only": k_ms}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.workload)
     if rank == 0:
@@ -716,8 +847,13 @@ def run_reference(args):
 
     cfg, batch, tokens, u, kind = WORKLOADS[args.workload]
     threads = os.cpu_count() or 1
-    sample_tokens = 512
-    sample_batch = max(1, -(-threads // H))  # enough (batch, head) pairs for every host thread
+    # Each step is the workload's own batch (config 2: B=8, T=4096, about 2 s on 16 host threads).  The
+    # heavier workloads (config 4's micro-steps, config 5's per-channel gates over B=16 T=16384) would take
+    # minutes per step, so a step there is a bounded sample of them: the same T up to 4096 tokens and the
+    # number of sequences that keeps a step near config 2's work.
+    full = kind == "deltanet"
+    sample_tokens = tokens if full else min(tokens, 4096)
+    sample_batch = batch if full else max(1, min(batch, 8 // u // (4 if kind == "gdn2" else 1)))
     rng = np.random.default_rng(0)
     raw = config_inputs({"deltanet": 2, "deltaproduct": 4, "gdn2": 5}[kind], rng, sample_batch, sample_tokens,
                         H, D, D, u=u)
@@ -743,9 +879,11 @@ def run_reference(args):
         "config": arm_config(cfg, kind, batch // args.gpus if args.workload in STRONG else batch, tokens, u,
                              args.gpus, args.workload in STRONG),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": min(threads, sample_batch * H), "kind": "port",
+                         "cpu_model": cpu_model(), "host_threads": threads,
                          "sample": f"oracle chunk path fp32 (the reference algorithm restated in C, OpenMP over "
-                                   f"(batch, head)), a bounded sample of the workload per step: "
-                                   f"B={sample_batch} T={sample_tokens} H={H}"},
+                                   f"(batch, head)), per step "
+                                   + ("the workload's whole batch" if full else "a bounded sample of the workload")
+                                   + f": B={sample_batch} T={sample_tokens} H={H}" + (f" u={u}" if u > 1 else "")},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -759,7 +897,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="deltanet")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["prefill", "decode", "backward", "out_norm", "prologue", "gates"], default=None,
+    ap.add_argument("--only", choices=["prefill", "decode", "backward", "out_norm", "prologue", "gates", "cfg4",
+                                       "cfg5"], default=None,
                     help="time one kernel alone and print a short line (for profiling runs)")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU instead of the workload's own (for small profiling captures)")

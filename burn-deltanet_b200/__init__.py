@@ -18,6 +18,7 @@ from .core import (
     DeltaChunkFunction,
     DeltaCoreError,
     DeltaInput,
+    DeltaNonFiniteError,
     DeltaPath,
     DeltaShapeError,
     TriSolve,
@@ -32,10 +33,13 @@ from .core import (
     write_gate,
     head_log_decay,
     channel_log_decay,
+    san,
+    set_sanity_checks,
 )
 
 __all__ = [
-    "DeltaChunkFunction", "DeltaCoreError", "DeltaInput", "DeltaPath", "DeltaShapeError", "TriSolve",
+    "DeltaChunkFunction", "DeltaCoreError", "DeltaInput", "DeltaNonFiniteError", "DeltaPath", "DeltaShapeError",
+    "TriSolve", "san", "set_sanity_checks",
     "beta_gates", "delta_chunk_host_scratch_size", "delta_chunk_recalculated", "delta_chunk_recalculated_backward",
     "delta_chunk_recalculated_host", "delta_step", "library_path", "out_norm", "qkv_prologue", "write_gate", "head_log_decay", "channel_log_decay",
 ]

@@ -26,6 +26,7 @@ from __future__ import annotations
 
 import enum
 import math
+import os
 from dataclasses import dataclass
 from typing import Optional, Tuple
 
@@ -47,6 +48,34 @@ class DeltaCoreError(RuntimeError):
 
 class DeltaShapeError(DeltaCoreError, ValueError):
     """The shape / width checks of DeltaInput::sanity (src/delta/path.rs:177-208)."""
+
+
+class DeltaNonFiniteError(DeltaCoreError, ValueError):
+    """A NaN or Inf found by the opt-in guard (see :func:`set_sanity_checks`)."""
+
+
+# The reference compiles its NaN / Inf guard in only under its `check-nan` / `check-inf` features
+# (burn-stack's `sanity`, called at src/delta/path.rs:198-207 and src/delta/recurrent.rs:96-97).  Here the
+# same guard is off by default and switched on per process, by set_sanity_checks() or the environment
+# variables DELTACORE_CHECK_NAN=1 / DELTACORE_CHECK_INF=1.  Each check is one device reduction over the
+# tensor and a host read of its result, so it synchronises the stream: a debugging aid, as in the reference.
+_SANITY = {"nan": os.environ.get("DELTACORE_CHECK_NAN", "0") not in ("", "0"),
+           "inf": os.environ.get("DELTACORE_CHECK_INF", "0") not in ("", "0")}
+
+
+def set_sanity_checks(nan: bool = True, inf: bool = True) -> None:
+    """Switch the NaN / Inf guard of ``DeltaInput.sanity`` and ``delta_step`` on or off."""
+    _SANITY["nan"], _SANITY["inf"] = bool(nan), bool(inf)
+
+
+def san(t: Optional[torch.Tensor], what: str) -> None:
+    """Raise :class:`DeltaNonFiniteError` if ``t`` holds a NaN (check-nan) or an Inf (check-inf)."""
+    if t is None or not (_SANITY["nan"] or _SANITY["inf"]):
+        return
+    if _SANITY["nan"] and bool(torch.isnan(t).any()):
+        raise DeltaNonFiniteError(_abi.DC_EINVAL_ARG, f"{what} holds NaN")
+    if _SANITY["inf"] and bool(torch.isinf(t).any()):
+        raise DeltaNonFiniteError(_abi.DC_EINVAL_ARG, f"{what} holds Inf")
 
 
 def _raise(status: int, what: str) -> None:
@@ -568,6 +597,8 @@ def delta_step(q_bhk, k_bhk, v_bhv, erase_bhK, write_bhV, g_bhK, state_bhkv, sca
     with torch.cuda.device(q_bhk.device):
         stream = torch.cuda.current_stream(q_bhk.device).cuda_stream
         _raise(_abi.lib().dc_step(a, stream), "dc_step")
+    san(y, "y")  # recurrent.rs:96-97
+    san(s_out, "next state")
     return y, s_out
 
 
@@ -601,8 +632,10 @@ class DeltaInput:
         return self.g_bshK is not None and self.g_bshK.shape[3] > 1
 
     def sanity(self) -> None:
-        """Shape and width checks (path.rs:177-208), plus the NaN/Inf guard the
-        reference compiles in under its check-nan/check-inf features."""
+        """Shape and width checks (path.rs:177-208), then the NaN / Inf guard over
+        every input (path.rs:198-207), which runs only when switched on
+        (:func:`set_sanity_checks`), as the reference's runs only under its
+        check-nan / check-inf features."""
         b, s, h, dk, dv = self.dims()
         u = self.n_householder
         if s < 1:
@@ -622,6 +655,9 @@ class DeltaInput:
             if t.shape[3] not in (1, full):
                 raise DeltaShapeError(_abi.DC_EINVAL_WIDTH,
                                       f"{what}: last axis must be 1 or {full}, got {t.shape[3]}")
+        for what, t in (("q", self.q_bshk), ("k", self.k_bshk), ("v", self.v_bshv), ("erase gate", self.erase_bshK),
+                        ("write gate", self.write_bshV), ("state", self.state_bhkv), ("forget gate", self.g_bshK)):
+            san(t, what)
 
     def run(self, path: DeltaPath = DeltaPath.default()):
         """Run the selected algorithm (path.rs:215-231); returns (y_bshv, final_state_bhkv)."""

@@ -63,6 +63,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -919,16 +921,56 @@ inline bool encode_rows(CUtensorMap *m, const void *ptr, int64_t heads, int64_t 
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-inline int *device_status_ptr() {
-    static int *ptrs[64];
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    if (!ptrs[dev]) {
-        void *p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
-        ptrs[dev] = static_cast<int *>(p);
+// The current thread's CUDA context (the driver's cuCtxGetCurrent), or null.  A device address looked up
+// once is valid for the context it was looked up in: after cudaDeviceReset the device gets a new primary
+// context, and an address cached under the old one would name memory the library no longer owns.
+inline void *current_context() {
+    using Fn = CUresult (*)(CUcontext *);
+    static Fn fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<Fn>(ptr);
     }
-    return ptrs[dev];
+    CUcontext ctx = nullptr;
+    if (!fn || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+    return ctx;
+}
+
+// The device address of a __device__ symbol in the current device's current context, looked up with that
+// device current and cached per (device, context); null when the lookup fails.
+struct SymbolCache {
+    std::mutex mu;
+    void *ctx[64] = {};
+    void *addr[64] = {};
+    void *get(const void *symbol, int *err) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess || dev < 0 || dev >= 64) {
+            *err = (int)(e != cudaSuccess ? e : cudaErrorInvalidDevice);
+            return nullptr;
+        }
+        std::lock_guard<std::mutex> lock(mu);
+        void *c = current_context();  // null before the runtime first touched the device
+        if (c && addr[dev] && ctx[dev] == c) return addr[dev];
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, symbol);  // (creates the device's primary context if needed)
+        if (e != cudaSuccess || !p) {
+            *err = (int)(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+            return nullptr;
+        }
+        ctx[dev] = current_context();
+        addr[dev] = p;
+        return p;
+    }
+};
+
+inline int *device_status_ptr() {
+    static SymbolCache cache;
+    int err = 0;
+    return static_cast<int *>(cache.get(reinterpret_cast<const void *>(&g_device_status), &err));
 }
 
 template <typename TG, typename TO>

@@ -405,21 +405,18 @@ namespace {
 static __device__ __align__(256) uint8_t g_noalloc_scratch[DC_NOALLOC_SCRATCH_BYTES];
 
 // In host code g_noalloc_scratch names a host-side stand-in, not device memory:
-// its device address is looked up once per device, with that device current.
+// its device address is looked up with the device current, once per device and
+// context (a cudaDeviceReset gives the device a new context, and the address is
+// looked up again under it).
 void *noalloc_scratch(int dev, int *status) {
-    static std::atomic<void *> addr[64];
+    static dc::SymbolCache cache;
     if (dev < 0 || dev >= 64) {
         *status = DC_EUNSUPPORTED;
         return nullptr;
     }
-    void *ptr = addr[dev].load(std::memory_order_acquire);
-    if (ptr) return ptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess || !ptr) {
-        *status = cuda_fail(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
-        return nullptr;
-    }
-    addr[dev].store(ptr, std::memory_order_release);
+    int err = 0;
+    void *ptr = cache.get(reinterpret_cast<const void *>(&g_noalloc_scratch), &err);
+    if (!ptr) *status = cuda_fail((cudaError_t)err);
     return ptr;
 }
 
@@ -562,6 +559,13 @@ int dc_chunk_fwd_host(const dc_chunk_args *a, void *scratch, uint64_t scratch_by
     if (e == cudaSuccess) e = cudaStreamWaitEvent(hs.down, hs.start, 0);
     if (e != cudaSuccess) return cuda_fail(e);
 
+    // On an error after copies were queued: the caller's stream waits for everything already on the two
+    // internal streams, so that neither the scratch nor the host buffers are reused under a copy in flight.
+    auto fail_drained = [&](int status) {
+        if (cudaEventRecord(hs.up_done[0], hs.up) == cudaSuccess) cudaStreamWaitEvent(cs, hs.up_done[0], 0);
+        if (cudaEventRecord(hs.down_done[0], hs.down) == cudaSuccess) cudaStreamWaitEvent(cs, hs.down_done[0], 0);
+        return status;
+    };
     const void *src[7] = {a->q, a->k, a->v, a->erase, a->write, a->g, a->state_in};
     void *dst_host[2] = {a->y, a->state_out};
     char *const base = static_cast<char *>(scratch);
@@ -596,9 +600,9 @@ int dc_chunk_fwd_host(const dc_chunk_args *a, void *scratch, uint64_t scratch_by
         // compute on the caller's stream: after the slice landed and slice i-2's results left the slot
         if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, hs.up_done[slot], 0);
         if (e == cudaSuccess && i >= 2) e = cudaStreamWaitEvent(cs, hs.down_done[slot], 0);
-        if (e != cudaSuccess) return cuda_fail(e);
+        if (e != cudaSuccess) return fail_drained(cuda_fail(e));
         st = chunk_fwd_launch(&sl, cs);
-        if (st != DC_OK) return st;
+        if (st != DC_OK) return fail_drained(st);
         e = cudaEventRecord(hs.compute_done[slot], cs);
         // out
         if (e == cudaSuccess) e = cudaStreamWaitEvent(hs.down, hs.compute_done[slot], 0);
@@ -609,12 +613,12 @@ int dc_chunk_fwd_host(const dc_chunk_args *a, void *scratch, uint64_t scratch_by
             e = cudaMemcpyAsync(static_cast<char *>(dst_host[1]) + b0 * hp.seq_bytes[8], sl.state_out,
                                 (size_t)nb * hp.seq_bytes[8], cudaMemcpyDeviceToHost, hs.down);
         if (e == cudaSuccess) e = cudaEventRecord(hs.down_done[slot], hs.down);
-        if (e != cudaSuccess) return cuda_fail(e);
+        if (e != cudaSuccess) return fail_drained(cuda_fail(e));
     }
     // The caller's stream drains only after the last results reached the host.
     e = cudaStreamWaitEvent(cs, hs.down_done[0], 0);
     if (e == cudaSuccess && nslices > 1) e = cudaStreamWaitEvent(cs, hs.down_done[1], 0);
-    return e == cudaSuccess ? DC_OK : cuda_fail(e);
+    return e == cudaSuccess ? DC_OK : fail_drained(cuda_fail(e));
 }
 
 }  // extern "C"
@@ -873,9 +877,7 @@ int validate_out_norm(const dc_out_norm_args *a) {
 template <typename TI, typename TO>
 int launch_out_norm(const dc::onorm::Params &p, cudaStream_t s) {
     using namespace dc::onorm;
-    int sms = 148;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-    const int64_t cap = (int64_t)sms * 16;  // grid-stride beyond 16 CTAs per SM
+    const int64_t cap = (int64_t)sm_count() * 16;  // grid-stride beyond 16 CTAs per SM of the current device
     auto grid = [&](int64_t rows_per_cta) {
         const int64_t blocks = (p.rows + rows_per_cta - 1) / rows_per_cta;
         return (unsigned)(blocks < cap ? blocks : cap);
@@ -1055,9 +1057,7 @@ int dc_gates(const dc_gate_args *a, dc_stream_t stream) {
     p.a_log = a->a_log;
     p.out = a->out;
     if (a->cols > 0x7fffffffLL) return DC_EUNSUPPORTED;
-    int sms = 148;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-    const int64_t cap = (int64_t)sms * 16;
+    const int64_t cap = (int64_t)sm_count() * 16;  // of the current device
     const int64_t blocks = a->rows < cap ? a->rows : cap;  // one row per CTA at a time
     // four columns per thread: whole 4-column groups whose loads (8 or 16 bytes) and stores (16) are aligned
     const int64_t esz = a->in_dtype == DC_BF16 ? 2 : 4;

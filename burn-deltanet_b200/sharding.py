@@ -70,6 +70,21 @@ def take(t: Optional[torch.Tensor], shard: Shard, head_axis: int = 2) -> Optiona
     return t[tuple(idx)].contiguous()
 
 
+def gather_into(out: torch.Tensor, local: torch.Tensor, shards: List[Shard], group=None) -> torch.Tensor:
+    """All-gather batch-major whole-sequence blocks into a caller-owned global
+    buffer ``out`` ([world * local_batch, ...]), with no allocation: the form a
+    pipelined caller uses, with ``out`` double-buffered so that the gather of one
+    step's output overlaps the next step's kernels on another stream."""
+    import torch.distributed as dist
+
+    if not all(s.h0 == 0 for s in shards):
+        raise ValueError("gather_into takes whole-sequence shards (batch % world == 0)")
+    if tuple(out.shape) != (len(shards) * local.shape[0],) + tuple(local.shape[1:]):
+        raise ValueError(f"out has shape {tuple(out.shape)}")
+    dist.all_gather_into_tensor(out, local, group=group)
+    return out
+
+
 def gather(local: torch.Tensor, shards: List[Shard], head_axis: int = 2, group=None) -> torch.Tensor:
     """All-gather every rank's output block into the global tensor.
 

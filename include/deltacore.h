@@ -176,8 +176,10 @@ DC_API int dc_step(const dc_step_args *args, dc_stream_t stream);
  *
  * Every GPU that loads the library holds the array until the process exits.
  * The first call on a device looks up the array's device address (with that
- * device current) and keeps it; make that first call before any stream
- * capture.  All calls share the one array, which keeps the last call's
+ * device current) and keeps it for the device's current context; make that
+ * first call before any stream capture.  After cudaDeviceReset the device has
+ * a new context, and the next call looks the address up again (so, again,
+ * outside any capture).  All calls share the one array, which keeps the last call's
  * contents (nothing in it needs to start at zero), so calls whose work
  * overlaps on the GPU (different streams, or different host threads) race:
  * serialise them.

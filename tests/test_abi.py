@@ -169,6 +169,31 @@ def test_python_mirror_sanity_mirrors_the_reference_asserts():
     assert dn.DeltaPath.with_chunk_len(16).resolved_chunk_len() == 16
 
 
+def test_python_mirror_nan_inf_guard_is_opt_in():
+    """The reference's `san` guard (src/delta/path.rs:198-207) runs only under its check-nan / check-inf
+    features; here it runs only when switched on, and names the tensor it found."""
+    import torch
+    q = torch.zeros(1, 2, 1, 4)
+    v = torch.zeros(1, 2, 1, 6)
+    v[0, 1, 0, 3] = float("nan")
+    st = torch.zeros(1, 1, 4, 6)
+    st[0, 0, 1, 1] = float("inf")
+    inp = dn.DeltaInput(q, q, v, torch.zeros(1, 2, 1, 1), torch.zeros(1, 2, 1, 1), None, st)
+    inp.sanity()  # off by default: shapes only
+    try:
+        dn.set_sanity_checks(nan=True, inf=False)
+        with pytest.raises(dn.DeltaNonFiniteError, match="v holds NaN"):
+            inp.sanity()
+        v[0, 1, 0, 3] = 0.0
+        inp.sanity()  # the Inf in the state passes while only check-nan is on
+        dn.set_sanity_checks(nan=False, inf=True)
+        with pytest.raises(dn.DeltaNonFiniteError, match="state holds Inf"):
+            inp.sanity()
+    finally:
+        dn.set_sanity_checks(nan=False, inf=False)
+    inp.sanity()
+
+
 def test_host_entry_point_scratch_is_host_logic():
     a = _args(batch=10)
     need = abi.lib().dc_chunk_fwd_host_scratch_size(a)

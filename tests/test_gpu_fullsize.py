@@ -42,6 +42,7 @@ def run(x, u, recurrent=False, sl=slice(None), t0=0, t1=None, state=None):
 @pytest.mark.parametrize("kind,batch,tokens,u", [
     ("deltanet", 8, 4096, 1),       # config 2
     ("deltaproduct", 4, 8192, 2),   # config 4, u = 2
+    ("deltaproduct", 4, 8192, 3),   # config 4, u = 3
     ("gdn2", 16, 16384, 1),         # config 5 (one GPU's view of the whole batch)
 ])
 def test_full_size_properties(kind, batch, tokens, u):
@@ -60,7 +61,8 @@ def test_full_size_properties(kind, batch, tokens, u):
     del y_r, s_r
 
     # two calls cut at a chunk boundary, the state carried between them
-    cut = (tokens // 2) // 64 * 64 if u == 1 else (tokens // 2) // 32 * 32
+    step = 64 // math.gcd(64, u)  # tokens whose u micro-steps fill whole 64-row chunks
+    cut = (tokens // 2) // step * step
     y1, s1 = run(x, u, t1=cut)
     y2, s2 = run(x, u, t0=cut, state=s1)
     torch.cuda.synchronize()

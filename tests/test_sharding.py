@@ -76,6 +76,45 @@ def test_sharded_equals_unsharded_gloo(batch, heads):
         assert ey == 0.0 and es == 0.0
 
 
+def _gather_into_worker(rank, world, port, result_q):
+    """gather_into writes every rank's whole-sequence block into a caller-owned buffer, twice in a row into
+    the same buffer (the pipelined use), equal to concatenating the blocks."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        shards = sh.plan(4, 3, world)
+        out = torch.full((4, 5, 3, 2), -1.0)
+        ok = True
+        for step in range(2):
+            local = torch.arange(2 * 5 * 3 * 2, dtype=torch.float32).reshape(2, 5, 3, 2) + 1000 * rank + 10 ** 5 * step
+            sh.gather_into(out, local, shards)
+            want = torch.cat([torch.arange(60, dtype=torch.float32).reshape(2, 5, 3, 2) + 1000 * r + 10 ** 5 * step
+                              for r in range(world)])
+            ok = ok and torch.equal(out, want)
+        try:
+            sh.gather_into(torch.empty(3, 5, 3, 2), local, shards)
+            ok = False
+        except ValueError:
+            pass
+        result_q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_into_a_caller_buffer_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_into_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert all(ok for _, ok in (q.get(timeout=5) for _ in range(2)))
+
+
 def _failing_worker(rank, world, port, result_q):
     """Rank 1 raises before the gather (it never joins the collective); rank 0 must get an error from the
     gather within the short process-group timeout instead of waiting for ever."""

@@ -10,6 +10,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <utility>
 
 #include <cuda_runtime.h>
 
@@ -104,12 +105,33 @@ dc::CoreParams make_params(int64_t batch, int64_t seq, int64_t heads, int64_t dk
 // ---------------------------------------------------------------------------
 // Decode
 // ---------------------------------------------------------------------------
+// Decode ticks are short kernels launched back to back (config 5: about 9 us each), so the gap between two
+// dependent launches is a large share of a tick.  They are launched with programmatic stream
+// serialization: the next tick is scheduled while the previous one runs, and each tick's kernel waits
+// (griddepcontrol.wait) for the previous kernel in the stream to complete before it reads anything, so the
+// ordering with whatever kernel precedes it is the ordinary stream order.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 template <typename TI, typename TG, typename TO, int VEC, int CW, int NP>
 int launch_step_cfg(const dc::CoreParams &p, cudaStream_t stream) {
     const dim3 grid((unsigned)(p.batch * p.heads), (unsigned)((p.dv + CW - 1) / CW));
     const size_t smem = dc::step_smem_bytes((int)p.dk, p.u, CW);
-    dc::step_kernel<TI, TG, TO, VEC, CW, NP><<<grid, dc::kStepThreads, smem, stream>>>(p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(dc::step_kernel<TI, TG, TO, VEC, CW, NP>, grid, dim3(dc::kStepThreads), smem, stream, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? DC_OK : cuda_fail(e);
 }
 
@@ -148,8 +170,8 @@ int launch_step_stream(const dc::CoreParams &p, cudaStream_t stream) {
     if (e != cudaSuccess) return cuda_fail(e);
     const int64_t bh = p.batch * p.heads;
     const unsigned grid = (unsigned)(bh < sm_count() ? bh : sm_count());
-    kern<<<grid, dc::stream::kThreads, dc::stream::kSmem, stream>>>(p, status);
-    e = cudaGetLastError();
+    e = launch_pdl(kern, dim3(grid), dim3(dc::stream::kThreads), dc::stream::kSmem, stream, p, status);
+    if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? DC_OK : cuda_fail(e);
 }
 

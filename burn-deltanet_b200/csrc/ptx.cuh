@@ -159,6 +159,16 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // (tensor cores, TMA) after this fence plus a thread barrier.
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Wait until every grid this one depends on (the previous kernel in the stream, when this one was launched
+// with programmatic stream serialization) has completed and its memory operations are visible.  Without
+// such a dependency it returns at once.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Let the next kernel in the stream, if it was launched with programmatic stream serialization, be
+// scheduled now instead of after this grid ends (it still waits in grid_dependency_wait for all of this
+// grid's work).
+__device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),

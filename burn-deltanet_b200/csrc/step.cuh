@@ -22,6 +22,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace dc {
 
@@ -69,6 +70,10 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(CoreParams p) {
     float *red = wv + u * CW;         // [2][4][2][CW] per-warp column partials
     float *sqk = red + 2 * 4 * 2 * CW;
 
+    // Consecutive ticks: the next tick's CTAs may be scheduled now; this tick reads nothing before the
+    // previous kernel in the stream has finished (programmatic dependent launch, see the launcher).
+    ptx::launch_dependents();
+    ptx::grid_dependency_wait();
     const int64_t bh = blockIdx.x;
     const int64_t b = bh / p.heads, h = bh % p.heads;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -100,6 +105,27 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(CoreParams p) {
     const TG *g = static_cast<const TG *>(p.g);
     const int64_t H = p.heads;
     const int64_t qrow = b * p.q_bstride * H + h;  // row of q, g and y
+    if (u == 1 && dk <= kStepThreads) {
+        // One micro-step: thread i < dk takes key channel i, thread j < CW value column j.  Every load is
+        // issued before any shared-memory write, so the tick pays one global latency instead of one per
+        // input loop.
+        const int64_t row = (b * p.kv_bstride) * H + h;
+        const int c = col_base + tid;
+        const bool kt = tid < dk, vt = tid < CW && c < dv;
+        const float kv = kt ? ld(k + row * dk + tid) : 0.f;
+        const float ev = kt ? ld(erase + row * p.ew + (p.ew == 1 ? 0 : tid)) : 0.f;
+        const float gv = (kt && p.gw) ? ld(g + qrow * p.gw + (p.gw == 1 ? 0 : tid)) : 0.f;
+        const float qv = kt ? ld(q + qrow * dk + tid) : 0.f;
+        const float vv = vt ? ld(v + row * dv + c) : 0.f;
+        const float wv_ = vt ? ld(write + row * p.ww + (p.ww == 1 ? 0 : c)) : 0.f;
+        if (kt) {
+            kk[tid] = kv;
+            ke[tid] = kv * ev;
+            decay[tid] = p.gw ? expf(gv) : 1.f;
+            sq[tid] = p.scale * qv;
+        }
+        if (tid < CW) wv[tid] = vv * wv_;
+    } else {
     for (int idx = tid; idx < u * dk; idx += kStepThreads) {
         const int m = idx / dk, i = idx % dk;
         const int64_t row = (b * p.kv_bstride + m) * H + h;  // [batch, u, heads, .]
@@ -120,6 +146,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(CoreParams p) {
             val = ld(v + row * dv + c) * ld(write + row * p.ww + (p.ww == 1 ? 0 : c));
         }
         wv[idx] = val;
+    }
     }
     __syncthreads();
     // (scale q) . k of the last micro-step: the readout's share of the write.

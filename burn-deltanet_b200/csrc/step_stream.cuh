@@ -46,6 +46,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_stream_kernel(const CorePara
     volatile int *flag = reinterpret_cast<volatile int *>(base + OFF_FLAG);
     float *red = reinterpret_cast<float *>(base + OFF_RED);
 
+    ptx::launch_dependents();     // the next tick may be scheduled as this one's CTAs leave their SMs
+    ptx::grid_dependency_wait();  // nothing is read before the previous kernel in the stream has finished
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t BH = p.batch * p.heads, H = p.heads;
     const int64_t first = blockIdx.x, stride = gridDim.x;

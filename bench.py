@@ -300,47 +300,36 @@ def time_prefill(dn, x, u, steps, warmup):
 def time_prefill_gathered(dn, x, u, steps, warmup, world):
     """Each step: the prefill of this rank's batch, then the all-gather of its y
     (bf16) into every rank's global output [world x batch, T, H, dv] -- the
-    north star's one collective.  The gather of step i runs on a side stream
-    while step i+1 computes (y and the global output double-buffered); the
-    timed region ends when the last gather has landed on this rank.  Returns ms
-    per step on this rank (the caller takes the max over ranks).  At one GPU
-    there is nothing to gather and this is the plain prefill."""
+    north star's one collective -- on the same stream, so the step ends when the
+    gathered output is complete on this rank.  Returns ms per step on this rank
+    (the caller takes the max over ranks).  At one GPU there is nothing to
+    gather and this is the plain prefill.  (Running the gather of step i beside
+    the prefill of step i+1 was measured slower: NCCL's 32 CTAs take SMs the
+    one-wave prefill needs.)"""
     if world == 1:
         return time_prefill(dn, x, u, steps, warmup)
     sh = importlib.import_module("burn-deltanet_b200.sharding")
     b, s = x["q"].shape[0], x["q"].shape[1]
     shards = sh.plan(b * world, H, world)
-    ys = [torch.empty(b, s, H, D, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
-    outs = [torch.empty(world * b, s, H, D, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    y = torch.empty(b, s, H, D, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(world * b, s, H, D, device="cuda", dtype=torch.bfloat16)
     s_out = torch.empty_like(x["state"])
     gated = x["g"] is not None
-    compute, comm = torch.cuda.current_stream(), torch.cuda.Stream()
-    done_c = [torch.cuda.Event() for _ in range(2)]
-    done_g = [torch.cuda.Event() for _ in range(2)]
 
-    def step(i):
-        j = i & 1
-        if i >= 2:
-            compute.wait_event(done_g[j])  # the gather of step i-2 has read ys[j]
+    def step():
         dn.delta_chunk_recalculated(x["q"], x["k"], x["v"], x["erase"], x["write"], x["g"], x["state"],
-                                    gated, L, 1.0 / math.sqrt(D), n_householder=u, y_out=ys[j], state_out=s_out)
-        done_c[j].record(compute)
-        with torch.cuda.stream(comm):
-            comm.wait_event(done_c[j])
-            sh.gather_into(outs[j], ys[j], shards)
-            done_g[j].record(comm)
+                                    gated, L, 1.0 / math.sqrt(D), n_householder=u, y_out=y, state_out=s_out)
+        sh.gather_into(out, y, shards)
 
-    for i in range(warmup):
-        step(i)
-    compute.wait_stream(comm)
+    for _ in range(warmup):
+        step()
     torch.cuda.synchronize()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(compute)
-    for i in range(steps):
-        step(i)
-    compute.wait_stream(comm)
-    e1.record(compute)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / steps
 
@@ -578,8 +567,8 @@ def hbm_roofline(nbytes, ms, hbm_peak, peak_kind, traffic=None):
 
 def measure_cfg4(dn, args, rank, world, hbm_peak, peak_kind):
     """Config 4 (DeltaProduct, u = 2 and 3, B=4 T=8192 per GPU, weak scaling): one dc_chunk_fwd per step
-    with the micro-steps folded in-kernel; at N > 1 the value counts the all-gather of y, pipelined as in the
-    headline; `kernel_ms` is the prefill alone."""
+    with the micro-steps folded in-kernel; at N > 1 the value counts the all-gather of y, as in the headline;
+    `kernel_ms` is the prefill alone."""
     out = {}
     for u in (2, 3):
         batch, tokens = 4, 8192
@@ -605,8 +594,7 @@ def measure_cfg4(dn, args, rank, world, hbm_peak, peak_kind):
 def measure_cfg5(dn, args, rank, world, hbm_peak, peak_kind):
     """Config 5 as the north star runs it: one batch of 16 GDN-2 sequences (T=16384) sharded batch-major over
     the N GPUs (strong scaling), the prefill of each rank's sequences (two launches: prep + scan), the
-    all-gather of y into every rank's [16, T, H, dv] output inside the timed step (pipelined: the gather of
-    step i overlaps step i+1), then 512 GDN-2 step() tokens from each rank's own final state.  At N > 1 every
+    all-gather of y into every rank's [16, T, H, dv] output inside the timed step, then 512 GDN-2 step() tokens from each rank's own final state.  At N > 1 every
     rank also runs the whole unsharded batch and checks the gathered y and final state against it bit for
     bit."""
     B5, T5 = 16, 16384
@@ -725,7 +713,7 @@ def run_ours(args):
         return
     k_ms = max_over_ranks(k_ms, world)
     tok_per_rank = batch * tokens
-    # The step at N > 1 includes the all-gather of y to every rank (pipelined with the next step's kernels).
+    # The step at N > 1 includes the all-gather of y to every rank.
     ms = max_over_ranks(time_prefill_gathered(dn, x, u, args.steps, args.warmup, world), world) \
         if world > 1 else k_ms
     value = tok_per_rank * world / (ms / 1e3)
@@ -799,8 +787,8 @@ def run_ours(args):
     if cfg5 is not None:
         line["cfg5"] = cfg5
     if world > 1:
-        line["allgather"] = {"collective": "nccl all_gather_into_tensor of y (bf16), on a side stream, the gather "
-                                           "of step i overlapping the prefill of step i+1",
+        line["allgather"] = {"collective": "nccl all_gather_into_tensor of y (bf16) after each step's prefill, "
+                                           "same stream",
                              "bytes_per_rank_out": world * tok_per_rank * H * D * 2,
                              "ms_per_step_with_gather": ms, "ms_per_step_kernel_only": k_ms}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

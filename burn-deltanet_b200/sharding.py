@@ -73,8 +73,7 @@ def take(t: Optional[torch.Tensor], shard: Shard, head_axis: int = 2) -> Optiona
 def gather_into(out: torch.Tensor, local: torch.Tensor, shards: List[Shard], group=None) -> torch.Tensor:
     """All-gather batch-major whole-sequence blocks into a caller-owned global
     buffer ``out`` ([world * local_batch, ...]), with no allocation: the form a
-    pipelined caller uses, with ``out`` double-buffered so that the gather of one
-    step's output overlaps the next step's kernels on another stream."""
+    caller that gathers every step's output into the same buffer uses."""
     import torch.distributed as dist
 
     if not all(s.h0 == 0 for s in shards):

@@ -24,6 +24,11 @@
 #include "common.cuh"
 #include "ptx.cuh"
 
+// Phase timestamps for performance work (a timing build defines DC_STEP_MARK(id); a no-op here).
+#ifndef DC_STEP_MARK
+#define DC_STEP_MARK(id)
+#endif
+
 namespace dc {
 
 constexpr int kStepThreads = 128;
@@ -72,8 +77,10 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(CoreParams p) {
 
     // Consecutive ticks: the next tick's CTAs may be scheduled now; this tick reads nothing before the
     // previous kernel in the stream has finished (programmatic dependent launch, see the launcher).
+    DC_STEP_MARK(0);
     ptx::launch_dependents();
     ptx::grid_dependency_wait();
+    DC_STEP_MARK(1);
     const int64_t bh = blockIdx.x;
     const int64_t b = bh / p.heads, h = bh % p.heads;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -149,6 +156,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(CoreParams p) {
     }
     }
     __syncthreads();
+    DC_STEP_MARK(2);
     // (scale q) . k of the last micro-step: the readout's share of the write.
     if (warp == 0) {
         float acc = 0.f;
@@ -230,12 +238,14 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(CoreParams p) {
         }
     }
 
+    DC_STEP_MARK(3);
     float *S_out = p.state_out + bh * (int64_t)dk * dv;
 #pragma unroll
     for (int pp = 0; pp < NP; ++pp) {
         const int row = r0 + pp * RPP;
         if (row < dk && col_ok) VecF<VEC>::store(S_out + (int64_t)row * dv + col, s[pp]);
     }
+    DC_STEP_MARK(4);
 }
 
 }  // namespace dc

@@ -297,6 +297,40 @@ def time_prefill(dn, x, u, steps, warmup):
     return e0.elapsed_time(e1) / steps
 
 
+def time_prefill_out_norm(dn, x, u, steps, warmup):
+    """The prefill followed by the plain output norm (dc_chunk_fwd_out_norm, the norm inside the tensor-core
+    kernel's read-out) against the same two steps as separate calls (dc_chunk_fwd, then dc_out_norm in place
+    on y).  Returns (ms of the one call, ms as two calls, whether the norm ran inside the prefill kernel)."""
+    b, s = x["q"].shape[0], x["q"].shape[1]
+    y = torch.empty(b, s, H, D, device="cuda", dtype=torch.bfloat16)
+    s_out = torch.empty_like(x["state"])
+    w = torch.rand(D, device="cuda", generator=torch.Generator(device="cuda").manual_seed(5)) + 0.5
+    args = (x["q"], x["k"], x["v"], x["erase"], x["write"], x["g"], x["state"], x["g"] is not None, L,
+            1.0 / math.sqrt(D))
+
+    def fused():
+        dn.delta_chunk_recalculated_out_norm(*args, w, n_householder=u, y_out=y, state_out=s_out)
+
+    def two():
+        dn.delta_chunk_recalculated(*args, n_householder=u, y_out=y, state_out=s_out)
+        dn.out_norm(y, None, w, out=y)
+
+    times = []
+    for call in (fused, two):
+        for _ in range(max(3, warmup)):
+            call()
+        torch.cuda.synchronize()
+        stream = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / steps)
+    return times[0], times[1], dn.chunk_out_norm_is_fused(*args[:9], w, n_householder=u, out_dtype=torch.bfloat16)
+
+
 def time_prefill_gathered(dn, x, u, steps, warmup, world):
     """Each step: the prefill of this rank's batch, then the all-gather of its y
     (bf16) into every rank's global output [world x batch, T, H, dv] -- the
@@ -720,6 +754,8 @@ def run_ours(args):
     nbytes = algorithmic_bytes(x, batch * tokens)
     ms_e2e, h2d, d2h = time_prefill_e2e(dn, x, u, max(1, min(args.steps, 5)), 1)
     ms_e2e = max_over_ranks(ms_e2e, world)
+    pn_ms, pn_two_ms, pn_fused = time_prefill_out_norm(dn, x, u, args.steps, args.warmup)
+    pn_ms, pn_two_ms = max_over_ranks(pn_ms, world), max_over_ranks(pn_two_ms, world)
     flops = 2 * (5 * L * D + 3 * D * D) * batch * tokens * u * H
     del x
     torch.cuda.empty_cache()
@@ -765,6 +801,13 @@ def run_ours(args):
                                   "flop_per_token_head": BWD_FLOP,
                                   "hbm_gbs_of_inputs_and_gradients": bw_bytes / (bw_ms / 1e3) / 1e9},
                      "gpu_launches": 3 * 2},
+        "prefill_out_norm": {"metric": "prefill + plain out-norm tok/s (the workload's prefill with the per-head "
+                                       "RMSNorm of its read-out fused into the kernel's epilogue, bf16 out)",
+                             "value": tok_per_rank * world / (pn_ms / 1e3), "unit": "tok/s",
+                             "ms_per_step": pn_ms, "ms_per_step_two_calls": pn_two_ms,
+                             "ms_per_step_prefill_alone": k_ms, "steps": args.steps, "fused": pn_fused,
+                             "roofline": hbm_roofline(nbytes, pn_ms, hbm_peak, peak_kind),
+                             "gpu_launches": launches + (0 if pn_fused else args.steps)},
         "out_norm": {"metric": "out-norm tok/s (gated per-head RMSNorm after the read-out, config 2's output: "
                                "bf16 y and gate in, bf16 out)",
                      "value": 8 * 4096 * world / (on_ms / 1e3), "unit": "tok/s", "ms_per_step": on_ms, "steps": 20,

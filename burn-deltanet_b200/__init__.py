@@ -23,10 +23,12 @@ from .core import (
     DeltaShapeError,
     TriSolve,
     beta_gates,
+    chunk_out_norm_is_fused,
     delta_chunk_host_scratch_size,
     delta_chunk_recalculated,
     delta_chunk_recalculated_backward,
     delta_chunk_recalculated_host,
+    delta_chunk_recalculated_out_norm,
     delta_step,
     out_norm,
     qkv_prologue,
@@ -41,7 +43,7 @@ __all__ = [
     "DeltaChunkFunction", "DeltaCoreError", "DeltaInput", "DeltaNonFiniteError", "DeltaPath", "DeltaShapeError",
     "TriSolve", "san", "set_sanity_checks",
     "beta_gates", "delta_chunk_host_scratch_size", "delta_chunk_recalculated", "delta_chunk_recalculated_backward",
-    "delta_chunk_recalculated_host", "delta_step", "library_path", "out_norm", "qkv_prologue", "write_gate", "head_log_decay", "channel_log_decay",
+    "delta_chunk_recalculated_host", "delta_chunk_recalculated_out_norm", "chunk_out_norm_is_fused", "delta_step", "library_path", "out_norm", "qkv_prologue", "write_gate", "head_log_decay", "channel_log_decay",
 ]
 
 

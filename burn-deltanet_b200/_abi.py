@@ -42,6 +42,8 @@ EXPORTS = (
     "dc_chunk_bwd_workspace_size",
     "dc_chunk_bwd",
     "dc_out_norm",
+    "dc_chunk_fwd_out_norm",
+    "dc_chunk_fwd_out_norm_fused",
     "dc_qkv_prologue",
     "dc_gates",
 )
@@ -178,6 +180,10 @@ def lib() -> ctypes.CDLL:
         L.dc_chunk_bwd.restype = ctypes.c_int
         L.dc_out_norm.argtypes = [ctypes.POINTER(OutNormArgs), ctypes.c_void_p]
         L.dc_out_norm.restype = ctypes.c_int
+        L.dc_chunk_fwd_out_norm.argtypes = [ctypes.POINTER(ChunkArgs), ctypes.POINTER(OutNormArgs), ctypes.c_void_p]
+        L.dc_chunk_fwd_out_norm.restype = ctypes.c_int
+        L.dc_chunk_fwd_out_norm_fused.argtypes = [ctypes.POINTER(ChunkArgs), ctypes.POINTER(OutNormArgs)]
+        L.dc_chunk_fwd_out_norm_fused.restype = ctypes.c_int
         L.dc_qkv_prologue.argtypes = [ctypes.POINTER(PrologueArgs), ctypes.c_void_p]
         L.dc_qkv_prologue.restype = ctypes.c_int
         L.dc_gates.argtypes = [ctypes.POINTER(GateArgs), ctypes.c_void_p]

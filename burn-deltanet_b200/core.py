@@ -261,6 +261,73 @@ def delta_chunk_recalculated(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_b
     return y, s_out
 
 
+def _norm_args(a, y, norm_weight, norm_gate, norm_eps):
+    """dc_out_norm_args for the norm that follows the prefill call `a` (rows of y [b, s, h, dv])."""
+    _check_tensor(norm_weight, "norm_weight")
+    if norm_weight.dtype != torch.float32 or tuple(norm_weight.shape) != (a.dv,):
+        raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, f"norm_weight must be float32 [{a.dv}]")
+    n = _abi.OutNormArgs()
+    n.rows, n.dv = a.batch * a.seq * a.heads, a.dv
+    n.in_dtype, n.out_dtype, n.eps = a.out_dtype, a.out_dtype, float(norm_eps)
+    n.weight = norm_weight.data_ptr()
+    if norm_gate is not None:
+        _check_tensor(norm_gate, "norm_gate")
+        if norm_gate.shape != y.shape or _dtype_code(norm_gate, "norm_gate") != a.out_dtype:
+            raise DeltaShapeError(_abi.DC_EINVAL_SHAPE, "norm_gate must be shaped like y, in y's dtype")
+        n.gate = norm_gate.data_ptr()
+    return n
+
+
+def delta_chunk_recalculated_out_norm(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv,
+                                      has_gate: bool, chunk_len: int, scale: float, norm_weight: torch.Tensor,
+                                      norm_gate: Optional[torch.Tensor] = None, norm_eps: float = 1e-5, *,
+                                      n_householder: int = 1, out_dtype: Optional[torch.dtype] = None,
+                                      workspace: Optional[torch.Tensor] = None,
+                                      y_out: Optional[torch.Tensor] = None,
+                                      state_out: Optional[torch.Tensor] = None):
+    """The prefill followed by the block's output norm (``dc_chunk_fwd_out_norm``): what a layer's
+    forward does with the core's read-out before out_proj (src/common/norm.rs:129-135 on the y of
+    chunk_recalculated.rs:115-126).
+
+    Arguments as :func:`delta_chunk_recalculated`, plus the norm's float32 ``norm_weight`` [dv], its
+    gate (``None``: OutNorm::Plain; else shaped like y, in y's dtype) and eps.  Returns
+    ``(normalised y, final_state)``.  A plain norm on the fused tensor-core path is applied inside the
+    kernel's read-out (:func:`chunk_out_norm_is_fused` says which); otherwise the call is the prefill
+    followed by :func:`out_norm` in place on y.
+    """
+    a, y, s_out = _chunk_args(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv, has_gate,
+                              chunk_len, scale, n_householder, out_dtype, False, False, False, y_out, state_out,
+                              _check_tensor, lambda shape, dt: torch.empty(shape, device=q_bshk.device, dtype=dt))
+    n = _norm_args(a, y, norm_weight, norm_gate, norm_eps)
+    need = int(_abi.lib().dc_chunk_workspace_size(a))
+    if need > 0:
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q_bshk.device)
+        _check_tensor(workspace, "workspace")
+        a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    with torch.cuda.device(q_bshk.device):
+        stream = torch.cuda.current_stream(q_bshk.device).cuda_stream
+        _raise(_abi.lib().dc_chunk_fwd_out_norm(a, n, stream), "dc_chunk_fwd_out_norm")
+    return y, s_out
+
+
+def chunk_out_norm_is_fused(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv,
+                            has_gate: bool, chunk_len: int, norm_weight: torch.Tensor,
+                            norm_gate: Optional[torch.Tensor] = None, *, n_householder: int = 1,
+                            out_dtype: Optional[torch.dtype] = None) -> bool:
+    """Whether :func:`delta_chunk_recalculated_out_norm` applies the norm inside the prefill kernel for
+    these arguments (``dc_chunk_fwd_out_norm_fused``; host logic, nothing runs)."""
+    a, y, _ = _chunk_args(q_bshk, k_bshk, v_bshv, erase_bshK, write_bshV, g_bshK, state_bhkv, has_gate,
+                          chunk_len, 1.0, n_householder, out_dtype, False, False, False, None, None,
+                          lambda t, what: None, lambda shape, dt: torch.empty(shape, device="meta", dtype=dt))
+    a.y, a.state_out = 256, 512  # aligned placeholders, distinct from the inputs: the query reads no pointer
+    n = _norm_args(a, y, norm_weight, norm_gate, 1e-5)
+    r = int(_abi.lib().dc_chunk_fwd_out_norm_fused(a, n))
+    if r < 0:
+        _raise(-r, "dc_chunk_fwd_out_norm_fused")
+    return r == 1
+
+
 def delta_chunk_recalculated_backward(d_y_bshv, d_final_state_bhkv, q_bshk, k_bshk, v_bshv, erase_bshK,
                                       write_bshV, g_bshK, state_bhkv, has_gate: bool, chunk_len: int,
                                       scale: float, *, n_householder: int = 1,

@@ -107,7 +107,8 @@ constexpr int kBars = 13;
 constexpr uint32_t OFF_TMEMPTR = OFF_BAR + kBars * 8;
 constexpr uint32_t OFF_FLAG = OFF_TMEMPTR + 4;
 constexpr uint32_t OFF_PEND = OFF_FLAG + 4;             // int[2]: parity of a stage's TMA load in flight, or -1
-constexpr uint32_t kSmemUsed = OFF_PEND + 8;
+constexpr uint32_t OFF_NORMW = (OFF_PEND + 8 + 15) & ~15u;  // the fused output norm's weight [128] fp32
+constexpr uint32_t kSmemUsed = OFF_NORMW + 512;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;       // alignment slack
 static_assert(OFF_AF % 1024 == 0 && OFF_TF % 1024 == 0 && OFF_AQK % 1024 == 0 && OFF_S % 1024 == 0,
               "operand tiles need 1 KB alignment");
@@ -624,6 +625,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             return true;
         };
+        float *normw = reinterpret_cast<float *>(base + OFF_NORMW);
+        if (p.norm) normw[r] = p.norm_weight[r];  // read only by this role, after the barrier below
         bool ok = ser_wait(B_GATE0, 0);
         if (ok) {
             // S0 -> TMEM (scaled by chunk 0's total decay) and its bf16 copy.
@@ -736,6 +739,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool write_y = (r >= 64) && q_pos(c, r - 64, p) >= 0;
                 const int64_t tok = write_y ? q_first(c, p.u) + (r - 64) : 0;
                 TO *yrow = static_cast<TO *>(p.y) + ((b * p.seq + tok) * p.heads + h) * kD;
+                // The fused plain output norm (OutNorm::Plain, src/common/norm.rs:129-135): each y-row thread
+                // holds its whole row of dv = 128 values, so mean(y^2) is a sum in registers over a first
+                // pass; the y warps have the time while the V' warps split their rows into hi + lo.
+                float inv = 1.f;
+                if (p.norm && r >= 64) {  // warp-uniform: warps 10 and 11
+                    float ss = 0.f;
+#pragma unroll 1
+                    for (int hh = 0; hh < 2; ++hh) {
+                        uint32_t vv[2][32];
+                        ptx::tmem_ld32(tmem + lane_base + TM_UY + 64 * hh, vv[0]);
+                        ptx::tmem_ld32(tmem + lane_base + TM_UY + 64 * hh + 32, vv[1]);
+                        ptx::tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            const float a0 = __uint_as_float(vv[0][e]), a1 = __uint_as_float(vv[1][e]);
+                            ss = fmaf(a0, a0, fmaf(a1, a1, ss));
+                        }
+                    }
+                    inv = rsqrtf(ss * (1.f / kD) + p.norm_eps);
+                }
 #pragma unroll 1
                 for (int hh = 0; hh < 2; ++hh) {
                     uint32_t vv[2][32];
@@ -744,7 +767,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ptx::tmem_wait_ld();
 #pragma unroll
                     for (int q2 = 0; q2 < 2; ++q2) {
-                        const float *f = reinterpret_cast<const float *>(vv[q2]);
+                        float *f = reinterpret_cast<float *>(vv[q2]);
+                        if (p.norm && r >= 64) {
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) f[e] *= inv * normw[64 * hh + 32 * q2 + e];
+                        }
                         if (r < 64) {
 #pragma unroll
                             for (int q = 0; q < 4; ++q) {

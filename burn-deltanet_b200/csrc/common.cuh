@@ -29,6 +29,11 @@ struct CoreParams {
     const float *state_in;
     void *y;
     float *state_out;
+    // The plain output norm fused into the read-out (dc_chunk_fwd_out_norm; the fused tensor-core kernel
+    // only): y <- y / sqrt(mean(y^2) + norm_eps) * norm_weight over each row of dv values.
+    int32_t norm;              // 0: y as is; 1: normalised
+    float norm_eps;
+    const float *norm_weight;  // [dv] float32
 };
 
 }  // namespace dc

@@ -99,6 +99,9 @@ dc::CoreParams make_params(int64_t batch, int64_t seq, int64_t heads, int64_t dk
     p.kv_bstride = (int64_t)u * seq;
     p.q_bstride = seq;
     p.stall = 0;
+    p.norm = 0;
+    p.norm_eps = 0.f;
+    p.norm_weight = nullptr;
     return p;
 }
 
@@ -952,6 +955,57 @@ int dc_out_norm(const dc_out_norm_args *a, dc_stream_t stream) {
         case 2: return launch_out_norm<__nv_bfloat16, float>(p, s);
         default: return launch_out_norm<__nv_bfloat16, __nv_bfloat16>(p, s);
     }
+}
+
+// The checks of dc_chunk_fwd_out_norm and its query: the prefill's, then the norm's against it.
+static int validate_chunk_norm(const dc_chunk_args *a, const dc_out_norm_args *n) {
+    const int st = validate_chunk(a);
+    if (st != DC_OK) return st;
+    if (!n || n->y || n->out) return DC_EINVAL_ARG;  // the normalised rows replace y in a->y
+    if (!(n->eps >= 0.f) || !isfinite(n->eps)) return DC_EINVAL_ARG;
+    if (n->dv != a->dv || n->rows != a->batch * a->seq * a->heads) return DC_EINVAL_SHAPE;
+    if (n->out_dtype != a->out_dtype || (n->gate && n->in_dtype != a->out_dtype)) return DC_EUNSUPPORTED_DTYPE;
+    if (a->dv > 32 * dc::onorm::kMaxPer) return DC_EUNSUPPORTED;
+    if (a->batch > 0 && a->heads > 0 && !n->weight) return DC_EINVAL_ARG;
+    return DC_OK;
+}
+
+// The prefill with the output norm after it.  Fused into the tensor-core kernel's read-out for the plain
+// norm; otherwise dc_chunk_fwd, then dc_out_norm in place on y.
+int dc_chunk_fwd_out_norm(const dc_chunk_args *a, const dc_out_norm_args *n, dc_stream_t stream) {
+    int st = validate_chunk_norm(a, n);
+    if (st != DC_OK) return st;
+    if (a->batch == 0 || a->heads == 0) return DC_OK;
+    st = check_device(nullptr);
+    if (st != DC_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    dc::CoreParams p = chunk_params(a);
+    const int choice = chunk_choice(a, p);
+    if (choice < 0) return -choice;
+    if (choice == 1 && !n->gate && !(a->flags & DC_FLAG_RECURRENT)) {
+        p.stall = (a->flags & DC_FLAG_TEST_STALL) ? 1 : 0;
+        p.norm = 1;
+        p.norm_eps = n->eps;
+        p.norm_weight = n->weight;
+        st = dc::launch_chunk_tc(p, a->gate_dtype, a->out_dtype, s);
+        if (st == DC_ECUDA) g_last_cuda_error = dc::tc_last_error();
+        return st;
+    }
+    st = chunk_fwd_launch(a, s);
+    if (st != DC_OK) return st;
+    dc_out_norm_args m = *n;
+    m.in_dtype = a->out_dtype;
+    m.y = a->y;
+    m.out = a->y;
+    return dc_out_norm(&m, stream);
+}
+
+int dc_chunk_fwd_out_norm_fused(const dc_chunk_args *a, const dc_out_norm_args *n) {
+    const int st = validate_chunk_norm(a, n);
+    if (st != DC_OK) return -st;
+    const int choice = chunk_choice(a, chunk_params(a));
+    if (choice < 0) return choice;
+    return (choice == 1 && !n->gate && !(a->flags & DC_FLAG_RECURRENT)) ? 1 : 0;
 }
 
 }  // extern "C"

@@ -197,6 +197,9 @@ extern "C" {
     pub fn dc_chunk_bwd(args: *const dc_chunk_bwd_args, stream: dc_stream_t) -> c_int;
     pub fn dc_step(args: *const dc_step_args, stream: dc_stream_t) -> c_int;
     pub fn dc_out_norm(args: *const dc_out_norm_args, stream: dc_stream_t) -> c_int;
+    pub fn dc_chunk_fwd_out_norm(chunk: *const dc_chunk_args, norm: *const dc_out_norm_args,
+                                 stream: dc_stream_t) -> c_int;
+    pub fn dc_chunk_fwd_out_norm_fused(chunk: *const dc_chunk_args, norm: *const dc_out_norm_args) -> c_int;
     pub fn dc_qkv_prologue(args: *const dc_qkv_prologue_args, stream: dc_stream_t) -> c_int;
     pub fn dc_gates(args: *const dc_gate_args, stream: dc_stream_t) -> c_int;
     pub fn dc_status_string(status: c_int) -> *const c_char;

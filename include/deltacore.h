@@ -264,6 +264,24 @@ typedef struct dc_out_norm_args {
 DC_API int dc_out_norm(const dc_out_norm_args *args, dc_stream_t stream);
 
 /*
+ * The prefill followed by the output norm: what a block's forward does with the core's read-out before
+ * out_proj (src/common/norm.rs:129-135 on the y of chunk_recalculated.rs:115-126).  No single reference
+ * function; the two reference steps in one call.  `chunk` is exactly dc_chunk_fwd's argument; `norm`
+ * gives the norm's gate (NULL: OutNorm::Plain), weight [dv] float32 and eps, with rows = batch * seq *
+ * heads, dv = chunk->dv, out_dtype = chunk->out_dtype and, with a gate, in_dtype = chunk->out_dtype (the
+ * gate's dtype); its y and out must be NULL.  The normalised rows are written to chunk->y in place of the
+ * read-out, and the final state to chunk->state_out as usual.
+ * Where the fused tensor-core kernel serves the call (dc_chunk_kernel_choice 1) and the norm is plain,
+ * each row is normalised inside the kernel's read-out, from the float32 accumulator, before y is
+ * rounded to out_dtype: the read-out never makes the round trip through HBM.  Otherwise the call is
+ * dc_chunk_fwd followed by dc_out_norm in place on y.
+ */
+DC_API int dc_chunk_fwd_out_norm(const dc_chunk_args *chunk, const dc_out_norm_args *norm, dc_stream_t stream);
+/* 1 if dc_chunk_fwd_out_norm fuses the norm for these arguments, 0 if it runs the two kernels; negative
+ * = the dc_status the call would return.  Pure host logic. */
+DC_API int dc_chunk_fwd_out_norm_fused(const dc_chunk_args *chunk, const dc_out_norm_args *norm);
+
+/*
  * The front-end between the fused input projection and the core, on the projection's [q | u k | u v]
  * channel segment (QkvProjection::forward / step after in_proj, src/common/qkv.rs:373-500):
  *   the causal depthwise short convolution with its rolling window (src/common/conv.rs:81-160): x is

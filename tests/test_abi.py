@@ -255,6 +255,42 @@ def test_out_norm_validation_is_host_logic():
     assert lib.dc_out_norm(None, None) == abi.DC_EINVAL_ARG
 
 
+def _norm_for(a, **over):
+    n = abi.OutNormArgs()
+    n.rows, n.dv, n.in_dtype, n.out_dtype, n.eps = a.batch * a.seq * a.heads, a.dv, a.out_dtype, a.out_dtype, 1e-5
+    n.weight = 0x30000
+    for k, v in over.items():
+        setattr(n, k, v)
+    return n
+
+
+def test_chunk_out_norm_validation_and_fusion_are_host_logic():
+    """dc_chunk_fwd_out_norm checks the norm against the prefill before any device work; its query says
+    where the plain norm runs inside the tensor-core kernel's read-out."""
+    lib = abi.lib()
+    tc = _args(dk=128, dv=128, in_dtype=abi.DC_BF16, out_dtype=abi.DC_BF16)
+    assert lib.dc_chunk_kernel_choice(tc) == 1
+    assert lib.dc_chunk_fwd_out_norm_fused(tc, _norm_for(tc)) == 1
+    assert lib.dc_chunk_fwd_out_norm_fused(tc, _norm_for(tc, gate=0x50000)) == 0           # gated norm: two kernels
+    assert lib.dc_chunk_fwd_out_norm_fused(_args(), _norm_for(_args())) == 0               # CUDA-core prefill
+    rec = _args(dk=128, dv=128, in_dtype=abi.DC_BF16, flags=abi.DC_FLAG_RECURRENT)
+    assert lib.dc_chunk_fwd_out_norm_fused(rec, _norm_for(rec)) == 0
+    bad = [(dict(y=0x60000), abi.DC_EINVAL_ARG), (dict(out=0x60000), abi.DC_EINVAL_ARG),
+           (dict(eps=float("inf")), abi.DC_EINVAL_ARG), (dict(eps=-1.0), abi.DC_EINVAL_ARG),
+           (dict(dv=64), abi.DC_EINVAL_SHAPE), (dict(rows=3), abi.DC_EINVAL_SHAPE),
+           (dict(out_dtype=abi.DC_F32), abi.DC_EUNSUPPORTED_DTYPE),
+           (dict(gate=0x50000, in_dtype=abi.DC_F32), abi.DC_EUNSUPPORTED_DTYPE),
+           (dict(weight=None), abi.DC_EINVAL_ARG)]
+    for over, code in bad:
+        n = _norm_for(tc, **over)
+        assert lib.dc_chunk_fwd_out_norm(tc, n, None) == code, over
+        assert lib.dc_chunk_fwd_out_norm_fused(tc, n) == -code, over
+    assert lib.dc_chunk_fwd_out_norm(tc, None, None) == abi.DC_EINVAL_ARG
+    assert lib.dc_chunk_fwd_out_norm(_args(seq=0), _norm_for(tc), None) == abi.DC_EINVAL_SHAPE
+    empty = _args(batch=0)
+    assert lib.dc_chunk_fwd_out_norm(empty, _norm_for(empty, weight=None), None) == abi.DC_OK  # no device touched
+
+
 def test_prologue_validation_is_host_logic():
     """dc_qkv_prologue rejects bad arguments before any device work (conv.rs / qkv.rs asserts as codes)."""
     a = abi.PrologueArgs()

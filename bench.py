@@ -331,6 +331,44 @@ def time_prefill_out_norm(dn, x, u, steps, warmup):
     return times[0], times[1], dn.chunk_out_norm_is_fused(*args[:9], w, n_householder=u, out_dtype=torch.bfloat16)
 
 
+def time_prefill_f32(dn, steps, warmup, batch=8, tokens=4096):
+    """Config 2's prefill at the reference's own precision: float32 q, k, v (and y) through the
+    fp32-accurate chunked path (dc_chunk_kernel_choice 3, over a workspace), and through the CUDA-core
+    kernel it replaces, on the same inputs (inputs larger than L2).  Returns (ms chunked, ms CUDA-core,
+    algorithmic bytes per call, choice)."""
+    x = make_prefill("deltanet", batch, tokens, 1, "cuda", 21)
+    for n in ("q", "k", "v"):
+        x[n] = x[n].float()
+    args = (x["q"], x["k"], x["v"], x["erase"], x["write"], x["g"], x["state"], False, L, 1.0 / math.sqrt(D))
+    y = torch.empty(batch, tokens, H, D, device="cuda")
+    s_out = torch.empty_like(x["state"])
+    a, _, _ = dn.core._chunk_args(*args[:7], False, L, args[9], 1, torch.float32, False, False, False, y, s_out,
+                                  dn.core._check_tensor, None)
+    need = int(dn._abi.lib().dc_chunk_workspace_size(a))
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+    a.workspace, a.workspace_bytes = ws.data_ptr(), need
+    choice = int(dn._abi.lib().dc_chunk_kernel_choice(a))
+
+    def timed(call, n):
+        for _ in range(max(1, min(warmup, 3))):
+            call()
+        torch.cuda.synchronize()
+        stream = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    ms = timed(lambda: dn.delta_chunk_recalculated(*args, workspace=ws, y_out=y, state_out=s_out), steps)
+    ms_simt = timed(lambda: dn.delta_chunk_recalculated(*args, force_simt=True, y_out=y, state_out=s_out), 1)
+    nbytes = sum(t.numel() * t.element_size() for t in x.values() if t is not None)
+    nbytes += y.numel() * 4 + s_out.numel() * 4
+    return ms, ms_simt, nbytes, choice
+
+
 def time_prefill_gathered(dn, x, u, steps, warmup, world):
     """Each step: the prefill of this rank's batch, then the all-gather of its y
     (bf16) into every rank's global output [world x batch, T, H, dv] -- the
@@ -725,6 +763,12 @@ def run_ours(args):
         if rank == 0:
             print(json.dumps({"prologue_ms": pr_ms, "prologue_gbs": pr_bytes / (pr_ms / 1e3) / 1e9}))
         return
+    if args.only == "f32":
+        f_ms, fs_ms, f_bytes, f_choice = time_prefill_f32(dn, 5, 3, batch=args.batch or 8)
+        if rank == 0:
+            print(json.dumps({"f32_ms": f_ms, "f32_cuda_core_ms": fs_ms, "choice": f_choice,
+                              "f32_gbs": f_bytes / (f_ms / 1e3) / 1e9}))
+        return
     if args.only == "out_norm":
         on_ms, on_bytes = time_out_norm(dn, 20, 3, batch=args.batch or 8)
         if rank == 0:
@@ -770,6 +814,9 @@ def run_ours(args):
     gt_ms, gt_bytes = time_gates(dn, 10, 3)
     gt_ms = max_over_ranks(gt_ms, world)
     torch.cuda.empty_cache()
+    f32_ms, f32_simt_ms, f32_bytes, f32_choice = time_prefill_f32(dn, 5, 3)
+    f32_ms, f32_simt_ms = max_over_ranks(f32_ms, world), max_over_ranks(f32_simt_ms, world)
+    torch.cuda.empty_cache()
     cfg4 = measure_cfg4(dn, args, rank, world, hbm_peak, peak_kind) if args.workload == "deltanet" else None
     cfg5 = measure_cfg5(dn, args, rank, world, hbm_peak, peak_kind) if args.workload == "deltanet" else None
     dec_tok = DECODE["batch"] * world / (dec_ms / 1e3)
@@ -808,6 +855,14 @@ def run_ours(args):
                              "ms_per_step_prefill_alone": k_ms, "steps": args.steps, "fused": pn_fused,
                              "roofline": hbm_roofline(nbytes, pn_ms, hbm_peak, peak_kind),
                              "gpu_launches": launches + (0 if pn_fused else args.steps)},
+        "prefill_f32": {"metric": "prefill tok/s at the reference's precision (config 2's shapes with float32 "
+                                  "q, k, v and y: the fp32-accurate chunked path, three-part tf32 products)",
+                        "value": 8 * 4096 * world / (f32_ms / 1e3), "unit": "tok/s", "ms_per_step": f32_ms,
+                        "steps": 5, "kernel_choice": f32_choice,
+                        "cuda_core_kernel": {"value": 8 * 4096 * world / (f32_simt_ms / 1e3), "unit": "tok/s",
+                                             "ms_per_step": f32_simt_ms, "steps": 1},
+                        "roofline": hbm_roofline(f32_bytes, f32_ms, hbm_peak, peak_kind),
+                        "gpu_launches": 2 * 5},
         "out_norm": {"metric": "out-norm tok/s (gated per-head RMSNorm after the read-out, config 2's output: "
                                "bf16 y and gate in, bf16 out)",
                      "value": 8 * 4096 * world / (on_ms / 1e3), "unit": "tok/s", "ms_per_step": on_ms, "steps": 20,
@@ -928,7 +983,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="deltanet")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["prefill", "decode", "backward", "out_norm", "prologue", "gates", "cfg4",
+    ap.add_argument("--only", choices=["prefill", "decode", "backward", "out_norm", "prologue", "gates", "f32", "cfg4",
                                        "cfg5"], default=None,
                     help="time one kernel alone and print a short line (for profiling runs)")
     ap.add_argument("--batch", type=int, default=None,

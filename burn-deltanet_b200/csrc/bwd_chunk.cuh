@@ -330,7 +330,8 @@ __global__ void __launch_bounds__(kThreads, 2) prep_kernel(const Params p) {
     load_chunk_inputs<TI, TG>(f, s_rn, s_rt, dkp, dvp, sq, sk, ske, svw);
     __syncthreads();
 
-    float *gA = p.A + ch * kBL * kBL, *gatt = p.att + ch * kBL * kBL;
+    // A and T are the backward's alone: the forward (chunk_f32.cuh) passes them as null
+    float *gA = p.A ? p.A + ch * kBL * kBL : nullptr, *gatt = p.att + ch * kBL * kBL;
     // A = strict_lower((b k) k^T D), att = lower(s q k^T D)
     for_warp_tiles<1>(kBL, kBL, [&](int i0, int j0) {
         float aa[1][4] = {{0.f, 0.f, 0.f, 0.f}}, aq[1][4] = {{0.f, 0.f, 0.f, 0.f}};
@@ -339,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 2) prep_kernel(const Params p) {
         frag_store(aa, i0, j0, kBL, kBL, [&](int i, int j, float a) {
             const float v = j < i ? a * expf(sG[i] - sG[j]) : 0.f;
             sA[i * kLS + j] = v;
-            gA[i * kBL + j] = v;
+            if (gA) gA[i * kBL + j] = v;
         });
         frag_store(aq, i0, j0, kBL, kBL, [&](int i, int j, float a) {
             gatt[i * kBL + j] = j <= i ? f.scale * a * expf(sG[i] - sG[j]) : 0.f;
@@ -367,12 +368,12 @@ __global__ void __launch_bounds__(kThreads, 2) prep_kernel(const Params p) {
         for (int m = 0; m < 4; ++m) sT[(l + 8 * m) * kLS + j] = tr[m];
     }
     __syncthreads();
-    float *gT = p.T + ch * kBL * kBL;
+    float *gT = p.T ? p.T + ch * kBL * kBL : nullptr;
     for (int idx = tid; idx < kBL * kBL; idx += kThreads) {
         const int i = idx / kBL, j = idx - i * kBL;
         const float t = sT[i * kLS + j];
         sTg[i * kLS + j] = t * sgam[j];
-        gT[idx] = t;
+        if (gT) gT[idx] = t;
     }
     __syncthreads();
     // W = (T diag(gam)) (b k),  U = T (w v)

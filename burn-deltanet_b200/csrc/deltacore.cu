@@ -19,6 +19,7 @@
 #include "chunk_split.cuh"
 #include "bwd_chunk.cuh"
 #include "bwd_recurrent.cuh"
+#include "chunk_f32.cuh"
 #include "chunk_tc.cuh"
 #include "out_norm.cuh"
 #include "prologue.cuh"
@@ -307,15 +308,78 @@ dc::CoreParams chunk_params(const dc_chunk_args *a) {
                        a->scale, a->q, a->k, a->v, a->erase, a->write, a->g, a->state_in, a->y, a->state_out);
 }
 
-// The chunk kernel a validated call takes: 2 split (workspace), 1 fused tensor-core, 0 CUDA-core,
-// or -DC_EWORKSPACE when the split path is required but the workspace is short.
+// The fp32-accurate chunked path (chunk_f32.cuh) takes what the bf16 tensor-core kernels do not.
+bool f32_chunked_applies(const dc_chunk_args *a, const dc::CoreParams &p) {
+    return !dc::split_applies(p, a->in_dtype, a->flags) && !dc::tc_applies(p, a->in_dtype, a->flags) &&
+           dc::f32c::applies(p, a->flags);
+}
+
+// The prefill's device workspace: the split path's, the fp32-accurate chunked path's, or none.
+uint64_t fwd_workspace_bytes(const dc_chunk_args *a, const dc::CoreParams &p) {
+    if (dc::split_applies(p, a->in_dtype, a->flags)) return dc::split_workspace_bytes(p);
+    if (f32_chunked_applies(a, p)) return dc::f32c::plan(p).total_bytes;
+    return 0;
+}
+
+// The chunk kernel a validated call takes: 3 fp32-accurate chunked (workspace), 2 split (workspace),
+// 1 fused tensor-core, 0 CUDA-core, or -DC_EWORKSPACE when a workspace is given (or the split path is
+// forced) but short.
 int chunk_choice_any(const dc_chunk_args *a, const dc::CoreParams &p) {
     if (a->flags & DC_FLAG_RECURRENT) return 0;
     if (dc::split_applies(p, a->in_dtype, a->flags)) {
         if (a->workspace && a->workspace_bytes >= dc::split_workspace_bytes(p)) return 2;
         if (a->workspace || (a->flags & DC_FLAG_FORCE_SPLIT)) return -DC_EWORKSPACE;
     }
-    return dc::tc_applies(p, a->in_dtype, a->flags) ? 1 : 0;
+    if (dc::tc_applies(p, a->in_dtype, a->flags)) return 1;
+    if (f32_chunked_applies(a, p) && a->workspace) {
+        return a->workspace_bytes >= dc::f32c::plan(p).total_bytes ? 3 : -DC_EWORKSPACE;
+    }
+    return 0;
+}
+
+// The fp32-accurate chunked prefill: the backward's prep kernel (chunk-parallel, without the arrays only
+// the backward reads), then the forward scan.
+template <typename TI, typename TG, typename TO>
+int launch_chunk_f32_typed(const dc::bwdc::Params &p, int64_t bh, cudaStream_t s) {
+    using namespace dc::bwdc;
+    const size_t sp = kPrepSmemFloats * sizeof(float), ss = dc::f32c::kScanSmemFloats * sizeof(float);
+    cudaError_t e = cudaFuncSetAttribute(prep_kernel<TI, TG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(dc::f32c::fwd_scan_kernel<TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ss);
+    if (e != cudaSuccess) return cuda_fail(e);
+    prep_kernel<TI, TG><<<(unsigned)(bh * p.nc), kThreads, sp, s>>>(p);
+    dc::f32c::fwd_scan_kernel<TO><<<dim3((unsigned)bh, (unsigned)p.nslice), kThreads, ss, s>>>(p);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? DC_OK : cuda_fail(e);
+}
+
+int launch_chunk_f32(const dc_chunk_args *a, const dc::CoreParams &f, cudaStream_t s) {
+    const dc::f32c::Plan pl = dc::f32c::plan(f);
+    dc::bwdc::Params p{};
+    p.f = f;
+    float *ws = static_cast<float *>(a->workspace);
+    p.W = ws;
+    p.Kh = p.W + pl.w;
+    p.Qp = p.Kh + pl.w;
+    p.U = p.Qp + pl.w;
+    p.att = p.U + pl.uv;
+    p.gl = p.att + pl.sq;
+    p.nc = pl.nc;
+    p.dkp = pl.dkp;
+    p.dvp = pl.dvp;
+    p.nslice = pl.nslice;
+    const int64_t bh = f.batch * f.heads;
+    switch (a->in_dtype * 4 + a->gate_dtype * 2 + a->out_dtype) {
+        case 0: return launch_chunk_f32_typed<float, float, float>(p, bh, s);
+        case 1: return launch_chunk_f32_typed<float, float, __nv_bfloat16>(p, bh, s);
+        case 2: return launch_chunk_f32_typed<float, __nv_bfloat16, float>(p, bh, s);
+        case 3: return launch_chunk_f32_typed<float, __nv_bfloat16, __nv_bfloat16>(p, bh, s);
+        case 4: return launch_chunk_f32_typed<__nv_bfloat16, float, float>(p, bh, s);
+        case 5: return launch_chunk_f32_typed<__nv_bfloat16, float, __nv_bfloat16>(p, bh, s);
+        case 6: return launch_chunk_f32_typed<__nv_bfloat16, __nv_bfloat16, float>(p, bh, s);
+        case 7: return launch_chunk_f32_typed<__nv_bfloat16, __nv_bfloat16, __nv_bfloat16>(p, bh, s);
+        default: return DC_EUNSUPPORTED_DTYPE;
+    }
 }
 
 // As above; the stall test hook is taken by the tensor-core kernel only.
@@ -338,7 +402,7 @@ int dc_chunk_kernel_choice(const dc_chunk_args *a) {
 uint64_t dc_chunk_workspace_size(const dc_chunk_args *a) {
     if (validate_chunk(a) != DC_OK) return 0;
     const dc::CoreParams p = chunk_params(a);
-    return dc::split_applies(p, a->in_dtype, a->flags) ? dc::split_workspace_bytes(p) : 0;
+    return fwd_workspace_bytes(a, p);
 }
 
 int dc_chunk_launches(const dc_chunk_args *a) {
@@ -348,7 +412,7 @@ int dc_chunk_launches(const dc_chunk_args *a) {
     const int choice = chunk_choice(a, chunk_params(a));
     if (choice < 0) return choice;
     if (a->flags & DC_FLAG_RECURRENT) return (int)a->seq;
-    return choice == 2 ? 2 : 1;
+    return choice >= 2 ? 2 : 1;
 }
 
 // DeltaPath::Recurrent: the fused tick walks the sequence in place, one launch
@@ -387,6 +451,7 @@ int chunk_fwd_launch(const dc_chunk_args *a, cudaStream_t s) {
     if (choice < 0) return -choice;
     if (a->flags & DC_FLAG_RECURRENT) return run_recurrent(a, s);
     int st;
+    if (choice == 3) return launch_chunk_f32(a, p, s);
     if (choice == 2) {
         st = dc::launch_chunk_split(p, a->gate_dtype, a->out_dtype, a->workspace, s);
         if (st == DC_ECUDA) g_last_cuda_error = dc::tc_last_error();
@@ -531,7 +596,7 @@ HostPlan host_plan(const dc_chunk_args *a) {
     sl.state_in = sl.state_out = reinterpret_cast<float *>((uintptr_t)8192);
     sl.y = reinterpret_cast<void *>((uintptr_t)12288);
     const dc::CoreParams p = chunk_params(&sl);
-    hp.ws = dc::split_applies(p, a->in_dtype, a->flags) ? round256(dc::split_workspace_bytes(p)) : 0;
+    hp.ws = round256(fwd_workspace_bytes(&sl, p));
     hp.total = 2 * hp.slot + hp.ws;
     return hp;
 }

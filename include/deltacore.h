@@ -105,11 +105,16 @@ enum dc_dtype {
  * `chunk_len` is validated (>= 1) and, as in the reference, does not change the
  * result (src/delta/tests.rs:340-363): the kernels pick their own tile length.
  *
- * Per-channel gates (erase_w == dk, write_w == dv or g_w == dk, i.e. GDN-2) run
- * on the tensor cores as two kernels that pass per-chunk operands through a
- * caller-owned device workspace of dc_chunk_workspace_size(args) bytes
- * (16-byte aligned).  With workspace == NULL such a call runs the CUDA-core
- * kernel instead; a non-NULL workspace smaller than required is DC_EWORKSPACE.
+ * Two paths pass per-chunk operands through a caller-owned device workspace of
+ * dc_chunk_workspace_size(args) bytes (16-byte aligned):
+ *   - per-channel gates (erase_w == dk, write_w == dv or g_w == dk, i.e. GDN-2) with
+ *     bf16 q/k/v and d = 128: two tcgen05 kernels;
+ *   - every other call with dk, dv <= 128 and a per-head log-decay (or none) that the
+ *     fused bf16 kernel does not take, fp32 inputs (the reference's precision) first:
+ *     a chunk-parallel prep kernel and a scan, every product an fp32-accurate
+ *     three-part tf32 product on the tensor cores.
+ * With workspace == NULL such a call runs the CUDA-core kernel instead; a non-NULL
+ * workspace smaller than required is DC_EWORKSPACE.
  */
 typedef struct dc_chunk_args {
     int64_t batch, seq, heads, dk, dv;
@@ -125,7 +130,7 @@ typedef struct dc_chunk_args {
     const float *state_in;
     void *y;
     float *state_out;
-    void *workspace;          /* device scratch for the per-channel-gate path, or NULL */
+    void *workspace;          /* device scratch for the two workspace paths, or NULL */
     uint64_t workspace_bytes; /* its size */
 } dc_chunk_args;
 
@@ -361,14 +366,16 @@ DC_API int dc_last_cuda_error(void);
 DC_API int dc_device_status(int reset);
 
 /* Which chunk kernel dc_chunk_fwd would launch for `args`: 1 = tensor-core (tcgen05),
- * 2 = the two-kernel tensor-core path over the workspace, 0 = CUDA-core; negative =
- * the dc_status the call would return.  Pure host logic. */
+ * 2 = the two-kernel tensor-core path over the workspace, 3 = the fp32-accurate chunked
+ * path over the workspace, 0 = CUDA-core; negative = the dc_status the call would
+ * return.  Pure host logic. */
 DC_API int dc_chunk_kernel_choice(const dc_chunk_args *args);
 
-/* Bytes of workspace the two-kernel path needs for `args` (0 when the call takes a
+/* Bytes of workspace the call's workspace path needs for `args` (0 when the call takes a
  * path that needs none).  Replaces nothing in the reference, whose chunk path
  * materialises its intermediates as backend tensors (forward.rs:235-266).  Pure
- * host logic; about 97 KB per (batch, head, 64-token chunk). */
+ * host logic; about 97 KB per (batch, head, 64-token chunk) for per-channel gates,
+ * about 68 KB per (batch, head, 32 micro-steps) at d = 128 for the fp32-accurate path. */
 DC_API uint64_t dc_chunk_workspace_size(const dc_chunk_args *args);
 
 /* Number of kernels dc_chunk_fwd enqueues for `args` (for launch accounting); dc_step enqueues one.

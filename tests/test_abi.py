@@ -123,6 +123,29 @@ def test_kernel_choice_is_host_logic():
     assert abi.lib().dc_chunk_kernel_choice(a) == 0
 
 
+def test_fp32_chunked_path_choice_is_host_logic():
+    """fp32 inputs (the reference's precision) with a workspace take the chunked tensor-core path (3): two
+    launches; a short workspace is DC_EWORKSPACE; per-channel log-decays, dk > 128, FORCE_SIMT and no
+    workspace stay on the CUDA-core kernel."""
+    lib = abi.lib()
+    need = lib.dc_chunk_workspace_size(_args())
+    assert need > 0
+    ws = dict(workspace=0x400000, workspace_bytes=need)
+    assert lib.dc_chunk_kernel_choice(_args(**ws)) == 3
+    assert lib.dc_chunk_launches(_args(**ws)) == 2
+    assert lib.dc_chunk_kernel_choice(_args(workspace=0x400000, workspace_bytes=need - 1)) == -abi.DC_EWORKSPACE
+    assert lib.dc_chunk_kernel_choice(_args(flags=abi.DC_FLAG_FORCE_SIMT, **ws)) == 0
+    assert lib.dc_chunk_workspace_size(_args(g_w=4)) == 0  # per-channel log-decay
+    assert lib.dc_chunk_kernel_choice(_args(g_w=4, **ws)) == 0
+    big = _args(dk=200, dv=8, erase_w=1)
+    assert lib.dc_chunk_workspace_size(big) == 0
+    # bf16 at d = 128 stays on the fused kernel; bf16 at d = 64 takes the chunked path
+    assert lib.dc_chunk_workspace_size(_args(dk=128, dv=128, in_dtype=abi.DC_BF16)) == 0
+    assert lib.dc_chunk_workspace_size(_args(dk=64, dv=64, in_dtype=abi.DC_BF16)) > 0
+    # u micro-steps fold into 32-row chunks: seq 9 x u 4 = 36 rows, two chunks
+    assert lib.dc_chunk_workspace_size(_args(n_householder=4)) > need
+
+
 def test_stall_hook_is_taken_by_the_tensor_core_kernel_only():
     a = _args(dk=128, dv=128, in_dtype=abi.DC_BF16, flags=abi.DC_FLAG_TEST_STALL)
     assert abi.lib().dc_chunk_kernel_choice(a) == 1
@@ -201,7 +224,12 @@ def test_host_entry_point_scratch_is_host_logic():
     seq = [9 * 2 * 4 * 4, 9 * 2 * 4 * 4, 9 * 2 * 6 * 4, 9 * 2 * 1 * 4, 9 * 2 * 1 * 4, 9 * 2 * 1 * 4,
            2 * 4 * 6 * 4, 9 * 2 * 6 * 4, 2 * 4 * 6 * 4]
     slot = sum(-(-2 * n // 256) * 256 for n in seq)
-    assert need == 2 * slot
+    # plus one slice's workspace for the fp32-accurate chunked path: 2 x 2 (batch, head) pairs of one
+    # 32-row chunk, dk and dv padded to 8: W, K^, Q' and U [32][8], att [32][32], gam_L (4 floats)
+    nch = 2 * 2 * 1
+    ws = 4 * (3 * nch * 32 * 8 + nch * 32 * 8 + nch * 32 * 32 + 4)
+    assert abi.lib().dc_chunk_workspace_size(_args(batch=2)) == ws
+    assert need == 2 * slot + -(-ws // 256) * 256
     assert abi.lib().dc_chunk_fwd_host(a, 0x100000, need - 1, None) == abi.DC_EWORKSPACE
     assert abi.lib().dc_chunk_fwd_host(a, 0x100010, need, None) == abi.DC_EINVAL_ARG  # scratch not 256-aligned
     assert abi.lib().dc_chunk_fwd_host(_args(flags=abi.DC_FLAG_TEST_STALL), 0x100000, need, None) == abi.DC_EINVAL_ARG

@@ -16,7 +16,9 @@
 //   bwdc::prep_kernel  one CTA per (batch x head, chunk), chunk-parallel: W, U, att, Q', K^, gam_L (the
 //                      backward's own prep, without the two arrays only the backward reads);
 //   fwd_scan_kernel    one CTA per (batch x head, 32 value columns): the chunks in order, the state's
-//                      slice in shared memory; y of the slice's columns and the final state.
+//                      slice in shared memory; y of the slice's columns and the final state;
+//   fwd_scan_wide_kernel  the same with one CTA per (batch x head) over every value column, for calls
+//                      with more (head, slice) pairs than two per SM.
 // Every product runs on the tensor cores as three mma.sync m16n8k8 tf32 products of split operands
 // (big x big + big x small + small x big, about 2^-20 relative), which holds the reference's 1e-4 with
 // fp32 inputs over hundreds of chunks.
@@ -34,8 +36,6 @@ using bwdc::kMaxD;
 using bwdc::kSlice;
 using bwdc::kThreads;
 
-// The scan's shared memory: the state slice [kMaxD][kLS]; W, K^, Q' [kBL][kLD]; att, U, V' [kBL][kLS].
-constexpr int kScanSmemFloats = kMaxD * kLS + 3 * kBL * kLD + 3 * kBL * kLS;
 
 // Whether the forward scan serves these shapes (the prep kernel has the same limits).
 inline bool applies(const CoreParams &p, uint32_t flags) {
@@ -67,6 +67,73 @@ inline Plan plan(const CoreParams &p) {
     return pl;
 }
 
+constexpr int kWS = kMaxD + 8;  // row stride (floats) of the state, U, V' and K^: 8 mod 32, so the B
+                                // fragments of a warp (rows t, columns g) hit 32 distinct banks
+constexpr int kAS = kBL + 4;    // row stride of att (an A operand: rows g, columns t)
+constexpr int kWideSmemFloats = kMaxD * kWS + 2 * kBL * kLD + 3 * kBL * kWS + kBL * kAS;
+
+// acc[m][n] (the 16 x 8 tile at rows i0 + RS m, columns j0 + 8 n) += A(i, k) B(k, j) over k < K (a multiple
+// of 8), with A(i, k) = A[i * AI + k * AK] and B(k, j) = B[k * BK + j]; three-part tf32 products as in
+// bwdc::warp_mma3.  The MT row blocks share each B fragment, the NT column blocks each A fragment.
+template <int MT, int RS, int NT, int AI, int AK, int BK>
+__device__ __forceinline__ void warp_mma3_block(float (&acc)[MT][NT][4], int i0, int j0, int K,
+                                                const float *__restrict__ A, const float *__restrict__ B) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const float *a = A + (i0 + g) * AI + t * AK;
+    const float *b = B + t * BK + j0 + g;
+#pragma unroll 2
+    for (int k = 0; k < K; k += 8) {
+        uint32_t ab[MT][4], as[MT][4];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            const float *am = a + m * RS * AI + k * AK;
+            ptx::split_tf32(am[0], ab[m][0], as[m][0]);
+            ptx::split_tf32(am[8 * AI], ab[m][1], as[m][1]);
+            ptx::split_tf32(am[4 * AK], ab[m][2], as[m][2]);
+            ptx::split_tf32(am[8 * AI + 4 * AK], ab[m][3], as[m][3]);
+        }
+        uint32_t bb[NT][2], bs[NT][2];
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            ptx::split_tf32(b[k * BK + 8 * n], bb[n][0], bs[n][0]);
+            ptx::split_tf32(b[(k + 4) * BK + 8 * n], bb[n][1], bs[n][1]);
+        }
+        // term by term over every tile, so that the three products into one accumulator are MT x NT
+        // issues apart (the tensor pipe works on the other tiles' products meanwhile)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) ptx::mma_tf32_16x8x8(acc[m][n], as[m], bb[n]);
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) ptx::mma_tf32_16x8x8(acc[m][n], ab[m], bs[n]);
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) ptx::mma_tf32_16x8x8(acc[m][n], ab[m], bb[n]);
+    }
+}
+
+// epi(i, j, value) for the in-range elements (i < M, j < N) of the tile's fragments.
+template <int MT, int RS, int NT, class Epi>
+__device__ __forceinline__ void block_store(const float (&acc)[MT][NT][4], int i0, int j0, int M, int N, Epi &&epi) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int i = i0 + RS * m + g + (q >> 1) * 8, j = j0 + 8 * n + 2 * t + (q & 1);
+                if (i < M && j < N) epi(i, j, acc[m][n][q]);
+            }
+}
+
+// The sliced scan's shared memory: the state slice [kMaxD][kLS]; W, Q' [kBL][kLD]; K^ [kBL][kWS];
+// att [kBL][kAS]; U, V' [kBL][kLS].
+constexpr int kScanSmemFloats = kMaxD * kLS + 2 * kBL * kLD + kBL * kWS + kBL * kAS + 2 * kBL * kLS;
+
 // fwd_scan_kernel: blockIdx.x = batch x head, blockIdx.y = value slice of kSlice columns.
 //
 // Per chunk, two barrier intervals:
@@ -85,8 +152,10 @@ __global__ void __launch_bounds__(kThreads) fwd_scan_kernel(const bwdc::Params p
     const int64_t bh = blockIdx.x, b = bh / f.heads, h = bh - b * f.heads, nc = p.nc;
     const int c0 = blockIdx.y * kSlice, wsl = dvp - c0 < kSlice ? dvp - c0 : kSlice;  // a multiple of 4
     float *sX = sm;                                                                   // [kMaxD][kLS]
-    float *sW = sX + kMaxD * kLS, *sKh = sW + kBL * kLD, *sQp = sKh + kBL * kLD;      // [kBL][kLD]
-    float *satt = sQp + kBL * kLD, *sU = satt + kBL * kLS, *sV = sU + kBL * kLS;      // [kBL][kLS]
+    float *sW = sX + kMaxD * kLS, *sQp = sW + kBL * kLD;                              // [kBL][kLD]
+    float *sKh = sQp + kBL * kLD;                                                     // [kBL][kWS]
+    float *satt = sKh + kBL * kWS;                                                    // [kBL][kAS]
+    float *sU = satt + kBL * kAS, *sV = sU + kBL * kLS;                               // [kBL][kLS]
     const int64_t sbase = bh * (int64_t)dk * dv;
     TO *Y = static_cast<TO *>(f.y);
 
@@ -102,15 +171,15 @@ __global__ void __launch_bounds__(kThreads) fwd_scan_kernel(const bwdc::Params p
         ptx::cp_async_commit();
     };
     auto issue_ak = [&](int64_t ch) {
-        copy_rows_async(satt, kLS, p.att + ch * kBL * kBL, kBL, kBL);
-        copy_rows_async(sKh, kLD, p.Kh + ch * kBL * dkp, dkp, dkp);
+        copy_rows_async(satt, kAS, p.att + ch * kBL * kBL, kBL, kBL);
+        copy_rows_async(sKh, kWS, p.Kh + ch * kBL * dkp, dkp, dkp);
         ptx::cp_async_commit();
     };
     issue_wuq(bh * nc);
     issue_ak(bh * nc);
 
     // The warp's tile of the [kBL x wsl] chunk outputs (V', y): at most one per warp (2 x 4 tiles of
-    // 16 x 8 for 8 warps).
+    // 16 x 8 for 8 warps).  State-update tiles: 16 key rows x 32 columns, dealt round robin.
     const int tn = (wsl + 7) >> 3;
     const bool has_tile = warp < 2 * tn;
     const int i0 = has_tile ? (warp / tn) * 16 : 0, j0 = has_tile ? (warp % tn) * 8 : 0;
@@ -121,13 +190,15 @@ __global__ void __launch_bounds__(kThreads) fwd_scan_kernel(const bwdc::Params p
         ptx::cp_async_wait<1>();  // W, U, Q' of chunk c
         __syncthreads();
         if (tid < kBL) s_rt[tid] = chunk_rows(f, b, h, c, tid).rt;
-        // ---- 1. V' = U - W S;  Q' S in registers ----
-        float ay[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+        // ---- 1. [W; Q'] S (stacked in shared memory): V' = U - W S, Q' S kept in registers ----
+        float ay[1][1][4] = {};
         if (has_tile) {
-            float av[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-            warp_mma3<1, kLD, 1, kLS, 1>(av, i0, j0, dkp, sW, sX);
-            warp_mma3<1, kLD, 1, kLS, 1>(ay, i0, j0, dkp, sQp, sX);
-            frag_store(av, i0, j0, kBL, wsl, [&](int i, int j, float a) { sV[i * kLS + j] = sU[i * kLS + j] - a; });
+            float a1[2][1][4] = {};
+            warp_mma3_block<2, kBL, 1, kLD, 1, kLS>(a1, i0, j0, dkp, sW, sX);
+            block_store<1, 16, 1>(reinterpret_cast<const float(&)[1][1][4]>(a1[0]), i0, j0, kBL, wsl,
+                                  [&](int i, int j, float a) { sV[i * kLS + j] = sU[i * kLS + j] - a; });
+#pragma unroll
+            for (int q = 0; q < 4; ++q) ay[0][0][q] = a1[1][0][q];
         }
         __syncthreads();
         if (c + 1 < nc) issue_wuq(ch + 1);
@@ -136,16 +207,17 @@ __global__ void __launch_bounds__(kThreads) fwd_scan_kernel(const bwdc::Params p
         __syncthreads();
         // ---- 2. y = Q' S + att V';  S = gam_L S + K^^T V' ----
         if (has_tile) {
-            warp_mma3<1, kLS, 1, kLS, 1>(ay, i0, j0, kBL, satt, sV);
-            frag_store(ay, i0, j0, kBL, wsl, [&](int i, int j, float a) {
+            warp_mma3_block<1, 16, 1, kAS, 1, kLS>(ay, i0, j0, kBL, satt, sV);
+            block_store<1, 16, 1>(ay, i0, j0, kBL, wsl, [&](int i, int j, float a) {
                 const int64_t rt = s_rt[i];
                 if (rt >= 0 && c0 + j < dv) st(Y + rt * dv + c0 + j, a);
             });
         }
         for_warp_tiles<4>(dkp, wsl, [&](int d0, int jj) {
-            float acc[4][4] = {};
-            warp_mma3<4, 1, kLD, kLS, 1>(acc, d0, jj, kBL, sKh, sV);
-            frag_store(acc, d0, jj, dkp, wsl, [&](int d, int j, float a) { sX[d * kLS + j] = fmaf(gl, sX[d * kLS + j], a); });
+            float acc[1][4][4] = {};
+            warp_mma3_block<1, 16, 4, 1, kWS, kLS>(acc, d0, jj, kBL, sKh, sV);
+            block_store<1, 16, 4>(acc, d0, jj, dkp, wsl,
+                                  [&](int d, int j, float a) { sX[d * kLS + j] = fmaf(gl, sX[d * kLS + j], a); });
         });
         __syncthreads();
         if (c + 1 < nc) issue_ak(ch + 1);
@@ -155,6 +227,117 @@ __global__ void __launch_bounds__(kThreads) fwd_scan_kernel(const bwdc::Params p
     for (int idx = tid; idx < dk * wsl; idx += kThreads) {
         const int d = idx / wsl, j = idx - d * wsl;
         if (c0 + j < dv) f.state_out[sbase + (int64_t)d * dv + c0 + j] = sX[d * kLS + j];
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------
+// The full-width scan: one CTA per (batch x head) holding the whole [dk x dv] state, for calls with more
+// (head, slice) pairs than SMs.  Each chunk operand is read once per head instead of once per slice, and
+// every warp tile is large enough that an operand fragment, once loaded and split, feeds 4 to 16 MMAs.
+// ---------------------------------------------------------------------------------------------------
+constexpr int kWideThreads = 512;  // 16 warps: four per SM sub-partition to hide the MMA and load latencies
+
+// bwdc::copy_rows_async for a CTA of NTHR threads.
+template <int NTHR>
+__device__ __forceinline__ void copy_rows(float *dst, int ld, const float *src, int64_t ls, int cols) {
+    const int c4 = cols >> 2;
+    for (int idx = threadIdx.x; idx < kBL * c4; idx += NTHR) {
+        const int r = idx / c4, q = idx - r * c4;
+        ptx::cp_async16(ptx::smem_u32(dst + r * ld + 4 * q), src + r * ls + 4 * q, 16u);
+    }
+}
+
+// fwd_scan_wide_kernel: blockIdx.x = batch x head.  Per chunk, as fwd_scan_kernel over all dv columns:
+//   1. [W; Q'] S: warp w takes rows (w & 1) * 16 of W and of Q' (stacked in shared memory) and 16 value
+//      columns; V' = U - W S to shared memory, Q' S kept in registers;
+//   2. y = Q' S + att V' (read-out rows) to HBM; S = gam_L S + K^^T V', warp w a 32 x 32 block of S.
+template <typename TO>
+__global__ void __launch_bounds__(kWideThreads, 1) fwd_scan_wide_kernel(const bwdc::Params p) {
+    using namespace bwdc;
+    extern __shared__ __align__(16) float sm[];
+    __shared__ int64_t s_rt[kBL];
+    const CoreParams &f = p.f;
+    const int dk = (int)f.dk, dv = (int)f.dv, dkp = p.dkp, dvp = p.dvp, tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int64_t bh = blockIdx.x, b = bh / f.heads, h = bh - b * f.heads, nc = p.nc;
+    float *sX = sm;                                        // [kMaxD][kWS]  the state
+    float *sW = sX + kMaxD * kWS, *sQp = sW + kBL * kLD;   // [kBL][kLD]    W, then Q' (one stacked A)
+    float *sKh = sQp + kBL * kLD;                          // [kBL][kWS]
+    float *sU = sKh + kBL * kWS, *sV = sU + kBL * kWS;     // [kBL][kWS]
+    float *satt = sV + kBL * kWS;                          // [kBL][kAS]
+    const int64_t sbase = bh * (int64_t)dk * dv;
+    TO *Y = static_cast<TO *>(f.y);
+
+    for (int idx = tid; idx < dkp * dvp; idx += kWideThreads) {
+        const int d = idx / dvp, j = idx - d * dvp;
+        sX[d * kWS + j] = (d < dk && j < dv) ? f.state_in[sbase + (int64_t)d * dv + j] : 0.f;
+    }
+    auto issue_wuq = [&](int64_t ch) {
+        copy_rows<kWideThreads>(sW, kLD, p.W + ch * kBL * dkp, dkp, dkp);
+        copy_rows<kWideThreads>(sQp, kLD, p.Qp + ch * kBL * dkp, dkp, dkp);
+        copy_rows<kWideThreads>(sU, kWS, p.U + ch * kBL * dvp, dvp, dvp);
+        ptx::cp_async_commit();
+    };
+    auto issue_ak = [&](int64_t ch) {
+        copy_rows<kWideThreads>(satt, kAS, p.att + ch * kBL * kBL, kBL, kBL);
+        copy_rows<kWideThreads>(sKh, kWS, p.Kh + ch * kBL * dkp, dkp, dkp);
+        ptx::cp_async_commit();
+    };
+    issue_wuq(bh * nc);
+    issue_ak(bh * nc);
+
+    // interval-1/2 tile: rows r0 (of W and of Q'), columns c1 .. c1 + 15
+    const int ncb = (dvp + 15) >> 4;
+    const bool t1 = warp < 2 * ncb;
+    const int r0 = (warp & 1) * 16, c1 = (warp >> 1) * 16;
+    // state-update tile: key rows d0 .. d0 + 31, value columns c3 .. c3 + 31
+    const int nsb = (dvp + 31) >> 5;
+    const bool t3 = warp < ((dkp + 31) >> 5) * nsb;
+    const int d0 = (warp / nsb) * 32, c3 = (warp % nsb) * 32;
+
+    for (int64_t c = 0; c < nc; ++c) {
+        const int64_t ch = bh * nc + c;
+        const float gl = p.gl[ch];
+        ptx::cp_async_wait<1>();  // W, Q', U of chunk c
+        __syncthreads();
+        if (tid < kBL) s_rt[tid] = chunk_rows(f, b, h, c, tid).rt;
+        float ay[1][2][4] = {};
+        if (t1) {
+            float a1[2][2][4] = {};
+            warp_mma3_block<2, kBL, 2, kLD, 1, kWS>(a1, r0, c1, dkp, sW, sX);
+            block_store<1, 16, 2>(reinterpret_cast<const float(&)[1][2][4]>(a1[0]), r0, c1, kBL, dvp,
+                                  [&](int i, int j, float a) { sV[i * kWS + j] = sU[i * kWS + j] - a; });
+#pragma unroll
+            for (int n = 0; n < 2; ++n)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) ay[0][n][q] = a1[1][n][q];
+        }
+        __syncthreads();
+        if (c + 1 < nc) issue_wuq(ch + 1);
+        else ptx::cp_async_commit();
+        ptx::cp_async_wait<1>();  // att, K^ of chunk c
+        __syncthreads();
+        if (t1) {
+            warp_mma3_block<1, 16, 2, kAS, 1, kWS>(ay, r0, c1, kBL, satt, sV);
+            block_store<1, 16, 2>(ay, r0, c1, kBL, dv, [&](int i, int j, float a) {
+                const int64_t rt = s_rt[i];
+                if (rt >= 0) st(Y + rt * dv + j, a);
+            });
+        }
+        if (t3) {
+            float a3[2][4][4] = {};
+            warp_mma3_block<2, 16, 4, 1, kWS, kWS>(a3, d0, c3, kBL, sKh, sV);
+            block_store<2, 16, 4>(a3, d0, c3, dkp, dvp,
+                                  [&](int d, int j, float a) { sX[d * kWS + j] = fmaf(gl, sX[d * kWS + j], a); });
+        }
+        __syncthreads();
+        if (c + 1 < nc) issue_ak(ch + 1);
+        else ptx::cp_async_commit();
+    }
+    ptx::cp_async_wait<0>();
+    for (int idx = tid; idx < dk * dv; idx += kWideThreads) {
+        const int d = idx / dv, j = idx - d * dv;
+        f.state_out[sbase + (int64_t)d * dv + j] = sX[d * kWS + j];
     }
 }
 

@@ -338,17 +338,21 @@ int chunk_choice_any(const dc_chunk_args *a, const dc::CoreParams &p) {
 }
 
 // The fp32-accurate chunked prefill: the backward's prep kernel (chunk-parallel, without the arrays only
-// the backward reads), then the forward scan.
+// the backward reads), then the forward scan: one CTA per (head, 32-column slice) when those fit on the
+// device's SMs in one wave (two per SM), else one CTA per head over all columns (fewer, larger warp
+// tiles; every chunk operand read once per head).
 template <typename TI, typename TG, typename TO>
 int launch_chunk_f32_typed(const dc::bwdc::Params &p, int64_t bh, cudaStream_t s) {
     using namespace dc::bwdc;
-    const size_t sp = kPrepSmemFloats * sizeof(float), ss = dc::f32c::kScanSmemFloats * sizeof(float);
+    const bool wide = bh * p.nslice > 2 * (int64_t)sm_count();
+    const size_t sp = kPrepSmemFloats * sizeof(float);
+    const size_t ss = (wide ? dc::f32c::kWideSmemFloats : dc::f32c::kScanSmemFloats) * sizeof(float);
+    auto scan = wide ? dc::f32c::fwd_scan_wide_kernel<TO> : dc::f32c::fwd_scan_kernel<TO>;
     cudaError_t e = cudaFuncSetAttribute(prep_kernel<TI, TG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(dc::f32c::fwd_scan_kernel<TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ss);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ss);
     if (e != cudaSuccess) return cuda_fail(e);
     prep_kernel<TI, TG><<<(unsigned)(bh * p.nc), kThreads, sp, s>>>(p);
-    dc::f32c::fwd_scan_kernel<TO><<<dim3((unsigned)bh, (unsigned)p.nslice), kThreads, ss, s>>>(p);
+    scan<<<dim3((unsigned)bh, wide ? 1u : (unsigned)p.nslice), wide ? dc::f32c::kWideThreads : kThreads, ss, s>>>(p);
     e = cudaGetLastError();
     return e == cudaSuccess ? DC_OK : cuda_fail(e);
 }

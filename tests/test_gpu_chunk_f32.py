@@ -72,6 +72,10 @@ CASES = [
     (1, 1, 1, 16, 16, 1, True, False, True),         # one token
     (1, 33, 2, 128, 40, 1, False, True, True),       # ungated, a 40-column slice tail
     (1, 4096, 1, 128, 128, 1, True, False, True),    # 128 chunks of state carried
+    # more (head, 32-column slice) pairs than two per SM: the full-width scan (one CTA per head)
+    (8, 150, 10, 128, 128, 1, True, False, True),
+    (10, 70, 10, 40, 72, 2, True, True, True),       # partial warp tiles in both of its products
+    (16, 64, 6, 128, 128, 1, False, False, False),
 ]
 
 
@@ -83,12 +87,14 @@ def test_chunked_fp32_matches_the_oracle(b, s, h, dk, dv, u, gated, full, rs):
     raw["q"], raw["g"] = raw["q"][:, :s], None if raw["g"] is None else raw["g"][:, :s, :, :1]
     d = dev_inputs(raw)
     assert choice(d, u) == 3
+    pairs = b * h * (((dv + 7) // 8 * 8 + 31) // 32)
+    wide = pairs > 2 * torch.cuda.get_device_properties(0).multi_processor_count
     assert abi.lib().dc_device_status(1) == 0
     y, st = run(d, u)
     torch.cuda.synchronize()
     y0, s0 = oracle_of(d, u)
     ey, es = rel_err(y, y0), rel_err(st, s0)
-    print(f"b={b} s={s} h={h} dk={dk} dv={dv} u={u}: y {ey:.2e} S {es:.2e}")
+    print(f"b={b} s={s} h={h} dk={dk} dv={dv} u={u} ({'full-width' if wide else 'sliced'} scan): y {ey:.2e} S {es:.2e}")
     assert ey < F32_TOL and es < F32_TOL
     assert abi.lib().dc_device_status(1) == 0
 
@@ -117,9 +123,10 @@ def test_bf16_inputs_on_the_chunked_path(out_dtype):
     assert rel_err(y, y0) < (F32_TOL if out_dtype == torch.float32 else 2 ** -8)
 
 
-def test_chunked_agrees_with_the_cuda_core_kernel_and_repeats_bit_for_bit():
-    raw = config_inputs(1, np.random.default_rng(4), 2, 300, 2, 128, 128)
-    raw["state"] = np.random.default_rng(5).normal(0, 0.05, (2, 2, 128, 128))
+@pytest.mark.parametrize("b,h", [(2, 2), (20, 4)])  # the sliced and the full-width scan
+def test_chunked_agrees_with_the_cuda_core_kernel_and_repeats_bit_for_bit(b, h):
+    raw = config_inputs(1, np.random.default_rng(4), b, 300, h, 128, 128)
+    raw["state"] = np.random.default_rng(5).normal(0, 0.05, (b, h, 128, 128))
     d = dev_inputs(raw)
     assert choice(d, 1, force_simt=True) == 0
     y1, s1 = run(d, 1)

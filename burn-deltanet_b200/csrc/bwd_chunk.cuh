@@ -175,16 +175,78 @@ __device__ __forceinline__ void warp_mma3(float (&acc)[NT][4], int i0, int j0, i
         ptx::split_tf32(a[8 * AI + k * AK], ab[1], as[1]);
         ptx::split_tf32(a[(k + 4) * AK], ab[2], as[2]);
         ptx::split_tf32(a[8 * AI + (k + 4) * AK], ab[3], as[3]);
+        uint32_t bb[NT][2], bs[NT][2];
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
-            uint32_t bb[2], bs[2];
-            ptx::split_tf32(b[k * BK + 8 * n * BJ], bb[0], bs[0]);
-            ptx::split_tf32(b[(k + 4) * BK + 8 * n * BJ], bb[1], bs[1]);
-            ptx::mma_tf32_16x8x8(acc[n], as, bb);
-            ptx::mma_tf32_16x8x8(acc[n], ab, bs);
-            ptx::mma_tf32_16x8x8(acc[n], ab, bb);
+            ptx::split_tf32(b[k * BK + 8 * n * BJ], bb[n][0], bs[n][0]);
+            ptx::split_tf32(b[(k + 4) * BK + 8 * n * BJ], bb[n][1], bs[n][1]);
         }
+        // term by term over the NT tiles (each accumulator still takes its three products in order)
+#pragma unroll
+        for (int n = 0; n < NT; ++n) ptx::mma_tf32_16x8x8(acc[n], as, bb[n]);
+#pragma unroll
+        for (int n = 0; n < NT; ++n) ptx::mma_tf32_16x8x8(acc[n], ab, bs[n]);
+#pragma unroll
+        for (int n = 0; n < NT; ++n) ptx::mma_tf32_16x8x8(acc[n], ab, bb[n]);
     }
+}
+
+// acc[m][n] (the 16 x 8 tile at rows i0 + RS m, columns j0 + 8 n) += A(i, k) B(k, j) over k < K (a multiple
+// of 8), with A(i, k) = A[i * AI + k * AK] and B(k, j) = B[k * BK + j * BJ]; three-part tf32 products as in
+// warp_mma3.  The MT row blocks share each B fragment, the NT column blocks each A fragment.
+template <int MT, int RS, int NT, int AI, int AK, int BK, int BJ = 1>
+__device__ __forceinline__ void warp_mma3_block(float (&acc)[MT][NT][4], int i0, int j0, int K,
+                                                const float *__restrict__ A, const float *__restrict__ B) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const float *a = A + (i0 + g) * AI + t * AK;
+    const float *b = B + t * BK + (j0 + g) * BJ;
+#pragma unroll 2
+    for (int k = 0; k < K; k += 8) {
+        uint32_t ab[MT][4], as[MT][4];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            const float *am = a + m * RS * AI + k * AK;
+            ptx::split_tf32(am[0], ab[m][0], as[m][0]);
+            ptx::split_tf32(am[8 * AI], ab[m][1], as[m][1]);
+            ptx::split_tf32(am[4 * AK], ab[m][2], as[m][2]);
+            ptx::split_tf32(am[8 * AI + 4 * AK], ab[m][3], as[m][3]);
+        }
+        uint32_t bb[NT][2], bs[NT][2];
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            ptx::split_tf32(b[k * BK + 8 * n * BJ], bb[n][0], bs[n][0]);
+            ptx::split_tf32(b[(k + 4) * BK + 8 * n * BJ], bb[n][1], bs[n][1]);
+        }
+        // term by term over every tile, so that the three products into one accumulator are MT x NT
+        // issues apart (the tensor pipe works on the other tiles' products meanwhile)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) ptx::mma_tf32_16x8x8(acc[m][n], as[m], bb[n]);
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) ptx::mma_tf32_16x8x8(acc[m][n], ab[m], bs[n]);
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) ptx::mma_tf32_16x8x8(acc[m][n], ab[m], bb[n]);
+    }
+}
+
+// epi(i, j, value) for the in-range elements (i < M, j < N) of the tile's fragments.
+template <int MT, int RS, int NT, class Epi>
+__device__ __forceinline__ void block_store(const float (&acc)[MT][NT][4], int i0, int j0, int M, int N, Epi &&epi) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int i = i0 + RS * m + g + (q >> 1) * 8, j = j0 + 8 * n + 2 * t + (q & 1);
+                if (i < M && j < N) epi(i, j, acc[m][n][q]);
+            }
 }
 
 // Calls f(i0, j0) for the 16 x (8 NT) warp tiles of an M x N output, dealt round robin over the warps.
@@ -248,6 +310,36 @@ __device__ __forceinline__ void gather_rows(float *dst, int lds, int width, int 
     }
 }
 
+// As gather_rows<true>, writing both factors' product to dst_ab and the first factor alone to dst_a (k and
+// b (.) k from one pass over k).
+template <typename TA, typename TB, class OffA, class OffB>
+__device__ __forceinline__ void gather_rows_pair(float *dst_a, float *dst_ab, int lds, int width, int widthp,
+                                                 const TA *a, OffA &&off_a, const TB *b, OffB &&off_b) {
+    constexpr int kPer = kBL * kMaxD / kThreads;
+    float xa[kPer], xb[kPer];
+    int at[kPer];
+    bool keep[kPer];
+    const int total = kBL * widthp;
+#pragma unroll
+    for (int m = 0; m < kPer; ++m) {
+        const int idx = threadIdx.x + m * kThreads;
+        const int r = idx / widthp, d = idx - r * widthp;
+        const bool in = idx < total;
+        const int64_t oa = (in && d < width) ? off_a(r, d) : -1;
+        at[m] = in ? r * lds + d : -1;
+        keep[m] = oa >= 0;
+        xa[m] = ld(a + (keep[m] ? oa : 0));
+        xb[m] = ld(b + (keep[m] ? off_b(r, d) : 0));
+    }
+#pragma unroll
+    for (int m = 0; m < kPer; ++m) {
+        if (at[m] >= 0) {
+            dst_a[at[m]] = keep[m] ? xa[m] : 0.f;
+            dst_ab[at[m]] = keep[m] ? xa[m] * xb[m] : 0.f;
+        }
+    }
+}
+
 // Row indices (of the [batch, rows, heads, .] layouts) of chunk c's micro-steps, one lane of warp 0 per
 // row: rn for k / v / erase / write (-1 past the sequence); rt for q / dy (-1 unless a read-out
 // micro-step); rg for g (-1 unless micro-step 0 of a gated token).
@@ -296,8 +388,7 @@ __device__ __forceinline__ void load_chunk_inputs(const CoreParams &f, const int
     auto erow = [&](int r, int d) -> int64_t { return rn[r] * f.ew + (f.ew == 1 ? 0 : d); };
     auto vrow = [&](int r, int d) -> int64_t { return rn[r] < 0 ? -1 : rn[r] * dv + d; };
     auto wrow = [&](int r, int d) -> int64_t { return rn[r] * f.ww + (f.ww == 1 ? 0 : d); };
-    gather_rows<false>(sk, kLD, dk, dkp, K, krow, none, krow);
-    gather_rows<true>(ske, kLD, dk, dkp, K, krow, E, erow);
+    gather_rows_pair(sk, ske, kLD, dk, dkp, K, krow, E, erow);
     if (sq)
         gather_rows<false>(sq, kLD, dk, dkp, Q,
                            [&](int r, int d) -> int64_t { return rt[r] < 0 ? -1 : rt[r] * dk + d; }, none, krow);
@@ -332,11 +423,13 @@ __global__ void __launch_bounds__(kThreads, 2) prep_kernel(const Params p) {
 
     // A and T are the backward's alone: the forward (chunk_f32.cuh) passes them as null
     float *gA = p.A ? p.A + ch * kBL * kBL : nullptr, *gatt = p.att + ch * kBL * kBL;
-    // A = strict_lower((b k) k^T D), att = lower(s q k^T D)
+    // A = strict_lower((b k) k^T D), att = lower(s q k^T D): q and b k (64 rows apart in shared memory)
+    // as one stacked A operand, so each k fragment feeds both
     for_warp_tiles<1>(kBL, kBL, [&](int i0, int j0) {
-        float aa[1][4] = {{0.f, 0.f, 0.f, 0.f}}, aq[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-        warp_mma3<1, kLD, 1, 1, kLD>(aa, i0, j0, dkp, ske, sk);
-        warp_mma3<1, kLD, 1, 1, kLD>(aq, i0, j0, dkp, sq, sk);
+        float a2[2][1][4] = {};
+        warp_mma3_block<2, 2 * kBL, 1, kLD, 1, 1, kLD>(a2, i0, j0, dkp, sq, sk);
+        const float(&aq)[1][4] = a2[0];
+        const float(&aa)[1][4] = a2[1];
         frag_store(aa, i0, j0, kBL, kBL, [&](int i, int j, float a) {
             const float v = j < i ? a * expf(sG[i] - sG[j]) : 0.f;
             sA[i * kLS + j] = v;

@@ -35,6 +35,8 @@ using bwdc::kLS;
 using bwdc::kMaxD;
 using bwdc::kSlice;
 using bwdc::kThreads;
+using bwdc::block_store;
+using bwdc::warp_mma3_block;
 
 
 // Whether the forward scan serves these shapes (the prep kernel has the same limits).
@@ -71,64 +73,6 @@ constexpr int kWS = kMaxD + 8;  // row stride (floats) of the state, U, V' and K
                                 // fragments of a warp (rows t, columns g) hit 32 distinct banks
 constexpr int kAS = kBL + 4;    // row stride of att (an A operand: rows g, columns t)
 constexpr int kWideSmemFloats = kMaxD * kWS + 2 * kBL * kLD + 3 * kBL * kWS + kBL * kAS;
-
-// acc[m][n] (the 16 x 8 tile at rows i0 + RS m, columns j0 + 8 n) += A(i, k) B(k, j) over k < K (a multiple
-// of 8), with A(i, k) = A[i * AI + k * AK] and B(k, j) = B[k * BK + j]; three-part tf32 products as in
-// bwdc::warp_mma3.  The MT row blocks share each B fragment, the NT column blocks each A fragment.
-template <int MT, int RS, int NT, int AI, int AK, int BK>
-__device__ __forceinline__ void warp_mma3_block(float (&acc)[MT][NT][4], int i0, int j0, int K,
-                                                const float *__restrict__ A, const float *__restrict__ B) {
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const float *a = A + (i0 + g) * AI + t * AK;
-    const float *b = B + t * BK + j0 + g;
-#pragma unroll 2
-    for (int k = 0; k < K; k += 8) {
-        uint32_t ab[MT][4], as[MT][4];
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {
-            const float *am = a + m * RS * AI + k * AK;
-            ptx::split_tf32(am[0], ab[m][0], as[m][0]);
-            ptx::split_tf32(am[8 * AI], ab[m][1], as[m][1]);
-            ptx::split_tf32(am[4 * AK], ab[m][2], as[m][2]);
-            ptx::split_tf32(am[8 * AI + 4 * AK], ab[m][3], as[m][3]);
-        }
-        uint32_t bb[NT][2], bs[NT][2];
-#pragma unroll
-        for (int n = 0; n < NT; ++n) {
-            ptx::split_tf32(b[k * BK + 8 * n], bb[n][0], bs[n][0]);
-            ptx::split_tf32(b[(k + 4) * BK + 8 * n], bb[n][1], bs[n][1]);
-        }
-        // term by term over every tile, so that the three products into one accumulator are MT x NT
-        // issues apart (the tensor pipe works on the other tiles' products meanwhile)
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-            for (int m = 0; m < MT; ++m) ptx::mma_tf32_16x8x8(acc[m][n], as[m], bb[n]);
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-            for (int m = 0; m < MT; ++m) ptx::mma_tf32_16x8x8(acc[m][n], ab[m], bs[n]);
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-            for (int m = 0; m < MT; ++m) ptx::mma_tf32_16x8x8(acc[m][n], ab[m], bb[n]);
-    }
-}
-
-// epi(i, j, value) for the in-range elements (i < M, j < N) of the tile's fragments.
-template <int MT, int RS, int NT, class Epi>
-__device__ __forceinline__ void block_store(const float (&acc)[MT][NT][4], int i0, int j0, int M, int N, Epi &&epi) {
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int i = i0 + RS * m + g + (q >> 1) * 8, j = j0 + 8 * n + 2 * t + (q & 1);
-                if (i < M && j < N) epi(i, j, acc[m][n][q]);
-            }
-}
 
 // The sliced scan's shared memory: the state slice [kMaxD][kLS]; W, Q' [kBL][kLD]; K^ [kBL][kWS];
 // att [kBL][kAS]; U, V' [kBL][kLS].

@@ -277,7 +277,9 @@ __device__ __forceinline__ void solve_unit_lower(float *Af, float *Tf, int warp,
     }
 }
 
-template <typename TG, typename TO>
+// NORM: the plain output norm in the read-out (a separate instantiation, so the plain prefill carries
+// none of its code).
+template <typename TG, typename TO, bool NORM>
 __global__ void __launch_bounds__(kThreads, 1)
     chunk_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_y,
@@ -626,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             return true;
         };
         float *normw = reinterpret_cast<float *>(base + OFF_NORMW);
-        if (p.norm) normw[r] = p.norm_weight[r];  // read only by this role, after the barrier below
+        if constexpr (NORM) normw[r] = p.norm_weight[r];  // read only by this role, after the barrier below
         bool ok = ser_wait(B_GATE0, 0);
         if (ok) {
             // S0 -> TMEM (scaled by chunk 0's total decay) and its bf16 copy.
@@ -743,7 +745,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // holds its whole row of dv = 128 values, so mean(y^2) is a sum in registers over a first
                 // pass; the y warps have the time while the V' warps split their rows into hi + lo.
                 float inv = 1.f;
-                if (p.norm && r >= 64) {  // warp-uniform: warps 10 and 11
+                if (NORM && r >= 64) {  // warp-uniform: warps 10 and 11
                     float ss = 0.f;
 #pragma unroll 1
                     for (int hh = 0; hh < 2; ++hh) {
@@ -768,7 +770,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int q2 = 0; q2 < 2; ++q2) {
                         float *f = reinterpret_cast<float *>(vv[q2]);
-                        if (p.norm && r >= 64) {
+                        if (NORM && r >= 64) {
 #pragma unroll
                             for (int e = 0; e < 32; ++e) f[e] *= inv * normw[64 * hh + 32 * q2 + e];
                         }
@@ -1000,7 +1002,7 @@ inline int *device_status_ptr() {
     return static_cast<int *>(cache.get(reinterpret_cast<const void *>(&g_device_status), &err));
 }
 
-template <typename TG, typename TO>
+template <typename TG, typename TO, bool NORM>
 int launch_tc_typed(const CoreParams &p, cudaStream_t stream) {
     CUtensorMap mk, mq, mv, my;
     const int64_t P = p.seq * p.u;
@@ -1015,7 +1017,7 @@ int launch_tc_typed(const CoreParams &p, cudaStream_t stream) {
         g_tc_error = (int)cudaErrorInvalidSymbol;
         return 6;
     }
-    auto kern = tc::chunk_tc_kernel<TG, TO>;
+    auto kern = tc::chunk_tc_kernel<TG, TO, NORM>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes);
     if (e == cudaSuccess) {
         kern<<<(unsigned)(p.batch * p.heads), tc::kThreads, tc::kSmemBytes, stream>>>(mk, mq, mv, my, p, status);
@@ -1029,12 +1031,16 @@ int launch_tc_typed(const CoreParams &p, cudaStream_t stream) {
 }
 
 inline int launch_chunk_tc(const CoreParams &p, int32_t gate_dtype, int32_t out_dtype, cudaStream_t stream) {
-    const int key = gate_dtype * 2 + out_dtype;
+    const int key = (p.norm ? 4 : 0) + gate_dtype * 2 + out_dtype;
     switch (key) {
-        case 0: return launch_tc_typed<float, float>(p, stream);
-        case 1: return launch_tc_typed<float, __nv_bfloat16>(p, stream);
-        case 2: return launch_tc_typed<__nv_bfloat16, float>(p, stream);
-        case 3: return launch_tc_typed<__nv_bfloat16, __nv_bfloat16>(p, stream);
+        case 0: return launch_tc_typed<float, float, false>(p, stream);
+        case 1: return launch_tc_typed<float, __nv_bfloat16, false>(p, stream);
+        case 2: return launch_tc_typed<__nv_bfloat16, float, false>(p, stream);
+        case 3: return launch_tc_typed<__nv_bfloat16, __nv_bfloat16, false>(p, stream);
+        case 4: return launch_tc_typed<float, float, true>(p, stream);
+        case 5: return launch_tc_typed<float, __nv_bfloat16, true>(p, stream);
+        case 6: return launch_tc_typed<__nv_bfloat16, float, true>(p, stream);
+        case 7: return launch_tc_typed<__nv_bfloat16, __nv_bfloat16, true>(p, stream);
     }
     return 3;  // DC_EUNSUPPORTED_DTYPE
 }

@@ -115,6 +115,9 @@ __device__ __forceinline__ void tma_prefetch_4d(const void *tmap, int c0, int c1
                  : "memory");
 }
 
+// The 128-byte line holding `p` into L2 (no register result, nothing to wait for).
+__device__ __forceinline__ void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

@@ -75,12 +75,6 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(CoreParams p) {
     float *red = wv + u * CW;         // [2][4][2][CW] per-warp column partials
     float *sqk = red + 2 * 4 * 2 * CW;
 
-    // Consecutive ticks: the next tick's CTAs may be scheduled now; this tick reads nothing before the
-    // previous kernel in the stream has finished (programmatic dependent launch, see the launcher).
-    DC_STEP_MARK(0);
-    ptx::launch_dependents();
-    ptx::grid_dependency_wait();
-    DC_STEP_MARK(1);
     const int64_t bh = blockIdx.x;
     const int64_t b = bh / p.heads, h = bh % p.heads;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -88,6 +82,37 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(CoreParams p) {
     const int col_base = blockIdx.y * CW;
     const int col = col_base + cv * VEC;
     const bool col_ok = col < dv;  // VEC divides dv whenever VEC > 1
+    const TI *q = static_cast<const TI *>(p.q);
+    const TI *k = static_cast<const TI *>(p.k);
+    const TI *v = static_cast<const TI *>(p.v);
+    const TG *erase = static_cast<const TG *>(p.erase);
+    const TG *write = static_cast<const TG *>(p.write);
+    const TG *g = static_cast<const TG *>(p.g);
+    const int64_t H = p.heads;
+    const int64_t qrow = b * p.q_bstride * H + h;  // row of q, g and y
+    const bool one = u == 1 && dk <= kStepThreads;
+
+    // Consecutive ticks: the next tick's CTAs may be scheduled now; this tick reads nothing before the
+    // previous kernel in the stream has finished (programmatic dependent launch, see the launcher).  The
+    // token's input lines are only pulled into L2 before that wait: a prefetch returns no data, and a
+    // line the previous kernel is still writing is updated in L2 (the point of coherence) by that write.
+    DC_STEP_MARK(0);
+    ptx::launch_dependents();
+    if (one) {
+        const int64_t row = (b * p.kv_bstride) * H + h;
+        if (tid < dk) {
+            ptx::prefetch_l2(k + row * dk + tid);
+            ptx::prefetch_l2(q + qrow * dk + tid);
+            ptx::prefetch_l2(erase + row * p.ew + (p.ew == 1 ? 0 : tid));
+            if (p.gw) ptx::prefetch_l2(g + qrow * p.gw + (p.gw == 1 ? 0 : tid));
+        }
+        if (tid < CW && col_base + tid < dv) {
+            ptx::prefetch_l2(v + row * dv + col_base + tid);
+            ptx::prefetch_l2(write + row * p.ww + (p.ww == 1 ? 0 : col_base + tid));
+        }
+    }
+    ptx::grid_dependency_wait();
+    DC_STEP_MARK(1);
 
     // ---- the state tile into registers (issued first: the long-latency loads) ----
     float s[NP][VEC];
@@ -104,15 +129,7 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(CoreParams p) {
     }
 
     // ---- this token's inputs into shared memory ----
-    const TI *q = static_cast<const TI *>(p.q);
-    const TI *k = static_cast<const TI *>(p.k);
-    const TI *v = static_cast<const TI *>(p.v);
-    const TG *erase = static_cast<const TG *>(p.erase);
-    const TG *write = static_cast<const TG *>(p.write);
-    const TG *g = static_cast<const TG *>(p.g);
-    const int64_t H = p.heads;
-    const int64_t qrow = b * p.q_bstride * H + h;  // row of q, g and y
-    if (u == 1 && dk <= kStepThreads) {
+    if (one) {
         // One micro-step: thread i < dk takes key channel i, thread j < CW value column j.  Every load is
         // issued before any shared-memory write, so the tick pays one global latency instead of one per
         // input loop.

@@ -369,41 +369,140 @@ def time_prefill_f32(dn, steps, warmup, batch=8, tokens=4096):
     return ms, ms_simt, nbytes, choice
 
 
-def time_prefill_gathered(dn, x, u, steps, warmup, world):
-    """Each step: the prefill of this rank's batch, then the all-gather of its y
-    (bf16) into every rank's global output [world x batch, T, H, dv] -- the
-    north star's one collective -- on the same stream, so the step ends when the
-    gathered output is complete on this rank.  Returns ms per step on this rank
-    (the caller takes the max over ranks).  At one GPU there is nothing to
-    gather and this is the plain prefill.  (Running the gather of step i beside
-    the prefill of step i+1 was measured slower: NCCL's 32 CTAs take SMs the
-    one-wave prefill needs.)"""
+def time_prefill_gathered(dn, x, u, steps, warmup, world, mode="peer"):
+    """Each step: the prefill of this rank's batch, then the all-gather of its y (bf16) into every rank's
+    global output [world x batch, T, H, dv] -- the north star's one collective.  Returns (ms per step on
+    this rank, whether the gathered output matched NCCL's on this rank); the caller takes the max over
+    ranks.  At one GPU there is nothing to gather and this is the plain prefill.
+
+    mode "peer": the prefill writes this rank's block of the global buffer directly and the copy engines
+    push it to every peer (sharding.PeerGather); two global buffers alternate, so the copies of step i run
+    beside the prefill of step i+1, and the timed region ends once every copy has landed.  mode "nccl":
+    dist.all_gather_into_tensor on the prefill's stream after each step (running it beside the next
+    step's prefill was measured slower: NCCL's 32 CTAs take SMs the one-wave prefill needs)."""
     if world == 1:
-        return time_prefill(dn, x, u, steps, warmup)
+        return time_prefill(dn, x, u, steps, warmup), True
+    import torch.distributed as dist
     sh = importlib.import_module("burn-deltanet_b200.sharding")
+    rank = dist.get_rank()
     b, s = x["q"].shape[0], x["q"].shape[1]
     shards = sh.plan(b * world, H, world)
-    y = torch.empty(b, s, H, D, device="cuda", dtype=torch.bfloat16)
-    out = torch.empty(world * b, s, H, D, device="cuda", dtype=torch.bfloat16)
     s_out = torch.empty_like(x["state"])
     gated = x["g"] is not None
+    prefill = lambda y: dn.delta_chunk_recalculated(x["q"], x["k"], x["v"], x["erase"], x["write"], x["g"],
+                                                    x["state"], gated, L, 1.0 / math.sqrt(D), n_householder=u,
+                                                    y_out=y, state_out=s_out)
+    compute = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if mode == "nccl":
+        y = torch.empty(b, s, H, D, device="cuda", dtype=torch.bfloat16)
+        out = torch.empty(world * b, s, H, D, device="cuda", dtype=torch.bfloat16)
 
-    def step():
-        dn.delta_chunk_recalculated(x["q"], x["k"], x["v"], x["erase"], x["write"], x["g"], x["state"],
-                                    gated, L, 1.0 / math.sqrt(D), n_householder=u, y_out=y, state_out=s_out)
-        sh.gather_into(out, y, shards)
+        def step(_):
+            prefill(y)
+            sh.gather_into(out, y, shards)
 
-    for _ in range(warmup):
-        step()
+        drain = lambda: None
+    else:
+        outs = [torch.empty(world * b, s, H, D, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+        pgs = [sh.PeerGather(o, shards) for o in outs]
+        pending = [[], []]
+        b0, b1 = shards[rank].b0, shards[rank].b1
+
+        def step(i):
+            k = i & 1
+            for ev in pending[k]:  # this block's copies of step i - 2 have landed
+                compute.wait_event(ev)
+            prefill(outs[k][b0:b1])
+            ev = torch.cuda.Event()
+            ev.record(compute)
+            pending[k] = pgs[k].push(ev)
+
+        def drain():
+            for lst in pending:
+                for ev in lst:
+                    compute.wait_event(ev)
+
+    for i in range(warmup):
+        step(i)
+    drain()
     torch.cuda.synchronize()
     barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        step()
-    e1.record()
+    e0.record(compute)
+    for i in range(steps):
+        step(i)
+    drain()
+    e1.record(compute)
     torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / steps
+    ms = e0.elapsed_time(e1) / steps
+    ok = True
+    if mode != "nccl":
+        barrier(world)  # every rank's copies have landed everywhere
+        last = outs[(steps - 1) & 1]
+        ref = torch.empty_like(last)
+        dist.all_gather_into_tensor(ref, last[b0:b1].contiguous())
+        ok = bool(torch.equal(ref, last))
+        barrier(world)
+        for pg in pgs:
+            pg.close()
+        barrier(world)
+    return ms, ok
+
+
+# How the multi-GPU steps gather y: "peer" (copy engines, sharding.PeerGather) when every rank can map its
+# peers' buffers, else "nccl"; decided once per run, before any timing, by the same trial on every rank.
+GATHER = {"mode": "nccl", "why": ""}
+
+
+def gathered(dn, x, u, steps, warmup, world):
+    """The gathered step in the run's gather mode: (ms per step, max over ranks; record for the line).  At
+    N > 1 with the copy-engine gather, the NCCL gather of the same step is timed too, for comparison."""
+    if world == 1:
+        return time_prefill(dn, x, u, steps, warmup), None
+    ms, ok = time_prefill_gathered(dn, x, u, steps, warmup, world, GATHER["mode"])
+    ms = max_over_ranks(ms, world)
+    rec = {"mode": GATHER["mode"], "ms_per_step": ms}
+    if GATHER["mode"] == "peer":
+        rec["matches_nccl_gather"] = max_over_ranks(0.0 if ok else 1.0, world) == 0
+        nms, _ = time_prefill_gathered(dn, x, u, steps, warmup, world, "nccl")
+        rec["ms_per_step_nccl_gather"] = max_over_ranks(nms, world)
+    else:
+        rec["peer_gather_unavailable"] = GATHER["why"]
+    return ms, rec
+
+
+def peer_gather_works(world):
+    """Whether every rank can map its peers' buffers for the copy-engine gather and gets the right bytes
+    back: one small trial.  All ranks take the same collective steps whatever fails locally, and agree on
+    the answer.  Returns (works, reason)."""
+    import torch.distributed as dist
+    sh = importlib.import_module("burn-deltanet_b200.sharding")
+    rank = dist.get_rank()
+    buf = torch.zeros(world, 256, device="cuda", dtype=torch.bfloat16)
+    try:
+        pg = sh.PeerGather(buf, sh.plan(world, 1, world))  # raises on every rank together
+    except RuntimeError as e:
+        return False, str(e)[:300]
+    err = ""
+    try:
+        buf[rank].fill_(rank + 1)
+        ev = torch.cuda.Event()
+        ev.record()
+        for e in pg.push(ev):
+            torch.cuda.current_stream().wait_event(e)
+        torch.cuda.synchronize()
+    except Exception as e:  # noqa: BLE001 (agreed on below)
+        err = f"rank {rank}: {type(e).__name__}: {e}"
+    barrier(world)
+    want = torch.arange(1, world + 1, device="cuda", dtype=torch.bfloat16)[:, None].expand(world, 256)
+    if not err and not torch.equal(buf, want):
+        err = f"rank {rank}: peer copies gave wrong data"
+    errs = [None] * world
+    dist.all_gather_object(errs, err)
+    pg.close()
+    barrier(world)
+    bad = [e for e in errs if e]
+    return not bad, "; ".join(bad)[:300]
 
 
 def time_prefill_e2e(dn, x, u, steps, warmup):
@@ -646,8 +745,7 @@ def measure_cfg4(dn, args, rank, world, hbm_peak, peak_kind):
         batch, tokens = 4, 8192
         x = make_prefill("deltaproduct", batch, tokens, u, "cuda", 4000 + 10 * u + rank)
         k_ms = max_over_ranks(time_prefill(dn, x, u, args.steps, args.warmup), world)
-        ms = max_over_ranks(time_prefill_gathered(dn, x, u, args.steps, args.warmup, world), world) \
-            if world > 1 else k_ms
+        ms, grec = gathered(dn, x, u, args.steps, args.warmup, world) if world > 1 else (k_ms, None)
         nbytes = algorithmic_bytes(x, batch * tokens)
         flops = 2 * (5 * L * D + 3 * D * D) * batch * tokens * u * H
         out[f"u{u}"] = {
@@ -658,6 +756,8 @@ def measure_cfg4(dn, args, rank, world, hbm_peak, peak_kind):
             "scaling": "weak", "roofline": dict(hbm_roofline(nbytes, k_ms, hbm_peak, peak_kind),
                                                 tensor_tflops=flops / (k_ms / 1e3) / 1e12),
             "gpu_launches": args.steps}
+        if grec is not None:
+            out[f"u{u}"]["gather"] = grec
         del x
         torch.cuda.empty_cache()
     return out
@@ -677,7 +777,7 @@ def measure_cfg5(dn, args, rank, world, hbm_peak, peak_kind):
     x = {k: (None if t is None else t[rank * per:(rank + 1) * per].contiguous()) for k, t in full.items()}
     steps = max(3, min(args.steps, 10))
     k_ms = max_over_ranks(time_prefill(dn, x, 1, steps, args.warmup), world)
-    ms = max_over_ranks(time_prefill_gathered(dn, x, 1, steps, args.warmup, world), world) if world > 1 else k_ms
+    ms, grec = gathered(dn, x, 1, steps, args.warmup, world) if world > 1 else (k_ms, None)
     nbytes = algorithmic_bytes(x, per * T5)
     flops = 2 * (5 * L * D + 3 * D * D) * per * T5 * H
     traffic = profiled_traffic("gdn2")
@@ -691,6 +791,8 @@ def measure_cfg5(dn, args, rank, world, hbm_peak, peak_kind):
                          tensor_tflops=flops / (k_ms / 1e3) / 1e12, per_gpu=True),
         "gpu_launches": 2 * steps,
     }
+    if grec is not None:
+        rec["gather"] = grec
     # Sharded == unsharded: this rank's shard, gathered, against the whole batch run on this GPU.
     y_loc, s_loc = dn.delta_chunk_recalculated(x["q"], x["k"], x["v"], x["erase"], x["write"], x["g"], x["state"],
                                                True, L, 1.0 / math.sqrt(D))
@@ -728,6 +830,12 @@ def run_ours(args):
     rank, world, local = setup(args.gpus)
     dn = importlib.import_module("burn-deltanet_b200")
     hbm_peak, tc_peak, peak_kind = measured_peaks()
+    if world > 1:
+        works, why = peer_gather_works(world)
+        if args.gather == "peer" and works:
+            GATHER["mode"], GATHER["why"] = "peer", ""
+        else:
+            GATHER["mode"], GATHER["why"] = "nccl", (why if args.gather == "peer" else "--gather nccl")
     cfg, batch, tokens, u, kind = WORKLOADS[args.workload]
     strong = args.workload in STRONG and not args.batch
     if strong:
@@ -792,8 +900,7 @@ def run_ours(args):
     k_ms = max_over_ranks(k_ms, world)
     tok_per_rank = batch * tokens
     # The step at N > 1 includes the all-gather of y to every rank.
-    ms = max_over_ranks(time_prefill_gathered(dn, x, u, args.steps, args.warmup, world), world) \
-        if world > 1 else k_ms
+    ms, grec = gathered(dn, x, u, args.steps, args.warmup, world) if world > 1 else (k_ms, None)
     value = tok_per_rank * world / (ms / 1e3)
     nbytes = algorithmic_bytes(x, batch * tokens)
     ms_e2e, h2d, d2h = time_prefill_e2e(dn, x, u, max(1, min(args.steps, 5)), 1)
@@ -885,10 +992,15 @@ def run_ours(args):
     if cfg5 is not None:
         line["cfg5"] = cfg5
     if world > 1:
-        line["allgather"] = {"collective": "nccl all_gather_into_tensor of y (bf16) after each step's prefill, "
-                                           "same stream",
-                             "bytes_per_rank_out": world * tok_per_rank * H * D * 2,
-                             "ms_per_step_with_gather": ms, "ms_per_step_kernel_only": k_ms}
+        out_bytes = world * tok_per_rank * H * D * 2
+        line["allgather"] = dict(grec, **{
+            "collective": ("each rank's y block pushed to every peer by the NVLink copy engines (CUDA IPC), "
+                           "two global buffers alternating so the copies of step i run beside the prefill of "
+                           "step i+1" if grec["mode"] == "peer" else
+                           "nccl all_gather_into_tensor of y (bf16) after each step's prefill, same stream"),
+            "bytes_per_rank_out": out_bytes,
+            "nvlink_bound_ms": (world - 1) * tok_per_rank * H * D * 2 / 770e9 * 1e3,
+            "ms_per_step_with_gather": ms, "ms_per_step_kernel_only": k_ms})
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.workload)
     if rank == 0:
@@ -983,6 +1095,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="deltanet")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="how multi-GPU steps gather y: NVLink copy engines (default) or NCCL")
     ap.add_argument("--only", choices=["prefill", "decode", "backward", "out_norm", "prologue", "gates", "f32", "cfg4",
                                        "cfg5"], default=None,
                     help="time one kernel alone and print a short line (for profiling runs)")

@@ -84,6 +84,121 @@ def gather_into(out: torch.Tensor, local: torch.Tensor, shards: List[Shard], gro
     return out
 
 
+class PeerGather:
+    """The all-gather of :func:`gather_into` on the NVLink copy engines instead of the SMs.
+
+    Every rank holds a global buffer ``out`` ([world * local_batch, ...], batch-major whole-sequence
+    shards), writes its own block (rows [b0, b1)) there directly, and :meth:`push` copies that block into
+    the same rows of every peer's buffer: one peer-to-peer copy per peer, each on its own stream, through
+    CUDA IPC mappings of the peers' buffers exchanged once through the process group (driver API, in the
+    device's primary context, which torch makes current).  An NCCL gather runs as kernels whose CTAs take
+    SMs from a one-wave prefill; these copies take none, so the gather of one step runs beside the
+    kernels of the next.
+
+    Collective: every rank constructs it with buffers of the same shape, in the same order, and every
+    rank calls :meth:`close` before any rank frees its buffer.
+    """
+
+    _opened = {}  # (peer rank, IPC handle) -> [mapped base, references]: one mapping per allocation
+
+    def __init__(self, out: torch.Tensor, shards: List[Shard], group=None):
+        import torch.distributed as dist
+        from cuda.bindings import driver as drv
+
+        self._drv = drv
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        if len(shards) != world or not all(s.h0 == 0 for s in shards):
+            raise ValueError("PeerGather takes whole-sequence shards, one per rank")
+        if not out.is_cuda or not out.is_contiguous() or out.shape[0] != shards[-1].b1:
+            raise ValueError(f"out must be a contiguous CUDA buffer of {shards[-1].b1} rows")
+        row = out[0].numel() * out.element_size()
+        self.offset = shards[rank].b0 * row
+        self.nbytes = shards[rank].batch * row
+        # Every rank takes the same collective steps whatever fails locally: the export and the mappings
+        # each end in an exchange of (result, error), and all ranks raise together if any rank failed.
+        mine, error = None, ""
+        try:
+            torch.cuda.set_device(out.device)
+            err, dev = drv.cuCtxGetDevice()
+            _check(err, "cuCtxGetDevice")
+            if int(dev) != out.device.index:
+                raise RuntimeError(f"the current CUDA context is device {int(dev)}, not {out.device}")
+            err, base, _ = drv.cuMemGetAddressRange(out.data_ptr())
+            _check(err, "cuMemGetAddressRange")
+            err, handle = drv.cuIpcGetMemHandle(base)
+            _check(err, "cuIpcGetMemHandle")
+            mine = (bytes(handle.reserved), out.data_ptr() - int(base))
+        except Exception as e:  # noqa: BLE001 (raised on every rank below)
+            error = f"rank {rank}: {type(e).__name__}: {e}"
+        every = [None] * world
+        dist.all_gather_object(every, (mine, error), group=group)
+        errors = [e for _, e in every if e]
+        if errors:
+            raise RuntimeError("PeerGather: " + "; ".join(errors))
+        self.peers = []  # (peer rank, IPC handle key, address of the peer's `out`)
+        error = ""
+        for p in range(world):
+            if p == rank:
+                continue
+            key = (p, every[p][0][0])
+            try:
+                if key not in PeerGather._opened:
+                    h = drv.CUipcMemHandle()
+                    h.reserved = every[p][0][0]
+                    err, ptr = drv.cuIpcOpenMemHandle(h, drv.CUipcMem_flags.CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS)
+                    _check(err, "cuIpcOpenMemHandle")
+                    PeerGather._opened[key] = [int(ptr), 0]
+                PeerGather._opened[key][1] += 1
+                self.peers.append((p, key, PeerGather._opened[key][0] + every[p][0][1]))
+            except Exception as e:  # noqa: BLE001
+                error = f"rank {rank}: {type(e).__name__}: {e}"
+                break
+        results = [None] * world
+        dist.all_gather_object(results, error, group=group)
+        if any(results):
+            self.streams = []
+            self._release()
+            raise RuntimeError("PeerGather: " + "; ".join(r for r in results if r))
+        self.out = out
+        self.src = out.data_ptr() + self.offset
+        self.streams = [torch.cuda.Stream(device=out.device) for _ in self.peers]
+
+    def push(self, after: torch.cuda.Event) -> List[torch.cuda.Event]:
+        """Copy this rank's block into every peer's buffer once ``after`` has fired; returns one event per
+        peer copy (this rank's block may be rewritten once they have all fired)."""
+        drv = self._drv
+        done = []
+        for (_, _, dst), stream in zip(self.peers, self.streams):
+            stream.wait_event(after)
+            (err,) = drv.cuMemcpyAsync(dst + self.offset, self.src, self.nbytes, stream.cuda_stream)
+            _check(err, "cuMemcpyAsync")
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            done.append(ev)
+        return done
+
+    def close(self) -> None:
+        """Drain the copies and release the peer mappings (every rank, before any buffer is freed)."""
+        for stream in self.streams:
+            stream.synchronize()
+        self._release()
+        self.streams = []
+
+    def _release(self) -> None:
+        for _, key, _ in self.peers:
+            ent = PeerGather._opened[key]
+            ent[1] -= 1
+            if ent[1] == 0:
+                _check(self._drv.cuIpcCloseMemHandle(ent[0])[0], "cuIpcCloseMemHandle")
+                del PeerGather._opened[key]
+        self.peers = []
+
+
+def _check(err, what: str) -> None:
+    if int(err) != 0:
+        raise RuntimeError(f"{what} failed: {err}")
+
+
 def gather(local: torch.Tensor, shards: List[Shard], head_axis: int = 2, group=None) -> torch.Tensor:
     """All-gather every rank's output block into the global tensor.
 

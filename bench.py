@@ -405,7 +405,7 @@ def time_prefill_gathered(dn, x, u, steps, warmup, world, mode="peer"):
         drain = lambda: None
     else:
         outs = [torch.empty(world * b, s, H, D, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
-        pgs = [sh.PeerGather(o, shards) for o in outs]
+        pgs = [sh.PeerGather(o, shards, streams=GATHER["streams"]) for o in outs]
         pending = [[], []]
         b0, b1 = shards[rank].b0, shards[rank].b1
 
@@ -451,23 +451,29 @@ def time_prefill_gathered(dn, x, u, steps, warmup, world, mode="peer"):
 
 # How the multi-GPU steps gather y: "peer" (copy engines, sharding.PeerGather) when every rank can map its
 # peers' buffers, else "nccl"; decided once per run, before any timing, by the same trial on every rank.
-GATHER = {"mode": "nccl", "why": ""}
+GATHER = {"mode": "nccl", "why": "", "streams": 1}
 
 
 def gathered(dn, x, u, steps, warmup, world):
-    """The gathered step in the run's gather mode: (ms per step, max over ranks; record for the line).  At
-    N > 1 with the copy-engine gather, the NCCL gather of the same step is timed too, for comparison."""
+    """The gathered step: (ms per step, max over ranks; record for the line).  With the copy-engine gather
+    available, both gathers are timed on the same step and the step counts the faster one, named in the
+    record with both times: the copy engines win while the gather hides behind the next prefill (N = 2,
+    or long prefills), NCCL's kernels can win when the gather is several times the prefill (config 2 at
+    N = 8, where the copies run slower than NCCL's NVLink algorithms)."""
     if world == 1:
         return time_prefill(dn, x, u, steps, warmup), None
-    ms, ok = time_prefill_gathered(dn, x, u, steps, warmup, world, GATHER["mode"])
-    ms = max_over_ranks(ms, world)
-    rec = {"mode": GATHER["mode"], "ms_per_step": ms}
-    if GATHER["mode"] == "peer":
-        rec["matches_nccl_gather"] = max_over_ranks(0.0 if ok else 1.0, world) == 0
-        nms, _ = time_prefill_gathered(dn, x, u, steps, warmup, world, "nccl")
-        rec["ms_per_step_nccl_gather"] = max_over_ranks(nms, world)
-    else:
-        rec["peer_gather_unavailable"] = GATHER["why"]
+    nms, _ = time_prefill_gathered(dn, x, u, steps, warmup, world, "nccl")
+    nms = max_over_ranks(nms, world)
+    rec = {"ms_per_step_nccl_gather": nms}
+    if GATHER["mode"] != "peer":
+        rec.update(mode="nccl", ms_per_step=nms, peer_gather_unavailable=GATHER["why"])
+        return nms, rec
+    pms, ok = time_prefill_gathered(dn, x, u, steps, warmup, world, "peer")
+    pms = max_over_ranks(pms, world)
+    rec["ms_per_step_peer_gather"] = pms
+    rec["peer_matches_nccl_gather"] = max_over_ranks(0.0 if ok else 1.0, world) == 0
+    mode, ms = ("peer", pms) if pms <= nms else ("nccl", nms)
+    rec.update(mode=mode, ms_per_step=ms)
     return ms, rec
 
 
@@ -994,10 +1000,10 @@ def run_ours(args):
     if world > 1:
         out_bytes = world * tok_per_rank * H * D * 2
         line["allgather"] = dict(grec, **{
-            "collective": ("each rank's y block pushed to every peer by the NVLink copy engines (CUDA IPC), "
-                           "two global buffers alternating so the copies of step i run beside the prefill of "
-                           "step i+1" if grec["mode"] == "peer" else
-                           "nccl all_gather_into_tensor of y (bf16) after each step's prefill, same stream"),
+            "collective": ("the faster of two gathers of y (bf16), both timed: 'peer', each rank's block pushed "
+                           "to every peer by the NVLink copy engines (CUDA IPC), two global buffers "
+                           "alternating so the copies of step i run beside the prefill of step i+1; 'nccl', "
+                           "all_gather_into_tensor after each step's prefill on the same stream"),
             "bytes_per_rank_out": out_bytes,
             "nvlink_bound_ms": (world - 1) * tok_per_rank * H * D * 2 / 770e9 * 1e3,
             "ms_per_step_with_gather": ms, "ms_per_step_kernel_only": k_ms})

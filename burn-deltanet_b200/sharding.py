@@ -89,7 +89,7 @@ class PeerGather:
 
     Every rank holds a global buffer ``out`` ([world * local_batch, ...], batch-major whole-sequence
     shards), writes its own block (rows [b0, b1)) there directly, and :meth:`push` copies that block into
-    the same rows of every peer's buffer: one peer-to-peer copy per peer, each on its own stream, through
+    the same rows of every peer's buffer: one peer-to-peer copy per peer, in ring order on one stream, through
     CUDA IPC mappings of the peers' buffers exchanged once through the process group (driver API, in the
     device's primary context, which torch makes current).  An NCCL gather runs as kernels whose CTAs take
     SMs from a one-wave prefill; these copies take none, so the gather of one step runs beside the
@@ -101,7 +101,7 @@ class PeerGather:
 
     _opened = {}  # (peer rank, IPC handle) -> [mapped base, references]: one mapping per allocation
 
-    def __init__(self, out: torch.Tensor, shards: List[Shard], group=None):
+    def __init__(self, out: torch.Tensor, shards: List[Shard], group=None, streams: int = 1):
         import torch.distributed as dist
         from cuda.bindings import driver as drv
 
@@ -156,22 +156,32 @@ class PeerGather:
         results = [None] * world
         dist.all_gather_object(results, error, group=group)
         if any(results):
-            self.streams = []
+            self.streams, self._pool = [], []
             self._release()
             raise RuntimeError("PeerGather: " + "; ".join(r for r in results if r))
+        # Peers in ring order from this rank (rank + 1, rank + 2, ...), so that ranks copying in step
+        # send to different peers at any moment; `streams` copy streams (0: one per peer) take the peers
+        # round robin, each stream's copies in that order.  One stream measured fastest: config 2 at
+        # N = 8, 1.71 ms per gathered step against 2.09 (2 streams), 2.22 (4) and 2.23 (7), and 1.95
+        # with NCCL's gather.
+        self.peers.sort(key=lambda e: (e[0] - rank) % world)
         self.out = out
         self.src = out.data_ptr() + self.offset
-        self.streams = [torch.cuda.Stream(device=out.device) for _ in self.peers]
+        n = len(self.peers) if streams <= 0 else min(streams, len(self.peers))
+        self._pool = [torch.cuda.Stream(device=out.device) for _ in range(n)]
+        self.streams = [self._pool[i % n] for i in range(len(self.peers))] if n else []
 
     def push(self, after: torch.cuda.Event) -> List[torch.cuda.Event]:
         """Copy this rank's block into every peer's buffer once ``after`` has fired; returns one event per
-        peer copy (this rank's block may be rewritten once they have all fired)."""
+        copy stream (this rank's block may be rewritten once they have all fired)."""
         drv = self._drv
-        done = []
-        for (_, _, dst), stream in zip(self.peers, self.streams):
+        for stream in self._pool:
             stream.wait_event(after)
+        for (_, _, dst), stream in zip(self.peers, self.streams):
             (err,) = drv.cuMemcpyAsync(dst + self.offset, self.src, self.nbytes, stream.cuda_stream)
             _check(err, "cuMemcpyAsync")
+        done = []
+        for stream in self._pool:
             ev = torch.cuda.Event()
             ev.record(stream)
             done.append(ev)
@@ -179,10 +189,10 @@ class PeerGather:
 
     def close(self) -> None:
         """Drain the copies and release the peer mappings (every rank, before any buffer is freed)."""
-        for stream in self.streams:
+        for stream in getattr(self, "_pool", []):
             stream.synchronize()
         self._release()
-        self.streams = []
+        self.streams, self._pool = [], []
 
     def _release(self) -> None:
         for _, key, _ in self.peers:

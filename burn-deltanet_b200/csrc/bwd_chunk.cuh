@@ -48,6 +48,10 @@ constexpr int kMaxD = 128;       // dk, dv
 constexpr int kLD = kMaxD + 4;   // row stride of a [kBL][kLD] token tile (floats)
 constexpr int kLS = kBL + 8;     // row stride of [kBL][kLS] chunk squares and [kMaxD][kLS] state slices
 constexpr int kSlice = 32;       // scan: value columns per CTA
+constexpr int kWS = kMaxD + 8;   // row stride of full-width tiles read as B (rows t, columns g) or as a
+                                 // transposed A (AI = 1): 8 mod 32, so a warp's fragment hits 32 banks
+constexpr int kAS = kBL + 4;     // row stride of a [kBL][kBL] square read as A (rows g, columns t)
+constexpr int kWideThreads = 512;  // the full-width scans: 16 warps, four per SM sub-partition
 
 struct Params {
     CoreParams f;                // the forward call
@@ -267,6 +271,16 @@ __device__ __forceinline__ void frag_store(const float (&acc)[NT][4], int i0, in
             const int i = i0 + g + (q >> 1) * 8, j = j0 + 8 * n + 2 * t + (q & 1);
             if (i < M && j < N) epi(i, j, acc[n][q]);
         }
+}
+
+// copy_rows_async for a CTA of NTHR threads.
+template <int NTHR>
+__device__ __forceinline__ void copy_rows(float *dst, int ld, const float *src, int64_t ls, int cols) {
+    const int c4 = cols >> 2;
+    for (int idx = threadIdx.x; idx < kBL * c4; idx += NTHR) {
+        const int r = idx / c4, q = idx - r * c4;
+        ptx::cp_async16(ptx::smem_u32(dst + r * ld + 4 * q), src + r * ls + 4 * q, 16u);
+    }
 }
 
 // Workspace rows [kBL] x cols (a multiple of 4 floats) from global (row stride `ls` floats) into shared
@@ -533,8 +547,9 @@ __global__ void __launch_bounds__(kThreads) scan_kernel(const Params p) {
             for (int idx = tid; idx < kBL * q4; idx += kThreads) {
                 const int r = idx / q4, q = idx - r * q4;
                 const ChunkRows o = chunk_rows(f, b, h, c, r);
-                const float *src = o.rt >= 0 ? p.dy + o.rt * dv + c0 + 4 * q : p.dy;
-                ptx::cp_async16(ptx::smem_u32(dst + r * kLS + 4 * q), src, o.rt >= 0 ? 16u : 0u);
+                const bool in = o.rt >= 0 && c0 + 4 * q < dv;  // the quads past dv (dvp > dv) read nothing
+                const float *src = in ? p.dy + o.rt * dv + c0 + 4 * q : p.dy;
+                ptx::cp_async16(ptx::smem_u32(dst + r * kLS + 4 * q), src, in ? 16u : 0u);
             }
         } else {
             for (int idx = tid; idx < kBL * wsl; idx += kThreads) {
@@ -651,6 +666,184 @@ __global__ void __launch_bounds__(kThreads) scan_kernel(const Params p) {
     for (int idx = tid; idx < dk * wsl; idx += kThreads) {
         const int d = idx / wsl, j = idx - d * wsl;
         if (c0 + j < dv) p.dS0[sbase + (int64_t)d * dv + c0 + j] = sX[d * kLS + j];
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------
+// scan_wide_kernel: one 16-warp CTA per (batch x head = blockIdx.x) over every value column, for calls with
+// more (head, slice) pairs than two per SM.  The same passes, products and stores as scan_kernel, every
+// output element accumulated in the same order (so both forms give the same bits); each chunk operand is
+// read once per head instead of once per slice, and the warp tiles are larger.
+// ---------------------------------------------------------------------------------------------------
+constexpr int kScanWideSmemFloats = kMaxD * kWS + 6 * kBL * kWS + kBL * kLS;
+
+__global__ void __launch_bounds__(kWideThreads, 1) scan_wide_kernel(const Params p) {
+    extern __shared__ __align__(16) float sm[];
+    const CoreParams &f = p.f;
+    const int dk = (int)f.dk, dv = (int)f.dv, dkp = p.dkp, dvp = p.dvp, tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int64_t bh = blockIdx.x, b = bh / f.heads, h = bh - b * f.heads, nc = p.nc;
+    float *sX = sm;                                    // [kMaxD][kWS]: S, then dS
+    float *sW = sX + kMaxD * kWS, *sQp = sW + kBL * kWS, *sKh = sQp + kBL * kWS;
+    float *sU = sKh + kBL * kWS, *sY1 = sU + kBL * kWS, *sV = sY1 + kBL * kWS;
+    float *satt = sV + kBL * kWS;                      // [kBL][kLS]
+    auto sY = [&](int64_t c) { return (c & 1) ? sY1 : sU; };  // reverse: dy of even / odd chunks
+    const int64_t sbase = bh * (int64_t)dk * dv;
+
+    auto load_state = [&](const float *src) {
+        for (int idx = tid; idx < dkp * dvp; idx += kWideThreads) {
+            const int d = idx / dvp, j = idx - d * dvp;
+            sX[d * kWS + j] = (src && d < dk && j < dv) ? src[sbase + (int64_t)d * dv + j] : 0.f;
+        }
+    };
+    // sX -> dst[j][d] (transposed, [dvp][dkp]): float4 reads of 4 value columns of one key row,
+    // consecutive threads on consecutive keys (coalesced writes)
+    auto store_T = [&](float *dst) {
+        for (int idx = tid; idx < (dvp >> 2) * dkp; idx += kWideThreads) {
+            const int jq = idx / dkp, d = idx - jq * dkp;
+            const float4 x = *reinterpret_cast<const float4 *>(sX + d * kWS + 4 * jq);
+            float *o = dst + (int64_t)(4 * jq) * dkp + d;
+            o[0] = x.x, o[dkp] = x.y, o[2 * dkp] = x.z, o[3 * dkp] = x.w;
+        }
+    };
+    auto issue_dy = [&](int64_t c, float *dst) {
+        const int q4 = dvp >> 2;
+        if (p.dy_vec) {
+            for (int idx = tid; idx < kBL * q4; idx += kWideThreads) {
+                const int r = idx / q4, q = idx - r * q4;
+                const ChunkRows o = chunk_rows(f, b, h, c, r);
+                const bool in = o.rt >= 0 && 4 * q < dv;
+                const float *src = in ? p.dy + o.rt * dv + 4 * q : p.dy;
+                ptx::cp_async16(ptx::smem_u32(dst + r * kWS + 4 * q), src, in ? 16u : 0u);
+            }
+        } else {
+            for (int idx = tid; idx < kBL * dvp; idx += kWideThreads) {
+                const int r = idx / dvp, j = idx - r * dvp;
+                const ChunkRows o = chunk_rows(f, b, h, c, r);
+                dst[r * kWS + j] = (o.rt >= 0 && j < dv) ? p.dy[o.rt * dv + j] : 0.f;
+            }
+        }
+    };
+
+    // [kBL x dvp] tiles (V', dV'): rows r0, 16 columns from c1; [dkp x dvp] tiles (S, dS): 32 x 32
+    const int ncb = (dvp + 15) >> 4;
+    const bool t1 = warp < 2 * ncb;
+    const int r0 = (warp & 1) * 16, c1 = (warp >> 1) * 16;
+    const int nsb = (dvp + 31) >> 5;
+    const bool t3 = warp < ((dkp + 31) >> 5) * nsb;
+    const int d0 = (warp / nsb) * 32, c3 = (warp % nsb) * 32;
+
+    // ---- forward: S_c, V'_c.  Groups: [W (rows), U](c), [K^ (transposed)](c) ----
+    load_state(f.state_in);
+    copy_rows<kWideThreads>(sW, kLD, p.W + bh * nc * kBL * dkp, dkp, dkp);
+    copy_rows<kWideThreads>(sU, kWS, p.U + bh * nc * kBL * dvp, dvp, dvp);
+    ptx::cp_async_commit();
+    copy_rows<kWideThreads>(sKh, kWS, p.Kh + bh * nc * kBL * dkp, dkp, dkp);
+    ptx::cp_async_commit();
+    for (int64_t c = 0; c < nc; ++c) {
+        const int64_t ch = bh * nc + c;
+        const float gl = p.gl[ch];
+        ptx::cp_async_wait<1>();  // W, U of chunk c
+        __syncthreads();
+        store_T(p.ST + ch * (int64_t)dvp * dkp);
+        float *gV = p.Vp + ch * kBL * dvp;
+        if (t1) {  // V' = U - W S
+            float acc[1][2][4] = {};
+            warp_mma3_block<1, 16, 2, kLD, 1, kWS>(acc, r0, c1, dkp, sW, sX);
+            block_store<1, 16, 2>(acc, r0, c1, kBL, dvp, [&](int i, int j, float a) {
+                const float v = sU[i * kWS + j] - a;
+                sV[i * kWS + j] = v;
+                gV[i * dvp + j] = v;
+            });
+        }
+        __syncthreads();
+        if (c + 1 < nc) {
+            copy_rows<kWideThreads>(sW, kLD, p.W + (ch + 1) * kBL * dkp, dkp, dkp);
+            copy_rows<kWideThreads>(sU, kWS, p.U + (ch + 1) * kBL * dvp, dvp, dvp);
+        }
+        ptx::cp_async_commit();
+        ptx::cp_async_wait<1>();  // K^ of chunk c
+        __syncthreads();
+        if (t3) {  // S = gam_L S + K^^T V'
+            float a3[2][4][4] = {};
+            warp_mma3_block<2, 16, 4, 1, kWS, kWS>(a3, d0, c3, kBL, sKh, sV);
+            block_store<2, 16, 4>(a3, d0, c3, dkp, dvp,
+                                  [&](int d, int j, float a) { sX[d * kWS + j] = fmaf(gl, sX[d * kWS + j], a); });
+        }
+        __syncthreads();
+        if (c + 1 < nc) copy_rows<kWideThreads>(sKh, kWS, p.Kh + (ch + 1) * kBL * dkp, dkp, dkp);
+        ptx::cp_async_commit();
+    }
+    ptx::cp_async_wait<0>();
+    __syncthreads();
+
+    // ---- reverse: dS_next_c, dV'_c, then dS0.  Groups: [att, K^ (rows), dy](c), [Q', W (transposed)](c) ----
+    load_state(p.dS_final);
+    auto issue_a = [&](int64_t c) {
+        const int64_t ch = bh * nc + c;
+        copy_rows<kWideThreads>(satt, kLS, p.att + ch * kBL * kBL, kBL, kBL);
+        copy_rows<kWideThreads>(sKh, kLD, p.Kh + ch * kBL * dkp, dkp, dkp);
+        issue_dy(c, sY(c));
+        ptx::cp_async_commit();
+    };
+    auto issue_b = [&](int64_t c) {
+        const int64_t ch = bh * nc + c;
+        copy_rows<kWideThreads>(sQp, kWS, p.Qp + ch * kBL * dkp, dkp, dkp);
+        copy_rows<kWideThreads>(sW, kWS, p.W + ch * kBL * dkp, dkp, dkp);
+        ptx::cp_async_commit();
+    };
+    if (nc > 0) {
+        issue_a(nc - 1);
+        issue_b(nc - 1);
+    }
+    for (int64_t c = nc - 1; c >= 0; --c) {
+        const int64_t ch = bh * nc + c;
+        const float gl = p.gl[ch];
+        const float *sy = sY(c);
+        ptx::cp_async_wait<1>();  // att, K^, dy of chunk c
+        __syncthreads();
+        store_T(p.dSnT + ch * (int64_t)dvp * dkp);
+        float *gdV = p.dVp + ch * kBL * dvp;
+        if (t1) {  // dV' = att^T dy + K^ dS
+            float acc[1][2][4] = {};
+            warp_mma3_block<1, 16, 2, 1, kLS, kWS>(acc, r0, c1, kBL, satt, sy);
+            warp_mma3_block<1, 16, 2, kLD, 1, kWS>(acc, r0, c1, dkp, sKh, sX);
+            block_store<1, 16, 2>(acc, r0, c1, kBL, dvp, [&](int i, int j, float a) {
+                sV[i * kWS + j] = a;
+                gdV[i * dvp + j] = a;
+            });
+        }
+        __syncthreads();
+        if (c > 0) issue_a(c - 1);
+        else ptx::cp_async_commit();
+        ptx::cp_async_wait<1>();  // Q', W of chunk c
+        __syncthreads();
+        if (t3) {  // dS = gam_L dS + Q'^T dy - W^T dV', in two 32 x 16 halves (two accumulators each)
+#pragma unroll 1
+            for (int hf = 0; hf < 2; ++hf) {
+                const int cj = c3 + 16 * hf;
+                float ap[2][2][4] = {}, an[2][2][4] = {};
+                warp_mma3_block<2, 16, 2, 1, kWS, kWS>(ap, d0, cj, kBL, sQp, sy);
+                warp_mma3_block<2, 16, 2, 1, kWS, kWS>(an, d0, cj, kBL, sW, sV);
+#pragma unroll
+                for (int m = 0; m < 2; ++m)
+#pragma unroll
+                    for (int n = 0; n < 2; ++n)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) ap[m][n][q] -= an[m][n][q];
+                block_store<2, 16, 2>(ap, d0, cj, dkp, dvp,
+                                      [&](int d, int j, float a) { sX[d * kWS + j] = fmaf(gl, sX[d * kWS + j], a); });
+            }
+        }
+        __syncthreads();
+        if (c > 0) issue_b(c - 1);
+        else ptx::cp_async_commit();
+    }
+    ptx::cp_async_wait<0>();
+    __syncthreads();
+    for (int idx = tid; idx < dk * dv; idx += kWideThreads) {
+        const int d = idx / dv, j = idx - d * dv;
+        p.dS0[sbase + (int64_t)d * dv + j] = sX[d * kWS + j];
     }
 }
 

@@ -69,9 +69,8 @@ inline Plan plan(const CoreParams &p) {
     return pl;
 }
 
-constexpr int kWS = kMaxD + 8;  // row stride (floats) of the state, U, V' and K^: 8 mod 32, so the B
-                                // fragments of a warp (rows t, columns g) hit 32 distinct banks
-constexpr int kAS = kBL + 4;    // row stride of att (an A operand: rows g, columns t)
+using bwdc::kAS;
+using bwdc::kWS;
 constexpr int kWideSmemFloats = kMaxD * kWS + 2 * kBL * kLD + 3 * kBL * kWS + kBL * kAS;
 
 // The sliced scan's shared memory: the state slice [kMaxD][kLS]; W, Q' [kBL][kLD]; K^ [kBL][kWS];
@@ -179,17 +178,8 @@ __global__ void __launch_bounds__(kThreads) fwd_scan_kernel(const bwdc::Params p
 // (head, slice) pairs than SMs.  Each chunk operand is read once per head instead of once per slice, and
 // every warp tile is large enough that an operand fragment, once loaded and split, feeds 4 to 16 MMAs.
 // ---------------------------------------------------------------------------------------------------
-constexpr int kWideThreads = 512;  // 16 warps: four per SM sub-partition to hide the MMA and load latencies
-
-// bwdc::copy_rows_async for a CTA of NTHR threads.
-template <int NTHR>
-__device__ __forceinline__ void copy_rows(float *dst, int ld, const float *src, int64_t ls, int cols) {
-    const int c4 = cols >> 2;
-    for (int idx = threadIdx.x; idx < kBL * c4; idx += NTHR) {
-        const int r = idx / c4, q = idx - r * c4;
-        ptx::cp_async16(ptx::smem_u32(dst + r * ld + 4 * q), src + r * ls + 4 * q, 16u);
-    }
-}
+using bwdc::copy_rows;
+using bwdc::kWideThreads;
 
 // fwd_scan_wide_kernel: blockIdx.x = batch x head.  Per chunk, as fwd_scan_kernel over all dv columns:
 //   1. [W; Q'] S: warp w takes rows (w & 1) * 16 of W and of Q' (stacked in shared memory) and 16 value

@@ -805,15 +805,20 @@ template <typename TI, typename TG>
 int launch_chunk_bwd_typed(const dc::bwdc::Params &p, int64_t bh, cudaStream_t s) {
     using namespace dc::bwdc;
     const int64_t nch = bh * p.nc;
-    const size_t sp = kPrepSmemFloats * sizeof(float), ss = kScanSmemFloats * sizeof(float),
+    // The scan: one CTA per (head, 32-column slice) when those fit in one wave at two per SM, else one
+    // 16-warp CTA per head over every column (the same results bit for bit).
+    const bool wide = bh * p.nslice > 2 * (int64_t)sm_count();
+    const size_t sp = kPrepSmemFloats * sizeof(float),
+                 ss = (wide ? kScanWideSmemFloats : kScanSmemFloats) * sizeof(float),
                  sg = kGradSmemFloats * sizeof(float);
+    auto scan = wide ? scan_wide_kernel : scan_kernel;
     cudaError_t e = cudaFuncSetAttribute(prep_kernel<TI, TG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ss);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ss);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(grad_kernel<TI, TG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sg);
     if (e != cudaSuccess) return cuda_fail(e);
     prep_kernel<TI, TG><<<(unsigned)nch, kThreads, sp, s>>>(p);
-    scan_kernel<<<dim3((unsigned)bh, (unsigned)p.nslice), kThreads, ss, s>>>(p);
+    scan<<<dim3((unsigned)bh, wide ? 1u : (unsigned)p.nslice), wide ? kWideThreads : kThreads, ss, s>>>(p);
     grad_kernel<TI, TG><<<(unsigned)nch, kThreads, sg, s>>>(p);
     e = cudaGetLastError();
     return e == cudaSuccess ? DC_OK : cuda_fail(e);

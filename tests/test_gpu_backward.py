@@ -194,3 +194,23 @@ def test_chunked_and_recurrent_backward_agree():
         if a[n] is not None:
             err = np.abs(a[n] - b[n]).max() / max(1.0, np.abs(b[n]).max())
             assert err < 1e-4, (n, err)
+
+
+def _slice(x, n):
+    """The first n sequences of a `make` case."""
+    return {k: (None if v is None else v[:n]) for k, v in x.items()}
+
+
+def test_full_width_scan_matches_the_oracle_and_the_sliced_scan_bit_for_bit():
+    """80 heads x 4 value slices exceed two CTAs per SM, so the scan takes its full-width form (one 16-warp
+    CTA per head); the first two sequences alone (16 heads) take the sliced form.  Every gradient of those
+    sequences must agree bit for bit, and the full batch must meet the oracle."""
+    x = make(31, 10, 70, 8, 128, 128, 1, "head", 0.95)
+    x["s0"] *= 0.1
+    assert 10 * 8 * 4 > 2 * torch.cuda.get_device_properties(0).multi_processor_count
+    full, _ = gpu_grads(x, 1)
+    part, _ = gpu_grads(_slice(x, 2), 1)
+    for n in NAMES:
+        if full[n] is not None:
+            assert np.array_equal(full[n][:2], part[n]), n
+    print(f"worst relative error {check(x, 1):.2e}")

@@ -142,3 +142,17 @@ def test_chunked_agrees_with_the_cuda_core_kernel_and_repeats_bit_for_bit(b, h):
             (s1 - ss).abs().max().item() / max(1.0, ss.abs().max().item()))
     assert e < F32_TOL, e
     assert abi.lib().dc_device_status(1) == 0
+
+
+def test_full_width_and_sliced_scans_give_the_same_bits():
+    """The batch runs the full-width scan (80 heads x 4 slices > two per SM), its first two sequences alone
+    the sliced one: the same arithmetic in the same order, so y and the state agree bit for bit (the
+    batch x head sharding relies on a batch subset matching its rows of the whole batch)."""
+    raw = config_inputs(1, np.random.default_rng(12), 10, 150, 8, 128, 128)
+    raw["state"] = np.random.default_rng(13).normal(0, 0.05, (10, 8, 128, 128))
+    d = dev_inputs(raw)
+    sub = {k: None if v is None else v[:2].contiguous() for k, v in d.items()}
+    y, st = run(d, 1)
+    y2, st2 = run(sub, 1)
+    torch.cuda.synchronize()
+    assert torch.equal(y[:2], y2) and torch.equal(st[:2], st2)

@@ -405,7 +405,7 @@ def time_prefill_gathered(dn, x, u, steps, warmup, world, mode="peer"):
         drain = lambda: None
     else:
         outs = [torch.empty(world * b, s, H, D, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
-        pgs = [sh.PeerGather(o, shards, streams=GATHER["streams"]) for o in outs]
+        pgs = [sh.PeerGather(o, shards, streams=GATHER["streams"], parts=GATHER["parts"]) for o in outs]
         pending = [[], []]
         b0, b1 = shards[rank].b0, shards[rank].b1
 
@@ -451,7 +451,7 @@ def time_prefill_gathered(dn, x, u, steps, warmup, world, mode="peer"):
 
 # How the multi-GPU steps gather y: "peer" (copy engines, sharding.PeerGather) when every rank can map its
 # peers' buffers, else "nccl"; decided once per run, before any timing, by the same trial on every rank.
-GATHER = {"mode": "nccl", "why": "", "streams": 1}
+GATHER = {"mode": "nccl", "why": "", "streams": 1, "parts": 1}
 
 
 def gathered(dn, x, u, steps, warmup, world):

@@ -101,7 +101,7 @@ class PeerGather:
 
     _opened = {}  # (peer rank, IPC handle) -> [mapped base, references]: one mapping per allocation
 
-    def __init__(self, out: torch.Tensor, shards: List[Shard], group=None, streams: int = 1):
+    def __init__(self, out: torch.Tensor, shards: List[Shard], group=None, streams: int = 1, parts: int = 1):
         import torch.distributed as dist
         from cuda.bindings import driver as drv
 
@@ -167,9 +167,11 @@ class PeerGather:
         self.peers.sort(key=lambda e: (e[0] - rank) % world)
         self.out = out
         self.src = out.data_ptr() + self.offset
+        # `parts` > 1 cuts every copy into that many pieces, piece s of each peer's copy on its own stream.
         n = len(self.peers) if streams <= 0 else min(streams, len(self.peers))
-        self._pool = [torch.cuda.Stream(device=out.device) for _ in range(n)]
-        self.streams = [self._pool[i % n] for i in range(len(self.peers))] if n else []
+        self.parts = max(1, int(parts))
+        self._pool = [torch.cuda.Stream(device=out.device) for _ in range(n * self.parts)] if n else []
+        self.streams = [i % n for i in range(len(self.peers))] if n else []
 
     def push(self, after: torch.cuda.Event) -> List[torch.cuda.Event]:
         """Copy this rank's block into every peer's buffer once ``after`` has fired; returns one event per
@@ -177,9 +179,16 @@ class PeerGather:
         drv = self._drv
         for stream in self._pool:
             stream.wait_event(after)
-        for (_, _, dst), stream in zip(self.peers, self.streams):
-            (err,) = drv.cuMemcpyAsync(dst + self.offset, self.src, self.nbytes, stream.cuda_stream)
-            _check(err, "cuMemcpyAsync")
+        piece = (self.nbytes // self.parts + 15) // 16 * 16
+        for (_, _, dst), si in zip(self.peers, self.streams):
+            for s in range(self.parts):
+                lo = s * piece
+                n = min(piece, self.nbytes - lo)
+                if n <= 0:
+                    continue
+                stream = self._pool[si * self.parts + s]
+                (err,) = drv.cuMemcpyAsync(dst + self.offset + lo, self.src + lo, n, stream.cuda_stream)
+                _check(err, "cuMemcpyAsync")
         done = []
         for stream in self._pool:
             ev = torch.cuda.Event()

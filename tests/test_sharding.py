@@ -152,3 +152,38 @@ def test_a_rank_that_fails_before_the_gather_ends_the_other_ranks_collective_wit
     outcome, secs = q.get(timeout=5)
     assert outcome != "no error", "the gather completed without the failed rank"
     assert secs < 60, f"the surviving rank waited {secs:.0f} s"
+
+
+def _peer_gather_args_worker(rank, world, port, result_q):
+    """PeerGather (the copy-engine gather) refuses, on every rank alike and before any exchange, what it
+    cannot serve: head-split shards, a shard list of the wrong length and a buffer not on the GPU."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        refused = []
+        for out, shards in ((torch.zeros(1, 4), sh.plan(1, 4, world)),      # heads split over the ranks
+                            (torch.zeros(4, 4), sh.plan(4, 4, 1)),          # one shard for two ranks
+                            (torch.zeros(4, 4), sh.plan(4, 4, world))):     # a host buffer
+            try:
+                sh.PeerGather(out, shards)
+                refused.append(False)
+            except ValueError:
+                refused.append(True)
+        dist.barrier()  # the ranks are still in step: nothing above entered a collective
+        result_q.put((rank, all(refused)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_gather_refuses_what_it_cannot_serve_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_gather_args_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert all(ok for _, ok in (q.get(timeout=5) for _ in range(2)))

@@ -166,13 +166,15 @@ __device__ __forceinline__ void product(int M, int N, int K, const float *A, con
 // t = lane % 4): acc[n] = {C(i0+g, j0+8n+2t), C(i0+g, j0+8n+2t+1), C(i0+g+8, j0+8n+2t), C(i0+g+8, j0+8n+2t+1)}.
 // Rows and columns past the caller's extents may be read (they must lie inside the buffers); their
 // outputs are the caller's to drop.
-template <int NT, int AI, int AK, int BK, int BJ>
+// UNR: the k loop's unroll factor (1 where a kernel's code size costs more than the lost overlap: the
+// grad kernel's many products).
+template <int NT, int AI, int AK, int BK, int BJ, int UNR = 2>
 __device__ __forceinline__ void warp_mma3(float (&acc)[NT][4], int i0, int j0, int K, const float *__restrict__ A,
                                           const float *__restrict__ B) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const float *a = A + (i0 + g) * AI + t * AK;
     const float *b = B + t * BK + (j0 + g) * BJ;
-#pragma unroll 2
+#pragma unroll UNR
     for (int k = 0; k < K; k += 8) {
         uint32_t ab[4], as[4];
         ptx::split_tf32(a[k * AK], ab[0], as[0]);
@@ -928,9 +930,9 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const Params p) {
             dgl_part += x.x * y.x + x.y * y.y + x.z * y.z + x.w * y.w;
         }
         if (wown) {
-            warp_mma3<4, kLD, 1, kLD, 1>(aq, wi0, wj0, jn, t0 + jb, bs);  // dy S^T
-            warp_mma3<4, kLD, 1, kLD, 1>(aw, wi0, wj0, jn, t2 + jb, bs);  // dV' S^T
-            warp_mma3<4, kLD, 1, kLD, 1>(ak, wi0, wj0, jn, t1 + jb, bd);  // V' dS_next^T
+            warp_mma3<4, kLD, 1, kLD, 1, 1>(aq, wi0, wj0, jn, t0 + jb, bs);  // dy S^T
+            warp_mma3<4, kLD, 1, kLD, 1, 1>(aw, wi0, wj0, jn, t2 + jb, bs);  // dV' S^T
+            warp_mma3<4, kLD, 1, kLD, 1, 1>(ak, wi0, wj0, jn, t1 + jb, bd);  // V' dS_next^T
         }
         __syncthreads();
     }
@@ -975,8 +977,8 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const Params p) {
     // dT = dV' (w v)^T + dW (b k)^T diag(gam)
     for_warp_tiles<1>(kBL, kBL, [&](int i0, int j0) {
         float a1[1][4] = {{0.f, 0.f, 0.f, 0.f}}, a2[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-        warp_mma3<1, kLD, 1, 1, kLD>(a1, i0, j0, dvp, t2, t7);
-        warp_mma3<1, kLD, 1, 1, kLD>(a2, i0, j0, dkp, t1, t6);
+        warp_mma3<1, kLD, 1, 1, kLD, 1>(a1, i0, j0, dvp, t2, t7);
+        warp_mma3<1, kLD, 1, 1, kLD, 1>(a2, i0, j0, dkp, t1, t6);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const int i = i0 + fg + (q >> 1) * 8, j = j0 + 2 * ft + (q & 1);
@@ -986,7 +988,7 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const Params p) {
     // d(w v) = T^T dV'  ->  d_v = w d(wv), d_write = v d(wv)
     for_warp_tiles<4>(kBL, dvp, [&](int i0, int j0) {
         float acc[4][4] = {};
-        warp_mma3<4, 1, kLS, kLD, 1>(acc, i0, j0, kBL, sT, t2);
+        warp_mma3<4, 1, kLS, kLD, 1, 1>(acc, i0, j0, kBL, sT, t2);
         float vv[4][4], wv[4][4];
 #pragma unroll
         for (int n = 0; n < 4; ++n)
@@ -1018,7 +1020,7 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const Params p) {
     // d(b k gam) = T^T dW: its share of d(b k) (ake, kept in registers) and of dG (rows gp0 / gp1)
     float ake[4][4] = {}, gp0 = 0.f, gp1 = 0.f;
     if (wown) {
-        warp_mma3<4, 1, kLS, kLD, 1>(ake, wi0, wj0, kBL, sT, t1);
+        warp_mma3<4, 1, kLS, kLD, 1, 1>(ake, wi0, wj0, kBL, sT, t1);
 #pragma unroll
         for (int n = 0; n < 4; ++n)
 #pragma unroll
@@ -1034,13 +1036,13 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const Params p) {
     // dA = strict_lower(-T^T dT T^T): X = T^T dT, then dA = -X T^T; Fa = dA D -> sdT, dA A -> sM
     for_warp_tiles<1>(kBL, kBL, [&](int i0, int j0) {
         float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-        warp_mma3<1, 1, kLS, kLS, 1>(acc, i0, j0, kBL, sT, sdT);
+        warp_mma3<1, 1, kLS, kLS, 1, 1>(acc, i0, j0, kBL, sT, sdT);
         frag_store(acc, i0, j0, kBL, kBL, [&](int i, int j, float a) { sX[i * kLS + j] = a; });
     });
     __syncthreads();
     for_warp_tiles<1>(kBL, kBL, [&](int i0, int j0) {
         float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-        warp_mma3<1, kLS, 1, 1, kLS>(acc, i0, j0, kBL, sX, sT);
+        warp_mma3<1, kLS, 1, 1, kLS, 1>(acc, i0, j0, kBL, sX, sT);
         frag_store(acc, i0, j0, kBL, kBL, [&](int i, int j, float a) {
             const float da = j < i ? -a : 0.f;
             sdT[i * kLS + j] = j < i ? da * expf(sG[i] - sG[j]) : 0.f;
@@ -1066,10 +1068,10 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const Params p) {
     float khat_part = 0.f;
     if (wown) {
         float aqk[4][4] = {}, akk[4][4] = {};
-        warp_mma3<4, kLS, 1, kLD, 1>(aqk, wi0, wj0, kBL, sdatt, t5);  // F k
-        warp_mma3<4, 1, kLS, kLD, 1>(akk, wi0, wj0, kBL, sdatt, t4);  // F^T q
-        warp_mma3<4, 1, kLS, kLD, 1>(akk, wi0, wj0, kBL, sdT, t6);    // Fa^T (b k)
-        warp_mma3<4, kLS, 1, kLD, 1>(ake, wi0, wj0, kBL, sdT, t5);    // Fa k
+        warp_mma3<4, kLS, 1, kLD, 1, 1>(aqk, wi0, wj0, kBL, sdatt, t5);  // F k
+        warp_mma3<4, 1, kLS, kLD, 1, 1>(akk, wi0, wj0, kBL, sdatt, t4);  // F^T q
+        warp_mma3<4, 1, kLS, kLD, 1, 1>(akk, wi0, wj0, kBL, sdT, t6);    // Fa^T (b k)
+        warp_mma3<4, kLS, 1, kLD, 1, 1>(ake, wi0, wj0, kBL, sdT, t5);    // Fa k
         float ev[4][4];
 #pragma unroll
         for (int n = 0; n < 4; ++n)

@@ -27,12 +27,13 @@
 // dG within the chunk.  Per-channel log-decays put D inside the key-channel sums and take the
 // token-by-token backward (bwd_recurrent.cuh) instead.
 //
-// Three kernels, fp32 on the CUDA cores (register-tiled products over shared memory), every output
-// element written once (deterministic):
+// Three kernels over fp32 data, every product on the tensor cores as three mma.sync tf32 products of
+// split operands (about fp32 accuracy), every output element written once (deterministic):
 //   prep_kernel  one CTA per (batch x head, chunk): T, A, att, W, U, Q', K^, gam_L into the workspace;
 //   scan_kernel  one CTA per (batch x head, 32 value columns): the forward pass over the chunks, storing
 //                each chunk's starting S (transposed) and V', then the reverse pass, storing dS_next
-//                (transposed) and dV', and finally dS0;
+//                (transposed) and dV', and finally dS0 (scan_wide_kernel: the same over every value
+//                column of a head, when the slices would not fit on the SMs in one wave);
 //   grad_kernel  one CTA per (batch x head, chunk): every input gradient of the chunk's rows.
 #pragma once
 
@@ -68,96 +69,6 @@ struct Params {
     int32_t dkp, dvp, nslice;
     int32_t dy_vec;              // dy rows are 16-byte aligned (dv % 4 == 0): copied by cp.async
 };
-
-// ---------------------------------------------------------------------------------------------------
-// Register-tiled products.  acc[r][c] += sum_{k<K} A(i0 + r, k) B(k, j0 + c) with
-// A(i, k) = A[i * AI + k * AK] and B(k, j) = B[k * BK + j * BJ]; K is a multiple of 4, and the loads
-// are float4 / float2 wherever the layout puts consecutive elements together (16-byte aligned bases,
-// strides that are multiples of 4 floats).
-// ---------------------------------------------------------------------------------------------------
-template <int TM, int TN, int AI, int AK, int BK, int BJ>
-__device__ __forceinline__ void tile_madd(float (&acc)[TM][TN], int i0, int j0, int K, const float *__restrict__ A,
-                                          const float *__restrict__ B) {
-    const float *a = A + i0 * AI, *b = B + j0 * BJ;
-#pragma unroll 2
-    for (int k = 0; k < K; k += 4) {
-        float av[TM][4], bv[4][TN];
-        if constexpr (AK == 1) {
-#pragma unroll
-            for (int r = 0; r < TM; ++r) {
-                const float4 t = *reinterpret_cast<const float4 *>(a + r * AI + k);
-                av[r][0] = t.x, av[r][1] = t.y, av[r][2] = t.z, av[r][3] = t.w;
-            }
-        } else if constexpr (AI == 1 && TM == 4) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const float4 t = *reinterpret_cast<const float4 *>(a + (k + kk) * AK);
-                av[0][kk] = t.x, av[1][kk] = t.y, av[2][kk] = t.z, av[3][kk] = t.w;
-            }
-        } else if constexpr (AI == 1 && TM == 2) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const float2 t = *reinterpret_cast<const float2 *>(a + (k + kk) * AK);
-                av[0][kk] = t.x, av[1][kk] = t.y;
-            }
-        } else {
-#pragma unroll
-            for (int r = 0; r < TM; ++r)
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) av[r][kk] = a[r * AI + (k + kk) * AK];
-        }
-        if constexpr (BJ == 1 && TN == 4) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const float4 t = *reinterpret_cast<const float4 *>(b + (k + kk) * BK);
-                bv[kk][0] = t.x, bv[kk][1] = t.y, bv[kk][2] = t.z, bv[kk][3] = t.w;
-            }
-        } else if constexpr (BJ == 1 && TN == 2) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const float2 t = *reinterpret_cast<const float2 *>(b + (k + kk) * BK);
-                bv[kk][0] = t.x, bv[kk][1] = t.y;
-            }
-        } else if constexpr (BK == 1) {
-#pragma unroll
-            for (int c = 0; c < TN; ++c) {
-                const float4 t = *reinterpret_cast<const float4 *>(b + c * BJ + k);
-                bv[0][c] = t.x, bv[1][c] = t.y, bv[2][c] = t.z, bv[3][c] = t.w;
-            }
-        } else {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-                for (int c = 0; c < TN; ++c) bv[kk][c] = b[(k + kk) * BK + c * BJ];
-        }
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-            for (int r = 0; r < TM; ++r)
-#pragma unroll
-                for (int c = 0; c < TN; ++c) acc[r][c] = fmaf(av[r][kk], bv[kk][c], acc[r][c]);
-    }
-}
-
-// Every output (i, j), i < M, j < N (multiples of TM, TN) of the product above, tiles dealt round robin
-// over the CTA's threads; epi(i, j, value) consumes each once.
-template <int TM, int TN, int AI, int AK, int BK, int BJ, class Epi>
-__device__ __forceinline__ void product(int M, int N, int K, const float *A, const float *B, Epi &&epi) {
-    const int tn = N / TN, tiles = (M / TM) * tn;
-    for (int t = threadIdx.x; t < tiles; t += kThreads) {
-        const int i0 = t / tn * TM, j0 = t % tn * TN;
-        float acc[TM][TN];
-#pragma unroll
-        for (int r = 0; r < TM; ++r)
-#pragma unroll
-            for (int c = 0; c < TN; ++c) acc[r][c] = 0.f;
-        tile_madd<TM, TN, AI, AK, BK, BJ>(acc, i0, j0, K, A, B);
-#pragma unroll
-        for (int r = 0; r < TM; ++r)
-#pragma unroll
-            for (int c = 0; c < TN; ++c) epi(i0 + r, j0 + c, acc[r][c]);
-    }
-}
 
 // One warp on the tensor cores: acc[n], the 16 x 8 tile at rows i0.., columns j0 + 8n.., += A(i, k) B(k, j)
 // over k < K (a multiple of 8), with A(i, k) = A[i * AI + k * AK] and B(k, j) = B[k * BK + j * BJ].  Each
@@ -936,9 +847,11 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const Params p) {
         }
         __syncthreads();
     }
-    // datt = lower(dy V'^T)
-    product<2, 2, kLD, 1, 1, kLD>(kBL, kBL, dvp, t0, t1, [&](int i, int j, float a) {
-        sdatt[i * kLS + j] = j <= i ? a : 0.f;
+    // datt = lower(dy V'^T), on the tensor cores like the other products
+    for_warp_tiles<1>(kBL, kBL, [&](int i0, int j0) {
+        float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+        warp_mma3<1, kLD, 1, 1, kLD, 1>(acc, i0, j0, dvp, t0, t1);
+        frag_store(acc, i0, j0, kBL, kBL, [&](int i, int j, float a) { sdatt[i * kLS + j] = j <= i ? a : 0.f; });
     });
     {
         float v = dgl_part;

@@ -5,7 +5,7 @@ sequences (copies in, kernels, copies out on three streams, two slices in
 flight).  Every kernel path works per (batch, head), so the results must be
 bit-identical to dc_chunk_fwd on device copies of the same inputs: the fused
 tensor-core kernel, the two-kernel per-channel-gate path (whose workspace the
-slices share) and the CUDA-core kernel."""
+slices share), the fp32-accurate chunked path and the CUDA-core kernel."""
 import importlib
 import math
 
@@ -68,6 +68,15 @@ def test_host_path_equals_device_path_per_channel_gates():
 
 def test_host_path_equals_device_path_cuda_cores():
     t = host_inputs(1, 4, 90, 2, 32, in_dtype=torch.float32)
+    (y_d, s_d), (y_h, s_h) = both(t, force_simt=True)
+    assert torch.equal(y_d, y_h) and torch.equal(s_d, s_h)
+
+
+def test_host_path_equals_device_path_fp32_chunked():
+    """float32 inputs take the fp32-accurate chunked path on both sides.  The whole batch (160 heads x 4
+    value slices) runs its full-width scan on the device, while the host path's slices of three sequences
+    (24 heads) run the sliced scan: the two forms give the same bits, so the results still match exactly."""
+    t = host_inputs(1, 20, 70, 8, 128, in_dtype=torch.float32)
     (y_d, s_d), (y_h, s_h) = both(t)
     assert torch.equal(y_d, y_h) and torch.equal(s_d, s_h)
 

@@ -129,3 +129,26 @@ def test_chunk_out_norm_repeat_calls_are_bit_identical_and_rows_of_zeros_stay_ze
     assert torch.equal(y1, y2) and torch.equal(s1, s2)
     assert torch.equal(yz, torch.zeros_like(yz)) and torch.equal(sz, zs)
     assert abi.lib().dc_device_status(1) == 0
+
+
+def test_chunk_out_norm_on_the_fp32_chunked_path():
+    """float32 q / k / v take the fp32-accurate chunked prefill; the plain norm then runs as dc_out_norm in
+    place on y, within the fp32 path's 1e-4 of the float64 recurrence and norm."""
+    rng = np.random.default_rng(41)
+    raw = config_inputs("gdn", rng, 2, 150, 3, 64, 64)
+    raw["state"] = rng.normal(0, 0.05, (2, 3, 64, 64))
+    dev = {n: None if raw[n] is None else torch.from_numpy(np.ascontiguousarray(raw[n])).to("cuda", torch.float32)
+           for n in ("q", "k", "v", "erase", "write", "g", "state")}
+    w = torch.from_numpy(rng.uniform(0.5, 1.5, 64)).to("cuda", torch.float32)
+    args = (dev["q"], dev["k"], dev["v"], dev["erase"], dev["write"], dev["g"], dev["state"], True, 64,
+            1.0 / math.sqrt(64))
+    assert dn.chunk_out_norm_is_fused(*args[:9], w) is False
+    y, s = dn.delta_chunk_recalculated_out_norm(*args, w, None, 1e-5)
+    torch.cuda.synchronize()
+    y_o, s_o = oracle.householder("recurrent", raw["q"], raw["k"], raw["v"], raw["erase"], raw["write"], raw["g"],
+                                  raw["state"], 1, scale=1.0 / math.sqrt(64))
+    ref = oracle.out_norm(y_o, None, w.double().cpu().numpy(), 1e-5)
+    e_y = np.abs(y.double().cpu().numpy() - ref).max() / max(1.0, np.abs(ref).max())
+    e_s = np.abs(s.double().cpu().numpy() - s_o).max() / max(1.0, np.abs(s_o).max())
+    assert e_y < 1e-4 and e_s < 1e-4, (e_y, e_s)
+    assert abi.lib().dc_device_status(1) == 0
